@@ -1,0 +1,428 @@
+"""DSpark draft + verify attention benchmark on B200 (see BASELINE.json `metric`).
+
+One step = one speculative round's attention on one GPU:
+  * draft (config 2): 64 requests, context ~ U[128, 4096] (seed 1), one 7-row block
+    each, non-causal attention for each of the 5 draft layers (B200DraftKernel);
+  * verify (config 3): 128 requests, cached context ~ U[256, 8192] (seed 2), 7 new
+    tokens each; for each of 28 layers the fused QK-norm + RoPE(1e6) + KV append +
+    bottom-right attention (B200PersistentTargetKV.verify_layer), then one commit of
+    the accepted prefixes (accept ~ U{0..6} + anchor) and rollback of the rest.
+Metric: query-token-layers per second = (64*7*5 + 128*7*28) / step time, summed
+over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank).
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
+path; one NCCL all_gather of per-rank stats after timing.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, 'tests', 'golden'))
+
+HQ, HKV, D, BLOCK = 16, 8, 128, 7
+KV_ROW = 2 * HKV * D * 2             # bytes of one token's K+V for one layer (bf16)
+Q_ROW = HQ * D * 2                   # bytes of one query row (bf16)
+DRAFT = dict(requests=64, ctx_lo=128, ctx_hi=4096, seed=1, layers=5)
+VERIFY = dict(requests=128, ctx_lo=256, ctx_hi=8192, seed=2, layers=28, q=7)
+METRIC = 'draft+verify attn query-tok/s per GPU & at 1/2/4/8 B200; % of HBM roofline'
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, 'MEASURED_PEAKS.json')) as f:
+            p = json.load(f)
+        return float(p['hbm_gbs']), 'measured'
+    except Exception:
+        return FALLBACK_HBM_GBS, 'fallback'
+
+
+def dist_env():
+    return int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), int(os.environ.get('LOCAL_RANK', 0))
+
+
+def contexts(cfg, rank):
+    import numpy as np
+    g = np.random.Generator(np.random.PCG64(cfg['seed'] * 1000 + rank))
+    return [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
+
+
+def query_units():
+    return DRAFT['requests'] * BLOCK * DRAFT['layers'] + VERIFY['requests'] * VERIFY['q'] * VERIFY['layers']
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
+              'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
+              'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
+
+    def __init__(self, gpu):
+        self.gpu, self.proc = gpu, None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.gpu), f'--query-gpu={self.FIELDS}',
+                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except Exception:
+                self.proc.kill()
+                out = ''
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
+        for ln in getattr(self, 'lines', []):
+            f = [x.strip() for x in ln.split(',')]
+            try:
+                sm.append(float(f[1]))
+                mx = max(mx, float(f[2]))
+            except (ValueError, IndexError):
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == 'active':
+                    reasons.add(name)
+        return dict(sm_mhz=statistics.median(sm) if sm else None, sm_max_mhz=mx or None,
+                    reasons=sorted(reasons), samples=len(sm))
+
+
+# --------------------------------------------------------------------------- workload
+class Workload:
+    """Device-resident synthetic inputs of one rank (inputs larger than L2: ~62 GB of KV)."""
+
+    def __init__(self, pkg, device, rank, steps_total):
+        import torch
+        self.pkg, self.device = pkg, device
+        gen = torch.Generator(device=device)
+        gen.manual_seed(1234 + rank)
+        bf = torch.bfloat16
+
+        def randn(*shape):
+            return torch.randn(*shape, device=device, dtype=bf, generator=gen)
+
+        # draft: packed [sum(c+7), 8, 128] K/V per layer (context cache rows + block rows)
+        self.draft_ctx = contexts(DRAFT, rank)
+        self.draft_qlens = [BLOCK] * DRAFT['requests']
+        self.draft_klens = [c + BLOCK for c in self.draft_ctx]
+        self.draft_layout = pkg.PackedLayout.from_lengths(self.draft_qlens, self.draft_klens, device)
+        nk = sum(self.draft_klens)
+        nq = sum(self.draft_qlens)
+        self.draft_k = [randn(nk, HKV, D) for _ in range(DRAFT['layers'])]
+        self.draft_v = [randn(nk, HKV, D) for _ in range(DRAFT['layers'])]
+        self.draft_q = [randn(nq, HQ, D) for _ in range(DRAFT['layers'])]
+        self.draft_kernel = pkg.B200DraftKernel(device)
+        # verify: ragged persistent store, capacity = context + growth of every step
+        self.verify_ctx = contexts(VERIFY, rank)
+        L, R, Q = VERIFY['layers'], VERIFY['requests'], VERIFY['q']
+        growth = Q * (steps_total + 2)
+        caps = [c + growth for c in self.verify_ctx]
+        self.store = pkg.B200PersistentTargetKV(layers=L, slots=R, context_capacity=max(caps),
+                                                max_query_tokens=R * Q, device=device, slot_capacities=caps)
+        self.handles = [self.store.add_request(f'r{i}') for i in range(R)]
+        # fill resident prefixes layer by layer (random N(0,1) bf16; values do not affect speed)
+        rows = self.store.rows_per_layer
+        for buf in (self.store._keys, self.store._values):
+            for layer in range(L):
+                buf[layer * rows:(layer + 1) * rows].normal_(generator=gen)
+        for h, c in zip(self.handles, self.verify_ctx):
+            self.store._lengths[h.index] = c
+        nqv = R * Q
+        self.vq = [randn(nqv, HQ, D) for _ in range(L)]
+        self.vk = [randn(nqv, HKV, D) for _ in range(L)]
+        self.vv = [randn(nqv, HKV, D) for _ in range(L)]
+        self.qw = torch.ones(D, dtype=bf, device=device)
+        self.kw = torch.ones(D, dtype=bf, device=device)
+        self.inv_freq = pkg.rope_inv_freq(1e6, device=device)
+        import numpy as np
+        self.accept_rng = np.random.Generator(np.random.PCG64(VERIFY['seed'] * 7919 + rank))
+        torch.cuda.synchronize(device)
+
+    # algorithmic bytes (K/V read once, Q read, O written) -------------------------
+    def draft_layer_bytes(self):
+        return sum(self.draft_klens) * KV_ROW + 2 * sum(self.draft_qlens) * Q_ROW
+
+    def verify_layer_bytes(self, contexts_now):
+        R, Q = VERIFY['requests'], VERIFY['q']
+        attn = (sum(contexts_now) + R * Q) * KV_ROW + 2 * R * Q * Q_ROW
+        prologue = R * Q * (Q_ROW + KV_ROW) * 2      # raw q/k/v read, roped q + k/v written
+        return attn + prologue
+
+    def step(self, events=None, host=None):
+        """One round. ``events``: list to append (start, end, kind) CUDA event pairs per layer.
+        ``host``: pinned host buffers for the end-to-end path (inputs copied in, outputs out)."""
+        import torch
+        launches = 0
+        for layer in range(DRAFT['layers']):
+            e0 = self._event(events)
+            q = self.draft_q[layer]
+            if host is not None:
+                q = host['dq'][layer].to(self.device, non_blocking=True)
+            out = self.draft_kernel(q, self.draft_k[layer], self.draft_v[layer], self.draft_layout,
+                                    scale=D ** -0.5)
+            if host is not None:
+                host['do'][layer].copy_(out, non_blocking=True)
+            launches += 2
+            self._close(events, e0, 'draft')
+        store = self.store
+        tx = store.begin(self.handles, query_lengths=[VERIFY['q']] * VERIFY['requests'])
+        ctx_now = tx.context_lengths
+        for layer in range(VERIFY['layers']):
+            e0 = self._event(events)
+            qr, kr, vr = self.vq[layer], self.vk[layer], self.vv[layer]
+            if host is not None:
+                qr = host['vq'][layer].to(self.device, non_blocking=True)
+                kr = host['vk'][layer].to(self.device, non_blocking=True)
+                vr = host['vv'][layer].to(self.device, non_blocking=True)
+            out = store.verify_layer(tx, layer, qr, kr, vr, self.qw, self.kw, inv_freq=self.inv_freq)
+            if host is not None:
+                host['vo'][layer].copy_(out, non_blocking=True)
+            launches += 3
+            self._close(events, e0, 'verify', ctx_now)
+        accept = self.accept_rng.integers(0, 7, VERIFY['requests'])
+        store.commit(tx, {h: int(a) + 1 for h, a in zip(self.handles, accept)})
+        launches += 1
+        return launches
+
+    @staticmethod
+    def _event(events):
+        if events is None:
+            return None
+        import torch
+        e = torch.cuda.Event(enable_timing=True)
+        e.record()
+        return e
+
+    @staticmethod
+    def _close(events, e0, kind, ctx=None):
+        if events is None:
+            return
+        import torch
+        e1 = torch.cuda.Event(enable_timing=True)
+        e1.record()
+        events.append((e0, e1, kind, ctx))
+
+    def pinned_host(self):
+        import torch
+        pin = lambda t: t.cpu().pin_memory()  # noqa: E731
+        return dict(dq=[pin(q) for q in self.draft_q], vq=[pin(x) for x in self.vq], vk=[pin(x) for x in self.vk],
+                    vv=[pin(x) for x in self.vv],
+                    do=[torch.empty(q.shape, dtype=q.dtype).pin_memory() for q in self.draft_q],
+                    vo=[torch.empty(x.shape, dtype=x.dtype).pin_memory() for x in self.vq])
+
+    def host_bytes(self, host):
+        h2d = sum(t.numel() * t.element_size() for k in ('dq', 'vq', 'vk', 'vv') for t in host[k])
+        d2h = sum(t.numel() * t.element_size() for k in ('do', 'vo') for t in host[k])
+        return h2d, d2h
+
+
+# --------------------------------------------------------------------------- CPU legs
+def cpu_sample(seconds=12.0, rank=0):
+    """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
+    per repetition 8 draft requests (1 layer) + 8 verify requests (1 layer, QK-norm/RoPE +
+    bottom-right attention), until ``seconds`` of wall time. Returns query-tok/s."""
+    import numpy as np
+    from oracle import bottom_right_varlen, noncausal_varlen, qk_norm_rope_bf16
+    import inputs as I
+    g = I.rng(99)
+    dctx = contexts(DRAFT, rank)[:8]
+    vctx = contexts(VERIFY, rank)[:8]
+    dq = g.standard_normal((8 * BLOCK, HQ, D), dtype=np.float32)
+    dk = g.standard_normal((sum(dctx) + 8 * BLOCK, HKV, D), dtype=np.float32)
+    dv = g.standard_normal(dk.shape, dtype=np.float32)
+    vq = g.standard_normal((8 * VERIFY['q'], HQ, D), dtype=np.float32)
+    vk = g.standard_normal((sum(vctx) + 8 * VERIFY['q'], HKV, D), dtype=np.float32)
+    vv = g.standard_normal(vk.shape, dtype=np.float32)
+    from oracle import f32_to_bf16_bits
+    qb = f32_to_bf16_bits(vq)
+    kb = f32_to_bf16_bits(vk[:8 * VERIFY['q']])
+    ones = f32_to_bf16_bits(np.ones(D, np.float32))
+    pos = np.concatenate([np.arange(c, c + VERIFY['q']) for c in vctx])
+    reps, units, t0 = 0, 0, time.perf_counter()
+    while True:
+        noncausal_varlen(dq, dk, dv, [BLOCK] * 8, [c + BLOCK for c in dctx], D ** -0.5, np.float32)
+        qk_norm_rope_bf16(qb, kb, ones, ones, pos, 1e6, 1e-6)
+        bottom_right_varlen(vq, vk, vv, [VERIFY['q']] * 8, [c + VERIFY['q'] for c in vctx], D ** -0.5, np.float32)
+        reps += 1
+        units += 8 * BLOCK + 8 * VERIFY['q']
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return units / el, reps, el
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import numpy as np  # noqa: F401
+    cores = host_threads()
+    os.environ.setdefault('OMP_NUM_THREADS', str(cores))
+    vals = []
+    for _ in range(args.warmup):
+        cpu_sample(seconds=1.0)
+    t_all = 0.0
+    for _ in range(args.steps):
+        v, reps, el = cpu_sample(seconds=max(2.0, 20.0 / max(args.steps, 1)))
+        vals.append(v)
+        t_all += el
+    value = statistics.median(vals)
+    units = query_units()
+    print(json.dumps(dict(
+        impl='reference', metric=METRIC, value=value, unit='query-tok/s', n_gpus=args.gpus, steps=args.steps,
+        warmup=args.warmup, ms_per_step=units / value * 1e3, higher_is_better=True, scaling='weak',
+        vs_baseline=None, dtype='f32', data='synthetic',
+        config=dict(workload='cfg2 draft x5 layers + cfg3 verify x28 layers (CPU oracle port, bounded sample)',
+                    parallelism='host threads'),
+        cpu_baseline=dict(value=value, unit='query-tok/s', cores=cores, kind='port',
+                          sample='per step: 8 cfg2 draft requests x1 layer + 8 cfg3 verify requests x1 layer '
+                                 '(QK-norm/RoPE + bottom-right attention), numpy float32, repeated ~%.0f s'
+                                 % (t_all / max(args.steps, 1))),
+        e2e=dict(value=value, unit='query-tok/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def run_b200(args):
+    import importlib
+    import torch
+    import torch.distributed as dist
+    rank, world, local = dist_env()
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120))
+    device = torch.device('cuda', local)
+    torch.cuda.set_device(device)
+    pkg = importlib.import_module('qwen3-dspark_b200')
+    pkg.read_device_status(clear=True)
+    wl = Workload(pkg, device, rank, args.warmup + 2 * args.steps + 4)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    for _ in range(args.warmup):
+        wl.step()
+    barrier()
+    # ---- device-resident timed region (value) ----
+    events = []
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        start.record()
+        launches = 0
+        for _ in range(args.steps):
+            launches += wl.step(events)
+        end.record()
+        barrier()
+    elapsed_ms = start.elapsed_time(end)
+    # ---- end-to-end through the public API with pinned host buffers ----
+    host = wl.pinned_host()
+    wl.step(host=host)
+    barrier()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record()
+    for _ in range(args.steps):
+        wl.step(host=host)
+    e_end.record()
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+    status = pkg.read_device_status(clear=True)
+    # per-layer event durations inside the timed region
+    per = {'draft': [], 'verify': []}
+    vbytes = []
+    for e0, e1, kind, ctx in events:
+        per[kind].append(e0.elapsed_time(e1))
+        if kind == 'verify':
+            vbytes.append(wl.verify_layer_bytes(ctx))
+    stats = torch.tensor([elapsed_ms, e2e_ms, float(status)], dtype=torch.float64, device=device)
+    if world > 1:
+        gathered = [torch.zeros_like(stats) for _ in range(world)]
+        dist.all_gather(gathered, stats)
+        allstats = torch.stack(gathered).cpu()
+    else:
+        allstats = stats[None].cpu()
+    if rank == 0:
+        max_ms = float(allstats[:, 0].max())
+        max_e2e = float(allstats[:, 1].max())
+        units = query_units() * args.steps * world
+        value = units / (max_ms / 1e3)
+        e2e_value = units / (max_e2e / 1e3)
+        hbm, peak_kind = peaks()
+        v_ms = statistics.mean(per['verify'])
+        v_bytes = statistics.mean(vbytes)
+        achieved = v_bytes / (v_ms / 1e3) / 1e9
+        d_ms = statistics.mean(per['draft'])
+        d_achieved = wl.draft_layer_bytes() / (d_ms / 1e3) / 1e9
+        h2d, d2h = wl.host_bytes(host)
+        cpu_v, reps, el = cpu_sample(seconds=12.0)
+        line = dict(
+            metric=METRIC, value=value, unit='query-tok/s', n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=max_ms / args.steps, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
+            data='synthetic (seeded N(0,1) q/k/v and KV cache; shapes of BASELINE configs 2 and 3)',
+            config=dict(workload='cfg2 draft x5 layers + cfg3 verify x28 layers (+ commit/rollback) per step',
+                        draft_requests=DRAFT['requests'], draft_ctx='U[128,4096] seed 1', verify_requests=VERIFY['requests'],
+                        verify_ctx='U[256,8192] seed 2', verify_q=VERIFY['q'], heads='16/8', head_dim=D,
+                        rope_theta=1e6, rms_eps=1e-6, parallelism=f'dp{world} (independent request batches)',
+                        l2='inputs larger than L2 (~62 GB resident KV per GPU)'),
+            roofline=dict(kernel='verify layer: qk-norm/rope/append + bottom-right attention + split merge',
+                          bound='hbm', achieved=achieved, peak=hbm, unit='GB/s', frac=achieved / hbm,
+                          peak_source=f'{peak_kind} hbm_gbs', traffic=None,
+                          alg_bytes_per_launch=v_bytes, avg_launch_ms=v_ms),
+            draft_roofline=dict(kernel='draft layer: non-causal attention + split merge', achieved=d_achieved,
+                                frac=d_achieved / hbm, alg_bytes_per_launch=wl.draft_layer_bytes(), avg_launch_ms=d_ms),
+            cpu_baseline=dict(value=cpu_v, unit='query-tok/s', cores=host_threads(), kind='port',
+                              sample=f'{reps} reps of 8 cfg2 draft + 8 cfg3 verify requests x1 layer, numpy float32, '
+                                     f'{el:.1f} s'),
+            e2e=dict(value=e2e_value, unit='query-tok/s', h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                     path='B200DraftKernel / B200PersistentTargetKV.verify_layer with pinned host q/k/v in, '
+                          'attention outputs out'),
+            gpu_launches=launches * world, clocks=clocks.summary(), device_status=int(allstats[:, 2].max()))
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument('--gpus', type=int, default=1)
+    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--warmup', type=int, default=5)
+    ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == 'reference':
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == '__main__':
+    main()

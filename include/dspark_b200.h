@@ -1,0 +1,145 @@
+/*
+ * dspark_b200.h - C ABI of the B200 (sm_100a) DSpark draft/verify attention library.
+ *
+ * All tensors are device pointers on the calling thread's current CUDA device;
+ * every launch goes to `stream`. Shapes follow the Qwen3-0.6B attention of the
+ * reference: 16 query heads, 8 KV heads, head dim 128, packed "THD" rows:
+ *   queries  [total_q, 16, 128]      keys/values  [rows, 8, 128]
+ * Query head h reads KV head h / 2 (GQA). `cu_q`/`cu_k` are int32 cumulative
+ * row offsets with num_requests + 1 entries, as in the reference's PackedLayout.
+ *
+ * Return value: DSPARK_OK or an error status; nothing is launched when an
+ * argument check fails. Values inside device arrays are not read on the host;
+ * kernels that meet an out-of-range index skip it and set a bit in the device
+ * status word (dspark_read_device_status). No entry point allocates memory;
+ * bf16 attention needs a caller-owned workspace of
+ * dspark_attention_workspace_size() bytes, which calls on one stream may share.
+ */
+#ifndef DSPARK_B200_H_
+#define DSPARK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+#include <cuda_runtime_api.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DSPARK_ABI_VERSION 1
+
+#define DSPARK_OK 0
+#define DSPARK_ERR_INVALID_ARGUMENT 1
+#define DSPARK_ERR_UNSUPPORTED 2
+#define DSPARK_ERR_CUDA 3
+
+#define DSPARK_DTYPE_BF16 0
+#define DSPARK_DTYPE_F32 1
+
+/* Device status bits (set by kernels, read with dspark_read_device_status). */
+#define DSPARK_DEVICE_WAIT_TIMEOUT 1u
+#define DSPARK_DEVICE_BAD_SCHEDULE 2u
+#define DSPARK_DEVICE_BAD_ARGUMENT 4u
+
+int dspark_abi_version(void);
+const char* dspark_status_string(int status);
+
+/* Bytes of workspace the bf16 attention entry points need on `device`
+ * (split-item partials; scales with the SM count, ~19 MB on a B200). */
+int dspark_attention_workspace_size(int device, size_t* bytes);
+
+/* Copies the device status word of the current device (synchronising), and
+ * clears it when `clear` is non-zero. */
+int dspark_read_device_status(unsigned int* status, int clear);
+
+/*
+ * Non-causal packed varlen attention: every query row of request i sees all
+ * keys rows [cu_k[i], cu_k[i+1]).
+ * Replaces PinnedRocmDraftKernel.__call__ (dspark_qwen/packed_draft.py:23-32),
+ * i.e. aten::_flash_attention_forward(q, k, v, cu_q, cu_k, max_q, max_k, 0.0,
+ * is_causal=False, ...); CPU oracle test_only_noncausal_varlen (packed_draft.py:35-47).
+ * dtype DSPARK_DTYPE_BF16 (tensor cores) or DSPARK_DTYPE_F32 (exact CUDA-core path).
+ * key_rows = rows of k/v (>= cu_k[num_requests]); max_q/max_k as in the reference call.
+ */
+int dspark_draft_attn(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                      int num_requests, int total_q, long long key_rows, int max_q, int max_k, float scale,
+                      int dtype, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Bottom-right causal packed varlen attention: query r of a request with q
+ * queries and k keys sees key j iff j <= k - q + r. Rows of k/v after
+ * cu_k[num_requests] (a capacity tail, key_rows beyond it) are never read.
+ * Replaces PinnedRocmVarlenKernel.__call__ (dspark_qwen/rocm_varlen.py:108-117)
+ * and the capacity-tail call PersistentQwenTarget._native_attention
+ * (dspark_qwen/persistent_qwen_target.py:223-234); CPU oracles
+ * test_only_dense_varlen (varlen_target.py:98-112) and test_only_persistent_sdpa
+ * (persistent_qwen_target.py:30-42).
+ */
+int dspark_varlen_attn(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                       int num_requests, int total_q, long long key_rows, int max_q, int max_k, float scale,
+                       int dtype, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Two-source attention without a gather copy: keys of request i are rows
+ * [a_off + a_start[i], + a_len[i]) of (ka, va) followed by rows
+ * [b_off + b_start[i], + b_len[i]) of (kb, vb). kb == NULL drops the second
+ * source; b_start == NULL means b_off + cu_q[i] and b_len == NULL means the
+ * request's query count (the verify-scratch convention). causal selects the
+ * bottom-right mask over the concatenated keys.
+ * Replaces the concat + index_select + kernel call of PackedDraft.backbone
+ * (dspark_qwen/packed_draft.py:215-236), the resident+scratch gather of
+ * PersistentTargetKV.prepare_attention (persistent_target_kv.py:441-460) feeding
+ * _native_attention, and the training-layout block-mask SDPA of
+ * DraftAttention.forward with block_mask (dspark_qwen/model.py:12-19,47-61)
+ * when each block is one request (context rows [0, anchor) + its 7 block rows).
+ */
+int dspark_segment_attn(const void* q, const void* ka, const void* va, long long rows_a, const void* kb,
+                        const void* vb, long long rows_b, const int32_t* cu_q, const int32_t* a_start,
+                        const int32_t* a_len, const int32_t* b_start, const int32_t* b_len, int a_off, int b_off,
+                        int num_requests, int total_q, int max_q, int causal, float scale, int dtype, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Fused verify layer for a persistent KV store (bf16):
+ *  1. Qwen3 q_norm/k_norm (RMSNorm over the head dim, eps) and rotate-half RoPE
+ *     (inv_freq [64] float32) of the new tokens' raw projections, at position
+ *     ctx_len[i] + r for new row r of request i;
+ *  2. KV append: roped k and raw v into scratch rows layer*scratch_rows + cu_q[i] + r;
+ *     roped q into q_roped [total_q, 16, 128];
+ *  3. bottom-right causal attention over the resident prefix rows
+ *     layer*rows_per_layer + slot_row[i] + [0, ctx_len[i]) followed by the
+ *     request's scratch rows, read in place (no workspace gather).
+ * Resident K/V: [num_layers * rows_per_layer, 8, 128]; scratch K/V:
+ * [num_layers * scratch_rows, 8, 128].
+ * Replaces, per decoder layer, transformers Qwen3Attention.forward's
+ * q_norm/k_norm/apply_rotary_pos_emb (modeling_qwen3.py:263-268) plus
+ * _VerificationCache.update (dspark_qwen/persistent_qwen_target.py:73-83:
+ * PersistentTargetKV.stage_layer + prepare_attention, persistent_target_kv.py:427-460)
+ * plus persistent_attention_forward -> _native_attention (persistent_qwen_target.py:45-60,223-234).
+ */
+int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
+                        const void* k_norm_weight, const float* inv_freq, float eps, const int32_t* cu_q,
+                        const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
+                        void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* q_roped,
+                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * Commit / rollback for all layers in one launch: for every request copy
+ * scratch rows [cu_q[i], cu_q[i] + n_commit[i]) of each layer into resident rows
+ * slot_row[i] + [ctx_len[i], ctx_len[i] + n_commit[i]). Rows past n_commit
+ * (the rejected drafts) are not copied, which is the rollback. Requires
+ * 0 <= n_commit[i] <= q_i and ctx_len[i] + n_commit[i] <= slot_cap[i].
+ * Replaces PersistentTargetKV.commit (dspark_qwen/persistent_target_kv.py:463-491);
+ * abort (493-499) needs no device work.
+ */
+int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,
+                     const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
+                     const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
+                     int scratch_rows, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSPARK_B200_H_ */

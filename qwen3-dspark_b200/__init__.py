@@ -1,0 +1,28 @@
+"""B200-native (sm_100a) DSpark draft/verify attention.
+
+Drop-in replacements for the two attention hot paths of qwen3-dspark:
+
+* packed varlen block-draft attention (non-causal): ``B200DraftKernel``;
+* KV-cached GQA verify attention (bottom-right causal): ``B200VarlenKernel``,
+  ``B200CapacityKernel``, and ``B200PersistentTargetKV`` with the fused
+  QK-norm + RoPE + KV-append verify layer and one-launch commit/rollback.
+
+The kernels live in ``lib/libdspark_b200.so`` (C ABI, include/dspark_b200.h),
+built from ``csrc/`` by ``build.py``. Importing this package does not touch
+the GPU; constructing a kernel object loads the library and fails loudly if it
+is missing or the device is not an sm_100 GPU.
+"""
+from . import _lib
+from .build import LIB_PATH, build
+from .kernels import (BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, B200CapacityKernel, B200DraftKernel,
+                      B200VarlenKernel, runtime_identity, segment_attention)
+from .kv_store import B200PersistentTargetKV, Slot, Transaction, rope_inv_freq
+from .layout import PackedLayout, PersistentAttentionLayout
+
+load_library = _lib.load_library
+read_device_status = _lib.read_device_status
+
+__all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'B200CapacityKernel', 'B200DraftKernel',
+           'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH', 'PackedLayout', 'PersistentAttentionLayout',
+           'Slot', 'Transaction', 'build', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
+           'segment_attention']

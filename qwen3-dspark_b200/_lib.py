@@ -1,0 +1,87 @@
+"""ctypes binding of the C ABI in include/dspark_b200.h.
+
+The shared library is loaded from this package's ``lib/`` directory. There is
+no fallback: if the library is missing or cannot load, every native entry
+raises ``RuntimeError``.
+"""
+import ctypes
+import os
+import threading
+
+from .build import LIB_PATH
+
+OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
+DTYPE_BF16, DTYPE_F32 = 0, 1
+DEVICE_WAIT_TIMEOUT, DEVICE_BAD_SCHEDULE, DEVICE_BAD_ARGUMENT = 1, 2, 4
+
+_vp, _i, _ll, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_size_t
+
+# name -> (restype, argtypes); mirrors include/dspark_b200.h
+SIGNATURES = {
+    'dspark_abi_version': (_i, []),
+    'dspark_status_string': (ctypes.c_char_p, [_i]),
+    'dspark_attention_workspace_size': (_i, [_i, ctypes.POINTER(_sz)]),
+    'dspark_read_device_status': (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    'dspark_draft_attn': (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
+    'dspark_varlen_attn': (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
+    'dspark_segment_attn': (_i, [_vp, _vp, _vp, _ll, _vp, _vp, _ll, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
+                                 _i, _f, _i, _vp, _vp, _sz, _vp]),
+    'dspark_verify_fused': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _ll, _vp,
+                                 _vp, _i, _i, _i, _f, _vp, _vp, _vp, _sz, _vp]),
+    'dspark_commit_kv': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _vp]),
+}
+
+_lock = threading.Lock()
+_lib = None
+
+
+def load_library(path=LIB_PATH):
+    """Load (once) and return the ctypes library with typed entry points."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not os.path.exists(path):
+            raise RuntimeError(f'dspark B200 CUDA library not built ({path}); run build() first. '
+                               'There is no CPU fallback.')
+        lib = ctypes.CDLL(path)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.dspark_abi_version() != 1:
+            raise RuntimeError('dspark B200 library ABI version mismatch')
+        _lib = lib
+        return lib
+
+
+def check(status, what):
+    if status != OK:
+        msg = load_library().dspark_status_string(status).decode()
+        if status == ERR_INVALID_ARGUMENT:
+            raise ValueError(f'{what}: {msg}')
+        raise RuntimeError(f'{what}: {msg} (status {status})')
+
+
+def read_device_status(clear=True):
+    """Device status bits set by kernels since the last clear (synchronising)."""
+    v = ctypes.c_uint(0)
+    check(load_library().dspark_read_device_status(ctypes.byref(v), int(clear)), 'dspark_read_device_status')
+    return v.value
+
+
+_workspaces = {}
+
+
+def workspace(device, stream):
+    """Attention workspace for (device, stream); calls on one stream share it."""
+    import torch
+    key = (device.index, stream)
+    ws = _workspaces.get(key)
+    if ws is None:
+        size = ctypes.c_size_t(0)
+        check(load_library().dspark_attention_workspace_size(device.index, ctypes.byref(size)),
+              'dspark_attention_workspace_size')
+        ws = torch.empty(size.value, dtype=torch.uint8, device=device)
+        _workspaces[key] = ws
+    return ws

@@ -1,0 +1,735 @@
+// Packed varlen GQA attention for DSpark draft (non-causal) and verify
+// (bottom-right causal) on sm_100a.
+//
+// Geometry (Qwen3-0.6B attention): 16 query heads, 8 KV heads, head dim 128.
+// A work item is one request's block of up to 8 query rows. For KV head h the
+// item's 2 query heads (2h, 2h+1) x 8 rows form one 16-row MMA tile, so a
+// single m16n8k16 row block covers the whole GQA group; query row r of head
+// 2h+g sits in MMA row 8g + r, which gives both rows a thread holds the same
+// causal limit.
+//
+// Keys of an item are the concatenation of two row ranges ("source A" then
+// "source B") of [rows, 8, 128] bf16 tensors: the packed THD K/V of the
+// reference kernel contract (B empty), or a resident prefix followed by the
+// verify scratch rows, or a context cache followed by the draft block rows.
+//
+// Persistent schedule: the key tiles of all items (16 keys x 8 heads each,
+// 64 KB of K+V) are numbered in request order and split into equal contiguous
+// ranges, one per CTA (one CTA per SM). A CTA streams its range through a
+// 3-stage TMA pipeline: warp 8 issues the loads, warps 0-7 (one per KV head)
+// consume them. Items that lie wholly inside one range are normalised and
+// written directly; an item cut by a range boundary leaves fp32 partials that
+// a second small kernel merges (log-sum-exp combine).
+#pragma once
+#include <cfloat>
+#include <climits>
+#include "ptx.cuh"
+
+namespace dspark {
+
+constexpr int kHeadDim = 128;
+constexpr int kQHeads = 16;
+constexpr int kKVHeads = 8;
+constexpr int kQBlock = 8;                              // query rows per item
+constexpr int kTileN = 16;                              // keys per pipeline tile
+constexpr int kStages = 3;
+constexpr int kConsumerWarps = kKVHeads;                // warp w computes KV head w
+constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
+constexpr int kHalfBoxBytes = kKVHeads * kTileN * 128;  // 64 bf16 x 16 rows x 8 heads
+constexpr int kStageBytes = 4 * kHalfBoxBytes;          // K lo/hi + V lo/hi halves
+constexpr int kPartFloatsPerSlot = kKVHeads * 16 * kHeadDim;
+constexpr int kPartMlPerSlot = kKVHeads * 16 * 2;
+
+enum KeyMode : int { kModeVarlen = 0, kModeSegmented = 1 };
+
+struct AttnRecord {          // per CTA, consumed by the merge kernel
+  int needs_merge;
+  int req;
+  int qb;
+  int pad;
+  long long item_start;
+  long long total_tiles;
+};
+
+struct AttnParams {
+  const void* q;             // [total_q, 16, 128]
+  void* out;                 // [total_q, 16, 128]
+  const int* cu_q;           // [R+1]
+  int num_requests;
+  int total_q;
+  int mode;                  // KeyMode
+  int causal;                // bottom-right causal mask
+  // kModeVarlen: keys of request i are rows [cu_k[i], cu_k[i+1]) of source A.
+  const int* cu_k;
+  // kModeSegmented: rows [a_off + a_start[i], + a_len[i]) of A, then rows
+  // [b_off + (b_start ? b_start[i] : cu_q[i]), + (b_len ? b_len[i] : q_i)) of B.
+  // A null b_start/b_len selects the verify-scratch convention; b_none drops B.
+  const int* a_start;
+  const int* a_len;
+  const int* b_start;
+  const int* b_len;
+  int a_off;
+  int b_off;
+  int b_none;
+  long long rows_a;          // extents, used by the fp32 path's bounds checks
+  long long rows_b;
+  float scale;
+  float scale_log2;          // scale * log2(e)
+  // workspace (split items)
+  float* part_o;             // [grid][2][8][16][128]
+  float* part_ml;            // [grid][2][8][16][2]
+  AttnRecord* records;       // [grid]
+  int grid;
+};
+
+// ---------------------------------------------------------------------------
+// Item geometry and the tile walk shared by the scan, the producer, the
+// consumers and the merge kernel.
+// ---------------------------------------------------------------------------
+struct Item {
+  int req, qb;
+  int q0;        // first query row (global) of this block
+  int nrows;     // valid query rows in this block (1..8)
+  int q_len;     // request query rows
+  int a_row, a_len, b_row, b_len;
+  int k_len;     // a_len + b_len
+  int vis;       // keys visible to the block's last row
+  int tiles_a, tiles_b, tiles;
+};
+
+__device__ __forceinline__ int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+__device__ __forceinline__ int request_q_len(const AttnParams& p, int req) {
+  return p.cu_q[req + 1] - p.cu_q[req];
+}
+
+__device__ __forceinline__ void load_item(const AttnParams& p, int req, int qb, Item& it) {
+  it.req = req;
+  it.qb = qb;
+  const int qs = p.cu_q[req];
+  it.q_len = p.cu_q[req + 1] - qs;
+  it.q0 = qs + qb * kQBlock;
+  it.nrows = min(kQBlock, it.q_len - qb * kQBlock);
+  if (p.mode == kModeVarlen) {
+    it.a_row = p.cu_k[req];
+    it.a_len = p.cu_k[req + 1] - it.a_row;
+    it.b_row = 0;
+    it.b_len = 0;
+  } else {
+    it.a_row = p.a_off + p.a_start[req];
+    it.a_len = p.a_len[req];
+    if (p.b_none) {
+      it.b_row = 0;
+      it.b_len = 0;
+    } else {
+      it.b_row = p.b_off + (p.b_start ? p.b_start[req] : qs);
+      it.b_len = p.b_len ? p.b_len[req] : it.q_len;
+    }
+  }
+  if (it.a_len < 0 || it.b_len < 0 || it.nrows < 1) {
+    atomicOr(&g_device_status, kStatusBadArgument);
+    it.a_len = max(it.a_len, 0);
+    it.b_len = max(it.b_len, 0);
+    it.nrows = max(it.nrows, 1);
+  }
+  it.k_len = it.a_len + it.b_len;
+  if (p.causal) {
+    const int last_row = min(it.q_len, (qb + 1) * kQBlock);     // exclusive
+    it.vis = min(it.k_len, it.k_len - it.q_len + last_row);
+  } else {
+    it.vis = it.k_len;
+  }
+  it.vis = max(it.vis, 0);
+  const int va = min(it.vis, it.a_len);
+  it.tiles_a = cdiv(va, kTileN);
+  it.tiles_b = cdiv(it.vis - va, kTileN);
+  // Every item owns at least one tile so the walk always advances; an item
+  // with no visible key (rejected on the host) then reads nothing useful.
+  it.tiles = max(it.tiles_a + it.tiles_b, 1);
+}
+
+__device__ __forceinline__ int request_qblocks(const AttnParams& p, int req) {
+  return max(cdiv(request_q_len(p, req), kQBlock), 1);
+}
+
+__device__ long long request_tiles(const AttnParams& p, int req) {
+  const int nqb = request_qblocks(p, req);
+  long long t = 0;
+  Item it;
+  for (int qb = 0; qb < nqb; ++qb) {
+    load_item(p, req, qb, it);
+    t += it.tiles;
+  }
+  return t;
+}
+
+struct Tile {
+  int src_b;      // 0: source A, 1: source B
+  int row;        // first row of the tile in its source tensor
+  int n_valid;    // keys of this tile inside the item's visible range
+  int key_base;   // index of the tile's first key in the item's key order
+};
+
+__device__ __forceinline__ Tile tile_of(const Item& it, int t) {
+  Tile ti;
+  if (t < it.tiles_a) {
+    ti.src_b = 0;
+    ti.row = it.a_row + t * kTileN;
+    ti.n_valid = min(kTileN, min(it.vis, it.a_len) - t * kTileN);
+    ti.key_base = t * kTileN;
+  } else {
+    const int tb = t - it.tiles_a;
+    ti.src_b = 1;
+    ti.row = it.b_row + tb * kTileN;
+    ti.n_valid = min(kTileN, (it.vis - it.a_len) - tb * kTileN);
+    ti.key_base = it.a_len + tb * kTileN;
+  }
+  ti.n_valid = max(ti.n_valid, 0);
+  return ti;
+}
+
+struct Walker {
+  Item it;
+  int t;          // tile index inside the item
+  __device__ void begin(const AttnParams& p, int req, int qb, int t0) {
+    load_item(p, req, qb, it);
+    t = t0;
+  }
+  // Moves to the next tile; returns true when a new item was entered.
+  __device__ bool advance(const AttnParams& p) {
+    if (++t < it.tiles) return false;
+    int req = it.req, qb = it.qb + 1;
+    if (qb >= request_qblocks(p, req)) {
+      ++req;
+      qb = 0;
+    }
+    if (req < p.num_requests) load_item(p, req, qb, it);
+    t = 0;
+    return true;
+  }
+};
+
+// CTA c owns global tiles [c*T/G, (c+1)*T/G).
+__device__ __forceinline__ long long range_start(long long c, long long total, long long grid) {
+  return (c * total) / grid;
+}
+
+// The CTA whose range holds global tile x (largest c with range_start(c) <= x).
+__device__ __forceinline__ int cta_of_tile(long long x, long long total, long long grid) {
+  return static_cast<int>(((x + 1) * grid - 1) / total);
+}
+
+// Inclusive block-wide scan of v over all threads of the CTA.
+template <int kThreads>
+__device__ long long block_scan(long long v, long long* tmp, long long& total) {
+  constexpr int kWarps = kThreads / 32;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const long long n = __shfl_up_sync(0xffffffffu, v, o);
+    if (lane >= o) v += n;
+  }
+  if (lane == 31) tmp[warp] = v;
+  __syncthreads();
+  if (warp == 0) {
+    long long w = lane < kWarps ? tmp[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const long long n = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += n;
+    }
+    if (lane < kWarps) tmp[lane] = w;
+  }
+  __syncthreads();
+  const long long prefix = warp > 0 ? tmp[warp - 1] : 0;
+  total = tmp[kWarps - 1];
+  __syncthreads();
+  return v + prefix;
+}
+
+struct SchedShared {
+  long long scan_tmp[32];
+  long long total;
+  long long start, end;
+  long long req_prefix;
+  int req0, qb0, t0;
+  int issued[kStages];
+};
+
+// Finds the total tile count and the (request, q-block, tile) where this
+// CTA's range starts. All threads of the CTA must call it.
+template <int kThreads>
+__device__ void locate_range(const AttnParams& p, SchedShared& s) {
+  const int tid = threadIdx.x;
+  long long running = 0, chunk_total;
+  for (int base = 0; base < p.num_requests; base += kThreads) {
+    const int i = base + tid;
+    const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+    block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+    running += chunk_total;
+  }
+  const long long total = running;
+  const long long start = range_start(blockIdx.x, total, p.grid);
+  const long long end = range_start(blockIdx.x + 1, total, p.grid);
+  if (tid == 0) {
+    s.total = total;
+    s.start = start;
+    s.end = end;
+    s.req0 = -1;
+  }
+  __syncthreads();
+  if (start < end) {
+    running = 0;
+    for (int base = 0; base < p.num_requests; base += kThreads) {
+      const int i = base + tid;
+      const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+      const long long incl = running + block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+      if (i < p.num_requests && incl - t <= start && start < incl) {
+        s.req0 = i;
+        s.req_prefix = incl - t;
+      }
+      running += chunk_total;
+    }
+  }
+  __syncthreads();
+  if (tid == 0 && start < end) {
+    if (s.req0 < 0) {
+      atomicOr(&g_device_status, kStatusBadSchedule);
+      s.end = s.start;   // nothing to do
+    } else {
+      long long off = start - s.req_prefix;
+      const int nqb = request_qblocks(p, s.req0);
+      Item it;
+      int qb = 0;
+      for (; qb < nqb; ++qb) {
+        load_item(p, s.req0, qb, it);
+        if (off < it.tiles) break;
+        off -= it.tiles;
+      }
+      s.qb0 = qb;
+      s.t0 = static_cast<int>(off);
+      AttnRecord r;
+      r.req = s.req0;
+      r.qb = qb;
+      r.pad = 0;
+      r.item_start = start - off;
+      r.total_tiles = total;
+      r.needs_merge = (off > 0) && (r.item_start + it.tiles <= end);
+      p.records[blockIdx.x] = r;
+    }
+  }
+  if (tid == 0 && !(start < end)) {
+    AttnRecord r{};
+    r.total_tiles = total;
+    p.records[blockIdx.x] = r;
+  }
+  __syncthreads();
+}
+
+__device__ __forceinline__ float quad_max(float v) {
+  v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
+  return fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 2));
+}
+
+__device__ __forceinline__ float quad_sum(float v) {
+  v += __shfl_xor_sync(0xffffffffu, v, 1);
+  return v + __shfl_xor_sync(0xffffffffu, v, 2);
+}
+
+// ---------------------------------------------------------------------------
+// bf16 tensor-core kernel
+// ---------------------------------------------------------------------------
+template <bool kCausal>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    attn_bf16_kernel(const __grid_constant__ CUtensorMap tm_ka, const __grid_constant__ CUtensorMap tm_va,
+                     const __grid_constant__ CUtensorMap tm_kb, const __grid_constant__ CUtensorMap tm_vb,
+                     const AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
+  SchedShared& sched = *reinterpret_cast<SchedShared*>(empty + kStages);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), kConsumerWarps);
+      sched.issued[s] = 0;
+    }
+    fence_barrier_init();
+  }
+  locate_range<kAttnThreads>(p, sched);   // contains __syncthreads
+  const long long start = sched.start, end = sched.end;
+  if (start >= end) return;
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------ producer ------------------------------
+    if (lane == 0) {
+      prefetch_tmap(&tm_ka);
+      prefetch_tmap(&tm_va);
+      prefetch_tmap(&tm_kb);
+      prefetch_tmap(&tm_vb);
+      Walker w;
+      w.begin(p, sched.req0, sched.qb0, sched.t0);
+      int issued[kStages] = {};
+      for (long long gk = start; gk < end; ++gk) {
+        const int kl = static_cast<int>(gk - start);
+        const int stage = kl % kStages;
+        const uint32_t parity = ((kl / kStages) & 1) ^ 1;
+        if (!mbar_wait(smem_u32(&empty[stage]), parity)) break;
+        const Tile ti = tile_of(w.it, w.t);
+        const CUtensorMap* mk = ti.src_b ? &tm_kb : &tm_ka;
+        const CUtensorMap* mv = ti.src_b ? &tm_vb : &tm_va;
+        const uint32_t bar = smem_u32(&full[stage]);
+        const uint32_t dst = smem_u32(smem + stage * kStageBytes);
+        mbar_arrive_expect_tx(bar, kStageBytes);
+        tma_load_3d(dst, mk, 0, ti.row, 0, bar);
+        tma_load_3d(dst + kHalfBoxBytes, mk, 64, ti.row, 0, bar);
+        tma_load_3d(dst + 2 * kHalfBoxBytes, mv, 0, ti.row, 0, bar);
+        tma_load_3d(dst + 3 * kHalfBoxBytes, mv, 64, ti.row, 0, bar);
+        ++issued[stage];
+        w.advance(p);
+      }
+      for (int s = 0; s < kStages; ++s) sched.issued[s] = issued[s];
+    }
+  } else {
+    // ------------------------------ consumers -----------------------------
+    const int h = warp;
+    const int g = lane >> 2, t4 = lane & 3;
+    const float sl2 = p.scale_log2;
+    const __nv_bfloat16* qg = static_cast<const __nv_bfloat16*>(p.q);
+    __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
+
+    Walker w;
+    w.begin(p, sched.req0, sched.qb0, sched.t0);
+    long long item_start = start - sched.t0;
+    bool fresh = true;
+    uint32_t qf[8][4];
+    float o[16][4];
+    float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+
+    for (long long gk = start; gk < end; ++gk) {
+      const int kl = static_cast<int>(gk - start);
+      const int stage = kl % kStages;
+      const uint32_t parity = (kl / kStages) & 1;
+      const Item& it = w.it;
+      if (fresh) {
+        // Q fragments of heads 2h (MMA rows 0-7) and 2h+1 (rows 8-15), query row g.
+        const int row = it.q0 + g;
+        const bool rv = g < it.nrows && row >= 0 && row < p.total_q;
+        const __nv_bfloat16* qa = qg + (static_cast<size_t>(row) * kQHeads + 2 * h) * kHeadDim;
+        const __nv_bfloat16* qb = qa + kHeadDim;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int d = ks * 16 + 2 * t4;
+          qf[ks][0] = rv ? ld_nc_u32(qa + d) : 0u;
+          qf[ks][1] = rv ? ld_nc_u32(qb + d) : 0u;
+          qf[ks][2] = rv ? ld_nc_u32(qa + d + 8) : 0u;
+          qf[ks][3] = rv ? ld_nc_u32(qb + d + 8) : 0u;
+        }
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        m_a = m_b = -INFINITY;
+        l_a = l_b = 0.f;
+        fresh = false;
+      }
+      if (!mbar_wait(smem_u32(&full[stage]), parity)) break;
+      const Tile ti = tile_of(it, w.t);
+      const uint32_t sbase = smem_u32(smem + stage * kStageBytes);
+      const uint32_t head_off = static_cast<uint32_t>(h * kTileN * 128);
+
+      // S = Q K^T over 16 keys (two n8 tiles).
+      float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+      {
+        const int n = ((lane >> 4) << 3) + (lane & 7);
+        const uint32_t rowaddr = sbase + head_off + n * 128;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks) {
+          const int chunk = ((ks & 3) << 1) + ((lane >> 3) & 1);
+          const uint32_t addr = rowaddr + (ks >> 2) * kHalfBoxBytes + ((chunk ^ (n & 7)) << 4);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(addr, b0, b1, b2, b3);
+          mma_bf16(s0, qf[ks], b0, b1);
+          mma_bf16(s1, qf[ks], b2, b3);
+        }
+      }
+      // Mask: keys past the tile's valid count, and (causal) past the row limit.
+      const int j0 = 2 * t4, j2 = 8 + 2 * t4;
+      int lim = ti.n_valid;
+      if (kCausal) {
+        const int row_lim = it.k_len - it.q_len + it.qb * kQBlock + g - ti.key_base + 1;
+        lim = min(lim, row_lim);
+      }
+      const bool v0 = j0 < lim, v1 = j0 + 1 < lim, v2 = j2 < lim, v3 = j2 + 1 < lim;
+      s0[0] = v0 ? s0[0] : -INFINITY;
+      s0[1] = v1 ? s0[1] : -INFINITY;
+      s0[2] = v0 ? s0[2] : -INFINITY;
+      s0[3] = v1 ? s0[3] : -INFINITY;
+      s1[0] = v2 ? s1[0] : -INFINITY;
+      s1[1] = v3 ? s1[1] : -INFINITY;
+      s1[2] = v2 ? s1[2] : -INFINITY;
+      s1[3] = v3 ? s1[3] : -INFINITY;
+
+      // Online softmax (fp32), rows A = head 2h, B = head 2h+1.
+      const float mx_a = quad_max(fmaxf(fmaxf(s0[0], s0[1]), fmaxf(s1[0], s1[1])));
+      const float mx_b = quad_max(fmaxf(fmaxf(s0[2], s0[3]), fmaxf(s1[2], s1[3])));
+      const float mn_a = fmaxf(m_a, mx_a), mn_b = fmaxf(m_b, mx_b);
+      const float mu_a = mn_a == -INFINITY ? 0.f : mn_a;
+      const float mu_b = mn_b == -INFINITY ? 0.f : mn_b;
+      const float alpha_a = ex2((m_a - mu_a) * sl2), alpha_b = ex2((m_b - mu_b) * sl2);
+      m_a = mn_a;
+      m_b = mn_b;
+      const float nb_a = -mu_a * sl2, nb_b = -mu_b * sl2;
+      float p0[4], p1[4];
+      p0[0] = ex2(fmaf(s0[0], sl2, nb_a));
+      p0[1] = ex2(fmaf(s0[1], sl2, nb_a));
+      p1[0] = ex2(fmaf(s1[0], sl2, nb_a));
+      p1[1] = ex2(fmaf(s1[1], sl2, nb_a));
+      p0[2] = ex2(fmaf(s0[2], sl2, nb_b));
+      p0[3] = ex2(fmaf(s0[3], sl2, nb_b));
+      p1[2] = ex2(fmaf(s1[2], sl2, nb_b));
+      p1[3] = ex2(fmaf(s1[3], sl2, nb_b));
+      l_a = l_a * alpha_a + (p0[0] + p0[1] + p1[0] + p1[1]);
+      l_b = l_b * alpha_b + (p0[2] + p0[3] + p1[2] + p1[3]);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        o[j][0] *= alpha_a;
+        o[j][1] *= alpha_a;
+        o[j][2] *= alpha_b;
+        o[j][3] *= alpha_b;
+      }
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(p0[0], p0[1]);
+      pa[1] = pack_bf16x2(p0[2], p0[3]);
+      pa[2] = pack_bf16x2(p1[0], p1[1]);
+      pa[3] = pack_bf16x2(p1[2], p1[3]);
+
+      // O += P V. Rows of V past the valid count may hold anything (next
+      // request, capacity tail, NaN): zero them in the B fragments.
+      const bool partial = ti.n_valid < kTileN;
+      const uint32_t m_lo = (j0 < ti.n_valid ? 0x0000ffffu : 0u) | (j0 + 1 < ti.n_valid ? 0xffff0000u : 0u);
+      const uint32_t m_hi = (j2 < ti.n_valid ? 0x0000ffffu : 0u) | (j2 + 1 < ti.n_valid ? 0xffff0000u : 0u);
+      {
+        const int n = (((lane >> 3) & 1) << 3) + (lane & 7);
+        const uint32_t rowaddr = sbase + 2 * kHalfBoxBytes + head_off + n * 128;
+#pragma unroll
+        for (int j = 0; j < 16; j += 2) {
+          const int chunk = (j & 7) + (lane >> 4);
+          const uint32_t addr = rowaddr + (j >> 3) * kHalfBoxBytes + ((chunk ^ (n & 7)) << 4);
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(addr, b0, b1, b2, b3);
+          if (partial) {
+            b0 &= m_lo;
+            b1 &= m_hi;
+            b2 &= m_lo;
+            b3 &= m_hi;
+          }
+          mma_bf16(o[j], pa, b0, b1);
+          mma_bf16(o[j + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
+
+      const bool item_done = (w.t + 1 >= it.tiles) || (gk + 1 == end);
+      if (item_done) {
+        const float la = quad_sum(l_a), lb = quad_sum(l_b);
+        const long long item_end = item_start + it.tiles;
+        if (item_start >= start && item_end <= end) {
+          if (g < it.nrows && it.q0 + g < p.total_q && it.q0 + g >= 0) {
+            const float ia = la > 0.f ? 1.f / la : 0.f, ib = lb > 0.f ? 1.f / lb : 0.f;
+            __nv_bfloat16* oa = og + (static_cast<size_t>(it.q0 + g) * kQHeads + 2 * h) * kHeadDim;
+            __nv_bfloat16* ob = oa + kHeadDim;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int d = j * 8 + 2 * t4;
+              *reinterpret_cast<uint32_t*>(oa + d) = pack_bf16x2(o[j][0] * ia, o[j][1] * ia);
+              *reinterpret_cast<uint32_t*>(ob + d) = pack_bf16x2(o[j][2] * ib, o[j][3] * ib);
+            }
+          }
+        } else {
+          const int slot = item_start <= start ? 0 : 1;
+          const size_t base = (static_cast<size_t>(blockIdx.x) * 2 + slot) * kKVHeads + h;
+          float* po = p.part_o + base * 16 * kHeadDim;
+#pragma unroll
+          for (int j = 0; j < 16; ++j) {
+            const int d = j * 8 + 2 * t4;
+            *reinterpret_cast<float2*>(po + g * kHeadDim + d) = make_float2(o[j][0], o[j][1]);
+            *reinterpret_cast<float2*>(po + (g + 8) * kHeadDim + d) = make_float2(o[j][2], o[j][3]);
+          }
+          if (t4 == 0) {
+            float* pml = p.part_ml + base * 32;
+            pml[2 * g] = m_a;
+            pml[2 * g + 1] = la;
+            pml[2 * (g + 8)] = m_b;
+            pml[2 * (g + 8) + 1] = lb;
+          }
+        }
+      }
+      if (w.advance(p)) {
+        item_start = gk + 1;
+        fresh = true;
+      }
+    }
+  }
+  // Never leave the CTA with a TMA write still in flight (only possible after
+  // a timed-out wait): wait, bounded, for the last load issued to each stage.
+  __syncthreads();
+  if (threadIdx.x == kConsumerWarps * 32) {
+    for (int s = 0; s < kStages; ++s)
+      if (sched.issued[s] > 0) mbar_wait(smem_u32(&full[s]), (sched.issued[s] - 1) & 1);
+  }
+}
+
+// Combines the fp32 partials of items cut by CTA range boundaries. Block c
+// handles the item that starts before its range and ends inside it.
+__global__ void __launch_bounds__(256) attn_merge_kernel(const AttnParams p) {
+  const AttnRecord r = p.records[blockIdx.x];
+  if (!r.needs_merge) return;
+  Item it;
+  load_item(p, r.req, r.qb, it);
+  const long long total = r.total_tiles;
+  const int first = cta_of_tile(r.item_start, total, p.grid);
+  const int last = blockIdx.x;
+  __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
+  for (int u = threadIdx.x; u < kKVHeads * 16 * 32; u += blockDim.x) {
+    const int h = u / (16 * 32);
+    const int m = (u / 32) % 16;
+    const int d = (u % 32) * 4;
+    const int r_in = m & 7;
+    if (r_in >= it.nrows || it.q0 + r_in < 0 || it.q0 + r_in >= p.total_q) continue;
+    float mstar = -INFINITY;
+    for (int c = first; c <= last; ++c) {
+      const long long cs = range_start(c, total, p.grid);
+      if (cs == range_start(c + 1, total, p.grid)) continue;   // empty range: no partial
+      const int slot = r.item_start <= cs ? 0 : 1;
+      const size_t base = (static_cast<size_t>(c) * 2 + slot) * kKVHeads + h;
+      mstar = fmaxf(mstar, p.part_ml[base * 32 + 2 * m]);
+    }
+    const float mu = mstar == -INFINITY ? 0.f : mstar;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float l = 0.f;
+    for (int c = first; c <= last; ++c) {
+      const long long cs = range_start(c, total, p.grid);
+      if (cs == range_start(c + 1, total, p.grid)) continue;
+      const int slot = r.item_start <= cs ? 0 : 1;
+      const size_t base = (static_cast<size_t>(c) * 2 + slot) * kKVHeads + h;
+      const float w = ex2((p.part_ml[base * 32 + 2 * m] - mu) * p.scale_log2);
+      l += w * p.part_ml[base * 32 + 2 * m + 1];
+      const float4 v = *reinterpret_cast<const float4*>(p.part_o + (base * 16 + m) * kHeadDim + d);
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+    __nv_bfloat16* dst = og + (static_cast<size_t>(it.q0 + r_in) * kQHeads + 2 * h + (m >> 3)) * kHeadDim + d;
+    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc.x * inv, acc.y * inv);
+    *reinterpret_cast<uint32_t*>(dst + 2) = pack_bf16x2(acc.z * inv, acc.w * inv);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// fp32 CUDA-core path: exact-precision companion for float32 inputs (the
+// reference's CPU configurations). One CTA per (request, q-block, KV head).
+// ---------------------------------------------------------------------------
+constexpr int kF32Threads = 128;
+constexpr int kF32Keys = 32;
+
+__global__ void __launch_bounds__(kF32Threads)
+    attn_f32_kernel(const float* __restrict__ ka, const float* __restrict__ va, const float* __restrict__ kb,
+                    const float* __restrict__ vb, const AttnParams p) {
+  __shared__ float sq[16][kHeadDim];
+  __shared__ float sk[kF32Keys][kHeadDim + 1];
+  __shared__ float sv[kF32Keys][kHeadDim];
+  __shared__ float sp[16][kF32Keys];
+  const int req = blockIdx.x, qb = blockIdx.y, h = blockIdx.z;
+  if (qb >= request_qblocks(p, req)) return;
+  Item it;
+  load_item(p, req, qb, it);
+  const float* qg = static_cast<const float*>(p.q);
+  float* og = static_cast<float*>(p.out);
+  const int tid = threadIdx.x;
+  for (int u = tid; u < 16 * kHeadDim; u += kF32Threads) {
+    const int m = u / kHeadDim, d = u % kHeadDim;
+    const int r = m & 7, row = it.q0 + r;
+    const bool ok = r < it.nrows && row < p.total_q;
+    sq[m][d] = ok ? qg[(static_cast<size_t>(row) * kQHeads + 2 * h + (m >> 3)) * kHeadDim + d] : 0.f;
+  }
+  // thread -> (row m = tid/8, key group kq = tid%8): scores of keys 4kq..4kq+3
+  const int m = tid >> 3, kq = tid & 7;
+  float mrow = -INFINITY, lrow = 0.f;
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.f;
+  const int r = m & 7;
+  const int row_lim = p.causal ? it.k_len - it.q_len + qb * kQBlock + r : INT_MAX;
+  for (int kb0 = 0; kb0 < it.vis; kb0 += kF32Keys) {
+    __syncthreads();
+    for (int u = tid; u < kF32Keys * kHeadDim; u += kF32Threads) {
+      const int n = u / kHeadDim, d = u % kHeadDim, j = kb0 + n;
+      float kv = 0.f, vv = 0.f;
+      if (j < it.vis) {
+        long long row;
+        const float *kp, *vp;
+        long long rows;
+        if (j < it.a_len) { row = static_cast<long long>(it.a_row) + j; kp = ka; vp = va; rows = p.rows_a; }
+        else { row = static_cast<long long>(it.b_row) + (j - it.a_len); kp = kb; vp = vb; rows = p.rows_b; }
+        if (row >= 0 && row < rows) {
+          const size_t off = (static_cast<size_t>(row) * kKVHeads + h) * kHeadDim + d;
+          kv = kp[off];
+          vv = vp[off];
+        } else {
+          atomicOr(&g_device_status, kStatusBadArgument);
+        }
+      }
+      sk[n][d] = kv;
+      sv[n][d] = vv;
+    }
+    __syncthreads();
+    float s[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int n = kq * 4 + i, j = kb0 + n;
+      float dot = 0.f;
+      for (int d = 0; d < kHeadDim; ++d) dot = fmaf(sq[m][d], sk[n][d], dot);
+      s[i] = (j < it.vis && j <= row_lim) ? dot * p.scale : -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(s[0], s[1]), fmaxf(s[2], s[3]));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float mn = fmaxf(mrow, mx);
+    const float mu = mn == -INFINITY ? 0.f : mn;
+    const float alpha = expf(mrow - mu);
+    float ps = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float e = expf(s[i] - mu);
+      sp[m][kq * 4 + i] = e;
+      ps += e;
+    }
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+    lrow = lrow * alpha + ps;
+    mrow = mn;
+    __syncwarp();
+    // acc covers d = kq*16 .. kq*16+15 of row m
+#pragma unroll
+    for (int i = 0; i < 16; ++i) acc[i] *= alpha;
+    for (int n = 0; n < kF32Keys; ++n) {
+      const float pn = sp[m][n];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = fmaf(pn, sv[n][kq * 16 + i], acc[i]);
+    }
+  }
+  const int row = it.q0 + r;
+  if (r < it.nrows && row < p.total_q) {
+    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
+    float* dst = og + (static_cast<size_t>(row) * kQHeads + 2 * h + (m >> 3)) * kHeadDim + kq * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[i] = acc[i] * inv;
+  }
+}
+
+}  // namespace dspark

@@ -1,0 +1,352 @@
+// C-ABI of the DSpark B200 attention library (declared in include/dspark_b200.h).
+// Host side: argument checks that need no device reads, TMA descriptor
+// encoding and kernel launches on the caller's stream. No allocation happens
+// here: scratch for split items is the caller's workspace.
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cstdint>
+#include <cstdio>
+#include <mutex>
+
+#include "attention.cuh"
+#include "verify.cuh"
+#include "../../include/dspark_b200.h"
+
+using namespace dspark;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceInfo {
+  bool ready = false;
+  int sms = 0;
+  int max_smem_optin = 0;
+  int cc_major = 0, cc_minor = 0;
+};
+
+std::mutex g_mu;
+DeviceInfo g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+constexpr size_t kAttnSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
+                                  sizeof(SchedShared);
+
+int device_info(int dev, DeviceInfo* out) {
+  if (dev < 0 || dev >= kMaxDevices) return DSPARK_ERR_INVALID_ARGUMENT;
+  std::lock_guard<std::mutex> lock(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    if (cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
+      return DSPARK_ERR_CUDA;
+    if (d.cc_major != 10) return DSPARK_ERR_UNSUPPORTED;   // built for sm_100a only
+    if (static_cast<size_t>(d.max_smem_optin) < kAttnSmemBytes) return DSPARK_ERR_UNSUPPORTED;
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (cur != dev) return DSPARK_ERR_INVALID_ARGUMENT;     // attributes are per current device
+    if (cudaFuncSetAttribute(attn_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kAttnSmemBytes)) != cudaSuccess)
+      return DSPARK_ERR_CUDA;
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || fn == nullptr)
+        return DSPARK_ERR_CUDA;
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    d.ready = true;
+  }
+  *out = d;
+  return DSPARK_OK;
+}
+
+int current_device_info(DeviceInfo* out) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSPARK_ERR_CUDA;
+  return device_info(dev, out);
+}
+
+size_t workspace_for_grid(int grid) {
+  const size_t part_o = static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float);
+  const size_t part_ml = static_cast<size_t>(grid) * 2 * kPartMlPerSlot * sizeof(float);
+  const size_t rec = static_cast<size_t>(grid) * sizeof(AttnRecord);
+  return part_o + part_ml + rec;
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// K/V rows tensor [rows, 8, 128] bf16 viewed as dims (d, row, head) so one box
+// (64 d, 16 rows, 8 heads) lands in shared memory as [head][row][64 d] with
+// the 128-byte swizzle keyed on the row, conflict-free for ldmatrix.
+int encode_kv_map(CUtensorMap* m, const void* base, long long rows) {
+  if (!aligned(base, 16) || rows < 1 || rows >= (1ll << 31)) return DSPARK_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(rows),
+                        static_cast<cuuint64_t>(kKVHeads)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kKVHeads * kHeadDim * 2), static_cast<cuuint64_t>(kHeadDim * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kTileN), static_cast<cuuint32_t>(kKVHeads)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSPARK_OK : DSPARK_ERR_CUDA;
+}
+
+int launch_status() {
+  const cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? DSPARK_OK : DSPARK_ERR_CUDA;
+}
+
+struct KeySources {
+  const void* ka;
+  const void* va;
+  long long rows_a;
+  const void* kb;
+  const void* vb;
+  long long rows_b;
+};
+
+// Shared launch path of every attention entry point.
+int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, void* workspace,
+                  size_t workspace_bytes, cudaStream_t stream) {
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  if (dtype == DSPARK_DTYPE_F32) {
+    if (max_q < 1) return DSPARK_ERR_INVALID_ARGUMENT;
+    p.rows_a = src.rows_a;
+    p.rows_b = src.rows_b;
+    dim3 grid(p.num_requests, (max_q + kQBlock - 1) / kQBlock, kKVHeads);
+    if (grid.y > 65535) return DSPARK_ERR_UNSUPPORTED;
+    attn_f32_kernel<<<grid, kF32Threads, 0, stream>>>(static_cast<const float*>(src.ka),
+                                                      static_cast<const float*>(src.va),
+                                                      static_cast<const float*>(src.kb),
+                                                      static_cast<const float*>(src.vb), p);
+    return launch_status();
+  }
+  if (dtype != DSPARK_DTYPE_BF16) return DSPARK_ERR_INVALID_ARGUMENT;
+  const int grid = dev.sms;
+  if (workspace == nullptr || workspace_bytes < workspace_for_grid(grid) || !aligned(workspace, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
+  p.records = reinterpret_cast<AttnRecord*>(ws + static_cast<size_t>(grid) * 2 *
+                                                     (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
+  p.grid = grid;
+  p.rows_a = src.rows_a;
+  p.rows_b = src.rows_b;
+  CUtensorMap ka, va, kb, vb;
+  if ((st = encode_kv_map(&ka, src.ka, src.rows_a)) != DSPARK_OK) return st;
+  if ((st = encode_kv_map(&va, src.va, src.rows_a)) != DSPARK_OK) return st;
+  if (src.kb != nullptr) {
+    if ((st = encode_kv_map(&kb, src.kb, src.rows_b)) != DSPARK_OK) return st;
+    if ((st = encode_kv_map(&vb, src.vb, src.rows_b)) != DSPARK_OK) return st;
+  } else {
+    kb = ka;
+    vb = va;
+  }
+  if (p.causal)
+    attn_bf16_kernel<true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
+  else
+    attn_bf16_kernel<false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
+  if ((st = launch_status()) != DSPARK_OK) return st;
+  attn_merge_kernel<<<grid, 256, 0, stream>>>(p);
+  return launch_status();
+}
+
+bool common_ok(const void* q, const void* out, const int32_t* cu_q, int num_requests, int total_q, float scale,
+               int dtype) {
+  const size_t align = dtype == DSPARK_DTYPE_F32 ? 4 : 16;
+  return q && out && cu_q && num_requests >= 1 && total_q >= 1 && scale > 0.f && aligned(q, align) &&
+         aligned(out, align) && aligned(cu_q, 4);
+}
+
+AttnParams base_params(const void* q, void* out, const int32_t* cu_q, int num_requests, int total_q, float scale,
+                       int causal) {
+  AttnParams p{};
+  p.q = q;
+  p.out = out;
+  p.cu_q = cu_q;
+  p.num_requests = num_requests;
+  p.total_q = total_q;
+  p.causal = causal;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
+  return p;
+}
+
+int varlen_common(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                  int num_requests, int total_q, long long key_rows, int max_q, float scale, int dtype, int causal,
+                  void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!common_ok(q, out, cu_q, num_requests, total_q, scale, dtype) || !k || !v || !cu_k || key_rows < 1)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  AttnParams p = base_params(q, out, cu_q, num_requests, total_q, scale, causal);
+  p.mode = kModeVarlen;
+  p.cu_k = cu_k;
+  KeySources src{k, v, key_rows, nullptr, nullptr, 0};
+  return run_attention(p, src, dtype, max_q, workspace, workspace_bytes, stream);
+}
+
+}  // namespace
+
+extern "C" {
+
+int dspark_abi_version(void) { return DSPARK_ABI_VERSION; }
+
+const char* dspark_status_string(int status) {
+  switch (status) {
+    case DSPARK_OK: return "ok";
+    case DSPARK_ERR_INVALID_ARGUMENT: return "invalid argument";
+    case DSPARK_ERR_UNSUPPORTED: return "unsupported device or shape";
+    case DSPARK_ERR_CUDA: return "CUDA runtime error";
+    default: return "unknown status";
+  }
+}
+
+int dspark_attention_workspace_size(int device, size_t* bytes) {
+  if (bytes == nullptr) return DSPARK_ERR_INVALID_ARGUMENT;
+  int sms = 0;
+  if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device) != cudaSuccess) return DSPARK_ERR_CUDA;
+  *bytes = workspace_for_grid(sms);
+  return DSPARK_OK;
+}
+
+int dspark_read_device_status(unsigned int* status, int clear) {
+  if (status == nullptr) return DSPARK_ERR_INVALID_ARGUMENT;
+  if (cudaMemcpyFromSymbol(status, g_device_status, sizeof(unsigned int)) != cudaSuccess) return DSPARK_ERR_CUDA;
+  if (clear) {
+    const unsigned int zero = 0;
+    if (cudaMemcpyToSymbol(g_device_status, &zero, sizeof(unsigned int)) != cudaSuccess) return DSPARK_ERR_CUDA;
+  }
+  return DSPARK_OK;
+}
+
+int dspark_draft_attn(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                      int num_requests, int total_q, long long key_rows, int max_q, int max_k, float scale,
+                      int dtype, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  (void)max_k;
+  return varlen_common(q, k, v, cu_q, cu_k, num_requests, total_q, key_rows, max_q, scale, dtype, 0, out, workspace,
+                       workspace_bytes, stream);
+}
+
+int dspark_varlen_attn(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
+                       int num_requests, int total_q, long long key_rows, int max_q, int max_k, float scale,
+                       int dtype, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  (void)max_k;
+  return varlen_common(q, k, v, cu_q, cu_k, num_requests, total_q, key_rows, max_q, scale, dtype, 1, out, workspace,
+                       workspace_bytes, stream);
+}
+
+int dspark_segment_attn(const void* q, const void* ka, const void* va, long long rows_a, const void* kb,
+                        const void* vb, long long rows_b, const int32_t* cu_q, const int32_t* a_start,
+                        const int32_t* a_len, const int32_t* b_start, const int32_t* b_len, int a_off, int b_off,
+                        int num_requests, int total_q, int max_q, int causal, float scale, int dtype, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!common_ok(q, out, cu_q, num_requests, total_q, scale, dtype) || !ka || !va || !a_start || !a_len ||
+      rows_a < 1 || (causal != 0 && causal != 1))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  const bool has_b = kb != nullptr;
+  if (has_b && (!vb || rows_b < 1)) return DSPARK_ERR_INVALID_ARGUMENT;
+  if (!has_b && (b_start || b_len)) return DSPARK_ERR_INVALID_ARGUMENT;
+  AttnParams p = base_params(q, out, cu_q, num_requests, total_q, scale, causal);
+  p.mode = kModeSegmented;
+  p.a_start = a_start;
+  p.a_len = a_len;
+  p.b_start = b_start;
+  p.b_len = b_len;
+  p.a_off = a_off;
+  p.b_off = b_off;
+  p.b_none = has_b ? 0 : 1;
+  KeySources src{ka, va, rows_a, kb, vb, has_b ? rows_b : 0};
+  return run_attention(p, src, dtype, max_q, workspace, workspace_bytes, stream);
+}
+
+int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
+                        const void* k_norm_weight, const float* inv_freq, float eps, const int32_t* cu_q,
+                        const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
+                        void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* q_roped,
+                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (!common_ok(q_raw, out, cu_q, num_requests, total_q, scale, DSPARK_DTYPE_BF16) || !k_raw || !v_raw ||
+      !q_norm_weight || !k_norm_weight || !inv_freq || !slot_row || !ctx_len || !resident_k || !resident_v ||
+      !scratch_k || !scratch_v || !q_roped || !aligned(q_roped, 16) || !aligned(k_raw, 8) || !aligned(v_raw, 8) ||
+      rows_per_layer < 1 || scratch_rows < total_q || num_layers < 1 || layer < 0 || layer >= num_layers ||
+      !(eps > 0.f))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  const size_t row_bytes = static_cast<size_t>(kKVHeads) * kHeadDim * 2;
+  __nv_bfloat16* sk = static_cast<__nv_bfloat16*>(scratch_k) + static_cast<size_t>(layer) * scratch_rows * row_bytes / 2;
+  __nv_bfloat16* sv = static_cast<__nv_bfloat16*>(scratch_v) + static_cast<size_t>(layer) * scratch_rows * row_bytes / 2;
+  VerifyParams vp;
+  vp.q_raw = static_cast<const __nv_bfloat16*>(q_raw);
+  vp.k_raw = static_cast<const __nv_bfloat16*>(k_raw);
+  vp.v_raw = static_cast<const __nv_bfloat16*>(v_raw);
+  vp.q_w = static_cast<const __nv_bfloat16*>(q_norm_weight);
+  vp.k_w = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  vp.inv_freq = inv_freq;
+  vp.cu_q = cu_q;
+  vp.ctx_len = ctx_len;
+  vp.num_requests = num_requests;
+  vp.total_q = total_q;
+  vp.eps = eps;
+  vp.q_out = static_cast<__nv_bfloat16*>(q_roped);
+  vp.scratch_k = sk;
+  vp.scratch_v = sv;
+  vp.scratch_rows = scratch_rows;
+  qk_norm_rope_append_kernel<<<total_q, 1024, 0, stream>>>(vp);
+  if ((st = launch_status()) != DSPARK_OK) return st;
+  // Attention: resident prefix rows of this layer, then this layer's scratch rows.
+  const long long layer_rows = rows_per_layer;
+  const long long res_row0 = static_cast<long long>(layer) * layer_rows;
+  if (res_row0 + layer_rows >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
+  AttnParams p = base_params(q_roped, out, cu_q, num_requests, total_q, scale, 1);
+  p.mode = kModeSegmented;
+  p.a_start = slot_row;
+  p.a_len = ctx_len;
+  p.b_start = nullptr;     // scratch rows follow cu_q
+  p.b_len = nullptr;       // and number q_i per request
+  p.a_off = 0;
+  p.b_off = 0;
+  p.b_none = 0;
+  const uint8_t* rk = static_cast<const uint8_t*>(resident_k) + res_row0 * row_bytes;
+  const uint8_t* rv = static_cast<const uint8_t*>(resident_v) + res_row0 * row_bytes;
+  KeySources src{rk, rv, layer_rows, sk, sv, scratch_rows};
+  return run_attention(p, src, DSPARK_DTYPE_BF16, max_q, workspace, workspace_bytes, stream);
+}
+
+int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,
+                     const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
+                     const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
+                     int scratch_rows, cudaStream_t stream) {
+  if (!resident_k || !resident_v || !scratch_k || !scratch_v || !cu_q || !slot_row || !ctx_len || !slot_cap ||
+      !n_commit || num_requests < 1 || num_layers < 1 || num_layers > 65535 || rows_per_layer < 1 ||
+      scratch_rows < 1 || !aligned(resident_k, 16) || !aligned(resident_v, 16) || !aligned(scratch_k, 16) ||
+      !aligned(scratch_v, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  CommitParams cp;
+  cp.resident_k = static_cast<__nv_bfloat16*>(resident_k);
+  cp.resident_v = static_cast<__nv_bfloat16*>(resident_v);
+  cp.scratch_k = static_cast<const __nv_bfloat16*>(scratch_k);
+  cp.scratch_v = static_cast<const __nv_bfloat16*>(scratch_v);
+  cp.cu_q = cu_q;
+  cp.slot_row = slot_row;
+  cp.ctx_len = ctx_len;
+  cp.slot_cap = slot_cap;
+  cp.n_commit = n_commit;
+  cp.num_requests = num_requests;
+  cp.num_layers = num_layers;
+  cp.rows_per_layer = rows_per_layer;
+  cp.scratch_rows = scratch_rows;
+  commit_kernel<<<dim3(num_requests, num_layers), 256, 0, stream>>>(cp);
+  return launch_status();
+}
+
+}  // extern "C"

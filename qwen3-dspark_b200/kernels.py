@@ -1,0 +1,205 @@
+"""Drop-in attention kernels with the reference's plugin signature.
+
+Every class is callable as ``kernel(query, key, value, layout, *, scale) -> out``
+(the boundary of dspark_qwen/packed_draft.py:23, rocm_varlen.py:108 and
+persistent_qwen_target.py:223) and carries ``backend_name`` and
+``native_varlen_calls_per_layer = 1``. Inputs are validated on the host before
+any launch with the refusals of ``PinnedRocmVarlenKernel._validate_inputs``
+(rocm_varlen.py:65-106); a launch error propagates as ``RuntimeError``; there is
+no fallback, retry or split tuning.
+
+* ``B200VarlenKernel``  - bottom-right causal, exact K (replaces PinnedRocmVarlenKernel)
+* ``B200DraftKernel``   - non-causal (replaces PinnedRocmDraftKernel)
+* ``B200CapacityKernel`` - bottom-right causal over a capacity-sized K whose tail
+  past ``cu_key[-1]`` is never read (replaces PersistentQwenTarget._native_attention)
+
+bf16 runs on the tensor-core kernel; float32 inputs (the reference's exact CPU
+configurations) run on the library's float32 CUDA-core kernel.
+"""
+import math
+
+import torch
+
+from . import _lib
+
+BACKEND = 'b200_sm100a_varlen_causal_v1'
+DRAFT_BACKEND = 'b200_sm100a_noncausal_v1'
+CAPACITY_BACKEND = 'b200_sm100a_capacity_causal_v1'
+HQ, HKV, HEAD_DIM = 16, 8, 128
+SCALE = HEAD_DIM ** -0.5
+_DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
+
+
+def runtime_identity(device):
+    """The native runtime this kernel binds to; refuses anything but an sm_100 CUDA GPU."""
+    if device.type != 'cuda' or not torch.cuda.is_available():
+        raise RuntimeError('B200 attention requires an explicitly selected CUDA GPU; no CPU fallback')
+    major, minor = torch.cuda.get_device_capability(device)
+    if major != 10:
+        raise RuntimeError(f'B200 attention is built for sm_100a only; device has sm_{major}{minor}')
+    return dict(torch=torch.__version__, cuda=torch.version.cuda, device=torch.cuda.get_device_name(device),
+                capability=(major, minor), library_abi=_lib.load_library().dspark_abi_version())
+
+
+def _stream(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _NativeEntry:
+    """Calls one C-ABI attention entry; replaceable by a test double on CPU."""
+
+    def __init__(self, name):
+        self.name = name
+
+    def __call__(self, *args):
+        _lib.check(getattr(_lib.load_library(), self.name)(*args), self.name)
+
+
+class B200VarlenKernel:
+    """Bottom-right causal packed varlen attention (exact-K contract of rocm_varlen.py:42-117)."""
+    backend_name = BACKEND
+    native_varlen_calls_per_layer = 1
+    causal = True
+    entry = 'dspark_varlen_attn'
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        if self.device.type == 'cuda' and self.device.index is None:
+            self.device = torch.device('cuda', torch.cuda.current_device())
+        self.runtime = runtime_identity(self.device)
+        self._operator = _NativeEntry(self.entry)
+        self._validated_layout = None
+        self._layout_versions = None
+
+    # -- validation (mirrors rocm_varlen.py:65-106) -------------------------
+    def _check_tensors(self, query, key, value, scale):
+        tensors = (query, key, value)
+        if any(not isinstance(t, torch.Tensor) or not t.is_cuda or t.device != self.device
+               or t.dtype not in _DTYPES or t.dtype != query.dtype or t.requires_grad or t.ndim != 3
+               or not t.is_contiguous() for t in tensors):
+            raise ValueError('B200 varlen requires no-autograd contiguous BF16 (or FP32) THD tensors on its GPU')
+        if (query.shape[1:] != (HQ, HEAD_DIM) or key.shape[1:] != (HKV, HEAD_DIM)
+                or value.shape != key.shape or query.shape[0] == 0 or key.shape[0] == 0):
+            raise ValueError('B200 varlen supports nonempty Hq16/Hkv8/D128 Qwen tensors only')
+        if not isinstance(scale, (float, int)) or not math.isfinite(scale) or scale != SCALE:
+            raise ValueError('B200 varlen requires the 1/sqrt(128) scale')
+
+    def _check_layout(self, layout, key_rows_expected, key):
+        for name in ('query_lengths', 'key_lengths', 'cu_query', 'cu_key'):
+            if not hasattr(layout, name):
+                raise ValueError('B200 varlen requires a packed layout')
+        cu = (layout.cu_query, layout.cu_key)
+        if any(not isinstance(t, torch.Tensor) or t.device != self.device or t.dtype != torch.int32
+               or t.ndim != 1 or not t.is_contiguous() for t in cu):
+            raise ValueError('B200 varlen requires contiguous int32 cumulative lengths on its GPU')
+        if key.shape[0] != key_rows_expected:
+            raise ValueError('Tensor token dimensions differ from packed layout')
+        try:
+            versions = tuple(t._version for t in cu)
+        except RuntimeError:
+            versions = None      # inference tensors: revalidate every call
+        if versions is not None and layout is self._validated_layout and versions == self._layout_versions:
+            return
+        qs, ks = layout.query_lengths, layout.key_lengths
+        markers = getattr(layout, 'request_markers', tuple(range(len(qs))))
+        if (not qs or len(qs) != len(ks) or len(markers) != len(qs) or len(set(markers)) != len(qs)
+                or any(type(q) is not int or type(k) is not int or not 0 < q <= k for q, k in zip(qs, ks))):
+            raise ValueError('Invalid packed lengths/markers for bottom-right causal suffixes')
+        if layout.cu_query.tolist() != _cumulative(qs) or layout.cu_key.tolist() != _cumulative(ks):
+            raise ValueError('Cumulative lengths differ from packed metadata')
+        self._validated_layout, self._layout_versions = layout, versions
+
+    def _validate_inputs(self, query, key, value, layout, scale):
+        self._check_tensors(query, key, value, scale)
+        for name in ('query_lengths', 'key_lengths'):
+            if not hasattr(layout, name):
+                raise ValueError('B200 varlen requires a packed layout')
+        if query.shape[0] != sum(layout.query_lengths):
+            raise ValueError('Tensor token dimensions differ from packed layout')
+        self._check_layout(layout, sum(layout.key_lengths), key)
+
+    def __call__(self, query, key, value, layout, *, scale):
+        self._validate_inputs(query, key, value, layout, scale)
+        return self._launch(query, key, value, layout, scale)
+
+    def _launch(self, query, key, value, layout, scale):
+        out = torch.empty_like(query)
+        ws = _lib.workspace(self.device, _stream(self.device))
+        self._operator(query.data_ptr(), key.data_ptr(), value.data_ptr(), layout.cu_query.data_ptr(),
+                       layout.cu_key.data_ptr(), len(layout.query_lengths), query.shape[0], key.shape[0],
+                       max(layout.query_lengths), max(layout.key_lengths), float(scale), _DTYPES[query.dtype],
+                       out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(self.device))
+        if out.shape != query.shape or out.dtype != query.dtype or out.device != query.device:
+            raise RuntimeError('B200 varlen returned incompatible output')
+        return out
+
+
+class B200DraftKernel(B200VarlenKernel):
+    """Non-causal packed varlen attention for the draft block (packed_draft.py:19-32)."""
+    backend_name = DRAFT_BACKEND
+    causal = False
+    entry = 'dspark_draft_attn'
+
+
+class B200CapacityKernel(B200VarlenKernel):
+    """Capacity-tail verify attention (persistent_qwen_target.py:223-234).
+
+    ``len(key) == layout.physical_key_capacity``; rows past ``cu_key[-1]`` are
+    never read, so a NaN or stale tail cannot reach the output.
+    """
+    backend_name = CAPACITY_BACKEND
+
+    def _validate_inputs(self, query, key, value, layout, scale):
+        self._check_tensors(query, key, value, scale)
+        cap = getattr(layout, 'physical_key_capacity', None)
+        if (query.dtype != torch.bfloat16 or type(cap) is not int or len(key) != cap
+                or len(query) != sum(layout.query_lengths) or sum(layout.key_lengths) > cap):
+            raise ValueError('B200 capacity attention shape/dtype/scale differs')
+        self._check_layout(layout, cap, key)
+
+
+def _cumulative(lengths):
+    out = [0]
+    for n in lengths:
+        out.append(out[-1] + n)
+    if out[-1] >= 2 ** 31:
+        raise ValueError('Packed cumulative length exceeds int32')
+    return out
+
+
+def segment_attention(query, cu_query, query_lengths, key_a, value_a, a_start, a_len, key_b=None, value_b=None,
+                      b_start=None, b_len=None, *, causal, scale=SCALE, a_off=0, b_off=0, out=None):
+    """Attention whose keys are two row ranges per request, read in place (no gather copy).
+
+    Keys of request i: rows ``[a_off + a_start[i], + a_len[i])`` of ``key_a``/``value_a``
+    then rows ``[b_off + b_start[i], + b_len[i])`` of ``key_b``/``value_b``. Used for the
+    draft context cache + block rows (packed_draft.py:215-236), the resident prefix +
+    verify scratch (persistent_target_kv.py:441-460) and the training layout, where each
+    anchor block reads context rows [0, anchor) plus its own block (model.py:12-19).
+    All index tensors are int32 on the query's device.
+    """
+    device = query.device
+    if not query.is_cuda:
+        raise RuntimeError('segment_attention requires CUDA tensors; no CPU fallback')
+    tensors = [query, key_a, value_a] + ([key_b, value_b] if key_b is not None else [])
+    if any(t.dtype != query.dtype or t.dtype not in _DTYPES or not t.is_contiguous() or t.device != device
+           for t in tensors):
+        raise ValueError('segment_attention requires contiguous same-dtype bf16/fp32 tensors on one device')
+    if query.shape[1:] != (HQ, HEAD_DIM) or key_a.shape[1:] != (HKV, HEAD_DIM) or value_a.shape != key_a.shape:
+        raise ValueError('segment_attention supports Hq16/Hkv8/D128 only')
+    if key_b is not None and (key_b.shape[1:] != (HKV, HEAD_DIM) or value_b.shape != key_b.shape):
+        raise ValueError('segment_attention supports Hq16/Hkv8/D128 only')
+    ints = [cu_query, a_start, a_len] + [x for x in (b_start, b_len) if x is not None]
+    if any(x.dtype != torch.int32 or x.device != device or not x.is_contiguous() for x in ints):
+        raise ValueError('segment_attention index tensors must be contiguous int32 on the query device')
+    if out is None:
+        out = torch.empty_like(query)
+    ws = _lib.workspace(device, _stream(device))
+    nul = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    _lib.check(_lib.load_library().dspark_segment_attn(
+        query.data_ptr(), key_a.data_ptr(), value_a.data_ptr(), key_a.shape[0], nul(key_b), nul(value_b),
+        key_b.shape[0] if key_b is not None else 0, cu_query.data_ptr(), a_start.data_ptr(), a_len.data_ptr(),
+        nul(b_start), nul(b_len), int(a_off), int(b_off), cu_query.numel() - 1, query.shape[0],
+        max(query_lengths), int(bool(causal)), float(scale), _DTYPES[query.dtype], out.data_ptr(),
+        ws.data_ptr(), ws.numel(), _stream(device)), 'dspark_segment_attn')
+    return out
