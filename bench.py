@@ -11,6 +11,10 @@ Metric: query-token-layers per second = (64*7*5 + 128*7*28) / step time, summed
 over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+                    [--case round|draft|verify] [--layers L]
+
+``--case``/``--layers`` select a smaller workload (one path, fewer layers) for
+profiler captures; the default is the full round the metric is quoted on.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -55,8 +59,8 @@ def contexts(cfg, rank):
     return [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
 
 
-def query_units():
-    return DRAFT['requests'] * BLOCK * DRAFT['layers'] + VERIFY['requests'] * VERIFY['q'] * VERIFY['layers']
+def query_units(draft_layers=DRAFT['layers'], verify_layers=VERIFY['layers']):
+    return DRAFT['requests'] * BLOCK * draft_layers + VERIFY['requests'] * VERIFY['q'] * verify_layers
 
 
 # --------------------------------------------------------------------------- clocks
@@ -71,7 +75,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.gpu), f'--query-gpu={self.FIELDS}',
-                                          '--format=csv,noheader,nounits', '-lms', '100'],
+                                          '--format=csv,noheader,nounits', '-lms', '50'],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
@@ -109,9 +113,11 @@ class ClockSampler:
 class Workload:
     """Device-resident synthetic inputs of one rank (inputs larger than L2: ~62 GB of KV)."""
 
-    def __init__(self, pkg, device, rank, steps_total):
+    def __init__(self, pkg, device, rank, steps_total, draft_layers=DRAFT['layers'],
+                 verify_layers=VERIFY['layers']):
         import torch
         self.pkg, self.device = pkg, device
+        self.draft_layers, self.verify_layers = draft_layers, verify_layers
         gen = torch.Generator(device=device)
         gen.manual_seed(1234 + rank)
         bf = torch.bfloat16
@@ -126,13 +132,13 @@ class Workload:
         self.draft_layout = pkg.PackedLayout.from_lengths(self.draft_qlens, self.draft_klens, device)
         nk = sum(self.draft_klens)
         nq = sum(self.draft_qlens)
-        self.draft_k = [randn(nk, HKV, D) for _ in range(DRAFT['layers'])]
-        self.draft_v = [randn(nk, HKV, D) for _ in range(DRAFT['layers'])]
-        self.draft_q = [randn(nq, HQ, D) for _ in range(DRAFT['layers'])]
+        self.draft_k = [randn(nk, HKV, D) for _ in range(draft_layers)]
+        self.draft_v = [randn(nk, HKV, D) for _ in range(draft_layers)]
+        self.draft_q = [randn(nq, HQ, D) for _ in range(draft_layers)]
         self.draft_kernel = pkg.B200DraftKernel(device)
         # verify: ragged persistent store, capacity = context + growth of every step
         self.verify_ctx = contexts(VERIFY, rank)
-        L, R, Q = VERIFY['layers'], VERIFY['requests'], VERIFY['q']
+        L, R, Q = max(verify_layers, 1), VERIFY['requests'], VERIFY['q']
         growth = Q * (steps_total + 2)
         caps = [c + growth for c in self.verify_ctx]
         self.store = pkg.B200PersistentTargetKV(layers=L, slots=R, context_capacity=max(caps),
@@ -171,7 +177,7 @@ class Workload:
         ``host``: pinned host buffers for the end-to-end path (inputs copied in, outputs out)."""
         import torch
         launches = 0
-        for layer in range(DRAFT['layers']):
+        for layer in range(self.draft_layers):
             e0 = self._event(events)
             q = self.draft_q[layer]
             if host is not None:
@@ -182,10 +188,12 @@ class Workload:
                 host['do'][layer].copy_(out, non_blocking=True)
             launches += 2
             self._close(events, e0, 'draft')
+        if not self.verify_layers:
+            return launches
         store = self.store
         tx = store.begin(self.handles, query_lengths=[VERIFY['q']] * VERIFY['requests'])
         ctx_now = tx.context_lengths
-        for layer in range(VERIFY['layers']):
+        for layer in range(self.verify_layers):
             e0 = self._event(events)
             qr, kr, vr = self.vq[layer], self.vk[layer], self.vv[layer]
             if host is not None:
@@ -319,7 +327,11 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
-    wl = Workload(pkg, device, rank, args.warmup + 2 * args.steps + 4)
+    dl = DRAFT['layers'] if args.case in ('round', 'draft') else 0
+    vl = VERIFY['layers'] if args.case in ('round', 'verify') else 0
+    if args.layers is not None:
+        dl, vl = min(dl, args.layers), min(vl, args.layers)
+    wl = Workload(pkg, device, rank, args.warmup + 2 * args.steps + 4, dl, vl)
 
     def barrier():
         if world > 1:
@@ -370,22 +382,22 @@ def run_b200(args):
     if rank == 0:
         max_ms = float(allstats[:, 0].max())
         max_e2e = float(allstats[:, 1].max())
-        units = query_units() * args.steps * world
+        units = query_units(dl, vl) * args.steps * world
         value = units / (max_ms / 1e3)
         e2e_value = units / (max_e2e / 1e3)
         hbm, peak_kind = peaks()
-        v_ms = statistics.mean(per['verify'])
-        v_bytes = statistics.mean(vbytes)
+        v_ms = statistics.mean(per['verify']) if per['verify'] else float('nan')
+        v_bytes = statistics.mean(vbytes) if vbytes else float('nan')
         achieved = v_bytes / (v_ms / 1e3) / 1e9
-        d_ms = statistics.mean(per['draft'])
+        d_ms = statistics.mean(per['draft']) if per['draft'] else float('nan')
         d_achieved = wl.draft_layer_bytes() / (d_ms / 1e3) / 1e9
         h2d, d2h = wl.host_bytes(host)
-        cpu_v, reps, el = cpu_sample(seconds=12.0)
+        cpu_v, reps, el = (float('nan'), 0, 0.0) if args.no_cpu_baseline else cpu_sample(seconds=12.0)
         line = dict(
             metric=METRIC, value=value, unit='query-tok/s', n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=max_ms / args.steps, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
             data='synthetic (seeded N(0,1) q/k/v and KV cache; shapes of BASELINE configs 2 and 3)',
-            config=dict(workload='cfg2 draft x5 layers + cfg3 verify x28 layers (+ commit/rollback) per step',
+            config=dict(workload=f'cfg2 draft x{dl} layers + cfg3 verify x{vl} layers (+ commit/rollback) per step',
                         draft_requests=DRAFT['requests'], draft_ctx='U[128,4096] seed 1', verify_requests=VERIFY['requests'],
                         verify_ctx='U[256,8192] seed 2', verify_q=VERIFY['q'], heads='16/8', head_dim=D,
                         rope_theta=1e6, rms_eps=1e-6, parallelism=f'dp{world} (independent request batches)',
@@ -412,9 +424,12 @@ def run_b200(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--gpus', type=int, default=1)
-    ap.add_argument('--steps', type=int, default=20)
+    ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify'])
+    ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
+    ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
