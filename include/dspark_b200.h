@@ -138,6 +138,27 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
                      const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
                      int scratch_rows, cudaStream_t stream);
 
+/*
+ * Allocation-free variant of dspark_varlen_attn (bf16 only). No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory for a
+ * workspace - an FFI host (Go, Java) without access to the allocator that owns
+ * the GPU, or a server that has reserved nearly all HBM for its KV-cache pool,
+ * where an extra cudaMalloc would fail and a cudaMalloc/cudaFree would stall the
+ * device mid-step. The split-item scratch is a static device array of
+ * dspark_varlen_attn_noalloc_scratch_bytes() bytes (18.8 MiB: partials of at
+ * most 148 CTAs) that every GPU loading the library holds until exit; the
+ * requirement does not grow with the inputs, and the call returns
+ * DSPARK_ERR_UNSUPPORTED if a launch would ever need more. The first call on a
+ * device looks up that device's address of the array (make it before any
+ * stream capture). All calls share the array and it keeps the last call's
+ * contents (nothing in it needs to start at zero); calls that overlap on the
+ * GPU, e.g. on two streams, race on it. Allocates nothing.
+ */
+size_t dspark_varlen_attn_noalloc_scratch_bytes(void);
+int dspark_varlen_attn_noalloc(const void* q, const void* k, const void* v, const int32_t* cu_q,
+                               const int32_t* cu_k, int num_requests, int total_q, long long key_rows, int max_q,
+                               int max_k, float scale, void* out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

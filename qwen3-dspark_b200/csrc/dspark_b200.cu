@@ -350,3 +350,80 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of dspark_varlen_attn.
+//
+// Some callers cannot allocate device memory for a workspace: a host that
+// embeds this library through a C FFI (Go, Java) and has no access to the
+// framework allocator that owns the GPU, or a serving process that has handed
+// nearly all HBM to its KV-cache pool up front, where an extra cudaMalloc
+// fails or fragments the pool and a cudaMalloc/cudaFree pair would also
+// synchronise the device in the middle of a decode step. For them the
+// split-item partials live in the static array below instead of a
+// caller-provided workspace.
+// ---------------------------------------------------------------------------
+namespace {
+
+// The scratch holds the partials of at most this many persistent CTAs; the
+// entry point never launches more. Its size does not depend on the inputs.
+constexpr int kNoAllocMaxCtas = 148;
+constexpr size_t kNoAllocScratchBytes =
+    static_cast<size_t>(kNoAllocMaxCtas) * (2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float) +
+                                            sizeof(AttnRecord));
+
+// 148 CTAs x (2 x 66 KB of fp32 partials + 32 B record) = 18.8 MiB. Every GPU
+// that loads this library holds it until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+}  // namespace
+
+extern "C" size_t dspark_varlen_attn_noalloc_scratch_bytes(void) { return kNoAllocScratchBytes; }
+
+extern "C" int dspark_varlen_attn_noalloc(const void* q, const void* k, const void* v, const int32_t* cu_q,
+                                          const int32_t* cu_k, int num_requests, int total_q, long long key_rows,
+                                          int max_q, int max_k, float scale, void* out, cudaStream_t stream) {
+  (void)max_q;
+  (void)max_k;
+  if (!common_ok(q, out, cu_q, num_requests, total_q, scale, DSPARK_DTYPE_BF16) || !k || !v || !cu_k ||
+      key_rows < 1)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess) return DSPARK_ERR_CUDA;
+  DeviceInfo info;
+  int st = device_info(dev, &info);
+  if (st != DSPARK_OK) return st;
+  void* scratch = nullptr;
+  {
+    // Once per device, with that device current: the host-side symbol is not a
+    // device address, so ask the runtime for this device's copy of the array.
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr) return DSPARK_ERR_CUDA;
+      g_noalloc_ptr[dev] = ptr;
+    }
+    scratch = g_noalloc_ptr[dev];
+  }
+  const int grid = info.sms < kNoAllocMaxCtas ? info.sms : kNoAllocMaxCtas;
+  if (workspace_for_grid(grid) > kNoAllocScratchBytes) return DSPARK_ERR_UNSUPPORTED;
+  AttnParams p = base_params(q, out, cu_q, num_requests, total_q, scale, 1);
+  p.mode = kModeVarlen;
+  p.cu_k = cu_k;
+  uint8_t* ws = static_cast<uint8_t*>(scratch);
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
+  p.records = reinterpret_cast<AttnRecord*>(ws + static_cast<size_t>(grid) * 2 *
+                                                     (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
+  p.grid = grid;
+  p.rows_a = key_rows;
+  CUtensorMap ka, va;
+  if ((st = encode_kv_map(&ka, k, key_rows)) != DSPARK_OK) return st;
+  if ((st = encode_kv_map(&va, v, key_rows)) != DSPARK_OK) return st;
+  attn_bf16_kernel<true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, ka, va, p);
+  if ((st = launch_status()) != DSPARK_OK) return st;
+  attn_merge_kernel<<<grid, 256, 0, stream>>>(p);
+  return launch_status();
+}
