@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 1
+#define DSPARK_ABI_VERSION 3
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -45,7 +45,9 @@ int dspark_abi_version(void);
 const char* dspark_status_string(int status);
 
 /* Bytes of workspace the bf16 attention entry points need on `device`
- * (split-item partials; scales with the SM count, ~19 MB on a B200). */
+ * (fp32 partials of items split between CTAs plus per-item arrival counters;
+ * scales with the SM count, ~19 MB on a B200). Its contents never need
+ * clearing: counters are tagged with a per-launch epoch. */
 int dspark_attention_workspace_size(int device, size_t* bytes);
 
 /* Copies the device status word of the current device (synchronising), and
@@ -100,17 +102,28 @@ int dspark_segment_attn(const void* q, const void* ka, const void* va, long long
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
- * Fused verify layer for a persistent KV store (bf16):
+ * cos/sin table of a verify transaction, shared by every layer: for new row r of
+ * request i (row cu_q[i] + r, position ctx_len[i] + r) and frequency f < 64,
+ * table[row * 64 + f] = bf16 cos | bf16 sin << 16 of float32(position) * inv_freq[f].
+ * table: [total_q, 64] uint32, 16-byte aligned. Replaces the per-forward
+ * Qwen3RotaryEmbedding.forward of transformers (modeling_qwen3.py:137-148) that the
+ * reference's verify runs once per model call (persistent_qwen_target.py:408-410).
+ */
+int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t* ctx_len, int num_requests,
+                      int total_q, void* table, cudaStream_t stream);
+
+/*
+ * Fused verify layer for a persistent KV store (bf16), one kernel launch:
  *  1. Qwen3 q_norm/k_norm (RMSNorm over the head dim, eps) and rotate-half RoPE
- *     (inv_freq [64] float32) of the new tokens' raw projections, at position
- *     ctx_len[i] + r for new row r of request i;
+ *     (cos/sin from dspark_rope_table) of the new tokens' raw projections, at
+ *     position ctx_len[i] + r for new row r of request i (q in registers, k in
+ *     shared memory after its TMA load);
  *  2. KV append: roped k and raw v into scratch rows layer*scratch_rows + cu_q[i] + r;
- *     roped q into q_roped [total_q, 16, 128];
  *  3. bottom-right causal attention over the resident prefix rows
  *     layer*rows_per_layer + slot_row[i] + [0, ctx_len[i]) followed by the
- *     request's scratch rows, read in place (no workspace gather).
+ *     request's new rows, read in place (no workspace gather).
  * Resident K/V: [num_layers * rows_per_layer, 8, 128]; scratch K/V:
- * [num_layers * scratch_rows, 8, 128].
+ * [num_layers * scratch_rows, 8, 128]; k_raw/v_raw: [total_q, 8, 128].
  * Replaces, per decoder layer, transformers Qwen3Attention.forward's
  * q_norm/k_norm/apply_rotary_pos_emb (modeling_qwen3.py:263-268) plus
  * _VerificationCache.update (dspark_qwen/persistent_qwen_target.py:73-83:
@@ -118,11 +131,11 @@ int dspark_segment_attn(const void* q, const void* ka, const void* va, long long
  * plus persistent_attention_forward -> _native_attention (persistent_qwen_target.py:45-60,223-234).
  */
 int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
-                        const void* k_norm_weight, const float* inv_freq, float eps, const int32_t* cu_q,
+                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
                         const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
                         void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
-                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* q_roped,
-                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Commit / rollback for all layers in one launch: for every request copy
@@ -145,8 +158,8 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
  * the GPU, or a server that has reserved nearly all HBM for its KV-cache pool,
  * where an extra cudaMalloc would fail and a cudaMalloc/cudaFree would stall the
  * device mid-step. The split-item scratch is a static device array of
- * dspark_varlen_attn_noalloc_scratch_bytes() bytes (18.8 MiB: partials of at
- * most 148 CTAs) that every GPU loading the library holds until exit; the
+ * dspark_varlen_attn_noalloc_scratch_bytes() bytes (18.8 MiB: partials and
+ * counters of at most 148 CTAs) that every GPU loading the library holds until exit; the
  * requirement does not grow with the inputs, and the call returns
  * DSPARK_ERR_UNSUPPORTED if a launch would ever need more. The first call on a
  * device looks up that device's address of the array (make it before any

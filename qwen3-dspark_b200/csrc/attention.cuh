@@ -18,8 +18,17 @@
 // ranges, one per CTA (one CTA per SM). A CTA streams its range through a
 // 3-stage TMA pipeline: warp 8 issues the loads, warps 0-7 (one per KV head)
 // consume them. Items that lie wholly inside one range are normalised and
-// written directly; an item cut by a range boundary leaves fp32 partials that
-// a second small kernel merges (log-sum-exp combine).
+// written directly. An item cut by range boundaries leaves fp32 partials; the
+// warp that contributes last (an epoch-tagged counter per item and head, no
+// waiting) merges them with a log-sum-exp combine and writes the output.
+//
+// Fused verify mode (kFused): q holds the layer's raw q projections and source
+// B is the raw k/v projections of the new tokens. Consumer warps apply Qwen3
+// RMSNorm + RoPE to their Q fragments in registers and to the new k rows in
+// shared memory after TMA delivers them, and append roped k / raw v to the
+// layer's scratch rows (the KV append). cos/sin come from a per-transaction
+// table (computed once for all layers, as the model's rotary module does); the
+// producer bulk-copies a new-row tile's table rows next to its K/V box.
 #pragma once
 #include <cfloat>
 #include <climits>
@@ -37,22 +46,20 @@ constexpr int kConsumerWarps = kKVHeads;                // warp w computes KV he
 constexpr int kAttnThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kHalfBoxBytes = kKVHeads * kTileN * 128;  // 64 bf16 x 16 rows x 8 heads
 constexpr int kStageBytes = 4 * kHalfBoxBytes;          // K lo/hi + V lo/hi halves
+constexpr int kRopeRowBytes = 64 * 4;                   // 64 (cos, sin) bf16 pairs per position
+constexpr int kRopeStageBytes = kTileN * kRopeRowBytes;  // table rows of one source-B tile
+// Dynamic shared memory: stages | rope rows per stage | q_norm, k_norm weights |
+// full/empty barriers | schedule scratch (the base is rounded up to 1024 B).
+constexpr int kSmemRopeOff = kStages * kStageBytes;
+constexpr int kSmemWeightOff = kSmemRopeOff + kStages * kRopeStageBytes;
+constexpr int kSmemBarOff = kSmemWeightOff + 2 * kHeadDim * 2;
 constexpr int kPartFloatsPerSlot = kKVHeads * 16 * kHeadDim;
 constexpr int kPartMlPerSlot = kKVHeads * 16 * 2;
 
 enum KeyMode : int { kModeVarlen = 0, kModeSegmented = 1 };
 
-struct AttnRecord {          // per CTA, consumed by the merge kernel
-  int needs_merge;
-  int req;
-  int qb;
-  int pad;
-  long long item_start;
-  long long total_tiles;
-};
-
 struct AttnParams {
-  const void* q;             // [total_q, 16, 128]
+  const void* q;             // [total_q, 16, 128] (raw q projections in fused mode)
   void* out;                 // [total_q, 16, 128]
   const int* cu_q;           // [R+1]
   int num_requests;
@@ -75,22 +82,35 @@ struct AttnParams {
   long long rows_b;
   float scale;
   float scale_log2;          // scale * log2(e)
+  // fused verify: new token row r of request i is global row cu_q[i] + r of
+  // k_new/v_new and of this layer's scratch; its position is a_len[i] + r.
+  const __nv_bfloat16* k_new;   // [total_q, 8, 128] raw k projections
+  const __nv_bfloat16* v_new;   // [total_q, 8, 128] raw v projections
+  const __nv_bfloat16* q_w;     // [128] q_norm weight
+  const __nv_bfloat16* k_w;     // [128] k_norm weight
+  const uint32_t* rope;         // [total_q][64] bf16x2 (cos low, sin high) at each new row's position
+  float eps;
+  __nv_bfloat16* scratch_k;     // this layer's scratch rows (source B)
+  __nv_bfloat16* scratch_v;
+  int scratch_rows;
   // workspace (split items)
   float* part_o;             // [grid][2][8][16][128]
   float* part_ml;            // [grid][2][8][16][2]
-  AttnRecord* records;       // [grid]
+  unsigned long long* counters;  // [grid][8]: (epoch << 32) | arrivals, per item and head
+  unsigned int epoch;        // unique per launch; stale counters never match it
   int grid;
 };
 
 // ---------------------------------------------------------------------------
-// Item geometry and the tile walk shared by the scan, the producer, the
-// consumers and the merge kernel.
+// Item geometry and the tile walk shared by the scan, the producer and the
+// consumers.
 // ---------------------------------------------------------------------------
 struct Item {
   int req, qb;
   int q0;        // first query row (global) of this block
   int nrows;     // valid query rows in this block (1..8)
   int q_len;     // request query rows
+  int q_start;   // cu_q[req]
   int a_row, a_len, b_row, b_len;
   int k_len;     // a_len + b_len
   int vis;       // keys visible to the block's last row
@@ -107,6 +127,7 @@ __device__ __forceinline__ void load_item(const AttnParams& p, int req, int qb, 
   it.req = req;
   it.qb = qb;
   const int qs = p.cu_q[req];
+  it.q_start = qs;
   it.q_len = p.cu_q[req + 1] - qs;
   it.q0 = qs + qb * kQBlock;
   it.nrows = min(kQBlock, it.q_len - qb * kQBlock);
@@ -168,6 +189,7 @@ struct Tile {
   int row;        // first row of the tile in its source tensor
   int n_valid;    // keys of this tile inside the item's visible range
   int key_base;   // index of the tile's first key in the item's key order
+  int b_first;    // source B: index of the tile's first row among the request's B rows
 };
 
 __device__ __forceinline__ Tile tile_of(const Item& it, int t) {
@@ -177,12 +199,14 @@ __device__ __forceinline__ Tile tile_of(const Item& it, int t) {
     ti.row = it.a_row + t * kTileN;
     ti.n_valid = min(kTileN, min(it.vis, it.a_len) - t * kTileN);
     ti.key_base = t * kTileN;
+    ti.b_first = 0;
   } else {
     const int tb = t - it.tiles_a;
     ti.src_b = 1;
     ti.row = it.b_row + tb * kTileN;
     ti.n_valid = min(kTileN, (it.vis - it.a_len) - tb * kTileN);
     ti.key_base = it.a_len + tb * kTileN;
+    ti.b_first = tb * kTileN;
   }
   ti.n_valid = max(ti.n_valid, 0);
   return ti;
@@ -217,6 +241,10 @@ __device__ __forceinline__ long long range_start(long long c, long long total, l
 // The CTA whose range holds global tile x (largest c with range_start(c) <= x).
 __device__ __forceinline__ int cta_of_tile(long long x, long long total, long long grid) {
   return static_cast<int>(((x + 1) * grid - 1) / total);
+}
+
+__device__ __forceinline__ bool range_empty(int c, long long total, long long grid) {
+  return range_start(c, total, grid) == range_start(c + 1, total, grid);
 }
 
 // Inclusive block-wide scan of v over all threads of the CTA.
@@ -308,20 +336,7 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
       }
       s.qb0 = qb;
       s.t0 = static_cast<int>(off);
-      AttnRecord r;
-      r.req = s.req0;
-      r.qb = qb;
-      r.pad = 0;
-      r.item_start = start - off;
-      r.total_tiles = total;
-      r.needs_merge = (off > 0) && (r.item_start + it.tiles <= end);
-      p.records[blockIdx.x] = r;
     }
-  }
-  if (tid == 0 && !(start < end)) {
-    AttnRecord r{};
-    r.total_tiles = total;
-    p.records[blockIdx.x] = r;
   }
   __syncthreads();
 }
@@ -336,21 +351,305 @@ __device__ __forceinline__ float quad_sum(float v) {
   return v + __shfl_xor_sync(0xffffffffu, v, 2);
 }
 
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+  return __bfloat1622float2(b);
+}
+
+// Qwen3 RMSNorm + rotate-half RoPE (bf16 arithmetic order of transformers) of
+// one head of one MMA A-fragment row: regs lo[ks] hold d = 16ks+2t, +1 and
+// hi[ks] hold d = 16ks+2t+8, +9 (t = lane & 3). The quad (4 lanes) holds the
+// full 128-d row; the RoPE partner d+64 of d < 64 is the same thread's ks+4.
+// cs/sn: bf16-rounded cos/sin of this thread's 16 frequencies (ks<4, e).
+__device__ __forceinline__ void norm_rope_fragment(uint32_t (&lo)[8], uint32_t (&hi)[8], const AttnParams& p,
+                                                   const __nv_bfloat16* w, const float (&cs)[4][4],
+                                                   const float (&sn)[4][4], int t4) {
+  float x[8][4];
+  float ss = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const float2 a = unpack_bf16x2(lo[ks]), b = unpack_bf16x2(hi[ks]);
+    x[ks][0] = a.x;
+    x[ks][1] = a.y;
+    x[ks][2] = b.x;
+    x[ks][3] = b.y;
+    ss += a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+  }
+  ss = quad_sum(ss);
+  const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int d = ks * 16 + 2 * t4 + (e & 1) + (e >> 1) * 8;
+      x[ks][e] = bf16r(__bfloat162float(w[d]) * bf16r(x[ks][e] * rs));
+    }
+#pragma unroll
+  for (int ks = 0; ks < 4; ++ks) {
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float c = cs[ks][e], s = sn[ks][e];
+      const float a = x[ks][e], b = x[ks + 4][e];
+      x[ks][e] = bf16r(bf16r(a * c) + bf16r(-b * s));
+      x[ks + 4][e] = bf16r(bf16r(b * c) + bf16r(a * s));
+    }
+  }
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    lo[ks] = pack_bf16x2(x[ks][0], x[ks][1]);
+    hi[ks] = pack_bf16x2(x[ks][2], x[ks][3]);
+  }
+}
+
+// Fused verify: a source-B tile holds the raw k/v projections of a request's
+// new rows (TMA-loaded from k_new/v_new like any other tile). The consumer
+// warp of KV head h applies k_norm + RoPE to its head's rows in shared memory
+// (row rr of the tile is request row b_first + rr, at position
+// a_len + b_first + rr) and appends roped k and raw v to the layer's scratch.
+// Lane l owns d = 4l..4l+3; the rotate-half partner of d lives in lane l ^ 16.
+__device__ __forceinline__ void rope_new_rows_in_smem(const AttnParams& p, const Item& it, const Tile& ti, int h,
+                                                      int lane, uint8_t* stage, const uint8_t* rope_rows,
+                                                      const __nv_bfloat16* kw_smem) {
+  const int d0 = lane * 4;
+  float w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) w[i] = __bfloat162float(kw_smem[d0 + i]);
+  const int half = lane >> 4;                 // d < 64 -> low half box
+  const int chunk = (lane & 15) >> 1;         // 16-byte chunk inside the 128-byte half row
+  const int sub = (lane & 1) * 8;             // byte offset inside the chunk
+  const int f0 = d0 & 63;                     // frequencies of d0..d0+3
+  for (int rr = 0; rr < ti.n_valid; ++rr) {   // warp-uniform bound
+    const int row = it.q_start + ti.b_first + rr;
+    if (row < 0 || row >= p.total_q || row >= p.scratch_rows) continue;
+    const int soff = (h * kTileN + rr) * 128 + ((chunk ^ (rr & 7)) << 4) + sub;
+    uint2* ks = reinterpret_cast<uint2*>(stage + half * kHalfBoxBytes + soff);
+    const uint2 raw = *ks;
+    const uint2 vraw = *reinterpret_cast<const uint2*>(stage + (2 + half) * kHalfBoxBytes + soff);
+    const uint4 cs4 = *reinterpret_cast<const uint4*>(rope_rows + rr * kRopeRowBytes + f0 * 4);
+    const uint32_t csw[4] = {cs4.x, cs4.y, cs4.z, cs4.w};
+    const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+    const float x[4] = {a.x, a.y, b.x, b.y};
+    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+    float y[4], partner[4], out[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) y[e] = bf16r(w[e] * bf16r(x[e] * rs));
+#pragma unroll
+    for (int e = 0; e < 4; ++e) partner[e] = __shfl_xor_sync(0xffffffffu, y[e], 16);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 c_s = unpack_bf16x2(csw[e]);
+      const float rot = lane < 16 ? -partner[e] : partner[e];
+      out[e] = bf16r(bf16r(y[e] * c_s.x) + bf16r(rot * c_s.y));
+    }
+    uint2 kv;
+    kv.x = pack_bf16x2(out[0], out[1]);
+    kv.y = pack_bf16x2(out[2], out[3]);
+    *ks = kv;
+    const size_t off = (static_cast<size_t>(row) * kKVHeads + h) * kHeadDim + d0;
+    *reinterpret_cast<uint2*>(p.scratch_k + off) = kv;
+    *reinterpret_cast<uint2*>(p.scratch_v + off) = vraw;
+  }
+}
+
+// Epoch-tagged arrival counter of one cut item and head: returns this
+// arrival's ordinal (1-based), 0 if the bounded CAS loop never succeeded.
+__device__ __forceinline__ unsigned int count_arrival(unsigned long long* ctr, unsigned int epoch) {
+  const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(ctr);
+  for (int i = 0; i < (1 << 20); ++i) {
+    const unsigned int cnt = static_cast<unsigned int>(cur >> 32) == epoch ? static_cast<unsigned int>(cur) : 0u;
+    const unsigned long long prev = atomicCAS(ctr, cur, tag | (cnt + 1u));
+    if (prev == cur) return cnt + 1u;
+    cur = prev;
+  }
+  atomicOr(&g_device_status, kStatusBadSchedule);
+  return 0u;
+}
+
+// Partial slot of contributor c for an item starting at tile item_start: slot
+// 1 only when the item began before c's range (c is then the item's first
+// contributor and the item is its last one).
+__device__ __forceinline__ int partial_slot(long long item_start, int c, long long total, long long grid) {
+  return item_start <= range_start(c, total, grid) ? 0 : 1;
+}
+
+// The last-arriving warp of a cut item merges all contributors' partials of
+// KV head h and writes the item's output rows. Rows are merged 8 at a time
+// (one head of the GQA pair) with an online log-sum-exp rescale, so each
+// contributor costs one round of independent loads. With at least as many
+// tiles as CTAs no range is empty and only the first contributor can hold the
+// item in slot 1, so the loop needs no division.
+__device__ __forceinline__ void merge_split_item(const AttnParams& p, int q0, int nrows, long long item_start,
+                                                 int first, int last, long long total, int h, int lane) {
+  __threadfence();
+  __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
+  const int d = lane * 4;
+  const bool dense = total >= p.grid;
+  const int slot_first = partial_slot(item_start, first, total, p.grid);
+  const float sl2 = p.scale_log2;
+#pragma unroll 1
+  for (int hh = 0; hh < 2; ++hh) {               // rows 8hh..8hh+7 = head 2h+hh
+    float4 acc[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float mrow = -INFINITY, lrow = 0.f;          // lane r < 8 tracks row r
+    for (int c = first; c <= last; ++c) {
+      if (!dense && range_empty(c, total, p.grid)) continue;
+      const int sl = c == first ? slot_first : (dense ? 0 : partial_slot(item_start, c, total, p.grid));
+      const size_t bi = (static_cast<size_t>(c) * 2 + sl) * kKVHeads + h;
+      const float* pml = p.part_ml + bi * 32 + 16 * hh;
+      const float* po = p.part_o + (bi * 16 + 8 * hh) * kHeadDim + d;
+      const float2 ml = __ldcg(reinterpret_cast<const float2*>(pml + 2 * (lane & 7)));
+      float4 v[8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r) v[r] = __ldcg(reinterpret_cast<const float4*>(po + r * kHeadDim));
+      const float mnew = fmaxf(mrow, ml.x);
+      const float mu = mnew == -INFINITY ? 0.f : mnew;
+      const float a_old = ex2((mrow - mu) * sl2), w = ex2((ml.x - mu) * sl2);
+      lrow = lrow * a_old + w * ml.y;
+      mrow = mnew;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float ar = __shfl_sync(0xffffffffu, a_old, r), wr = __shfl_sync(0xffffffffu, w, r);
+        acc[r].x = acc[r].x * ar + wr * v[r].x;
+        acc[r].y = acc[r].y * ar + wr * v[r].y;
+        acc[r].z = acc[r].z * ar + wr * v[r].z;
+        acc[r].w = acc[r].w * ar + wr * v[r].w;
+      }
+    }
+    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float ir = __shfl_sync(0xffffffffu, inv, r);
+      const int row = q0 + r;
+      if (r >= nrows || row < 0 || row >= p.total_q) continue;
+      __nv_bfloat16* dst = og + (static_cast<size_t>(row) * kQHeads + 2 * h + hh) * kHeadDim + d;
+      uint2 res;
+      res.x = pack_bf16x2(acc[r].x * ir, acc[r].y * ir);
+      res.y = pack_bf16x2(acc[r].z * ir, acc[r].w * ir);
+      *reinterpret_cast<uint2*>(dst) = res;
+    }
+  }
+}
+
+// A cut item's contribution from this CTA (warp of KV head h): store the fp32
+// partial O (unnormalised), row max m and row sum l; the warp that arrives
+// last over all contributing CTAs merges every partial and writes the output.
+__device__ __forceinline__ void finish_split_item(const AttnParams& p, const Item& it, long long item_start,
+                                                  long long item_end, long long start, long long total, int h,
+                                                  int lane, const float (&o)[16][4], float m_a, float m_b, float l_a,
+                                                  float l_b) {
+  const int g = lane >> 2, t4 = lane & 3;
+  const int slot = item_start <= start ? 0 : 1;
+  const size_t base = (static_cast<size_t>(blockIdx.x) * 2 + slot) * kKVHeads + h;
+  float* po = p.part_o + base * 16 * kHeadDim;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int d = j * 8 + 2 * t4;
+    __stcg(reinterpret_cast<float2*>(po + g * kHeadDim + d), make_float2(o[j][0], o[j][1]));
+    __stcg(reinterpret_cast<float2*>(po + (g + 8) * kHeadDim + d), make_float2(o[j][2], o[j][3]));
+  }
+  if (t4 == 0) {
+    float* pml = p.part_ml + base * 32;
+    __stcg(reinterpret_cast<float2*>(pml + 2 * g), make_float2(m_a, l_a));
+    __stcg(reinterpret_cast<float2*>(pml + 2 * (g + 8)), make_float2(m_b, l_b));
+  }
+  __threadfence();
+  __syncwarp();
+  const int first = cta_of_tile(item_start, total, p.grid);
+  const int last = cta_of_tile(item_end - 1, total, p.grid);
+  unsigned int merge = 0;
+  if (lane == 0) {
+    int n = last - first + 1;
+    if (total < p.grid)            // tiny launch: some ranges are empty and contribute nothing
+      for (int c = first; c <= last; ++c) n -= range_empty(c, total, p.grid) ? 1 : 0;
+    merge = count_arrival(p.counters + static_cast<size_t>(first) * kKVHeads + h, p.epoch) ==
+            static_cast<unsigned int>(n);
+  }
+  merge = __shfl_sync(0xffffffffu, merge, 0);
+  if (merge) merge_split_item(p, it.q0, it.nrows, item_start, first, last, total, h, lane);
+}
+
+// Q fragments of heads 2h (MMA rows 0-7) and 2h+1 (rows 8-15) for query row
+// g of item `it`; in fused verify mode they are normalised and rotated here.
+template <bool kFused>
+__device__ __forceinline__ void load_q_fragments(const AttnParams& p, const Item& it, int h, int lane,
+                                                 const __nv_bfloat16* qw_smem, uint32_t (&qf)[8][4]) {
+  const int g = lane >> 2, t4 = lane & 3;
+  const int row = it.q0 + g;
+  const bool rv = g < it.nrows && row >= 0 && row < p.total_q;
+  const __nv_bfloat16* qa =
+      static_cast<const __nv_bfloat16*>(p.q) + (static_cast<size_t>(row) * kQHeads + 2 * h) * kHeadDim;
+  const __nv_bfloat16* qb = qa + kHeadDim;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+    const int d = ks * 16 + 2 * t4;
+    qf[ks][0] = rv ? ld_nc_u32(qa + d) : 0u;
+    qf[ks][1] = rv ? ld_nc_u32(qb + d) : 0u;
+    qf[ks][2] = rv ? ld_nc_u32(qa + d + 8) : 0u;
+    qf[ks][3] = rv ? ld_nc_u32(qb + d + 8) : 0u;
+  }
+  if (kFused) {
+    // q_norm + RoPE of the raw projections; row g sits at position a_len + qb*8 + g.
+    // cos/sin of this row's position for d = 16ks+2t+{0,1} and +{8,9} (ks < 4).
+    float cs[4][4], sn[4][4];
+    const uint32_t* tr = p.rope + static_cast<size_t>(rv ? row : 0) * 64 + 2 * t4;
+#pragma unroll
+    for (int ks = 0; ks < 4; ++ks) {
+      const uint2 lo2 = __ldg(reinterpret_cast<const uint2*>(tr + ks * 16));
+      const uint2 hi2 = __ldg(reinterpret_cast<const uint2*>(tr + ks * 16 + 8));
+      const uint32_t e4[4] = {lo2.x, lo2.y, hi2.x, hi2.y};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 cv = unpack_bf16x2(e4[e]);
+        cs[ks][e] = cv.x;
+        sn[ks][e] = cv.y;
+      }
+    }
+    uint32_t lo[8], hi[8];
+#pragma unroll
+    for (int hh = 0; hh < 2; ++hh) {
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        lo[ks] = qf[ks][hh];
+        hi[ks] = qf[ks][hh + 2];
+      }
+      norm_rope_fragment(lo, hi, p, qw_smem, cs, sn, t4);
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        qf[ks][hh] = rv ? lo[ks] : 0u;
+        qf[ks][hh + 2] = rv ? hi[ks] : 0u;
+      }
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // bf16 tensor-core kernel
 // ---------------------------------------------------------------------------
-template <bool kCausal>
+template <bool kCausal, bool kFused>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     attn_bf16_kernel(const __grid_constant__ CUtensorMap tm_ka, const __grid_constant__ CUtensorMap tm_va,
                      const __grid_constant__ CUtensorMap tm_kb, const __grid_constant__ CUtensorMap tm_vb,
                      const AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kSmemBarOff);
   uint64_t* empty = full + kStages;
   SchedShared& sched = *reinterpret_cast<SchedShared*>(empty + kStages);
+  __nv_bfloat16* qw_smem = reinterpret_cast<__nv_bfloat16*>(smem + kSmemWeightOff);
+  __nv_bfloat16* kw_smem = qw_smem + kHeadDim;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (kFused && threadIdx.x < kHeadDim) {
+    qw_smem[threadIdx.x] = p.q_w[threadIdx.x];
+    kw_smem[threadIdx.x] = p.k_w[threadIdx.x];
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
@@ -360,7 +659,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     fence_barrier_init();
   }
   locate_range<kAttnThreads>(p, sched);   // contains __syncthreads
-  const long long start = sched.start, end = sched.end;
+  const long long start = sched.start, end = sched.end, total = sched.total;
   if (start >= end) return;
 
   if (warp == kConsumerWarps) {
@@ -379,11 +678,16 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t parity = ((kl / kStages) & 1) ^ 1;
         if (!mbar_wait(smem_u32(&empty[stage]), parity)) break;
         const Tile ti = tile_of(w.it, w.t);
+        const uint32_t bar = smem_u32(&full[stage]);
         const CUtensorMap* mk = ti.src_b ? &tm_kb : &tm_ka;
         const CUtensorMap* mv = ti.src_b ? &tm_vb : &tm_va;
-        const uint32_t bar = smem_u32(&full[stage]);
         const uint32_t dst = smem_u32(smem + stage * kStageBytes);
-        mbar_arrive_expect_tx(bar, kStageBytes);
+        // fused new-row tile: also its rows of the cos/sin table (clamped to the table)
+        const int rope_rows = (kFused && ti.src_b) ? max(0, min(kTileN, p.total_q - ti.row)) : 0;
+        mbar_arrive_expect_tx(bar, kStageBytes + rope_rows * kRopeRowBytes);
+        if (rope_rows > 0)
+          bulk_load(smem_u32(smem + kSmemRopeOff + stage * kRopeStageBytes),
+                    p.rope + static_cast<size_t>(ti.row) * 64, rope_rows * kRopeRowBytes, bar);
         tma_load_3d(dst, mk, 0, ti.row, 0, bar);
         tma_load_3d(dst + kHalfBoxBytes, mk, 64, ti.row, 0, bar);
         tma_load_3d(dst + 2 * kHalfBoxBytes, mv, 0, ti.row, 0, bar);
@@ -398,44 +702,31 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int h = warp;
     const int g = lane >> 2, t4 = lane & 3;
     const float sl2 = p.scale_log2;
-    const __nv_bfloat16* qg = static_cast<const __nv_bfloat16*>(p.q);
     __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
 
     Walker w;
     w.begin(p, sched.req0, sched.qb0, sched.t0);
     long long item_start = start - sched.t0;
-    bool fresh = true;
     uint32_t qf[8][4];
     float o[16][4];
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    load_q_fragments<kFused>(p, w.it, h, lane, qw_smem, qf);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
 
     for (long long gk = start; gk < end; ++gk) {
       const int kl = static_cast<int>(gk - start);
       const int stage = kl % kStages;
       const uint32_t parity = (kl / kStages) & 1;
       const Item& it = w.it;
-      if (fresh) {
-        // Q fragments of heads 2h (MMA rows 0-7) and 2h+1 (rows 8-15), query row g.
-        const int row = it.q0 + g;
-        const bool rv = g < it.nrows && row >= 0 && row < p.total_q;
-        const __nv_bfloat16* qa = qg + (static_cast<size_t>(row) * kQHeads + 2 * h) * kHeadDim;
-        const __nv_bfloat16* qb = qa + kHeadDim;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const int d = ks * 16 + 2 * t4;
-          qf[ks][0] = rv ? ld_nc_u32(qa + d) : 0u;
-          qf[ks][1] = rv ? ld_nc_u32(qb + d) : 0u;
-          qf[ks][2] = rv ? ld_nc_u32(qa + d + 8) : 0u;
-          qf[ks][3] = rv ? ld_nc_u32(qb + d + 8) : 0u;
-        }
-#pragma unroll
-        for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
-        m_a = m_b = -INFINITY;
-        l_a = l_b = 0.f;
-        fresh = false;
-      }
       if (!mbar_wait(smem_u32(&full[stage]), parity)) break;
       const Tile ti = tile_of(it, w.t);
+      const bool self_filled = kFused && ti.src_b;
+      if (self_filled) {
+        rope_new_rows_in_smem(p, it, ti, h, lane, smem + stage * kStageBytes,
+                              smem + kSmemRopeOff + stage * kRopeStageBytes, kw_smem);
+        __syncwarp();
+      }
       const uint32_t sbase = smem_u32(smem + stage * kStageBytes);
       const uint32_t head_off = static_cast<uint32_t>(h * kTileN * 128);
 
@@ -529,11 +820,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           mma_bf16(o[j + 1], pa, b2, b3);
         }
       }
+      // Generic-proxy writes into the stage must be ordered before the next TMA
+      // write into it.
+      if (self_filled) fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
 
-      const bool item_done = (w.t + 1 >= it.tiles) || (gk + 1 == end);
-      if (item_done) {
+      const bool last_tile = w.t + 1 >= it.tiles;
+      if (last_tile || gk + 1 == end) {
         const float la = quad_sum(l_a), lb = quad_sum(l_b);
         const long long item_end = item_start + it.tiles;
         if (item_start >= start && item_end <= end) {
@@ -549,28 +843,20 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             }
           }
         } else {
-          const int slot = item_start <= start ? 0 : 1;
-          const size_t base = (static_cast<size_t>(blockIdx.x) * 2 + slot) * kKVHeads + h;
-          float* po = p.part_o + base * 16 * kHeadDim;
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const int d = j * 8 + 2 * t4;
-            *reinterpret_cast<float2*>(po + g * kHeadDim + d) = make_float2(o[j][0], o[j][1]);
-            *reinterpret_cast<float2*>(po + (g + 8) * kHeadDim + d) = make_float2(o[j][2], o[j][3]);
-          }
-          if (t4 == 0) {
-            float* pml = p.part_ml + base * 32;
-            pml[2 * g] = m_a;
-            pml[2 * g + 1] = la;
-            pml[2 * (g + 8)] = m_b;
-            pml[2 * (g + 8) + 1] = lb;
-          }
+          finish_split_item(p, it, item_start, item_end, start, total, h, lane, o, m_a, m_b, la, lb);
         }
-      }
-      if (w.advance(p)) {
+        if (!last_tile || gk + 1 == end) break;      // this CTA's range ends here
+        // Next item: its Q replaces qf and its accumulators restart.
+        w.advance(p);
         item_start = gk + 1;
-        fresh = true;
+        load_q_fragments<kFused>(p, w.it, h, lane, qw_smem, qf);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+        m_a = m_b = -INFINITY;
+        l_a = l_b = 0.f;
+        continue;
       }
+      w.advance(p);
     }
   }
   // Never leave the CTA with a TMA write still in flight (only possible after
@@ -579,54 +865,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == kConsumerWarps * 32) {
     for (int s = 0; s < kStages; ++s)
       if (sched.issued[s] > 0) mbar_wait(smem_u32(&full[s]), (sched.issued[s] - 1) & 1);
-  }
-}
-
-// Combines the fp32 partials of items cut by CTA range boundaries. Block c
-// handles the item that starts before its range and ends inside it.
-__global__ void __launch_bounds__(256) attn_merge_kernel(const AttnParams p) {
-  const AttnRecord r = p.records[blockIdx.x];
-  if (!r.needs_merge) return;
-  Item it;
-  load_item(p, r.req, r.qb, it);
-  const long long total = r.total_tiles;
-  const int first = cta_of_tile(r.item_start, total, p.grid);
-  const int last = blockIdx.x;
-  __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
-  for (int u = threadIdx.x; u < kKVHeads * 16 * 32; u += blockDim.x) {
-    const int h = u / (16 * 32);
-    const int m = (u / 32) % 16;
-    const int d = (u % 32) * 4;
-    const int r_in = m & 7;
-    if (r_in >= it.nrows || it.q0 + r_in < 0 || it.q0 + r_in >= p.total_q) continue;
-    float mstar = -INFINITY;
-    for (int c = first; c <= last; ++c) {
-      const long long cs = range_start(c, total, p.grid);
-      if (cs == range_start(c + 1, total, p.grid)) continue;   // empty range: no partial
-      const int slot = r.item_start <= cs ? 0 : 1;
-      const size_t base = (static_cast<size_t>(c) * 2 + slot) * kKVHeads + h;
-      mstar = fmaxf(mstar, p.part_ml[base * 32 + 2 * m]);
-    }
-    const float mu = mstar == -INFINITY ? 0.f : mstar;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float l = 0.f;
-    for (int c = first; c <= last; ++c) {
-      const long long cs = range_start(c, total, p.grid);
-      if (cs == range_start(c + 1, total, p.grid)) continue;
-      const int slot = r.item_start <= cs ? 0 : 1;
-      const size_t base = (static_cast<size_t>(c) * 2 + slot) * kKVHeads + h;
-      const float w = ex2((p.part_ml[base * 32 + 2 * m] - mu) * p.scale_log2);
-      l += w * p.part_ml[base * 32 + 2 * m + 1];
-      const float4 v = *reinterpret_cast<const float4*>(p.part_o + (base * 16 + m) * kHeadDim + d);
-      acc.x += w * v.x;
-      acc.y += w * v.y;
-      acc.z += w * v.z;
-      acc.w += w * v.w;
-    }
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    __nv_bfloat16* dst = og + (static_cast<size_t>(it.q0 + r_in) * kQHeads + 2 * h + (m >> 3)) * kHeadDim + d;
-    *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(acc.x * inv, acc.y * inv);
-    *reinterpret_cast<uint32_t*>(dst + 2) = pack_bf16x2(acc.z * inv, acc.w * inv);
   }
 }
 

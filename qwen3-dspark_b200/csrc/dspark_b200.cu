@@ -4,6 +4,7 @@
 // here: scratch for split items is the caller's workspace.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -28,8 +29,17 @@ struct DeviceInfo {
 std::mutex g_mu;
 DeviceInfo g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+// Launch counter: tags the split-item arrival counters of each launch so that
+// counters left by an earlier launch never need clearing.
+std::atomic<unsigned int> g_epoch{1};
 
-constexpr size_t kAttnSmemBytes = 1024 + static_cast<size_t>(kStages) * kStageBytes + 2 * kStages * sizeof(uint64_t) +
+unsigned int next_epoch() {
+  unsigned int e = g_epoch.fetch_add(1);
+  if (e == 0) e = g_epoch.fetch_add(1);
+  return e;
+}
+
+constexpr size_t kAttnSmemBytes = 1024 + static_cast<size_t>(kSmemBarOff) + 2 * kStages * sizeof(uint64_t) +
                                   sizeof(SchedShared);
 
 int device_info(int dev, DeviceInfo* out) {
@@ -47,9 +57,11 @@ int device_info(int dev, DeviceInfo* out) {
     int cur = -1;
     cudaGetDevice(&cur);
     if (cur != dev) return DSPARK_ERR_INVALID_ARGUMENT;     // attributes are per current device
-    if (cudaFuncSetAttribute(attn_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    if (cudaFuncSetAttribute(attn_bf16_kernel<false, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(attn_bf16_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_bf16_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kAttnSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (!g_encode) {
@@ -72,11 +84,21 @@ int current_device_info(DeviceInfo* out) {
   return device_info(dev, out);
 }
 
-size_t workspace_for_grid(int grid) {
-  const size_t part_o = static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float);
-  const size_t part_ml = static_cast<size_t>(grid) * 2 * kPartMlPerSlot * sizeof(float);
-  const size_t rec = static_cast<size_t>(grid) * sizeof(AttnRecord);
-  return part_o + part_ml + rec;
+// Workspace: fp32 partials of up to two cut items per CTA, then one
+// epoch-tagged arrival counter per (CTA, KV head).
+constexpr size_t workspace_for_grid(int grid) {
+  return static_cast<size_t>(grid) * (2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float) +
+                                      kKVHeads * sizeof(unsigned long long));
+}
+
+void bind_workspace(AttnParams& p, void* workspace, int grid) {
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  p.part_o = reinterpret_cast<float*>(ws);
+  p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
+  p.counters = reinterpret_cast<unsigned long long*>(
+      ws + static_cast<size_t>(grid) * 2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
+  p.grid = grid;
+  p.epoch = next_epoch();
 }
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -111,9 +133,10 @@ struct KeySources {
   long long rows_b;
 };
 
-// Shared launch path of every attention entry point.
+// Shared launch path of every attention entry point; `fused` selects the
+// verify kernel that normalises/rotates q and produces the source-B rows.
 int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream) {
+                  size_t workspace_bytes, cudaStream_t stream, bool fused = false) {
   DeviceInfo dev;
   int st = current_device_info(&dev);
   if (st != DSPARK_OK) return st;
@@ -133,12 +156,7 @@ int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, voi
   const int grid = dev.sms;
   if (workspace == nullptr || workspace_bytes < workspace_for_grid(grid) || !aligned(workspace, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
-  uint8_t* ws = static_cast<uint8_t*>(workspace);
-  p.part_o = reinterpret_cast<float*>(ws);
-  p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
-  p.records = reinterpret_cast<AttnRecord*>(ws + static_cast<size_t>(grid) * 2 *
-                                                     (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
-  p.grid = grid;
+  bind_workspace(p, workspace, grid);
   p.rows_a = src.rows_a;
   p.rows_b = src.rows_b;
   CUtensorMap ka, va, kb, vb;
@@ -151,12 +169,12 @@ int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, voi
     kb = ka;
     vb = va;
   }
-  if (p.causal)
-    attn_bf16_kernel<true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
+  if (fused)
+    attn_bf16_kernel<true, true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
+  else if (p.causal)
+    attn_bf16_kernel<true, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
   else
-    attn_bf16_kernel<false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
-  if ((st = launch_status()) != DSPARK_OK) return st;
-  attn_merge_kernel<<<grid, 256, 0, stream>>>(p);
+    attn_bf16_kernel<false, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
   return launch_status();
 }
 
@@ -267,59 +285,60 @@ int dspark_segment_attn(const void* q, const void* ka, const void* va, long long
   return run_attention(p, src, dtype, max_q, workspace, workspace_bytes, stream);
 }
 
+int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t* ctx_len, int num_requests,
+                      int total_q, void* table, cudaStream_t stream) {
+  if (!inv_freq || !cu_q || !ctx_len || !table || num_requests < 1 || total_q < 1 || !aligned(table, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  rope_table_kernel<<<(total_q + 3) / 4, 256, 0, stream>>>(inv_freq, cu_q, ctx_len, num_requests, total_q,
+                                                          static_cast<uint32_t*>(table));
+  return launch_status();
+}
+
 int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
-                        const void* k_norm_weight, const float* inv_freq, float eps, const int32_t* cu_q,
+                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
                         const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
                         void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
-                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* q_roped,
-                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* out,
+                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (!common_ok(q_raw, out, cu_q, num_requests, total_q, scale, DSPARK_DTYPE_BF16) || !k_raw || !v_raw ||
-      !q_norm_weight || !k_norm_weight || !inv_freq || !slot_row || !ctx_len || !resident_k || !resident_v ||
-      !scratch_k || !scratch_v || !q_roped || !aligned(q_roped, 16) || !aligned(k_raw, 8) || !aligned(v_raw, 8) ||
-      rows_per_layer < 1 || scratch_rows < total_q || num_layers < 1 || layer < 0 || layer >= num_layers ||
-      !(eps > 0.f))
+      !q_norm_weight || !k_norm_weight || !rope_table || !aligned(rope_table, 16) || !slot_row || !ctx_len ||
+      !resident_k || !resident_v ||
+      !scratch_k || !scratch_v || !aligned(k_raw, 16) || !aligned(v_raw, 16) || !aligned(scratch_k, 16) ||
+      !aligned(scratch_v, 16) || rows_per_layer < 1 || scratch_rows < total_q || num_layers < 1 || layer < 0 ||
+      layer >= num_layers || !(eps > 0.f))
     return DSPARK_ERR_INVALID_ARGUMENT;
-  DeviceInfo dev;
-  int st = current_device_info(&dev);
-  if (st != DSPARK_OK) return st;
   const size_t row_bytes = static_cast<size_t>(kKVHeads) * kHeadDim * 2;
-  __nv_bfloat16* sk = static_cast<__nv_bfloat16*>(scratch_k) + static_cast<size_t>(layer) * scratch_rows * row_bytes / 2;
-  __nv_bfloat16* sv = static_cast<__nv_bfloat16*>(scratch_v) + static_cast<size_t>(layer) * scratch_rows * row_bytes / 2;
-  VerifyParams vp;
-  vp.q_raw = static_cast<const __nv_bfloat16*>(q_raw);
-  vp.k_raw = static_cast<const __nv_bfloat16*>(k_raw);
-  vp.v_raw = static_cast<const __nv_bfloat16*>(v_raw);
-  vp.q_w = static_cast<const __nv_bfloat16*>(q_norm_weight);
-  vp.k_w = static_cast<const __nv_bfloat16*>(k_norm_weight);
-  vp.inv_freq = inv_freq;
-  vp.cu_q = cu_q;
-  vp.ctx_len = ctx_len;
-  vp.num_requests = num_requests;
-  vp.total_q = total_q;
-  vp.eps = eps;
-  vp.q_out = static_cast<__nv_bfloat16*>(q_roped);
-  vp.scratch_k = sk;
-  vp.scratch_v = sv;
-  vp.scratch_rows = scratch_rows;
-  qk_norm_rope_append_kernel<<<total_q, 1024, 0, stream>>>(vp);
-  if ((st = launch_status()) != DSPARK_OK) return st;
-  // Attention: resident prefix rows of this layer, then this layer's scratch rows.
-  const long long layer_rows = rows_per_layer;
-  const long long res_row0 = static_cast<long long>(layer) * layer_rows;
-  if (res_row0 + layer_rows >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
-  AttnParams p = base_params(q_roped, out, cu_q, num_requests, total_q, scale, 1);
+  const long long res_row0 = static_cast<long long>(layer) * rows_per_layer;
+  if (res_row0 + rows_per_layer >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
+  uint8_t* sk = static_cast<uint8_t*>(scratch_k) + static_cast<size_t>(layer) * scratch_rows * row_bytes;
+  uint8_t* sv = static_cast<uint8_t*>(scratch_v) + static_cast<size_t>(layer) * scratch_rows * row_bytes;
+  // One launch: q_norm/k_norm + RoPE + KV append of the new rows into this
+  // layer's scratch, and bottom-right attention over the resident prefix rows
+  // followed by the new rows.
+  AttnParams p = base_params(q_raw, out, cu_q, num_requests, total_q, scale, 1);
   p.mode = kModeSegmented;
   p.a_start = slot_row;
   p.a_len = ctx_len;
-  p.b_start = nullptr;     // scratch rows follow cu_q
+  p.b_start = nullptr;     // new rows follow cu_q
   p.b_len = nullptr;       // and number q_i per request
   p.a_off = 0;
   p.b_off = 0;
   p.b_none = 0;
+  p.k_new = static_cast<const __nv_bfloat16*>(k_raw);
+  p.v_new = static_cast<const __nv_bfloat16*>(v_raw);
+  p.q_w = static_cast<const __nv_bfloat16*>(q_norm_weight);
+  p.k_w = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  p.rope = static_cast<const uint32_t*>(rope_table);
+  p.eps = eps;
+  p.scratch_k = reinterpret_cast<__nv_bfloat16*>(sk);
+  p.scratch_v = reinterpret_cast<__nv_bfloat16*>(sv);
+  p.scratch_rows = scratch_rows;
   const uint8_t* rk = static_cast<const uint8_t*>(resident_k) + res_row0 * row_bytes;
   const uint8_t* rv = static_cast<const uint8_t*>(resident_v) + res_row0 * row_bytes;
-  KeySources src{rk, rv, layer_rows, sk, sv, scratch_rows};
-  return run_attention(p, src, DSPARK_DTYPE_BF16, max_q, workspace, workspace_bytes, stream);
+  // Source B = the raw new-row projections; the kernel normalises/rotates them
+  // in shared memory and writes the scratch rows itself.
+  KeySources src{rk, rv, rows_per_layer, k_raw, v_raw, total_q};
+  return run_attention(p, src, DSPARK_DTYPE_BF16, max_q, workspace, workspace_bytes, stream, true);
 }
 
 int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,
@@ -368,12 +387,10 @@ namespace {
 // The scratch holds the partials of at most this many persistent CTAs; the
 // entry point never launches more. Its size does not depend on the inputs.
 constexpr int kNoAllocMaxCtas = 148;
-constexpr size_t kNoAllocScratchBytes =
-    static_cast<size_t>(kNoAllocMaxCtas) * (2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float) +
-                                            sizeof(AttnRecord));
+constexpr size_t kNoAllocScratchBytes = workspace_for_grid(kNoAllocMaxCtas);
 
-// 148 CTAs x (2 x 66 KB of fp32 partials + 32 B record) = 18.8 MiB. Every GPU
-// that loads this library holds it until the process exits.
+// 148 CTAs x (2 x 66 KB of fp32 partials + 64 B of counters) = 18.8 MiB. Every
+// GPU that loads this library holds it until the process exits.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 void* g_noalloc_ptr[kMaxDevices] = {};
@@ -412,18 +429,11 @@ extern "C" int dspark_varlen_attn_noalloc(const void* q, const void* k, const vo
   AttnParams p = base_params(q, out, cu_q, num_requests, total_q, scale, 1);
   p.mode = kModeVarlen;
   p.cu_k = cu_k;
-  uint8_t* ws = static_cast<uint8_t*>(scratch);
-  p.part_o = reinterpret_cast<float*>(ws);
-  p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
-  p.records = reinterpret_cast<AttnRecord*>(ws + static_cast<size_t>(grid) * 2 *
-                                                     (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
-  p.grid = grid;
+  bind_workspace(p, scratch, grid);
   p.rows_a = key_rows;
   CUtensorMap ka, va;
   if ((st = encode_kv_map(&ka, k, key_rows)) != DSPARK_OK) return st;
   if ((st = encode_kv_map(&va, v, key_rows)) != DSPARK_OK) return st;
-  attn_bf16_kernel<true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, ka, va, p);
-  if ((st = launch_status()) != DSPARK_OK) return st;
-  attn_merge_kernel<<<grid, 256, 0, stream>>>(p);
+  attn_bf16_kernel<true, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, ka, va, p);
   return launch_status();
 }

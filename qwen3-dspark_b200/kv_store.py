@@ -6,9 +6,9 @@ slot handles with incarnations, ``load_prefix``, ``begin`` / ``stage_layer`` /
 ``pointers`` and ``work``, with the same refusals. What changes is where the
 bytes go:
 
-* ``verify_layer`` runs one decoder layer's verify attention as two kernels:
-  QK-RMSNorm + RoPE + KV append into scratch, then bottom-right causal
-  attention that reads the resident prefix and the scratch rows in place. The
+* ``verify_layer`` runs one decoder layer's verify attention as one kernel:
+  QK-RMSNorm + RoPE of the new tokens, their KV append into scratch, and
+  bottom-right causal attention that reads the resident prefix in place. The
   reference's per-bucket gather workspace (6 capacity-sized tensors) and its
   index_select/where/masked_fill staging do not exist here.
 * ``commit`` copies every request's accepted scratch prefix for all layers in
@@ -43,6 +43,7 @@ class Transaction:
     context_lengths: tuple
     query_lengths: tuple
     meta: torch.Tensor          # int32 [4R+1]: cu_q | slot_row | ctx_len | slot_cap
+    rope: dict = None           # inv_freq tensor -> [sum Q, 64] cos/sin table, built once per transaction
 
     @property
     def query_tokens(self):
@@ -85,7 +86,6 @@ class B200PersistentTargetKV:
         self._values = torch.zeros_like(self._keys)
         self.scratch_keys = torch.zeros((layers * max_query_tokens, heads, dim), dtype=dtype, device=self.device)
         self.scratch_values = torch.zeros_like(self.scratch_keys)
-        self._q_roped = torch.empty((max_query_tokens, HQ, dim), dtype=dtype, device=self.device)
         self._owners = [None] * slots
         self._handles = [None] * slots
         self._incarnations = [0] * slots
@@ -209,7 +209,7 @@ class B200PersistentTargetKV:
         host = cu + [self.slot_rows[i] for i in indices] + list(contexts) + [self.capacities[i] for i in indices]
         meta = torch.tensor(host, dtype=torch.int32).to(self.device)
         self._sequence += 1
-        tx = Transaction(self._sequence, handles, contexts, query_lengths, meta)
+        tx = Transaction(self._sequence, handles, contexts, query_lengths, meta, {})
         self._pending, self._staged = tx, set()
         return tx
 
@@ -254,14 +254,24 @@ class B200PersistentTargetKV:
             out = torch.empty_like(q_raw)
         cu_q, slot_row, ctx, _cap = self._meta(tx)
         stream = torch.cuda.current_stream(self.device).cuda_stream
+        lib = _lib.load_library()
+        key = (inv_freq.data_ptr(), inv_freq._version)
+        table = tx.rope.get(key)
+        if table is None:
+            # cos/sin of every new row's position, once for all layers of this transaction
+            table = torch.empty((n, HEAD_DIM // 2), dtype=torch.int32, device=self.device)
+            _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), cu_q.data_ptr(), ctx.data_ptr(), len(tx.slots), n,
+                                             table.data_ptr(), stream), 'dspark_rope_table')
+            tx.rope.clear()
+            tx.rope[key] = table
         ws = _lib.workspace(self.device, stream)
-        _lib.check(_lib.load_library().dspark_verify_fused(
+        _lib.check(lib.dspark_verify_fused(
             q_raw.data_ptr(), k_raw.data_ptr(), v_raw.data_ptr(), q_norm_weight.data_ptr(),
-            k_norm_weight.data_ptr(), inv_freq.data_ptr(), float(eps), cu_q.data_ptr(), slot_row.data_ptr(),
+            k_norm_weight.data_ptr(), table.data_ptr(), float(eps), cu_q.data_ptr(), slot_row.data_ptr(),
             ctx.data_ptr(), len(tx.slots), n, max(tx.query_lengths), self._keys.data_ptr(), self._values.data_ptr(),
             self.rows_per_layer, self.scratch_keys.data_ptr(), self.scratch_values.data_ptr(),
-            self.max_query_tokens, self.layers, layer, float(scale), self._q_roped.data_ptr(), out.data_ptr(),
-            ws.data_ptr(), ws.numel(), stream), 'dspark_verify_fused')
+            self.max_query_tokens, self.layers, layer, float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(),
+            stream), 'dspark_verify_fused')
         self._staged.add(layer)
         return out
 
