@@ -176,7 +176,6 @@ class Workload:
         """One round. ``events``: list to append (start, end, kind) CUDA event pairs per layer.
         ``host``: pinned host buffers for the end-to-end path (inputs copied in, outputs out)."""
         import torch
-        launches = 0
         for layer in range(self.draft_layers):
             e0 = self._event(events)
             q = self.draft_q[layer]
@@ -186,10 +185,9 @@ class Workload:
                                     scale=D ** -0.5)
             if host is not None:
                 host['do'][layer].copy_(out, non_blocking=True)
-            launches += 2
             self._close(events, e0, 'draft')
         if not self.verify_layers:
-            return launches
+            return
         store = self.store
         tx = store.begin(self.handles, query_lengths=[VERIFY['q']] * VERIFY['requests'])
         ctx_now = tx.context_lengths
@@ -203,12 +201,9 @@ class Workload:
             out = store.verify_layer(tx, layer, qr, kr, vr, self.qw, self.kw, inv_freq=self.inv_freq)
             if host is not None:
                 host['vo'][layer].copy_(out, non_blocking=True)
-            launches += 3
             self._close(events, e0, 'verify', ctx_now)
         accept = self.accept_rng.integers(0, 7, VERIFY['requests'])
         store.commit(tx, {h: int(a) + 1 for h, a in zip(self.handles, accept)})
-        launches += 1
-        return launches
 
     @staticmethod
     def _event(events):
@@ -314,6 +309,29 @@ def run_reference(args):
         e2e=dict(value=value, unit='query-tok/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
 
+# --------------------------------------------------------------------------- ranks
+def gather_stats(stats, world):
+    """All ranks' stats rows [elapsed_ms, e2e_ms, device_status, launches] -> [world, 4] on the host.
+
+    The only collective of the benchmark: one all_gather after timing (NCCL on GPUs)."""
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return stats[None].cpu()
+    gathered = [torch.zeros_like(stats) for _ in range(world)]
+    dist.all_gather(gathered, stats)
+    return torch.stack(gathered).cpu()
+
+
+def aggregate_stats(allstats):
+    """Whole-job numbers: the slowest rank's device times, OR of status bits, total launches."""
+    status = 0
+    for s in allstats[:, 2].tolist():
+        status |= int(s)
+    return dict(elapsed_ms=float(allstats[:, 0].max()), e2e_ms=float(allstats[:, 1].max()), status=status,
+                launches=int(allstats[:, 3].sum()))
+
+
 # --------------------------------------------------------------------------- GPU arm
 def run_b200(args):
     import importlib
@@ -347,9 +365,10 @@ def run_b200(args):
     with ClockSampler(local) as clocks:
         barrier()
         start.record()
-        launches = 0
+        launches0 = pkg.launch_count()
         for _ in range(args.steps):
-            launches += wl.step(events)
+            wl.step(events)
+        launches = pkg.launch_count() - launches0
         end.record()
         barrier()
     elapsed_ms = start.elapsed_time(end)
@@ -372,16 +391,11 @@ def run_b200(args):
         per[kind].append(e0.elapsed_time(e1))
         if kind == 'verify':
             vbytes.append(wl.verify_layer_bytes(ctx))
-    stats = torch.tensor([elapsed_ms, e2e_ms, float(status)], dtype=torch.float64, device=device)
-    if world > 1:
-        gathered = [torch.zeros_like(stats) for _ in range(world)]
-        dist.all_gather(gathered, stats)
-        allstats = torch.stack(gathered).cpu()
-    else:
-        allstats = stats[None].cpu()
+    stats = torch.tensor([elapsed_ms, e2e_ms, float(status), float(launches)], dtype=torch.float64, device=device)
+    allstats = gather_stats(stats, world)
     if rank == 0:
-        max_ms = float(allstats[:, 0].max())
-        max_e2e = float(allstats[:, 1].max())
+        agg = aggregate_stats(allstats)
+        max_ms, max_e2e = agg['elapsed_ms'], agg['e2e_ms']
         units = query_units(dl, vl) * args.steps * world
         value = units / (max_ms / 1e3)
         e2e_value = units / (max_e2e / 1e3)
@@ -414,7 +428,7 @@ def run_b200(args):
             e2e=dict(value=e2e_value, unit='query-tok/s', h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                      path='B200DraftKernel / B200PersistentTargetKV.verify_layer with pinned host q/k/v in, '
                           'attention outputs out'),
-            gpu_launches=launches * world, clocks=clocks.summary(), device_status=int(allstats[:, 2].max()))
+            gpu_launches=agg['launches'], clocks=clocks.summary(), device_status=agg['status'])
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

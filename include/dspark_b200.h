@@ -44,6 +44,10 @@ extern "C" {
 int dspark_abi_version(void);
 const char* dspark_status_string(int status);
 
+/* Number of kernels this library has launched since it was loaded (all devices
+ * and streams); lets a caller count the library's launches in a timed region. */
+unsigned long long dspark_launch_count(void);
+
 /* Bytes of workspace the bf16 attention entry points need on `device`
  * (fp32 partials of items split between CTAs plus per-item arrival counters;
  * scales with the SM count, ~19 MB on a B200). Its contents never need

@@ -21,8 +21,9 @@ from .layout import PackedLayout, PersistentAttentionLayout
 
 load_library = _lib.load_library
 read_device_status = _lib.read_device_status
+launch_count = _lib.launch_count
 
 __all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'B200CapacityKernel', 'B200DraftKernel',
            'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH', 'PackedLayout', 'PersistentAttentionLayout',
-           'Slot', 'Transaction', 'build', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
+           'Slot', 'Transaction', 'build', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
            'segment_attention']

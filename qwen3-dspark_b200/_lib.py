@@ -19,6 +19,7 @@ _vp, _i, _ll, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes
 # name -> (restype, argtypes); mirrors include/dspark_b200.h
 SIGNATURES = {
     'dspark_abi_version': (_i, []),
+    'dspark_launch_count': (ctypes.c_ulonglong, []),
     'dspark_status_string': (ctypes.c_char_p, [_i]),
     'dspark_attention_workspace_size': (_i, [_i, ctypes.POINTER(_sz)]),
     'dspark_read_device_status': (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
@@ -62,6 +63,11 @@ def check(status, what):
         if status == ERR_INVALID_ARGUMENT:
             raise ValueError(f'{what}: {msg}')
         raise RuntimeError(f'{what}: {msg} (status {status})')
+
+
+def launch_count():
+    """Kernels launched by the library since load (host-side counter)."""
+    return int(load_library().dspark_launch_count())
 
 
 def read_device_status(clear=True):

@@ -32,6 +32,8 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 // Launch counter: tags the split-item arrival counters of each launch so that
 // counters left by an earlier launch never need clearing.
 std::atomic<unsigned int> g_epoch{1};
+// Kernels launched by this library since load (all devices, all streams).
+std::atomic<unsigned long long> g_launches{0};
 
 unsigned int next_epoch() {
   unsigned int e = g_epoch.fetch_add(1);
@@ -121,7 +123,9 @@ int encode_kv_map(CUtensorMap* m, const void* base, long long rows) {
 
 int launch_status() {
   const cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? DSPARK_OK : DSPARK_ERR_CUDA;
+  if (e != cudaSuccess) return DSPARK_ERR_CUDA;
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return DSPARK_OK;
 }
 
 struct KeySources {
@@ -216,6 +220,8 @@ int varlen_common(const void* q, const void* k, const void* v, const int32_t* cu
 extern "C" {
 
 int dspark_abi_version(void) { return DSPARK_ABI_VERSION; }
+
+unsigned long long dspark_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* dspark_status_string(int status) {
   switch (status) {

@@ -1,0 +1,165 @@
+"""C-ABI library and host-side contract checks that need no GPU.
+
+* the shared library loads and exports every function include/dspark_b200.h declares;
+* argument checks that need no device run before any launch (status, not a crash);
+* the drop-in kernel classes refuse the reference's contract violations before the
+  native entry is called, pass the reference's argument meaning to it, cache layout
+  validation per layout object and propagate native failures without fallback
+  (the shape of the reference's tests/test_rocm_varlen.py, with the entry mocked).
+"""
+import ctypes
+import os
+import re
+from unittest.mock import Mock, PropertyMock, patch
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, 'include', 'dspark_b200.h')).read()
+    text = re.sub(r'/\*.*?\*/', '', text, flags=re.S)
+    return sorted(set(re.findall(r'\b(dspark_\w+)\s*\(', text)))
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.load_library()
+    raw = ctypes.CDLL(pkg.LIB_PATH)
+    names = header_functions()
+    assert len(names) >= 10
+    for name in names:
+        assert hasattr(raw, name), name
+    assert lib.dspark_abi_version() == 3
+    assert lib.dspark_status_string(1) == b'invalid argument'
+    assert pkg.launch_count() >= 0
+
+
+def test_null_arguments_are_refused_before_any_device_work(pkg):
+    lib = pkg.load_library()
+    st = lib.dspark_varlen_attn(None, None, None, None, None, 1, 1, 1, 1, 1, 128 ** -0.5, 0, None, None, 0, None)
+    assert st == 1
+    st = lib.dspark_commit_kv(None, None, None, None, None, None, None, None, None, 1, 1, 1, 1, None)
+    assert st == 1
+    st = lib.dspark_rope_table(None, None, None, 1, 1, None, None)
+    assert st == 1
+    size = ctypes.c_size_t(0)
+    assert lib.dspark_attention_workspace_size(0, None) == 1
+
+
+def _fixture(pkg):
+    q = torch.zeros(9, 16, 128, dtype=torch.bfloat16)
+    k = torch.zeros(46, 8, 128, dtype=torch.bfloat16)
+    layout = pkg.PackedLayout((1, 2), (1, 8), (17, 29), torch.tensor([0, 1, 9], dtype=torch.int32),
+                              torch.tensor([0, 17, 46], dtype=torch.int32), torch.arange(46), 46)
+    return q, k, k.clone(), layout
+
+
+def _kernel(pkg, cls):
+    with patch.object(pkg.kernels, 'runtime_identity', return_value={'device': 'fake'}) as ident:
+        kern = cls(torch.device('cpu'))
+    ident.assert_called_once()
+    kern._operator = Mock()
+    return kern
+
+
+@pytest.mark.parametrize('name,causal_entry', [('B200VarlenKernel', 'dspark_varlen_attn'),
+                                               ('B200DraftKernel', 'dspark_draft_attn')])
+def test_entry_arguments_and_layout_cache(pkg, name, causal_entry):
+    cls = getattr(pkg, name)
+    assert cls.entry == causal_entry and cls.native_varlen_calls_per_layer == 1
+    q, k, v, layout = _fixture(pkg)
+    kern = _kernel(pkg, cls)
+    with patch.object(torch.Tensor, 'is_cuda', new_callable=PropertyMock, return_value=True), \
+            patch.object(pkg.kernels._lib, 'workspace', return_value=torch.zeros(16, dtype=torch.uint8)), \
+            patch.object(pkg.kernels, '_stream', return_value=0):
+        kern(q, k, v, layout, scale=128 ** -0.5)
+        kern(q, k, v, layout, scale=128 ** -0.5)
+        assert kern._operator.call_count == 2
+        args = kern._operator.call_args[0]
+        # (q, k, v, cu_q, cu_k, R, total_q, key_rows, max_q, max_k, scale, dtype, out, ws, ws_bytes, stream)
+        assert args[5:12] == (2, 9, 46, 8, 29, 128 ** -0.5, 0)
+        assert kern._validated_layout is layout
+        layout.cu_query[1] = 2
+        with pytest.raises(ValueError, match='Cumulative lengths'):
+            kern(q, k, v, layout, scale=128 ** -0.5)
+    assert kern._operator.call_count == 2
+
+
+def test_contract_violations_refused_before_entry(pkg):
+    for mutation in ['dtype', 'heads', 'scale', 'cu_dtype', 'noncontiguous', 'tokens', 'requires_grad', 'q_gt_k']:
+        q, k, v, layout = _fixture(pkg)
+        kern = _kernel(pkg, pkg.B200VarlenKernel)
+        scale = 128 ** -0.5
+        if mutation == 'dtype':
+            q = q.half()
+        if mutation == 'requires_grad':
+            q = q.float().requires_grad_(True)
+        if mutation == 'heads':
+            q = q[:, :8].contiguous()
+        if mutation == 'scale':
+            scale = 1.0
+        if mutation == 'cu_dtype':
+            object.__setattr__(layout, 'cu_query', layout.cu_query.long())
+        if mutation == 'noncontiguous':
+            q = torch.zeros(9, 16, 256, dtype=torch.bfloat16)[:, :, ::2]
+        if mutation == 'tokens':
+            q = q[:1]
+        if mutation == 'q_gt_k':
+            layout = pkg.PackedLayout((1, 2), (1, 8), (17, 7), torch.tensor([0, 1, 9], dtype=torch.int32),
+                                      torch.tensor([0, 17, 24], dtype=torch.int32), torch.arange(24), 24)
+            k, v = k[:24].contiguous(), v[:24].contiguous()
+        with patch.object(torch.Tensor, 'is_cuda', new_callable=PropertyMock, return_value=True):
+            with pytest.raises(ValueError):
+                kern(q, k, v, layout, scale=scale)
+        kern._operator.assert_not_called()
+
+
+def test_native_failure_propagates_without_fallback(pkg):
+    kern = _kernel(pkg, pkg.B200VarlenKernel)
+    kern._operator.side_effect = RuntimeError('native fixture failure')
+    with patch.object(torch.Tensor, 'is_cuda', new_callable=PropertyMock, return_value=True), \
+            patch.object(pkg.kernels._lib, 'workspace', return_value=torch.zeros(16, dtype=torch.uint8)), \
+            patch.object(pkg.kernels, '_stream', return_value=0):
+        with pytest.raises(RuntimeError, match='native fixture failure'):
+            kern(*_fixture(pkg), scale=128 ** -0.5)
+
+
+def test_constructor_refuses_cpu_device(pkg):
+    with pytest.raises(RuntimeError, match='no CPU fallback'):
+        pkg.B200DraftKernel(torch.device('cpu'))
+
+
+def test_capacity_kernel_requires_capacity_rows(pkg):
+    kern = _kernel(pkg, pkg.B200CapacityKernel)
+    q = torch.zeros(9, 16, 128, dtype=torch.bfloat16)
+    k = torch.zeros(50, 8, 128, dtype=torch.bfloat16)
+    lay = pkg.PersistentAttentionLayout((1, 8), (17, 29), torch.tensor([0, 1, 9], dtype=torch.int32),
+                                        torch.tensor([0, 17, 46], dtype=torch.int32), 50, 29, 8)
+    bad = pkg.PersistentAttentionLayout((1, 8), (17, 29), lay.cu_query, lay.cu_key, 49, 29, 8)
+    with patch.object(torch.Tensor, 'is_cuda', new_callable=PropertyMock, return_value=True), \
+            patch.object(pkg.kernels._lib, 'workspace', return_value=torch.zeros(16, dtype=torch.uint8)), \
+            patch.object(pkg.kernels, '_stream', return_value=0):
+        with pytest.raises(ValueError):
+            kern(q, k, k.clone(), bad, scale=128 ** -0.5)
+        kern(q, k, k.clone(), lay, scale=128 ** -0.5)
+        assert kern._operator.call_args[0][7] == 50      # key_rows = capacity; the tail is never read
+
+
+def test_packed_layout_mirror_matches_reference_fixture(pkg, golden):
+    for idx in (0, 1):
+        g = golden(f'layout{idx}')
+        L = lambda x: torch.tensor(x.tolist(), dtype=torch.long)  # noqa: E731
+        lay = pkg.PackedLayout.from_metadata(L(g['qr']), L(g['qp']), L(g['kr']), L(g['kp']))
+        assert lay.request_markers == tuple(g['markers'].tolist())
+        assert lay.query_lengths == tuple(g['query_lengths'].tolist())
+        assert lay.key_lengths == tuple(g['key_lengths'].tolist())
+        assert lay.cu_query.tolist() == g['cu_query'].tolist()
+        assert lay.cu_key.tolist() == g['cu_key'].tolist()
+        assert lay.gather_indices.tolist() == g['gather'].tolist()
+        assert lay.pair_domain == int(g['pair_domain'])
+    for qreq, qpos, kreq, kpos in [([1, 2, 1], [0, 0, 1], [1, 1, 2], [0, 1, 0]), ([1], [0], [1, 1], [0, 1]),
+                                   ([1], [1], [1, 1], [0, 2]), ([], [], [], [])]:
+        with pytest.raises(ValueError):
+            pkg.PackedLayout.from_metadata(*(torch.tensor(x, dtype=torch.long) for x in [qreq, qpos, kreq, kpos]))
