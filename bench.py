@@ -49,6 +49,15 @@ def peaks():
         return FALLBACK_HBM_GBS, 'fallback'
 
 
+def captured_traffic(key):
+    """DRAM bytes per launch from the committed ncu capture summary, or None."""
+    try:
+        with open(os.path.join(ROOT, 'profiles', 'ncu_traffic.json')) as f:
+            return int(json.load(f)[key]['bytes'])
+    except Exception:
+        return None
+
+
 def dist_env():
     return int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), int(os.environ.get('LOCAL_RANK', 0))
 
@@ -418,10 +427,12 @@ def run_b200(args):
                         l2='inputs larger than L2 (~62 GB resident KV per GPU)'),
             roofline=dict(kernel='verify layer: qk-norm/rope/append + bottom-right attention + split merge',
                           bound='hbm', achieved=achieved, peak=hbm, unit='GB/s', frac=achieved / hbm,
-                          peak_source=f'{peak_kind} hbm_gbs', traffic=None,
+                          peak_source=f'{peak_kind} hbm_gbs', traffic=captured_traffic('verify_layer_cfg3'),
+                          traffic_source='ncu capture of one cfg3 verify layer (profiles/)',
                           alg_bytes_per_launch=v_bytes, avg_launch_ms=v_ms),
             draft_roofline=dict(kernel='draft layer: non-causal attention + split merge', achieved=d_achieved,
-                                frac=d_achieved / hbm, alg_bytes_per_launch=wl.draft_layer_bytes(), avg_launch_ms=d_ms),
+                                frac=d_achieved / hbm, alg_bytes_per_launch=wl.draft_layer_bytes(), avg_launch_ms=d_ms,
+                                traffic=captured_traffic('draft_layer_cfg2')),
             cpu_baseline=dict(value=cpu_v, unit='query-tok/s', cores=host_threads(), kind='port',
                               sample=f'{reps} reps of 8 cfg2 draft + 8 cfg3 verify requests x1 layer, numpy float32, '
                                      f'{el:.1f} s'),
