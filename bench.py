@@ -49,6 +49,17 @@ def peaks():
         return FALLBACK_HBM_GBS, 'fallback'
 
 
+def _finite(obj):
+    """JSON has no NaN/Inf: report unmeasured numbers as null."""
+    if isinstance(obj, float):
+        return obj if obj == obj and abs(obj) != float('inf') else None
+    if isinstance(obj, dict):
+        return {k: _finite(v) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return [_finite(v) for v in obj]
+    return obj
+
+
 def captured_traffic(key):
     """DRAM bytes per launch from the committed ncu capture summary, or None."""
     try:
@@ -347,10 +358,10 @@ def run_b200(args):
     import torch
     import torch.distributed as dist
     rank, world, local = dist_env()
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group('nccl', timeout=timedelta(seconds=120))
+    from datetime import timedelta
     device = torch.device('cuda', local)
+    if world > 1:
+        dist.init_process_group('nccl', timeout=timedelta(seconds=120), device_id=device)
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
@@ -440,7 +451,7 @@ def run_b200(args):
                      path='B200DraftKernel / B200PersistentTargetKV.verify_layer with pinned host q/k/v in, '
                           'attention outputs out'),
             gpu_launches=agg['launches'], clocks=clocks.summary(), device_status=agg['status'])
-        print(json.dumps(line), flush=True)
+        print(json.dumps(_finite(line)), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
