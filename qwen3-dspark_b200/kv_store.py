@@ -50,6 +50,13 @@ class Transaction:
         return sum(self.query_lengths)
 
 
+def _upload(values, device):
+    """int32 host list -> device tensor through pinned memory, without blocking the host
+    on the stream (a pageable copy could make the host wait for queued GPU work)."""
+    host = torch.tensor(values, dtype=torch.int32).pin_memory()
+    return host.to(device, non_blocking=True)
+
+
 def rope_inv_freq(theta, dim=HEAD_DIM, device='cpu'):
     """float32 ``1 / theta ** (arange(0, dim, 2) / dim)`` computed like the transformers
     rotary module (modeling_qwen3.py:124-133), then moved to ``device``."""
@@ -207,7 +214,7 @@ class B200PersistentTargetKV:
         for q in query_lengths:
             cu.append(cu[-1] + q)
         host = cu + [self.slot_rows[i] for i in indices] + list(contexts) + [self.capacities[i] for i in indices]
-        meta = torch.tensor(host, dtype=torch.int32).to(self.device)
+        meta = _upload(host, self.device)
         self._sequence += 1
         tx = Transaction(self._sequence, handles, contexts, query_lengths, meta, {})
         self._pending, self._staged = tx, set()
@@ -347,7 +354,7 @@ class B200PersistentTargetKV:
                 raise ValueError('Commit must be a valid verified prefix')
             counts.append(n)
         try:
-            ncommit = torch.tensor(counts, dtype=torch.int32).to(self.device)
+            ncommit = _upload(counts, self.device)
             cu_q, slot_row, ctx, cap = self._meta(tx)
             stream = torch.cuda.current_stream(self.device).cuda_stream
             _lib.check(_lib.load_library().dspark_commit_kv(
