@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 3
+#define DSPARK_ABI_VERSION 4
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -146,14 +146,15 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
  * scratch rows [cu_q[i], cu_q[i] + n_commit[i]) of each layer into resident rows
  * slot_row[i] + [ctx_len[i], ctx_len[i] + n_commit[i]). Rows past n_commit
  * (the rejected drafts) are not copied, which is the rollback. Requires
- * 0 <= n_commit[i] <= q_i and ctx_len[i] + n_commit[i] <= slot_cap[i].
+ * 0 <= n_commit[i] <= q_i and ctx_len[i] + n_commit[i] <= slot_cap[i]. dtype: the
+ * element type of the K/V rows (DSPARK_DTYPE_BF16 or DSPARK_DTYPE_F32).
  * Replaces PersistentTargetKV.commit (dspark_qwen/persistent_target_kv.py:463-491);
  * abort (493-499) needs no device work.
  */
 int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,
                      const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
                      const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
-                     int scratch_rows, cudaStream_t stream);
+                     int scratch_rows, int dtype, cudaStream_t stream);
 
 /*
  * Allocation-free variant of dspark_varlen_attn (bf16 only). No counterpart in

@@ -19,11 +19,27 @@ from .kernels import (BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, B200Capac
 from .kv_store import B200PersistentTargetKV, Slot, Transaction, rope_inv_freq
 from .layout import PackedLayout, PersistentAttentionLayout
 
+
+def __getattr__(name):
+    # model-level modules import transformers; load them on first use
+    if name in ('B200PackedDraft', 'DSparkDraftModel', 'DraftSpec'):
+        from . import draft
+        return getattr(draft, name)
+    if name == 'B200Qwen3Target':
+        from .target import B200Qwen3Target
+        return B200Qwen3Target
+    if name in ('speculative_greedy', 'accept_greedy'):
+        from . import speculative
+        return getattr(speculative, name)
+    raise AttributeError(name)
+
+
 load_library = _lib.load_library
 read_device_status = _lib.read_device_status
 launch_count = _lib.launch_count
 
 __all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'B200CapacityKernel', 'B200DraftKernel',
            'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH', 'PackedLayout', 'PersistentAttentionLayout',
-           'Slot', 'Transaction', 'build', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
+           'Slot', 'Transaction', 'B200PackedDraft', 'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target',
+           'speculative_greedy', 'accept_greedy', 'build', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
            'segment_attention']

@@ -350,17 +350,18 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
 int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,
                      const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
                      const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
-                     int scratch_rows, cudaStream_t stream) {
+                     int scratch_rows, int dtype, cudaStream_t stream) {
   if (!resident_k || !resident_v || !scratch_k || !scratch_v || !cu_q || !slot_row || !ctx_len || !slot_cap ||
       !n_commit || num_requests < 1 || num_layers < 1 || num_layers > 65535 || rows_per_layer < 1 ||
       scratch_rows < 1 || !aligned(resident_k, 16) || !aligned(resident_v, 16) || !aligned(scratch_k, 16) ||
-      !aligned(scratch_v, 16))
+      !aligned(scratch_v, 16) || (dtype != DSPARK_DTYPE_BF16 && dtype != DSPARK_DTYPE_F32))
     return DSPARK_ERR_INVALID_ARGUMENT;
   CommitParams cp;
-  cp.resident_k = static_cast<__nv_bfloat16*>(resident_k);
-  cp.resident_v = static_cast<__nv_bfloat16*>(resident_v);
-  cp.scratch_k = static_cast<const __nv_bfloat16*>(scratch_k);
-  cp.scratch_v = static_cast<const __nv_bfloat16*>(scratch_v);
+  cp.resident_k = static_cast<uint4*>(resident_k);
+  cp.resident_v = static_cast<uint4*>(resident_v);
+  cp.scratch_k = static_cast<const uint4*>(scratch_k);
+  cp.scratch_v = static_cast<const uint4*>(scratch_v);
+  cp.vec_per_row = kKVHeads * kHeadDim * (dtype == DSPARK_DTYPE_F32 ? 4 : 2) / 16;
   cp.cu_q = cu_q;
   cp.slot_row = slot_row;
   cp.ctx_len = ctx_len;

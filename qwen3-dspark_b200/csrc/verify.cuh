@@ -35,10 +35,11 @@ __global__ void __launch_bounds__(256) rope_table_kernel(const float* __restrict
 }
 
 struct CommitParams {
-  __nv_bfloat16* resident_k;     // [layers * rows_per_layer, 8, 128]
-  __nv_bfloat16* resident_v;
-  const __nv_bfloat16* scratch_k;  // [layers * scratch_rows, 8, 128]
-  const __nv_bfloat16* scratch_v;
+  uint4* resident_k;             // [layers * rows_per_layer, 8, 128] of bf16 or fp32
+  uint4* resident_v;
+  const uint4* scratch_k;        // [layers * scratch_rows, 8, 128]
+  const uint4* scratch_v;
+  int vec_per_row;               // 16-byte vectors per row: 128 (bf16) or 256 (fp32)
   const int* cu_q;               // [R+1] scratch row offsets
   const int* slot_row;           // [R] first resident row of each request's slot
   const int* ctx_len;            // [R] committed rows before this commit
@@ -60,14 +61,14 @@ __global__ void __launch_bounds__(256) commit_kernel(const CommitParams p) {
     if (threadIdx.x == 0) atomicOr(&g_device_status, kStatusBadArgument);
     return;
   }
-  constexpr int kVecPerRow = kKVHeads * 128 * 2 / 16;   // 128 x 16 B per row
+  const size_t vpr = static_cast<size_t>(p.vec_per_row);
   const size_t src_row = static_cast<size_t>(layer) * p.scratch_rows + q0;
   const size_t dst_row = static_cast<size_t>(layer) * p.rows_per_layer + p.slot_row[i] + c;
-  const uint4* sk = reinterpret_cast<const uint4*>(p.scratch_k) + src_row * kVecPerRow;
-  const uint4* sv = reinterpret_cast<const uint4*>(p.scratch_v) + src_row * kVecPerRow;
-  uint4* dk = reinterpret_cast<uint4*>(p.resident_k) + dst_row * kVecPerRow;
-  uint4* dv = reinterpret_cast<uint4*>(p.resident_v) + dst_row * kVecPerRow;
-  for (int u = threadIdx.x; u < n * kVecPerRow; u += blockDim.x) {
+  const uint4* sk = p.scratch_k + src_row * vpr;
+  const uint4* sv = p.scratch_v + src_row * vpr;
+  uint4* dk = p.resident_k + dst_row * vpr;
+  uint4* dv = p.resident_v + dst_row * vpr;
+  for (size_t u = threadIdx.x; u < n * vpr; u += blockDim.x) {
     dk[u] = sk[u];
     dv[u] = sv[u];
   }

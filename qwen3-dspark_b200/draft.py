@@ -1,0 +1,291 @@
+"""B200 packed draft: DSpark block drafting over a paged projected-context pool.
+
+Mirrors ``PackedDraft`` (dspark_qwen/packed_draft.py:63-252) for inference:
+``add_request`` / ``append_committed`` / ``crop`` / ``remove_request`` /
+``backbone`` / ``propose_greedy``. What changes is the cache layout and the
+attention call:
+
+* the projected context K/V of every draft layer live in a request-contiguous
+  pool (slot ``s`` owns rows ``[slot_row[s], slot_row[s] + capacity[s])``);
+  ``append_committed`` writes new rows in place and ``crop`` only moves a
+  length, where the reference concatenates the whole cache on every append
+  (packed_draft.py:146-158) and filters it on every crop (:170-179);
+* ``backbone`` attends over the pool rows and the block rows through the
+  two-source kernel (``segment_attention``), where the reference concatenates
+  cache + block and gathers every request's rows into packed K/V for each
+  layer (:215-226).
+
+``DSparkDraftModel`` holds the draft weights with the same module and
+parameter names as ``DSparkDraft`` (dspark_qwen/model.py:27-99), so its
+state dict loads unchanged; ``embedding`` and ``lm_head`` are the target's.
+"""
+from dataclasses import dataclass, field
+
+import torch
+from torch import nn
+from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
+
+from .kernels import HEAD_DIM, HKV, HQ, segment_attention
+from .kv_store import _upload
+
+
+def rotate_half_rope(x, cos, sin):
+    """x * cos + rotate_half(x) * sin over the last dim; cos/sin broadcast over heads
+    (the draft's ``rotate``, dspark_qwen/model.py:22-24)."""
+    half = x.shape[-1] // 2
+    rot = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
+    return x * cos[:, None] + rot * sin[:, None]
+
+
+@dataclass(frozen=True)
+class DraftSpec:
+    """The draft geometry fields of ``DraftConfig`` (dspark_qwen/config.py:5-14)."""
+    layer_ids: tuple = (1, 7, 14, 21, 26)
+    num_layers: int = 5
+    block_size: int = 7
+    markov_rank: int = 256
+    mask_token_id: int = 151669
+
+
+class _DraftAttention(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        h = config.hidden_size
+        self.heads, self.kv_heads, self.dim = config.num_attention_heads, config.num_key_value_heads, config.head_dim
+        self.q_proj = nn.Linear(h, self.heads * self.dim, bias=config.attention_bias)
+        self.k_proj = nn.Linear(h, self.kv_heads * self.dim, bias=config.attention_bias)
+        self.v_proj = nn.Linear(h, self.kv_heads * self.dim, bias=config.attention_bias)
+        self.o_proj = nn.Linear(self.heads * self.dim, h, bias=config.attention_bias)
+        self.q_norm = Qwen3RMSNorm(self.dim, eps=config.rms_norm_eps)
+        self.k_norm = Qwen3RMSNorm(self.dim, eps=config.rms_norm_eps)
+
+    def project_kv(self, states, cos, sin):
+        """[1, n, hidden] -> roped K [n, Hkv, D], V [n, Hkv, D] (model.py:41-45)."""
+        n = states.shape[1]
+        k = self.k_norm(self.k_proj(states).view(1, n, self.kv_heads, self.dim)).transpose(1, 2)
+        v = self.v_proj(states).view(1, n, self.kv_heads, self.dim).transpose(1, 2)
+        return rotate_half_rope(k, cos, sin)[0].transpose(0, 1), v[0].transpose(0, 1)
+
+    def project_q(self, states, cos, sin):
+        n = states.shape[1]
+        q = self.q_norm(self.q_proj(states).view(1, n, self.heads, self.dim)).transpose(1, 2)
+        return rotate_half_rope(q, cos, sin)[0].transpose(0, 1)
+
+
+class _DraftBlock(nn.Module):
+    def __init__(self, config):
+        super().__init__()
+        self.input_norm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.attention = _DraftAttention(config)
+        self.post_norm = Qwen3RMSNorm(config.hidden_size, eps=config.rms_norm_eps)
+        self.mlp = Qwen3MLP(config)
+
+
+class DSparkDraftModel(nn.Module):
+    """Draft weights with ``DSparkDraft``'s module tree; ``target`` supplies embedding/lm_head."""
+
+    def __init__(self, target, spec):
+        super().__init__()
+        c = target.config
+        if not spec.layer_ids or any(not 0 <= i < c.num_hidden_layers - 1 for i in spec.layer_ids):
+            raise ValueError('Draft layer_ids must be intermediate target layers')
+        if not 0 <= spec.mask_token_id < c.vocab_size:
+            raise ValueError('mask_token_id outside target vocabulary')
+        self.spec = spec
+        self.fc = nn.Linear(len(spec.layer_ids) * c.hidden_size, c.hidden_size, bias=False)
+        self.context_norm = Qwen3RMSNorm(c.hidden_size, eps=c.rms_norm_eps)
+        self.layers = nn.ModuleList([_DraftBlock(c) for _ in range(spec.num_layers)])
+        self.norm = Qwen3RMSNorm(c.hidden_size, eps=c.rms_norm_eps)
+        self.rotary = Qwen3RotaryEmbedding(c)
+        self.markov_embedding = nn.Embedding(c.vocab_size, spec.markov_rank)
+        self.markov_projection = nn.Linear(spec.markov_rank, c.vocab_size, bias=False)
+        self.confidence = nn.Linear(c.hidden_size + spec.markov_rank, 1)
+        self.embedding = target.get_input_embeddings().requires_grad_(False)
+        self.lm_head = target.get_output_embeddings().requires_grad_(False)
+
+
+@dataclass
+class DraftFeatures:
+    hidden: torch.Tensor          # [requests * block, hidden]
+    requests: tuple
+    block_size: int
+    context_lengths: tuple
+    work: dict = field(default_factory=dict)
+
+    def for_request(self, request):
+        i = self.requests.index(request)
+        return self.hidden[i * self.block_size:(i + 1) * self.block_size]
+
+
+class B200PackedDraft:
+    """Inference-only packed draft with a paged context pool in ``kv_dtype``.
+
+    ``kv_dtype`` is the attention dtype: float32 (exact path) or bfloat16, where
+    the reference keeps the cache in the projection dtype and casts it at the
+    attention boundary on every call (packed_draft.py:222-235); casting once at
+    append time gives the same values.
+    """
+
+    def __init__(self, draft, *, max_requests, context_capacity, kv_dtype=None, slot_capacities=None):
+        if draft.training:
+            raise ValueError('Packed draft is inference-only; call eval first')
+        self.draft = draft
+        self.device = draft.fc.weight.device
+        if self.device.type != 'cuda':
+            raise RuntimeError('B200 packed draft requires a CUDA device; no CPU fallback')
+        att = draft.layers[0].attention
+        if (att.heads, att.kv_heads, att.dim) != (HQ, HKV, HEAD_DIM):
+            raise ValueError('B200 draft attention supports Hq16/Hkv8/D128')
+        self.kv_dtype = kv_dtype or draft.fc.weight.dtype
+        if self.kv_dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError('Draft KV dtype must be bfloat16 or float32')
+        caps = [context_capacity] * max_requests if slot_capacities is None else [int(c) for c in slot_capacities]
+        if len(caps) != max_requests or any(c < 1 for c in caps):
+            raise ValueError('One positive capacity per request slot required')
+        rows = [0]
+        for c in caps:
+            rows.append(rows[-1] + c)
+        if rows[-1] >= 2 ** 31:
+            raise ValueError('Draft pool rows exceed the int32 row index')
+        self.capacities, self.slot_rows = tuple(caps), tuple(rows[:-1])
+        shape = (rows[-1], HKV, HEAD_DIM)
+        self.pool_k = [torch.zeros(shape, dtype=self.kv_dtype, device=self.device) for _ in draft.layers]
+        self.pool_v = [torch.zeros(shape, dtype=self.kv_dtype, device=self.device) for _ in draft.layers]
+        self._slots = {}          # request -> slot index
+        self._lengths = {}
+        self._free = list(range(max_requests))
+        self.last_projection_work = None
+
+    # -- request lifecycle (packed_draft.py:89-101,170-184) -----------------------
+    @property
+    def lengths(self):
+        return dict(self._lengths)
+
+    def add_request(self, request):
+        if not isinstance(request, str) or not request or request in self._slots:
+            raise ValueError('Require a fresh nonempty request name')
+        if not self._free:
+            raise ValueError('Draft pool slots exhausted')
+        self._slots[request] = self._free.pop(0)
+        self._lengths[request] = 0
+
+    def _request(self, request):
+        if request not in self._slots:
+            raise KeyError(request)
+
+    def crop(self, request, length):
+        self._request(request)
+        if type(length) is not int or not 0 <= length <= self._lengths[request]:
+            raise ValueError('Invalid committed draft crop length')
+        self._lengths[request] = length          # rows past length are never read
+
+    def remove_request(self, request):
+        self._request(request)
+        self._free.append(self._slots.pop(request))
+        self._free.sort()
+        del self._lengths[request]
+
+    def request_kv(self, request):
+        """Per draft layer (K, V) [n, Hkv, D] of the request's committed context."""
+        self._request(request)
+        r0, n = self.slot_rows[self._slots[request]], self._lengths[request]
+        return tuple((k[r0:r0 + n].clone(), v[r0:r0 + n].clone()) for k, v in zip(self.pool_k, self.pool_v))
+
+    # -- context append (packed_draft.py:129-168) ---------------------------------
+    @torch.no_grad()
+    def append_committed(self, chunks):
+        """Project committed target features [1, n, F] once and write K/V rows in place."""
+        if not chunks:
+            raise ValueError('Require at least one committed feature chunk')
+        d = self.draft
+        features, positions, rows, new_lengths = [], [], [], {}
+        for request, value in chunks.items():
+            self._request(request)
+            if (not isinstance(value, torch.Tensor) or value.ndim != 3 or value.shape[0] != 1 or value.shape[1] < 1
+                    or value.shape[2] != d.fc.in_features or value.device != self.device
+                    or not value.is_floating_point()):
+                raise ValueError('Expected nonempty [1, tokens, target_features] on draft device')
+            n, start = value.shape[1], self._lengths[request]
+            slot = self._slots[request]
+            if start + n > self.capacities[slot]:
+                raise ValueError('Draft context exceeds the request slot capacity')
+            features.append(value)
+            positions.extend(range(start, start + n))
+            rows.extend(range(self.slot_rows[slot] + start, self.slot_rows[slot] + start + n))
+            new_lengths[request] = start + n
+        context = d.context_norm(d.fc(torch.cat(features, dim=1).to(d.fc.weight.dtype)))
+        pos = torch.tensor(positions, dtype=torch.long, device=self.device)
+        cos, sin = d.rotary(context, pos[None])
+        idx = torch.tensor(rows, dtype=torch.long, device=self.device)
+        for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
+            k, v = layer.attention.project_kv(context, cos, sin)
+            pk.index_copy_(0, idx, k.to(self.kv_dtype))
+            pv.index_copy_(0, idx, v.to(self.kv_dtype))
+        self._lengths.update(new_lengths)
+        self.last_projection_work = dict(requests=len(chunks), new_context_tokens=len(positions),
+                                         context_projection_calls=1, kv_projection_calls=len(d.layers),
+                                         cache_concatenation_kv_bytes=0)
+
+    # -- backbone (packed_draft.py:186-252) -----------------------------------------
+    @torch.no_grad()
+    def backbone(self, anchors):
+        """One 7-row block per request: anchor + mask tokens at positions len..len+6."""
+        if not anchors:
+            raise ValueError('Require active anchor requests')
+        d, size = self.draft, self.draft.spec.block_size
+        requests = tuple(anchors)
+        tokens, positions = [], []
+        for request, anchor in anchors.items():
+            self._request(request)
+            if (not isinstance(anchor, torch.Tensor) or anchor.shape != (1, 1) or anchor.dtype != torch.long
+                    or anchor.device != self.device):
+                raise ValueError('Require one [1,1] long anchor per active request')
+            block = anchor.new_full((1, size), d.spec.mask_token_id)
+            block[:, :1] = anchor
+            tokens.append(block)
+            start = self._lengths[request]
+            positions.extend(range(start, start + size))
+        r = len(requests)
+        cu = [size * i for i in range(r + 1)]
+        meta = _upload(cu + [self.slot_rows[self._slots[q]] for q in requests]
+                       + [self._lengths[q] for q in requests] + [size] * r, self.device)
+        cu_q, a_start, a_len, b_len = meta[:r + 1], meta[r + 1:2 * r + 1], meta[2 * r + 1:3 * r + 1], meta[3 * r + 1:]
+        b_start = cu_q[:r]
+        z = d.embedding(torch.cat(tokens, dim=1)).to(d.fc.weight.dtype)
+        pos = torch.tensor(positions, dtype=torch.long, device=self.device)
+        cos, sin = d.rotary(z, pos[None])
+        qlens = [size] * r
+        for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
+            att = layer.attention
+            x = layer.input_norm(z)
+            q = att.project_q(x, cos, sin).to(self.kv_dtype).contiguous()
+            kb, vb = att.project_kv(x, cos, sin)
+            out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
+                                    vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
+            z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
+            z = z + layer.mlp(layer.post_norm(z))
+        hidden = d.norm(z)[0]
+        work = dict(requests=r, query_rows=r * size, attention_calls=len(d.layers),
+                    context_block_concatenation_kv_bytes=0, gathered_kv_bytes=0)
+        return DraftFeatures(hidden, requests, size, tuple(self._lengths[q] for q in requests), work)
+
+    @torch.no_grad()
+    def propose_greedy(self, anchors):
+        """Greedy block proposal per request: serial Markov argmax over the block rows
+        (DSparkDraft._sample_greedy, dspark_qwen/model.py:210-221), batched over requests.
+        Returns {request: (tokens, confidences)}."""
+        feats = self.backbone(anchors)
+        d, size = self.draft, feats.block_size
+        r = len(feats.requests)
+        hidden = feats.hidden.view(r, size, -1)
+        base = d.lm_head(hidden.to(d.lm_head.weight.dtype))
+        prev = torch.cat([anchors[q].view(1) for q in feats.requests])
+        tokens, conf = [], []
+        for k in range(size):
+            emb = d.markov_embedding(prev)
+            conf.append(d.confidence(torch.cat((hidden[:, k].to(emb.dtype), emb), -1)).sigmoid().flatten())
+            prev = (base[:, k] + d.markov_projection(emb).to(base.dtype)).argmax(-1)
+            tokens.append(prev)
+        toks = torch.stack(tokens, 1).tolist()
+        confs = torch.stack(conf, 1).tolist()
+        return {q: (toks[i], confs[i]) for i, q in enumerate(feats.requests)}

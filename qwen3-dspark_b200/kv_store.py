@@ -70,8 +70,8 @@ class B200PersistentTargetKV:
         dims = (layers, slots, context_capacity, max_query_tokens, heads, dim)
         if any(type(n) is not int or n < 1 for n in dims):
             raise ValueError('All capacities and dimensions must be positive integers')
-        if (heads, dim, dtype) != (HKV, HEAD_DIM, torch.bfloat16):
-            raise ValueError('B200 store holds bf16 Qwen3 KV: 8 heads x 128')
+        if (heads, dim) != (HKV, HEAD_DIM) or dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError('B200 store holds bf16 (or exact-path fp32) Qwen3 KV: 8 heads x 128')
         caps = [context_capacity] * slots if slot_capacities is None else [int(c) for c in slot_capacities]
         if len(caps) != slots or any(c < 1 or c > context_capacity for c in caps):
             raise ValueError('One positive capacity <= context_capacity per slot required')
@@ -249,6 +249,8 @@ class B200PersistentTargetKV:
         n = tx.query_tokens
         if scale != SCALE:
             raise ValueError('B200 verify requires the 1/sqrt(128) scale')
+        if self.dtype != torch.bfloat16:
+            raise ValueError('The fused verify layer is bf16; use stage_layer + attend on a float32 store')
         for x, shape in ((q_raw, (n, HQ, HEAD_DIM)), (k_raw, (n, HKV, HEAD_DIM)), (v_raw, (n, HKV, HEAD_DIM)),
                          (q_norm_weight, (HEAD_DIM,)), (k_norm_weight, (HEAD_DIM,))):
             if (not isinstance(x, torch.Tensor) or tuple(x.shape) != shape or x.dtype != self.dtype
@@ -361,7 +363,8 @@ class B200PersistentTargetKV:
                 self._keys.data_ptr(), self._values.data_ptr(), self.scratch_keys.data_ptr(),
                 self.scratch_values.data_ptr(), cu_q.data_ptr(), slot_row.data_ptr(), ctx.data_ptr(),
                 cap.data_ptr(), ncommit.data_ptr(), len(tx.slots), self.layers, self.rows_per_layer,
-                self.max_query_tokens, stream), 'dspark_commit_kv')
+                self.max_query_tokens, _lib.DTYPE_F32 if self.dtype == torch.float32 else _lib.DTYPE_BF16, stream),
+                'dspark_commit_kv')
             for h, n in zip(tx.slots, counts):
                 self._lengths[h.index] += n
         except Exception:

@@ -1,0 +1,71 @@
+"""Batched greedy speculative decoding on the B200 target and draft.
+
+Per request this is ``cached_speculative_greedy`` (dspark_qwen/cached_decode.py:45-122):
+prefill the prompt, emit the target's argmax, then repeat: the draft proposes one
+block from the latest token, the target verifies [anchor] + proposals in one pass,
+the longest prefix of proposals matching the target's argmax is accepted plus the
+target's correction (or the bonus token after a full accept), the target commits
+the verified rows up to (excluding) the newest output token and rolls back the rest,
+and the draft projects the committed features. Here all active requests share one
+draft backbone call and one target verify forward per round.
+Greedy acceptance makes the output equal to the target's own greedy decode.
+"""
+import torch
+
+
+def accept_greedy(proposals, predictions, eos_ids=()):
+    """Accept rule of cached_decode.py:84-98: returns (accepted, committed tokens)."""
+    accepted, committed = 0, []
+    for proposed, correct in zip(proposals, predictions):
+        if proposed != correct:
+            committed.append(correct)
+            break
+        committed.append(proposed)
+        accepted += 1
+        if proposed in eos_ids:
+            break
+    else:
+        committed.append(predictions[-1])
+    eos = next((i for i, t in enumerate(committed) if t in eos_ids), None)
+    if eos is not None:
+        committed = committed[:eos + 1]
+    return accepted, committed
+
+
+@torch.no_grad()
+def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=()):
+    """prompts: {request: ids [1, P]} on the target device. Returns ({request: tokens}, rounds)."""
+    if type(max_new_tokens) is not int or max_new_tokens < 0:
+        raise ValueError('max_new_tokens must be a nonnegative integer')
+    eos_ids = set(eos_ids)
+    for r in prompts:
+        target.add_request(r)
+        draft.add_request(r)
+    if max_new_tokens == 0:
+        return {r: [] for r in prompts}, []
+    features = target.prefill(prompts)
+    last = target.predict(features, last_only=True)
+    output = {r: [int(last[r].argmax(-1).item())] for r in prompts}
+    draft.append_committed({r: features.context_for(r) for r in prompts})
+    active = [r for r in prompts if output[r][-1] not in eos_ids and max_new_tokens > 1]
+    rounds = []
+    while active:
+        anchors = {r: torch.tensor([[output[r][-1]]], dtype=torch.long, device=target.device) for r in active}
+        proposals = {r: toks for r, (toks, _conf) in draft.propose_greedy(anchors).items()}
+        chunks = {r: torch.tensor([[output[r][-1]] + proposals[r]], dtype=torch.long, device=target.device)
+                  for r in active}
+        verified = target.verify(chunks)
+        logits = target.predict(verified)
+        predictions = {r: v[0].argmax(-1).tolist() for r, v in logits.items()}
+        commit, stats = {}, {}
+        for r in active:
+            accepted, committed = accept_greedy(proposals[r], predictions[r], eos_ids)
+            committed = committed[:max_new_tokens - len(output[r])]
+            output[r].extend(committed)
+            commit[r] = len(committed)          # old anchor .. newest-1 are now committed KV
+            stats[r] = dict(accepted=accepted, committed=len(committed))
+        target.commit(verified, commit)
+        draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
+        rounds.append(stats)
+        active = [r for r in active if len(output[r]) < max_new_tokens and output[r][-1] not in eos_ids]
+    return output, rounds

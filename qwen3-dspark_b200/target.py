@@ -1,0 +1,208 @@
+"""B200 verify target: a transformers Qwen3 model whose attention runs on the B200 kernels.
+
+Mirrors ``PersistentQwenTarget`` (dspark_qwen/persistent_qwen_target.py:100-472):
+requests own slots of a persistent KV store, ``verify`` runs one model forward over
+the packed new tokens of several requests without touching committed KV,
+``commit`` keeps each request's verified prefix (anchor included) and drops the
+rest, ``prefill`` is verify + commit-all, ``predict`` applies the LM head, and
+selected decoder outputs are captured as draft features.
+
+The reference routes attention through an HF attention callback plus a Cache
+subclass that stages K/V and gathers a capacity workspace every layer
+(persistent_qwen_target.py:45-83). Here each layer's ``Qwen3Attention.forward``
+is replaced by one that hands the raw q/k/v projections to the store:
+
+* bf16 model: ``verify_layer`` — one fused kernel does q_norm/k_norm, RoPE, the
+  KV append and bottom-right attention over the resident prefix;
+* float32 model (exact path): transformers' own q_norm/k_norm/RoPE, then
+  ``stage_layer`` + ``attend`` on the float32 attention kernel.
+"""
+import types
+from dataclasses import dataclass
+
+import torch
+from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
+
+from .kernels import HEAD_DIM, HKV, HQ
+from .kv_store import B200PersistentTargetKV
+
+
+@dataclass
+class TargetFeatures:
+    last: torch.Tensor            # [1, sum Q, hidden] final-norm hidden states
+    context: torch.Tensor | None  # [1, sum Q, len(layer_ids) * hidden] captured decoder outputs
+    spans: dict                   # request -> (row offset, query rows, committed context before)
+    work: dict
+
+    def context_for(self, request):
+        off, q, _ = self.spans[request]
+        return self.context[:, off:off + q]
+
+
+class B200Qwen3Target:
+    def __init__(self, model, layer_ids=(), *, slots, context_capacity, max_query_tokens, slot_capacities=None):
+        config = model.config
+        if (config.model_type != 'qwen3' or getattr(config, 'use_sliding_window', False)
+                or any(kind != 'full_attention' for kind in config.layer_types)
+                or config.rope_parameters.get('rope_type') != 'default'):
+            raise ValueError('Dense Qwen3 with default RoPE required')
+        if (config.num_attention_heads, config.num_key_value_heads, config.head_dim) != (HQ, HKV, HEAD_DIM):
+            raise ValueError('B200 attention supports Hq16/Hkv8/D128 Qwen3 geometry')
+        self.layer_ids = tuple(layer_ids)
+        if (tuple(sorted(set(self.layer_ids))) != self.layer_ids
+                or any(not 0 <= i < config.num_hidden_layers for i in self.layer_ids)):
+            raise ValueError('Unique increasing valid decoder layer IDs required')
+        weight = model.get_input_embeddings().weight
+        if weight.device.type != 'cuda' or weight.dtype not in (torch.bfloat16, torch.float32):
+            raise ValueError('B200 target needs a bf16 (or exact-path float32) model on a CUDA device')
+        self.model = model.eval().requires_grad_(False)
+        self.dtype = weight.dtype
+        self.pool = B200PersistentTargetKV(layers=config.num_hidden_layers, slots=slots,
+                                           context_capacity=context_capacity, max_query_tokens=max_query_tokens,
+                                           dtype=self.dtype, device=weight.device, slot_capacities=slot_capacities)
+        self.inv_freq = model.model.rotary_emb.inv_freq.float().contiguous()
+        self.eps = config.rms_norm_eps
+        self._handles = {}
+        self._tx = None
+        self._pending = None
+        self._captured = {}
+        self._hooks = [model.model.layers[i].register_forward_hook(self._hook(i)) for i in self.layer_ids]
+        self._orig_forward = {}
+        for layer in model.model.layers:
+            att = layer.self_attn
+            self._orig_forward[att] = att.forward
+            att.forward = types.MethodType(self._attention_forward(), att)
+
+    @property
+    def device(self):
+        return self.pool.device
+
+    @property
+    def lengths(self):
+        return {r: self.pool.length(h) for r, h in self._handles.items()}
+
+    def _hook(self, index):
+        def capture(_module, _inputs, output):
+            if self._tx is None:
+                raise RuntimeError('Foreign model forward while the B200 target owns the model')
+            self._captured[index] = output[0] if isinstance(output, tuple) else output
+        return capture
+
+    def _attention_forward(self):
+        target = self
+
+        def forward(att, hidden_states, position_embeddings=None, attention_mask=None, past_key_values=None,
+                    **kwargs):
+            tx = target._tx
+            if tx is None or hidden_states.shape[0] != 1:
+                raise RuntimeError('B200 attention runs inside a verify transaction on one packed row')
+            n = hidden_states.shape[1]
+            q = att.q_proj(hidden_states).view(n, HQ, HEAD_DIM)
+            k = att.k_proj(hidden_states).view(n, HKV, HEAD_DIM)
+            v = att.v_proj(hidden_states).view(n, HKV, HEAD_DIM)
+            if target.dtype == torch.bfloat16:
+                out = target.pool.verify_layer(tx, att.layer_idx, q.contiguous(), k.contiguous(), v.contiguous(),
+                                               att.q_norm.weight, att.k_norm.weight, inv_freq=target.inv_freq,
+                                               eps=target.eps)
+            else:
+                cos, sin = position_embeddings
+                qn = att.q_norm(q[None]).transpose(1, 2)
+                kn = att.k_norm(k[None]).transpose(1, 2)
+                qr, kr = apply_rotary_pos_emb(qn, kn, cos, sin)
+                target.pool.stage_layer(tx, att.layer_idx, kr[0].transpose(0, 1).contiguous(), v.contiguous())
+                out = target.pool.attend(tx, att.layer_idx, qr[0].transpose(0, 1).contiguous())
+            return att.o_proj(out.reshape(1, n, -1)), None
+
+        return forward
+
+    # -- requests -------------------------------------------------------------------
+    def add_request(self, request):
+        if self._pending is not None:
+            raise RuntimeError('Finish the outstanding verification first')
+        handle = self.pool.add_request(request)
+        self._handles[request] = handle
+        return handle
+
+    def remove_request(self, request):
+        if self._pending is not None:
+            raise RuntimeError('Finish the outstanding verification first')
+        self.pool.remove_request(self._handles.pop(request))
+
+    # -- verification transactions (persistent_qwen_target.py:389-457) ----------------
+    @torch.no_grad()
+    def verify(self, chunks):
+        """chunks: ordered {request: ids [1, Q]}; committed KV is not modified."""
+        if self._pending is not None:
+            raise RuntimeError('Finish the outstanding verification first')
+        if not chunks:
+            raise ValueError('Nonempty ordered token mapping required')
+        for request, ids in chunks.items():
+            if request not in self._handles:
+                raise ValueError('Request not resident')
+            if (not isinstance(ids, torch.Tensor) or ids.ndim != 2 or ids.shape[0] != 1 or ids.shape[1] < 1
+                    or ids.dtype != torch.long or ids.device != self.device):
+                raise ValueError('Each token chunk must be [1,Q] long on the target device')
+        handles = tuple(self._handles[r] for r in chunks)
+        qlens = tuple(ids.shape[1] for ids in chunks.values())
+        tx = self.pool.begin(handles, query_lengths=qlens)
+        spans, offset, positions = {}, 0, []
+        for request, c, q in zip(chunks, tx.context_lengths, qlens):
+            spans[request] = (offset, q, c)
+            positions.extend(range(c, c + q))
+            offset += q
+        pos = torch.tensor(positions, dtype=torch.long).pin_memory().to(self.device, non_blocking=True)
+        self._tx, self._captured = tx, {}
+        try:
+            out = self.model.model(input_ids=torch.cat(tuple(chunks.values()), dim=1), position_ids=pos[None],
+                                   attention_mask={'full_attention': None}, use_cache=False, return_dict=True)
+            context = (torch.cat([self._captured[i] for i in self.layer_ids], dim=-1) if self.layer_ids else None)
+            work = self.pool.work(tx)
+            features = TargetFeatures(out.last_hidden_state, context, spans, work)
+            self._pending = (features, tx)
+            return features
+        except BaseException:
+            if self.pool._pending is tx and not self.pool.failed:
+                self.pool.abort(tx)
+            raise
+        finally:
+            self._tx, self._captured = None, {}
+
+    @torch.no_grad()
+    def commit(self, features, committed_query_lengths):
+        """Keep each request's verified prefix (anchor included); the rest is rolled back."""
+        if self._pending is None or self._pending[0] is not features:
+            raise ValueError('Only the outstanding verification features can commit')
+        if set(committed_query_lengths) != set(features.spans):
+            raise ValueError('One committed query prefix per verified request required')
+        _, tx = self._pending
+        result = self.pool.commit(tx, {self._handles[r]: n for r, n in committed_query_lengths.items()})
+        self._pending = None
+        return result
+
+    def abort(self, features):
+        if self._pending is None or self._pending[0] is not features:
+            raise ValueError('Only outstanding verification features can abort')
+        self.pool.abort(self._pending[1])
+        self._pending = None
+
+    @torch.no_grad()
+    def prefill(self, chunks):
+        if any(self.pool.length(self._handles[r]) for r in chunks):
+            raise ValueError('Prefill is only for newly admitted empty requests')
+        features = self.verify(chunks)
+        self.commit(features, {r: ids.shape[1] for r, ids in chunks.items()})
+        return features
+
+    @torch.no_grad()
+    def predict(self, features, last_only=False):
+        """LM head over the verified rows; {request: logits [1, Q|1, vocab]}."""
+        logits = self.model.get_output_embeddings()(features.last)
+        return {r: (logits[:, off + q - 1] if last_only else logits[:, off:off + q])
+                for r, (off, q, _) in features.spans.items()}
+
+    def close(self):
+        for hook in self._hooks:
+            hook.remove()
+        for att, fwd in self._orig_forward.items():
+            att.forward = fwd
+        self._hooks, self._orig_forward = [], {}

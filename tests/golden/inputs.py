@@ -69,3 +69,36 @@ TRAIN_SEQS = ((40, (0, 2, 6, 39)), (64, (5, 17, 18, 63, 30)))
 ROPE_CONTEXTS = (0, 255, 4000, 8191)
 ROPE_THETA = 1e6
 RMS_EPS = 1e-6
+
+
+# Tiny Qwen3 target with the real attention geometry (16/8 heads, head dim 128)
+# for the greedy-speculative parity case; the draft reads target layers 1 and 2.
+TINY_TARGET = dict(vocab_size=1024, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                   num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=4096,
+                   rms_norm_eps=1e-6, tie_word_embeddings=False, attention_dropout=0.0,
+                   rope_parameters={'rope_type': 'default', 'rope_theta': 1e6})
+TINY_DRAFT = dict(layer_ids=(1, 2), num_layers=2, block_size=7, markov_rank=16, mask_token_id=1023)
+GREEDY_PROMPTS = (64, 256, 2048, 64, 256, 100)
+GREEDY_NEW_TOKENS = 48
+
+
+def deterministic_state(named_shapes, seed):
+    """Weights by parameter name: every name gets its own PCG64 stream, so any module
+    tree with the same names and shapes receives the same values on any machine."""
+    import zlib
+    out = {}
+    for name, shape in named_shapes.items():
+        g = rng(seed * 1_000_003 + zlib.crc32(name.encode()))
+        if name.endswith('norm.weight'):
+            x = 1.0 + 0.1 * g.standard_normal(shape)
+        elif name.endswith('.bias'):
+            x = 0.02 * g.standard_normal(shape)
+        else:
+            x = 0.05 * g.standard_normal(shape)
+        out[name] = x.astype(np.float32)
+    return out
+
+
+def greedy_prompts(seed=55):
+    g = rng(seed)
+    return [g.integers(0, TINY_TARGET['vocab_size'] - 1, n).astype(np.int64) for n in GREEDY_PROMPTS]

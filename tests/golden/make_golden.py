@@ -207,6 +207,53 @@ def kv_store_fixtures(out):
     out['kv_store'] = rec
 
 
+def greedy_fixtures(out):
+    """Config-5 style parity: the reference's target greedy tokens and its own greedy
+    speculative decode (cached_speculative_greedy) on a tiny fp32 model, plus the first
+    draft proposal of request 0."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from dspark_qwen.cached_decode import DraftContextCache, cached_speculative_greedy
+    from dspark_qwen.cached_target import CachedTarget
+    from dspark_qwen.config import DraftConfig
+    from dspark_qwen.model import DSparkDraft
+    cfg = Qwen3Config(**I.TINY_TARGET)
+    cfg._attn_implementation = 'sdpa'
+    model = Qwen3ForCausalLM(cfg).eval()
+    tshapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(tshapes, 1).items()})
+    spec = DraftConfig(**I.TINY_DRAFT)
+    draft = DSparkDraft(model, spec).eval()
+    dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items()
+               if not k.startswith(('embedding.', 'lm_head.'))}
+    missing = draft.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(dshapes, 2).items()},
+                                    strict=False)
+    assert set(missing.missing_keys) <= {'embedding.weight', 'lm_head.weight'} and not missing.unexpected_keys
+    target = CachedTarget(model, spec.layer_ids)
+    tokens, spec_tokens, accepted = [], [], []
+    with torch.no_grad():
+        for ids in I.greedy_prompts():
+            x = torch.from_numpy(ids)[None]
+            greedy = target.greedy(x, I.GREEDY_NEW_TOKENS)
+            sp, rounds = cached_speculative_greedy(target, draft, x, I.GREEDY_NEW_TOKENS)
+            assert sp == greedy, 'reference speculative greedy must equal target greedy'
+            tokens.append(greedy)
+            spec_tokens.append(sp)
+            accepted.append(sum(r['accepted'] for r in rounds))
+        ids = torch.from_numpy(I.greedy_prompts()[0])[None]
+        feats = target.prefill(ids)
+        first = int(target.predict(feats, last_only=True).argmax(-1).item())
+        cache = DraftContextCache(draft)
+        cache.append(feats.context)
+        anchor = torch.tensor([[first]])
+        hidden = draft.backbone_cached(anchor, cache.layers, cache.length)
+        proposals, _ = draft.propose_greedy_cached(anchor, cache.layers, cache.length)
+    out['greedy_round'] = dict(tokens=np.array(tokens), accepted=np.array(accepted),
+                               target_names=np.array(sorted(tshapes)), draft_names=np.array(sorted(dshapes)),
+                               first_token=np.array(first), first_hidden=hidden.numpy(),
+                               first_proposals=np.array(proposals))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True, help='path of a qwen3-dspark checkout')
@@ -219,7 +266,7 @@ def main():
     torch.set_num_threads(4)
     out = {}
     for fn in (draft_fixtures, varlen_fixtures, training_fixtures, layout_fixtures, rope_fixtures,
-               kv_store_fixtures):
+               kv_store_fixtures, greedy_fixtures):
         fn(out)
     for name, rec in out.items():
         np.savez_compressed(os.path.join(HERE, f'{name}.npz'), **{k: np.asarray(v) for k, v in rec.items()})

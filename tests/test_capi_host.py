@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 3
+    assert lib.dspark_abi_version() == 4
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -40,7 +40,7 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     lib = pkg.load_library()
     st = lib.dspark_varlen_attn(None, None, None, None, None, 1, 1, 1, 1, 1, 128 ** -0.5, 0, None, None, 0, None)
     assert st == 1
-    st = lib.dspark_commit_kv(None, None, None, None, None, None, None, None, None, 1, 1, 1, 1, None)
+    st = lib.dspark_commit_kv(None, None, None, None, None, None, None, None, None, 1, 1, 1, 1, 0, None)
     assert st == 1
     st = lib.dspark_rope_table(None, None, None, 1, 1, None, None)
     assert st == 1
