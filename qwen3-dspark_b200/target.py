@@ -187,6 +187,8 @@ class B200Qwen3Target:
 
     @torch.no_grad()
     def prefill(self, chunks):
+        if any(r not in self._handles for r in chunks):
+            raise ValueError('Request not resident')
         if any(self.pool.length(self._handles[r]) for r in chunks):
             raise ValueError('Prefill is only for newly admitted empty requests')
         features = self.verify(chunks)
