@@ -279,63 +279,106 @@ struct SchedShared {
   long long scan_tmp[32];
   long long total;
   long long start, end;
-  long long req_prefix;
-  int req0, qb0, t0;
+  long long req_prefix, last_prefix;
+  int req0, qb0, t0;        // item and tile offset of this CTA's first tile
+  int req_l, qb_l, t_l;     // item and tile offset of this CTA's last tile
+  int reorder;              // process the last item's part first (see locate_range)
   int issued[kStages];
 };
 
-// Finds the total tile count and the (request, q-block, tile) where this
-// CTA's range starts. All threads of the CTA must call it.
+// (q-block, tile offset) of the tile `off` tiles into request `req`.
+__device__ __forceinline__ void locate_in_request(const AttnParams& p, int req, long long off, int& qb_out,
+                                                  int& t_out, Item& it) {
+  const int nqb = request_qblocks(p, req);
+  int qb = 0;
+  for (; qb < nqb; ++qb) {
+    load_item(p, req, qb, it);
+    if (off < it.tiles) break;
+    off -= it.tiles;
+  }
+  qb_out = qb;
+  t_out = static_cast<int>(off);
+}
+
+// Finds the total tile count and the items holding this CTA's first and last
+// tiles. All threads of the CTA must call it. With at most one request per
+// thread the tile counts are scanned once; otherwise twice (total, then place).
+//
+// Walk order: if the CTA's last item began inside the range and continues into
+// the next CTA's range, the CTA processes that item's part first and then the
+// rest of its range. Its contribution to that cut item then arrives early and
+// the merge of the item (done by whichever contributor arrives last) overlaps
+// with streaming instead of trailing the kernel.
 template <int kThreads>
 __device__ void locate_range(const AttnParams& p, SchedShared& s) {
   const int tid = threadIdx.x;
-  long long running = 0, chunk_total;
-  for (int base = 0; base < p.num_requests; base += kThreads) {
-    const int i = base + tid;
-    const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
-    block_scan<kThreads>(t, s.scan_tmp, chunk_total);
-    running += chunk_total;
+  if (tid == 0) {
+    s.req0 = -1;
+    s.req_l = -1;
   }
-  const long long total = running;
-  const long long start = range_start(blockIdx.x, total, p.grid);
-  const long long end = range_start(blockIdx.x + 1, total, p.grid);
+  long long total, start, end, chunk_total;
+  if (p.num_requests <= kThreads) {
+    const long long t = tid < p.num_requests ? request_tiles(p, tid) : 0;
+    const long long incl = block_scan<kThreads>(t, s.scan_tmp, total);
+    start = range_start(blockIdx.x, total, p.grid);
+    end = range_start(blockIdx.x + 1, total, p.grid);
+    if (tid < p.num_requests && start < end) {
+      const long long excl = incl - t;
+      if (excl <= start && start < incl) {
+        s.req0 = tid;
+        s.req_prefix = excl;
+      }
+      if (excl <= end - 1 && end - 1 < incl) {
+        s.req_l = tid;
+        s.last_prefix = excl;
+      }
+    }
+  } else {
+    long long running = 0;
+    for (int base = 0; base < p.num_requests; base += kThreads) {
+      const int i = base + tid;
+      const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+      block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+      running += chunk_total;
+    }
+    total = running;
+    start = range_start(blockIdx.x, total, p.grid);
+    end = range_start(blockIdx.x + 1, total, p.grid);
+    if (start < end) {
+      running = 0;
+      for (int base = 0; base < p.num_requests; base += kThreads) {
+        const int i = base + tid;
+        const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+        const long long incl = running + block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+        if (i < p.num_requests && incl - t <= start && start < incl) {
+          s.req0 = i;
+          s.req_prefix = incl - t;
+        }
+        if (i < p.num_requests && incl - t <= end - 1 && end - 1 < incl) {
+          s.req_l = i;
+          s.last_prefix = incl - t;
+        }
+        running += chunk_total;
+      }
+    }
+  }
+  __syncthreads();
   if (tid == 0) {
     s.total = total;
     s.start = start;
     s.end = end;
-    s.req0 = -1;
-  }
-  __syncthreads();
-  if (start < end) {
-    running = 0;
-    for (int base = 0; base < p.num_requests; base += kThreads) {
-      const int i = base + tid;
-      const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
-      const long long incl = running + block_scan<kThreads>(t, s.scan_tmp, chunk_total);
-      if (i < p.num_requests && incl - t <= start && start < incl) {
-        s.req0 = i;
-        s.req_prefix = incl - t;
+    s.reorder = 0;
+    if (start < end) {
+      if (s.req0 < 0 || s.req_l < 0) {
+        atomicOr(&g_device_status, kStatusBadSchedule);
+        s.end = s.start;   // nothing to do
+      } else {
+        Item it;
+        locate_in_request(p, s.req0, start - s.req_prefix, s.qb0, s.t0, it);
+        locate_in_request(p, s.req_l, end - 1 - s.last_prefix, s.qb_l, s.t_l, it);
+        const long long last_start = end - 1 - s.t_l;
+        s.reorder = last_start > start && last_start + it.tiles > end;
       }
-      running += chunk_total;
-    }
-  }
-  __syncthreads();
-  if (tid == 0 && start < end) {
-    if (s.req0 < 0) {
-      atomicOr(&g_device_status, kStatusBadSchedule);
-      s.end = s.start;   // nothing to do
-    } else {
-      long long off = start - s.req_prefix;
-      const int nqb = request_qblocks(p, s.req0);
-      Item it;
-      int qb = 0;
-      for (; qb < nqb; ++qb) {
-        load_item(p, s.req0, qb, it);
-        if (off < it.tiles) break;
-        off -= it.tiles;
-      }
-      s.qb0 = qb;
-      s.t0 = static_cast<int>(off);
     }
   }
   __syncthreads();
@@ -645,6 +688,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __nv_bfloat16* qw_smem = reinterpret_cast<__nv_bfloat16*>(smem + kSmemWeightOff);
   __nv_bfloat16* kw_smem = qw_smem + kHeadDim;
 
+  // Measured: the two-segment walk helps the plain kernels (cut-item merges no
+  // longer trail the kernel) but slows the fused one, which walks in order.
+  constexpr bool kReorderWalk = !kFused;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (kFused && threadIdx.x < kHeadDim) {
     qw_smem[threadIdx.x] = p.q_w[threadIdx.x];
@@ -669,31 +715,48 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       prefetch_tmap(&tm_va);
       prefetch_tmap(&tm_kb);
       prefetch_tmap(&tm_vb);
-      Walker w;
-      w.begin(p, sched.req0, sched.qb0, sched.t0);
       int issued[kStages] = {};
-      for (long long gk = start; gk < end; ++gk) {
-        const int kl = static_cast<int>(gk - start);
-        const int stage = kl % kStages;
-        const uint32_t parity = ((kl / kStages) & 1) ^ 1;
-        if (!mbar_wait(smem_u32(&empty[stage]), parity)) break;
-        const Tile ti = tile_of(w.it, w.t);
-        const uint32_t bar = smem_u32(&full[stage]);
-        const CUtensorMap* mk = ti.src_b ? &tm_kb : &tm_ka;
-        const CUtensorMap* mv = ti.src_b ? &tm_vb : &tm_va;
-        const uint32_t dst = smem_u32(smem + stage * kStageBytes);
-        // fused new-row tile: also its rows of the cos/sin table (clamped to the table)
-        const int rope_rows = (kFused && ti.src_b) ? max(0, min(kTileN, p.total_q - ti.row)) : 0;
-        mbar_arrive_expect_tx(bar, kStageBytes + rope_rows * kRopeRowBytes);
-        if (rope_rows > 0)
-          bulk_load(smem_u32(smem + kSmemRopeOff + stage * kRopeStageBytes),
-                    p.rope + static_cast<size_t>(ti.row) * 64, rope_rows * kRopeRowBytes, bar);
-        tma_load_3d(dst, mk, 0, ti.row, 0, bar);
-        tma_load_3d(dst + kHalfBoxBytes, mk, 64, ti.row, 0, bar);
-        tma_load_3d(dst + 2 * kHalfBoxBytes, mv, 0, ti.row, 0, bar);
-        tma_load_3d(dst + 3 * kHalfBoxBytes, mv, 64, ti.row, 0, bar);
-        ++issued[stage];
-        w.advance(p);
+      int kl = 0;
+      const bool reorder = kReorderWalk && sched.reorder;
+      const long long last_start = end - 1 - sched.t_l;
+      bool ok = true;
+      for (int seg = 0; seg < (reorder ? 2 : 1) && ok; ++seg) {
+        Walker w;
+        long long lo, hi;
+        if (reorder && seg == 0) {
+          w.begin(p, sched.req_l, sched.qb_l, 0);
+          lo = last_start;
+          hi = end;
+        } else {
+          w.begin(p, sched.req0, sched.qb0, sched.t0);
+          lo = start;
+          hi = reorder ? last_start : end;
+        }
+        for (long long gk = lo; gk < hi; ++gk, ++kl) {
+          const int stage = kl % kStages;
+          const uint32_t parity = ((kl / kStages) & 1) ^ 1;
+          if (!mbar_wait(smem_u32(&empty[stage]), parity)) {
+            ok = false;
+            break;
+          }
+          const Tile ti = tile_of(w.it, w.t);
+          const uint32_t bar = smem_u32(&full[stage]);
+          const CUtensorMap* mk = ti.src_b ? &tm_kb : &tm_ka;
+          const CUtensorMap* mv = ti.src_b ? &tm_vb : &tm_va;
+          const uint32_t dst = smem_u32(smem + stage * kStageBytes);
+          // fused new-row tile: also its rows of the cos/sin table (clamped to the table)
+          const int rope_rows = (kFused && ti.src_b) ? max(0, min(kTileN, p.total_q - ti.row)) : 0;
+          mbar_arrive_expect_tx(bar, kStageBytes + rope_rows * kRopeRowBytes);
+          if (rope_rows > 0)
+            bulk_load(smem_u32(smem + kSmemRopeOff + stage * kRopeStageBytes),
+                      p.rope + static_cast<size_t>(ti.row) * 64, rope_rows * kRopeRowBytes, bar);
+          tma_load_3d(dst, mk, 0, ti.row, 0, bar);
+          tma_load_3d(dst + kHalfBoxBytes, mk, 64, ti.row, 0, bar);
+          tma_load_3d(dst + 2 * kHalfBoxBytes, mv, 0, ti.row, 0, bar);
+          tma_load_3d(dst + 3 * kHalfBoxBytes, mv, 64, ti.row, 0, bar);
+          ++issued[stage];
+          w.advance(p);
+        }
       }
       for (int s = 0; s < kStages; ++s) sched.issued[s] = issued[s];
     }
@@ -704,22 +767,40 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const float sl2 = p.scale_log2;
     __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
 
-    Walker w;
-    w.begin(p, sched.req0, sched.qb0, sched.t0);
-    long long item_start = start - sched.t0;
     uint32_t qf[8][4];
     float o[16][4];
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
+    int kl = 0;
+    const bool reorder = kReorderWalk && sched.reorder;
+    const long long last_start = end - 1 - sched.t_l;
+    bool ok = true;
+    for (int seg = 0; seg < (reorder ? 2 : 1) && ok; ++seg) {
+    Walker w;
+    long long lo, hi;
+    if (reorder && seg == 0) {
+      w.begin(p, sched.req_l, sched.qb_l, 0);
+      lo = last_start;
+      hi = end;
+    } else {
+      w.begin(p, sched.req0, sched.qb0, sched.t0);
+      lo = start;
+      hi = reorder ? last_start : end;
+    }
+    long long item_start = lo - w.t;
     load_q_fragments<kFused>(p, w.it, h, lane, qw_smem, qf);
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
+    m_a = m_b = -INFINITY;
+    l_a = l_b = 0.f;
 
-    for (long long gk = start; gk < end; ++gk) {
-      const int kl = static_cast<int>(gk - start);
+    for (long long gk = lo; gk < hi; ++gk, ++kl) {
       const int stage = kl % kStages;
       const uint32_t parity = (kl / kStages) & 1;
       const Item& it = w.it;
-      if (!mbar_wait(smem_u32(&full[stage]), parity)) break;
+      if (!mbar_wait(smem_u32(&full[stage]), parity)) {
+        ok = false;
+        break;
+      }
       const Tile ti = tile_of(it, w.t);
       const bool self_filled = kFused && ti.src_b;
       if (self_filled) {
@@ -827,7 +908,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
 
       const bool last_tile = w.t + 1 >= it.tiles;
-      if (last_tile || gk + 1 == end) {
+      if (last_tile || gk + 1 == hi) {
         const float la = quad_sum(l_a), lb = quad_sum(l_b);
         const long long item_end = item_start + it.tiles;
         if (item_start >= start && item_end <= end) {
@@ -845,7 +926,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         } else {
           finish_split_item(p, it, item_start, item_end, start, total, h, lane, o, m_a, m_b, la, lb);
         }
-        if (!last_tile || gk + 1 == end) break;      // this CTA's range ends here
+        if (!last_tile || gk + 1 == hi) {            // this segment ends here
+          ++kl;
+          break;
+        }
         // Next item: its Q replaces qf and its accumulators restart.
         w.advance(p);
         item_start = gk + 1;
@@ -857,6 +941,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       w.advance(p);
+    }
     }
   }
   // Never leave the CTA with a TMA write still in flight (only possible after
