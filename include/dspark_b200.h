@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 4
+#define DSPARK_ABI_VERSION 5
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -155,6 +155,35 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
                      const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
                      const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
                      int scratch_rows, int dtype, cudaStream_t stream);
+
+/*
+ * Training-layout block-draft attention (bf16, tcgen05 tensor cores).
+ * Replaces DraftAttention.forward's masked SDPA with block_mask
+ * (dspark_qwen/model.py:12-19,47-61) for several sequences packed back to back.
+ * Sequence s has ctx_len[s] context rows and num_blocks[s] anchors (its slice
+ * of `anchors`, in order); its queries are num_blocks[s]*block_size rows, its
+ * keys are [ctx_len[s] context rows ; the same block rows]. Block b's rows see
+ * context rows j < anchors[b] (anchors are clamped to [0, ctx_len[s]], which is
+ * what the mask does) and all rows of block b; sequences never see each other.
+ *
+ * dspark_train_plan runs on the host only (all pointers are HOST memory): it
+ * splits the queries into 64-row tiles per KV head and assigns them to at most
+ * grid_limit persistent CTAs (largest first onto the least-loaded CTA). Call it
+ * with plan == NULL to get the plan size in int32 words in *plan_words; the
+ * plan is then copied to the device once and reused by every call with the
+ * same layout. Returns DSPARK_ERR_UNSUPPORTED if the packed sizes reach 2^31.
+ * block_size must be in [6, 32].
+ *
+ * dspark_train_attn launches plan[2] CTAs (`grid` must equal it) on q
+ * [total_q, 16, 128], k/v [total_k, 8, 128] and writes out [total_q, 16, 128]
+ * (all bf16, 16-byte aligned, device memory; plan 16-byte aligned device
+ * memory). A plan built for other sizes sets DSPARK_DEVICE_BAD_ARGUMENT and
+ * computes nothing.
+ */
+int dspark_train_plan(int num_seqs, const int32_t* ctx_len, const int32_t* num_blocks, const int32_t* anchors,
+                      int block_size, int grid_limit, int32_t* plan, long long plan_capacity, long long* plan_words);
+int dspark_train_attn(const void* q, const void* k, const void* v, int total_q, long long total_k,
+                      const int32_t* plan, int grid, float scale, void* out, cudaStream_t stream);
 
 /*
  * Allocation-free variant of dspark_varlen_attn (bf16 only). No counterpart in

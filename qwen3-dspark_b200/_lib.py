@@ -31,6 +31,8 @@ SIGNATURES = {
                                  _vp, _i, _i, _i, _f, _vp, _vp, _sz, _vp]),
     'dspark_rope_table': (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
     'dspark_commit_kv': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _vp]),
+    'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
+    'dspark_train_attn': (_i, [_vp, _vp, _vp, _i, _ll, _vp, _i, _f, _vp, _vp]),
 }
 
 _lock = threading.Lock()
@@ -51,7 +53,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 4:
+        if lib.dspark_abi_version() != 5:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib
@@ -92,3 +94,18 @@ def workspace(device, stream):
         ws = torch.empty(size.value, dtype=torch.uint8, device=device)
         _workspaces[key] = ws
     return ws
+
+
+def train_plan(context_lengths, num_blocks, anchors, block_size, grid_limit):
+    """Host-built work plan of the training-layout kernel (int32 list); no GPU needed."""
+    lib = load_library()
+    n = len(context_lengths)
+    arr = lambda xs: (ctypes.c_int32 * max(len(xs), 1))(*xs)  # noqa: E731
+    ctx, nb, anc = arr(context_lengths), arr(num_blocks), arr(anchors)
+    words = ctypes.c_longlong(0)
+    check(lib.dspark_train_plan(n, ctx, nb, anc, block_size, grid_limit, None, 0, ctypes.byref(words)),
+          'dspark_train_plan')
+    plan = (ctypes.c_int32 * words.value)()
+    check(lib.dspark_train_plan(n, ctx, nb, anc, block_size, grid_limit, plan, words.value, ctypes.byref(words)),
+          'dspark_train_plan')
+    return list(plan)

@@ -4,12 +4,17 @@
 // here: scratch for split items is the caller's workspace.
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
+#include <algorithm>
 #include <atomic>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
+#include <numeric>
+#include <queue>
+#include <vector>
 
 #include "attention.cuh"
+#include "train.cuh"
 #include "verify.cuh"
 #include "../../include/dspark_b200.h"
 
@@ -55,7 +60,9 @@ int device_info(int dev, DeviceInfo* out) {
         cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (d.cc_major != 10) return DSPARK_ERR_UNSUPPORTED;   // built for sm_100a only
-    if (static_cast<size_t>(d.max_smem_optin) < kAttnSmemBytes) return DSPARK_ERR_UNSUPPORTED;
+    if (static_cast<size_t>(d.max_smem_optin) < kAttnSmemBytes ||
+        static_cast<size_t>(d.max_smem_optin) < train::kSmemBytes)
+      return DSPARK_ERR_UNSUPPORTED;
     int cur = -1;
     cudaGetDevice(&cur);
     if (cur != dev) return DSPARK_ERR_INVALID_ARGUMENT;     // attributes are per current device
@@ -64,7 +71,9 @@ int device_info(int dev, DeviceInfo* out) {
         cudaFuncSetAttribute(attn_bf16_kernel<true, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(attn_bf16_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(kAttnSmemBytes)) != cudaSuccess)
+                             static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(train::train_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(train::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
@@ -213,6 +222,22 @@ int varlen_common(const void* q, const void* k, const void* v, const int32_t* cu
   p.cu_k = cu_k;
   KeySources src{k, v, key_rows, nullptr, nullptr, 0};
   return run_attention(p, src, dtype, max_q, workspace, workspace_bytes, stream);
+}
+
+// Packed q or K/V [rows, heads, 128] bf16 as dims (d, head, row): one box of
+// (64 d, box_heads, box_rows) lands in shared memory as [row][head][64 d] rows of
+// 128 bytes in the 128-byte swizzle, the K-major operand layout of tcgen05.mma.
+int encode_rows_map(CUtensorMap* m, const void* base, long long rows, int heads, int box_heads, int box_rows) {
+  if (!aligned(base, 16) || rows < 1 || rows >= (1ll << 31)) return DSPARK_ERR_INVALID_ARGUMENT;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kHeadDim), static_cast<cuuint64_t>(heads),
+                        static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHeadDim * 2), static_cast<cuuint64_t>(heads * kHeadDim * 2)};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(box_heads), static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? DSPARK_OK : DSPARK_ERR_CUDA;
 }
 
 }  // namespace
@@ -372,6 +397,108 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
   cp.rows_per_layer = rows_per_layer;
   cp.scratch_rows = scratch_rows;
   commit_kernel<<<dim3(num_requests, num_layers), 256, 0, stream>>>(cp);
+  return launch_status();
+}
+
+int dspark_train_plan(int num_seqs, const int32_t* ctx_len, const int32_t* num_blocks, const int32_t* anchors,
+                      int block_size, int grid_limit, int32_t* plan, long long plan_capacity, long long* plan_words) {
+  using namespace train;
+  if (num_seqs < 1 || !ctx_len || !num_blocks || !anchors || !plan_words || block_size < kMinBlock ||
+      block_size > kMaxBlock || grid_limit < 1 || grid_limit > 65535)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  // Packed offsets of every sequence: queries = its blocks' rows, keys = context then block rows.
+  struct Tile {
+    int item[kItemWords];
+    int cost;
+  };
+  std::vector<Tile> tiles;
+  long long q_off = 0, k_off = 0, a_off = 0;
+  for (int s = 0; s < num_seqs; ++s) {
+    const long long ctx = ctx_len[s], nb = num_blocks[s];
+    if (ctx < 0 || nb < 0) return DSPARK_ERR_INVALID_ARGUMENT;
+    const long long nq = nb * block_size;
+    if (q_off + nq >= (1ll << 31) || k_off + ctx + nq >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
+    for (long long t0 = 0; t0 < nq; t0 += kTileQ) {
+      Tile tile{};
+      const int n = static_cast<int>(std::min<long long>(kTileQ, nq - t0));
+      const int b0 = static_cast<int>(t0 / block_size), b1 = static_cast<int>((t0 + n - 1) / block_size);
+      int ctx_keys = 0;
+      for (int b = b0; b <= b1; ++b) {
+        const int a = static_cast<int>(std::max<long long>(0, std::min<long long>(anchors[a_off + b], ctx)));
+        tile.item[kIAnchors + b - b0] = a;
+        ctx_keys = std::max(ctx_keys, a);
+      }
+      tile.item[kIQRow0] = static_cast<int>(q_off + t0);
+      tile.item[kINq] = n;
+      tile.item[kIKBase] = static_cast<int>(k_off);
+      tile.item[kICtxKeys] = ctx_keys;
+      tile.item[kIBlkKey0] = static_cast<int>(k_off + ctx + static_cast<long long>(b0) * block_size);
+      tile.item[kIPhase] = static_cast<int>(t0 % block_size);
+      tile.item[kINBlocks] = b1 - b0 + 1;
+      tile.item[kIBlockSize] = block_size;
+      // one key block of tile overhead (Q load, epilogue) on top of the key blocks
+      tile.cost = (ctx_keys + kKeyBlock - 1) / kKeyBlock + 2;
+      for (int h = 0; h < kKVHeads; ++h) {
+        tile.item[kIHead] = h;
+        tiles.push_back(tile);
+      }
+    }
+    q_off += nq;
+    k_off += ctx + nq;
+    a_off += nb;
+  }
+  const int n_items = static_cast<int>(tiles.size());
+  const int grid = std::max(1, std::min(grid_limit, n_items));
+  const long long words = plan_items_at(grid) + static_cast<long long>(n_items) * kItemWords;
+  *plan_words = words;
+  if (plan == nullptr) return DSPARK_OK;            // size query
+  if (plan_capacity < words) return DSPARK_ERR_INVALID_ARGUMENT;
+  // Largest tile first onto the least-loaded CTA.
+  std::vector<int> order(n_items);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return tiles[a].cost > tiles[b].cost; });
+  using Load = std::pair<long long, int>;
+  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
+  for (int c = 0; c < grid; ++c) heap.push({0, c});
+  std::vector<std::vector<int>> per_cta(grid);
+  for (int i : order) {
+    Load l = heap.top();
+    heap.pop();
+    per_cta[l.second].push_back(i);
+    heap.push({l.first + tiles[i].cost, l.second});
+  }
+  std::fill(plan, plan + words, 0);
+  plan[0] = kPlanMagic;
+  plan[1] = n_items;
+  plan[2] = grid;
+  plan[3] = static_cast<int>(q_off);
+  plan[4] = static_cast<int>(k_off);
+  int* items = plan + plan_items_at(grid);
+  int next = 0;
+  for (int c = 0; c < grid; ++c) {
+    plan[kPlanHeader + c] = next;
+    for (int i : per_cta[c]) std::copy(tiles[i].item, tiles[i].item + kItemWords, items + (next++) * kItemWords);
+  }
+  plan[kPlanHeader + grid] = next;
+  return DSPARK_OK;
+}
+
+int dspark_train_attn(const void* q, const void* k, const void* v, int total_q, long long total_k,
+                      const int32_t* plan, int grid, float scale, void* out, cudaStream_t stream) {
+  if (!q || !k || !v || !plan || !out || total_q < 1 || total_k < 1 || total_k >= (1ll << 31) || grid < 1 ||
+      grid > 65535 || !(scale > 0.f) || !aligned(q, 16) || !aligned(k, 16) || !aligned(v, 16) ||
+      !aligned(out, 16) || !aligned(plan, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  CUtensorMap qm, km, vm;
+  if ((st = encode_rows_map(&qm, q, total_q, 16, 2, train::kTileQ)) != DSPARK_OK) return st;
+  if ((st = encode_rows_map(&km, k, total_k, kKVHeads, 1, train::kKeyBlock)) != DSPARK_OK) return st;
+  if ((st = encode_rows_map(&vm, v, total_k, kKVHeads, 1, train::kKeyBlock)) != DSPARK_OK) return st;
+  train::train_attn_kernel<<<grid, train::kThreads, train::kSmemBytes, stream>>>(
+      qm, km, vm, plan, static_cast<__nv_bfloat16*>(out), total_q, static_cast<int>(total_k),
+      scale * 1.4426950408889634f);
   return launch_status();
 }
 

@@ -1,0 +1,507 @@
+// Training-layout block-draft attention on the 5th-generation tensor cores.
+//
+// Semantics (dspark_qwen/model.py:12-19,47-61, one sequence at a time, several
+// sequences packed back to back with no attention between them): sequence s has
+// ctx_s context rows and n_s anchors; its keys are [context rows ; block rows],
+// block b owns block rows [ctx_s + bs*b, +bs) and its queries are those same
+// bs rows. Query row r of block b sees context rows j < anchor_b and the bs rows
+// of its own block (bidirectional). GQA: q head h reads KV head h/2.
+//
+// Work unit ("tile"): 64 consecutive query rows of one sequence x the two q
+// heads of one KV head = 128 rows of S (row m = 2*query + head), so one
+// tcgen05.mma M=128 covers both heads sharing the K/V tile. Per tile the keys
+// are the context prefix up to the tile's largest anchor, in 128-row blocks,
+// then one 128-row block starting at the tile's first block row.
+//
+// Roles (192 threads, one CTA per SM):
+//   warps 0-3  softmax: thread m owns S/O row m (TMEM lane m); online softmax
+//              with the running max raised only when it grows by more than
+//              2^8 (exact: the final O/l does not depend on the max used),
+//              P written to shared memory as the next MMA's A operand;
+//   warp 4     MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
+//              two S buffers, O += P V into the O accumulator, completion
+//              reported through tcgen05.commit on mbarriers;
+//   warp 5     TMA producer (one thread): Q per tile, K and V per key block
+//              into two-stage rings with separate K and V barriers.
+// Every wait is bounded; a timed-out wait raises a CTA abort flag that ends all
+// roles, the MMA thread drains its MMAs, the producer waits for its copies in
+// flight, and TMEM is released before the CTA exits.
+#pragma once
+#include "ptx.cuh"
+
+namespace dspark {
+namespace train {
+
+constexpr int kThreads = 192;
+constexpr int kTileQ = 64;          // query rows per tile (x2 heads = 128 MMA rows)
+constexpr int kKeyBlock = 128;      // keys per S tile
+constexpr int kMaxTileBlocks = 12;  // anchor slots per tile
+constexpr int kMinBlock = 6, kMaxBlock = 32;
+
+// Plan (int32 words, built on the host by dspark_train_plan):
+//   [0] kPlanMagic [1] items [2] grid [3] total_q [4] total_k [5..7] 0
+//   [8 .. 8+grid]   first item of each CTA (grid+1 offsets)
+//   [items_at ..]   items of kItemWords words, in CTA order; items_at is a
+//                   multiple of 4 words.
+constexpr int kPlanMagic = 0x44535431;   // "DST1"
+constexpr int kPlanHeader = 8;
+constexpr int kItemWords = 24;
+enum ItemField {
+  kIQRow0 = 0,     // packed row of the tile's first query
+  kINq = 1,        // query rows in the tile (1..64)
+  kIHead = 2,      // KV head
+  kIKBase = 3,     // packed key row of the sequence's first context row
+  kICtxKeys = 4,   // context keys any row of the tile sees (= largest anchor)
+  kIBlkKey0 = 5,   // packed key row of the tile's first block row
+  kIPhase = 6,     // row of the first query inside its block
+  kINBlocks = 7,   // blocks the tile's queries belong to (1..12)
+  kIBlockSize = 8,
+  kIAnchors = 12,  // anchors (clamped to [0, ctx]) of the tile's blocks
+};
+
+__host__ __device__ constexpr int plan_items_at(int grid) { return ((kPlanHeader + grid + 1) + 3) & ~3; }
+
+// Shared memory (offsets from a 1024-byte aligned base). Every operand tile is
+// two 16 KB halves of 128 rows x 64 bf16 in the 128-byte swizzle.
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = 32768;           // 2 stages x 32 KB
+constexpr uint32_t kSmemV = 98304;           // 2 stages x 32 KB
+constexpr uint32_t kSmemP = 163840;          // 32 KB
+constexpr uint32_t kSmemBar = 196608;
+enum Barrier {
+  kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarKFull1, kBarKEmpty0, kBarKEmpty1, kBarVFull0, kBarVFull1,
+  kBarVEmpty0, kBarVEmpty1, kBarSFull0, kBarSFull1, kBarPFull, kBarODone, kBarOFree, kBarDrain, kNumBarriers
+};
+constexpr uint32_t kSmemTmemSlot = kSmemBar + kNumBarriers * 8;
+constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
+constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 4;
+
+// TMEM columns: two S buffers and the O accumulator, 128 fp32 columns each.
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0, kTmemO = 256;
+
+// ---------------------------------------------------------------- tcgen05 PTX
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem), "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, bf16 in, fp32 accumulate, one thread.
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier when every MMA this thread issued so far is done.
+__device__ __forceinline__ void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// Shared-memory matrix descriptor: 128-byte swizzle, sm_100 descriptor version.
+// lbo/sbo in bytes (leading / stride dimension byte offsets).
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) | (static_cast<uint64_t>(lbo >> 4) << 16) |
+         (static_cast<uint64_t>(sbo >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// Instruction descriptor of kind::f16: fp32 D, bf16 A and B, A K-major,
+// B K-major (b_mn = 0) or N-major (b_mn = 1), M = 128, N = 128.
+__host__ __device__ constexpr uint32_t instr_desc(uint32_t b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | (b_mn << 16) | ((128u >> 3) << 17) | ((128u >> 4) << 24);
+}
+
+// 32 lanes x 32 fp32 columns from TMEM, waited for inside the same statement so
+// no use of the registers can be scheduled before the data has arrived.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// Bounded wait that also gives up as soon as another role has raised the CTA
+// abort flag. A timeout raises the flag and the device status bit.
+__device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        atomicOr(&g_device_status, kStatusWaitTimeout);
+        *abort_flag = 1;
+        return false;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- item
+struct Item {
+  int q_row0, nq, head, k_base, ctx_keys, blk_key0, phase, nblocks, bs;
+  __device__ int key_blocks() const { return (ctx_keys + kKeyBlock - 1) / kKeyBlock + 1; }
+};
+
+__device__ __forceinline__ bool load_item(const int* it, int total_q, int total_k, Item& x) {
+  x.q_row0 = it[kIQRow0];
+  x.nq = it[kINq];
+  x.head = it[kIHead];
+  x.k_base = it[kIKBase];
+  x.ctx_keys = it[kICtxKeys];
+  x.blk_key0 = it[kIBlkKey0];
+  x.phase = it[kIPhase];
+  x.nblocks = it[kINBlocks];
+  x.bs = it[kIBlockSize];
+  return x.nq >= 1 && x.nq <= kTileQ && x.head >= 0 && x.head < 8 && x.q_row0 >= 0 && x.q_row0 + x.nq <= total_q &&
+         x.k_base >= 0 && x.ctx_keys >= 0 && x.k_base + x.ctx_keys <= total_k && x.blk_key0 >= 0 &&
+         x.blk_key0 < total_k && x.bs >= kMinBlock && x.bs <= kMaxBlock && x.phase >= 0 && x.phase < x.bs &&
+         x.nblocks >= 1 && x.nblocks <= kMaxTileBlocks && (x.phase + x.nq - 1) / x.bs < x.nblocks &&
+         x.nblocks * x.bs <= kKeyBlock;
+}
+
+// ---------------------------------------------------------------- roles
+__device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUtensorMap* kmap,
+                                              const CUtensorMap* vmap, const int* items, int first, int last,
+                                              int total_q, int total_k, uint32_t sbase, uint32_t bars,
+                                              volatile int* abort_flag) {
+  auto bar = [&](int i) { return bars + 8u * i; };
+  int gb = 0, it = 0;
+  int armed_q = 0, armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
+  bool ok = true;
+  for (int idx = first; idx < last && ok; ++idx) {
+    Item x;
+    if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
+    const int nb = x.key_blocks(), nctx = nb - 1;
+    if (!(ok = wait_or_abort(bar(kBarQEmpty), (it & 1) ^ 1, abort_flag))) break;
+    mbar_arrive_expect_tx(bar(kBarQFull), 32768);
+    tma_load_3d(sbase + kSmemQ, qmap, 0, 2 * x.head, x.q_row0, bar(kBarQFull));
+    tma_load_3d(sbase + kSmemQ + 16384, qmap, 64, 2 * x.head, x.q_row0, bar(kBarQFull));
+    ++armed_q;
+    // Consumption order is QK(0), QK(1), PV(0), QK(2), PV(1), ...: K runs one
+    // block ahead of V so a K stage is refilled as soon as its QK is done.
+    auto key_row = [&](int n) { return n < nctx ? x.k_base + n * kKeyBlock : x.blk_key0; };
+    for (int n = 0; n <= nb; ++n) {
+      if (n < nb) {
+        const int g = gb + n, st = g & 1;
+        if (!(ok = wait_or_abort(bar(kBarKEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(bar(kBarKFull0 + st), 32768);
+        tma_load_3d(sbase + kSmemK + st * 32768, kmap, 0, x.head, key_row(n), bar(kBarKFull0 + st));
+        tma_load_3d(sbase + kSmemK + st * 32768 + 16384, kmap, 64, x.head, key_row(n), bar(kBarKFull0 + st));
+        ++armed_k[st];
+      }
+      if (n >= 1) {
+        const int g = gb + n - 1, st = g & 1;
+        if (!(ok = wait_or_abort(bar(kBarVEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
+        mbar_arrive_expect_tx(bar(kBarVFull0 + st), 32768);
+        tma_load_3d(sbase + kSmemV + st * 32768, vmap, 0, x.head, key_row(n - 1), bar(kBarVFull0 + st));
+        tma_load_3d(sbase + kSmemV + st * 32768 + 16384, vmap, 64, x.head, key_row(n - 1), bar(kBarVFull0 + st));
+        ++armed_v[st];
+      }
+    }
+    gb += nb;
+    ++it;
+  }
+  if (!ok) *abort_flag = 1;
+  // Copies in flight land before the CTA can exit (a no-op when all were consumed).
+  volatile int never = 0;
+  if (armed_q) wait_or_abort(bar(kBarQFull), (armed_q - 1) & 1, &never);
+  for (int st = 0; st < 2; ++st) {
+    if (armed_k[st]) wait_or_abort(bar(kBarKFull0 + st), (armed_k[st] - 1) & 1, &never);
+    if (armed_v[st]) wait_or_abort(bar(kBarVFull0 + st), (armed_v[st] - 1) & 1, &never);
+  }
+}
+
+__device__ __forceinline__ void mma_role(const int* items, int first, int last, int total_q, int total_k,
+                                         uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
+  auto bar = [&](int i) { return bars + 8u * i; };
+  constexpr uint32_t kIdescQK = instr_desc(0);
+  constexpr uint32_t kIdescPV = instr_desc(1);
+  int gb = 0, it = 0;
+  bool ok = true;
+  // S(g) = Q K(g)^T: 8 MMAs of K=16 over the head dim (two 64-column halves).
+  auto issue_qk = [&](int g) -> bool {
+    const int st = g & 1;
+    if (!wait_or_abort(bar(kBarKFull0 + st), (g >> 1) & 1, abort_flag)) return false;
+    tc_fence_after();
+    const uint32_t kbase = sbase + kSmemK + st * 32768;
+#pragma unroll
+    for (int kk = 0; kk < 8; ++kk) {
+      const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+      umma_bf16(tmem + kTmemS + st * 128, smem_desc(sbase + kSmemQ + off, 16, 1024), smem_desc(kbase + off, 16, 1024),
+                kIdescQK, kk > 0);
+    }
+    umma_commit(bar(kBarSFull0 + st));
+    umma_commit(bar(kBarKEmpty0 + st));
+    return true;
+  };
+  for (int idx = first; idx < last && ok; ++idx) {
+    Item x;
+    if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
+    const int nb = x.key_blocks();
+    if (!(ok = wait_or_abort(bar(kBarQFull), it & 1, abort_flag))) break;
+    tc_fence_after();
+    if (!(ok = issue_qk(gb))) break;
+    if (nb > 1 && !(ok = issue_qk(gb + 1))) break;
+    if (nb <= 2) umma_commit(bar(kBarQEmpty));
+    for (int n = 0; n < nb; ++n) {
+      const int g = gb + n, st = g & 1;
+      if (!(ok = wait_or_abort(bar(kBarPFull), g & 1, abort_flag))) break;
+      if (n == 0 && !(ok = wait_or_abort(bar(kBarOFree), (it & 1) ^ 1, abort_flag))) break;
+      if (!(ok = wait_or_abort(bar(kBarVFull0 + st), (g >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      // O += P V(g): A = P (K-major over keys), B = V (N-major: d contiguous).
+      const uint32_t vbase = sbase + kSmemV + st * 32768;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+        umma_bf16(tmem + kTmemO, smem_desc(sbase + kSmemP + aoff, 16, 1024),
+                  smem_desc(vbase + kk * 2048, 16384, 1024), kIdescPV, (n > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(bar(kBarODone));
+      umma_commit(bar(kBarVEmpty0 + st));
+      if (n + 2 < nb) {
+        if (!(ok = issue_qk(g + 2))) break;
+        if (n + 2 == nb - 1) umma_commit(bar(kBarQEmpty));
+      }
+    }
+    gb += nb;
+    ++it;
+  }
+  if (!ok) *abort_flag = 1;
+  // Every MMA issued above completes before TMEM is released.
+  umma_commit(bar(kBarDrain));
+  volatile int never = 0;
+  wait_or_abort(bar(kBarDrain), 0, &never);
+}
+
+__device__ __forceinline__ void softmax_role(const int* items, int first, int last, int total_q, int total_k,
+                                             uint8_t* smem, uint32_t bars, uint32_t tmem, __nv_bfloat16* out,
+                                             float scale_log2, volatile int* abort_flag) {
+  auto bar = [&](int i) { return bars + 8u * i; };
+  const int m = threadIdx.x;                       // S/O row == TMEM lane
+  const int qi = m >> 1;                           // query row inside the tile
+  const uint32_t lane_addr = static_cast<uint32_t>(m & ~31) << 16;
+  uint8_t* prow = smem + kSmemP + m * 128;
+  const int swz = m & 7;
+  int gb = 0;
+  bool ok = true;
+  for (int idx = first; idx < last && ok; ++idx) {
+    const int* ip = items + static_cast<size_t>(idx) * kItemWords;
+    Item x;
+    if (!load_item(ip, total_q, total_k, x)) {
+      if (m == 0) atomicOr(&g_device_status, kStatusBadArgument);
+      continue;
+    }
+    const int nb = x.key_blocks(), nctx = nb - 1;
+    const bool row_ok = qi < x.nq;
+    const int rel = (x.phase + qi) / x.bs;         // block of this row inside the tile
+    int anchor = row_ok ? ip[kIAnchors + min(rel, kMaxTileBlocks - 1)] : 0;
+    anchor = max(0, min(anchor, x.ctx_keys));
+    float m_run = -1e30f, l = 0.f;
+    for (int n = 0; n < nb; ++n) {
+      const int g = gb + n;
+      ok = wait_or_abort(bar(kBarSFull0 + (g & 1)), (g >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      tc_fence_after();
+      float s[128];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        tmem_ld32(tmem + lane_addr + kTmemS + (g & 1) * 128 + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      int lo, hi;
+      if (n < nctx) {
+        lo = 0;
+        hi = min(max(anchor - n * kKeyBlock, 0), kKeyBlock);
+      } else {
+        lo = rel * x.bs;
+        hi = min(lo + x.bs, kKeyBlock);
+      }
+      if (!row_ok) hi = lo;
+      float mb = -INFINITY;
+      if (lo == 0 && hi == kKeyBlock) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) mb = fmaxf(mb, s[i]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+          const bool vis = i >= lo && i < hi;
+          s[i] = vis ? s[i] : -INFINITY;
+          mb = fmaxf(mb, s[i]);
+        }
+      }
+      const float m_new = fmaxf(m_run, mb * scale_log2);
+      const bool resc = m_new > m_run + 8.f;
+      float alpha = 1.f;
+      if (resc) {
+        alpha = ex2(m_run - m_new);
+        m_run = m_new;
+      }
+      float sum = 0.f;
+      uint32_t pk[64];
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const float p0 = ex2(fmaf(s[2 * i], scale_log2, -m_run));
+        const float p1 = ex2(fmaf(s[2 * i + 1], scale_log2, -m_run));
+        sum += p0 + p1;
+        pk[i] = pack_bf16x2(p0, p1);
+      }
+      l = l * alpha + sum;
+      if (n > 0) {
+        // PV(g-1) has finished: O may be rescaled and the P buffer rewritten.
+        ok = wait_or_abort(bar(kBarODone), (g - 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        tc_fence_after();
+        if (__any_sync(0xffffffffu, resc)) {
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            float o[32];
+            tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] *= alpha;
+            tmem_st32(tmem + lane_addr + kTmemO + c * 32, o);
+          }
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const uint4 v = make_uint4(pk[h * 32 + 4 * j], pk[h * 32 + 4 * j + 1], pk[h * 32 + 4 * j + 2],
+                                     pk[h * 32 + 4 * j + 3]);
+          *reinterpret_cast<uint4*>(prow + h * 16384 + ((j ^ swz) << 4)) = v;
+        }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      mbar_arrive(bar(kBarPFull));
+    }
+    if (!ok) break;
+    gb += nb;
+    ok = wait_or_abort(bar(kBarODone), (gb - 1) & 1, abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+    tc_fence_after();
+    const float inv_l = row_ok ? 1.f / l : 0.f;
+    __nv_bfloat16* orow = out + (static_cast<size_t>(x.q_row0 + (row_ok ? qi : 0)) * 16 + 2 * x.head + (m & 1)) * 128;
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      float o[32];
+      tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
+      if (row_ok) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          uint4 v;
+          v.x = pack_bf16x2(o[8 * j] * inv_l, o[8 * j + 1] * inv_l);
+          v.y = pack_bf16x2(o[8 * j + 2] * inv_l, o[8 * j + 3] * inv_l);
+          v.z = pack_bf16x2(o[8 * j + 4] * inv_l, o[8 * j + 5] * inv_l);
+          v.w = pack_bf16x2(o[8 * j + 6] * inv_l, o[8 * j + 7] * inv_l);
+          *reinterpret_cast<uint4*>(orow + c * 32 + 8 * j) = v;
+        }
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(bar(kBarOFree));
+  }
+  if (!ok) *abort_flag = 1;
+}
+
+// ---------------------------------------------------------------- kernel
+__global__ void __launch_bounds__(kThreads, 1)
+    train_attn_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const int* __restrict__ plan,
+                      __nv_bfloat16* __restrict__ out, int total_q, int total_k, float scale_log2) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + kSmemBar;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  // The plan must describe exactly the tensors this launch was given.
+  const int grid = plan[2];
+  const bool plan_ok = plan[0] == kPlanMagic && grid == static_cast<int>(gridDim.x) && plan[3] == total_q &&
+                       plan[4] == total_k;
+  int first = 0, last = 0;
+  if (plan_ok) {
+    first = plan[kPlanHeader + blockIdx.x];
+    last = plan[kPlanHeader + blockIdx.x + 1];
+    if (first < 0 || last < first || last > plan[1]) first = last = 0;
+  } else if (threadIdx.x == 0) {
+    atomicOr(&g_device_status, kStatusBadArgument);
+  }
+  const int* items = plan + plan_items_at(grid > 0 ? grid : 0);
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBarriers; ++i)
+      mbar_init(bars + 8u * i, (i == kBarPFull || i == kBarOFree) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5 && lane == 0) {
+    prefetch_tmap(&qmap);
+    prefetch_tmap(&kmap);
+    prefetch_tmap(&vmap);
+  }
+  if (warp == 4) tmem_alloc(sbase + kSmemTmemSlot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kSmemTmemSlot);
+
+  if (warp < 4) {
+    softmax_role(items, first, last, total_q, total_k, smem, bars, tmem, out, scale_log2, abort_flag);
+  } else if (warp == 4) {
+    if (lane == 0) mma_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
+    __syncwarp();
+  } else {
+    if (lane == 0)
+      producer_role(&qmap, &kmap, &vmap, items, first, last, total_q, total_k, sbase, bars, abort_flag);
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace train
+}  // namespace dspark

@@ -12,6 +12,9 @@ no fallback, retry or split tuning.
 * ``B200DraftKernel``   - non-causal (replaces PinnedRocmDraftKernel)
 * ``B200CapacityKernel`` - bottom-right causal over a capacity-sized K whose tail
   past ``cu_key[-1]`` is never read (replaces PersistentQwenTarget._native_attention)
+* ``B200TrainingLayoutKernel`` - the training-layout draft attention of
+  ``DraftAttention.forward`` + ``block_mask`` (model.py:12-19,47-61) for packed
+  sequences, on the tcgen05 tensor cores
 
 bf16 runs on the tensor-core kernel; float32 inputs (the reference's exact CPU
 configurations) run on the library's float32 CUDA-core kernel.
@@ -25,6 +28,7 @@ from . import _lib
 BACKEND = 'b200_sm100a_varlen_causal_v1'
 DRAFT_BACKEND = 'b200_sm100a_noncausal_v1'
 CAPACITY_BACKEND = 'b200_sm100a_capacity_causal_v1'
+TRAIN_BACKEND = 'b200_sm100a_train_layout_tcgen05_v1'
 HQ, HKV, HEAD_DIM = 16, 8, 128
 SCALE = HEAD_DIM ** -0.5
 _DTYPES = {torch.bfloat16: _lib.DTYPE_BF16, torch.float32: _lib.DTYPE_F32}
@@ -156,6 +160,50 @@ class B200CapacityKernel(B200VarlenKernel):
                 or len(query) != sum(layout.query_lengths) or sum(layout.key_lengths) > cap):
             raise ValueError('B200 capacity attention shape/dtype/scale differs')
         self._check_layout(layout, cap, key)
+
+
+class B200TrainingLayoutKernel:
+    """Training-layout draft attention for packed sequences (model.py:12-19,47-61).
+
+    ``kernel(query, key, value, layout, *, scale)`` with a ``TrainingLayout``:
+    query [sum blocks*block_size, 16, 128], key/value [sum(context + block rows),
+    8, 128], contiguous, one dtype. bf16 runs the tcgen05 kernel
+    (``dspark_train_attn``) over the layout's device plan; float32 (the exact
+    configuration) runs each block as a two-segment request of the float32
+    CUDA-core kernel.
+    """
+    backend_name = TRAIN_BACKEND
+    native_varlen_calls_per_layer = 1
+
+    def __init__(self, device):
+        self.device = torch.device(device)
+        if self.device.type == 'cuda' and self.device.index is None:
+            self.device = torch.device('cuda', torch.cuda.current_device())
+        self.runtime = runtime_identity(self.device)
+        self._operator = _NativeEntry('dspark_train_attn')
+
+    def __call__(self, query, key, value, layout, *, scale):
+        tensors = (query, key, value)
+        if any(not isinstance(t, torch.Tensor) or t.device != self.device or t.dtype not in _DTYPES
+               or t.dtype != query.dtype or t.requires_grad or t.ndim != 3 or not t.is_contiguous()
+               for t in tensors):
+            raise ValueError('B200 training layout requires no-autograd contiguous BF16 (or FP32) THD tensors '
+                             'on its GPU')
+        if query.shape[1:] != (HQ, HEAD_DIM) or key.shape[1:] != (HKV, HEAD_DIM) or value.shape != key.shape:
+            raise ValueError('B200 training layout supports Hq16/Hkv8/D128 Qwen tensors only')
+        if not isinstance(scale, (float, int)) or not math.isfinite(scale) or scale != SCALE:
+            raise ValueError('B200 training layout requires the 1/sqrt(128) scale')
+        if (not hasattr(layout, 'plan') or len(query) != layout.query_tokens or len(key) != layout.key_tokens
+                or layout.plan.device != self.device):
+            raise ValueError('Query/key rows must match the training layout on this device')
+        if query.dtype == torch.float32:
+            return segment_attention(query, layout.seg_cu_query, [layout.block_size] * (len(layout.seg_a_len)),
+                                     key, value, layout.seg_a_start, layout.seg_a_len, key, value,
+                                     layout.seg_b_start, layout.seg_b_len, causal=False, scale=scale)
+        out = torch.empty_like(query)
+        self._operator(query.data_ptr(), key.data_ptr(), value.data_ptr(), query.shape[0], key.shape[0],
+                       layout.plan.data_ptr(), layout.grid, float(scale), out.data_ptr(), _stream(self.device))
+        return out
 
 
 def _cumulative(lengths):

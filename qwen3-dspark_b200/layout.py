@@ -105,6 +105,81 @@ class PersistentAttentionLayout:
     maximum_query_length: int = 0
 
 
+@dataclass(frozen=True)
+class TrainingLayout:
+    """Packed training layout of the draft attention over several sequences.
+
+    Per sequence s (``DraftAttention.forward`` with ``block_mask``,
+    dspark_qwen/model.py:12-19,47-61): ``context_lengths[s]`` context rows and one
+    draft block of ``block_size`` rows per anchor in ``anchors[s]``. Queries are
+    the block rows (block b = rows ``[block_size*b, +block_size)``), keys are
+    ``[context rows ; block rows]`` (what ``project_kv(cat(context, z))`` builds).
+    Block b sees context rows ``j < anchors[s][b]`` and its own rows; sequences
+    never see each other (the packing rule of the vendored NeMo mask). Anchors
+    outside ``[0, context]`` act as the nearest end, exactly as in the mask.
+
+    ``plan`` is the tensor-core kernel's work plan (``dspark_train_plan``), built
+    once on the host and kept on the device; the per-block ``seg_*`` tensors
+    describe the same layout as two-segment requests for the float32 kernel.
+    """
+    context_lengths: tuple
+    anchors: tuple
+    block_size: int
+    query_lengths: tuple
+    key_lengths: tuple
+    plan: torch.Tensor
+    grid: int
+    seg_cu_query: torch.Tensor
+    seg_a_start: torch.Tensor
+    seg_a_len: torch.Tensor
+    seg_b_start: torch.Tensor
+    seg_b_len: torch.Tensor
+
+    @classmethod
+    def from_anchors(cls, context_lengths, anchors, block_size=7, device='cuda', grid_limit=None):
+        from . import _lib
+        ctx = tuple(int(c) for c in context_lengths)
+        anc = tuple(tuple(int(a) for a in seq) for seq in anchors)
+        if not ctx or len(ctx) != len(anc) or any(c < 0 for c in ctx):
+            raise ValueError('One nonnegative context length and one anchor list per sequence required')
+        if type(block_size) is not int or not 6 <= block_size <= 32:
+            raise ValueError('block_size must be an integer in [6, 32]')
+        if not any(anc):
+            raise ValueError('At least one anchor (draft block) is required')
+        device = torch.device(device)
+        if grid_limit is None:
+            grid_limit = torch.cuda.get_device_properties(device).multi_processor_count
+        plan = _lib.train_plan(ctx, [len(a) for a in anc], [a for seq in anc for a in seq], block_size,
+                               int(grid_limit))
+        qlens = tuple(len(a) * block_size for a in anc)
+        klens = tuple(c + q for c, q in zip(ctx, qlens))
+        a_start, a_len, b_start = [], [], []
+        ko = 0
+        for c, seq in zip(ctx, anc):
+            for b, a in enumerate(seq):
+                a_start.append(ko)
+                a_len.append(min(max(a, 0), c))
+                b_start.append(ko + c + block_size * b)
+            ko += c + len(seq) * block_size
+        nblk = len(a_start)
+
+        def dev(x):
+            t = torch.tensor(x, dtype=torch.int32)
+            return t.pin_memory().to(device, non_blocking=True) if device.type == 'cuda' else t
+
+        return cls(ctx, anc, block_size, qlens, klens, dev(plan), int(plan[2]),
+                   dev([block_size * i for i in range(nblk + 1)]), dev(a_start), dev(a_len), dev(b_start),
+                   dev([block_size] * nblk))
+
+    @property
+    def query_tokens(self):
+        return sum(self.query_lengths)
+
+    @property
+    def key_tokens(self):
+        return sum(self.key_lengths)
+
+
 def cumulative(lengths, device):
     ends = [0]
     for n in lengths:
