@@ -38,6 +38,8 @@ DRAFT = dict(requests=64, ctx_lo=128, ctx_hi=4096, seed=1, layers=5)
 VERIFY = dict(requests=128, ctx_lo=256, ctx_hi=8192, seed=2, layers=28, q=7)
 METRIC = 'draft+verify attn query-tok/s per GPU & at 1/2/4/8 B200; % of HBM roofline'
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_TFLOPS = 1590.0
+TRAIN = dict(seqs=8, ctx=2048, anchors=32, seed=3)
 
 
 def peaks():
@@ -47,6 +49,15 @@ def peaks():
         return float(p['hbm_gbs']), 'measured'
     except Exception:
         return FALLBACK_HBM_GBS, 'fallback'
+
+
+def tensor_peak():
+    """Dense bf16 TFLOP/s (burst: a kernel timed alone)."""
+    try:
+        with open(os.path.join(ROOT, 'MEASURED_PEAKS.json')) as f:
+            return float(json.load(f)['bf16_tflops']), 'measured'
+    except Exception:
+        return FALLBACK_TFLOPS, 'fallback'
 
 
 def _finite(obj):
@@ -316,6 +327,65 @@ class Workload:
         return h2d, d2h
 
 
+# --------------------------------------------------------------------------- config 4
+def train_layout_leg(pkg, device, rank, warmup, iters=20):
+    """Config 4: training-layout draft attention (8 sequences x 2048 context, 32 sorted
+    anchors each from 0..2046, block 7), one launch per timed iteration with a 256 MiB
+    write before each launch so every launch starts with K/V (89 MB, smaller than L2)
+    out of L2. The per-block two-segment path is timed the same way beside it."""
+    import numpy as np
+    import torch
+    g = np.random.Generator(np.random.PCG64(TRAIN['seed'] * 1000 + rank))
+    S, C, N = TRAIN['seqs'], TRAIN['ctx'], TRAIN['anchors']
+    anchors = [sorted(g.choice(C - 1, N, replace=False).tolist()) for _ in range(S)]
+    layout = pkg.TrainingLayout.from_anchors([C] * S, anchors, BLOCK, device=device)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(4321 + rank)
+    nq, nk = layout.query_tokens, layout.key_tokens
+    q = torch.randn(nq, HQ, D, device=device, dtype=torch.bfloat16, generator=gen)
+    k = torch.randn(nk, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    v = torch.randn(nk, HKV, D, device=device, dtype=torch.bfloat16, generator=gen)
+    kernel = pkg.B200TrainingLayoutKernel(device)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def tc():
+        return kernel(q, k, v, layout, scale=D ** -0.5)
+
+    def seg():
+        return pkg.segment_attention(q, layout.seg_cu_query, [BLOCK] * len(layout.seg_a_len), k, v,
+                                     layout.seg_a_start, layout.seg_a_len, k, v, layout.seg_b_start,
+                                     layout.seg_b_len, causal=False)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        pairs = []
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+    ms, seg_ms = timed(tc), timed(seg)
+    alg_bytes = nk * KV_ROW + 2 * nq * Q_ROW       # K+V read once, Q read, O written
+    flops = sum(4 * BLOCK * HQ * D * (min(max(a, 0), C) + BLOCK) for seq in anchors for a in seq)
+    hbm, hbm_kind = peaks()
+    tflops, t_kind = tensor_peak()
+    bound_ms = max(alg_bytes / (hbm * 1e9), flops / (tflops * 1e12)) * 1e3
+    return dict(
+        workload='cfg4 training-layout draft attention: 8 seqs x 2048 ctx, 32 sorted anchors/seq, block 7, '
+                 'tcgen05 kernel (B200TrainingLayoutKernel)',
+        query_rows=nq, key_rows=nk, ms_per_launch=ms, query_tok_per_s=nq / (ms / 1e3),
+        alg_bytes=alg_bytes, alg_flops=flops, achieved_gbs=alg_bytes / (ms / 1e3) / 1e9,
+        achieved_tflops=flops / (ms / 1e3) / 1e12, roofline_ms=bound_ms, frac=bound_ms / ms,
+        peaks=dict(hbm_gbs=hbm, bf16_tflops=tflops, source=f'{hbm_kind}/{t_kind}'),
+        l2='256 MiB written before every launch', segment_path_ms=seg_ms)
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_sample(seconds=12.0, rank=0):
     """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
@@ -463,6 +533,8 @@ def run_b200(args):
     e_end.record()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end)
+    # config 4 (training layout): its own roofline, reported beside the headline step
+    train = train_layout_leg(pkg, device, rank, args.warmup) if args.case == 'round' else None
     status = pkg.read_device_status(clear=True)
     # per-layer event durations inside the timed region
     per = {'draft': [], 'verify': []}
@@ -511,6 +583,8 @@ def run_b200(args):
                      path='B200DraftKernel / B200PersistentTargetKV.verify_layer with pinned host q/k/v in, '
                           'attention outputs out; copies on two copy streams overlapping the kernels'),
             gpu_launches=agg['launches'], clocks=clocks.summary(), device_status=agg['status'])
+        if train is not None:
+            line['train_layout'] = train
         print(json.dumps(_finite(line)), flush=True)
     if world > 1:
         dist.barrier()

@@ -13,16 +13,21 @@
 // are the context prefix up to the tile's largest anchor, in 128-row blocks,
 // then one 128-row block starting at the tile's first block row.
 //
-// Roles (192 threads, one CTA per SM):
+// Roles (256 threads, one CTA per SM):
 //   warps 0-3  softmax: thread m owns S/O row m (TMEM lane m); online softmax
 //              with the running max raised only when it grows by more than
 //              2^8 (exact: the final O/l does not depend on the max used),
-//              P written to shared memory as the next MMA's A operand;
-//   warp 4     MMA issuer (one thread) and TMEM owner: S = Q K^T into one of
-//              two S buffers, O += P V into the O accumulator, completion
-//              reported through tcgen05.commit on mbarriers;
-//   warp 5     TMA producer (one thread): Q per tile, K and V per key block
-//              into two-stage rings with separate K and V barriers.
+//              P written to one of two shared-memory buffers as the A operand
+//              of the next PV MMA. Only a raised max (rare after the first
+//              blocks) waits for the previous PV to rescale O in TMEM, so the
+//              softmax of block n+1 overlaps the PV MMA of block n;
+//   warp 4     TMEM owner and QK issuer (one thread): S = Q K^T into one of
+//              two S buffers;
+//   warp 7     PV issuer (one thread): O += P V into the O accumulator;
+//              completion is reported through tcgen05.commit on mbarriers;
+//   warp 5     TMA producer of Q (per tile) and K (2-stage ring), one thread;
+//   warp 6     TMA producer of V (2-stage ring), one thread. Separate K and V
+//              producers let a K stage refill as soon as its QK is done.
 // Every wait is bounded; a timed-out wait raises a CTA abort flag that ends all
 // roles, the MMA thread drains its MMAs, the producer waits for its copies in
 // flight, and TMEM is released before the CTA exits.
@@ -32,7 +37,7 @@
 namespace dspark {
 namespace train {
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 256;
 constexpr int kTileQ = 64;          // query rows per tile (x2 heads = 128 MMA rows)
 constexpr int kKeyBlock = 128;      // keys per S tile
 constexpr int kMaxTileBlocks = 12;  // anchor slots per tile
@@ -63,14 +68,17 @@ __host__ __device__ constexpr int plan_items_at(int grid) { return ((kPlanHeader
 
 // Shared memory (offsets from a 1024-byte aligned base). Every operand tile is
 // two 16 KB halves of 128 rows x 64 bf16 in the 128-byte swizzle.
+// Key block g uses K/V stage, S buffer and P buffer g&1.
 constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = 32768;           // 2 stages x 32 KB
-constexpr uint32_t kSmemV = 98304;           // 2 stages x 32 KB
-constexpr uint32_t kSmemP = 163840;          // 32 KB
-constexpr uint32_t kSmemBar = 196608;
+constexpr uint32_t kSmemK = 32768;                       // 2 stages x 32 KB
+constexpr uint32_t kSmemV = kSmemK + 2 * 32768;          // 2 stages x 32 KB
+constexpr uint32_t kSmemP = kSmemV + 2 * 32768;          // 2 buffers x 32 KB
+constexpr uint32_t kSmemBar = kSmemP + 2 * 32768;
+// Per-block barriers come in pairs indexed by the block's parity, so no waiter
+// can ever be two phases behind its barrier.
 enum Barrier {
-  kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarKFull1, kBarKEmpty0, kBarKEmpty1, kBarVFull0, kBarVFull1,
-  kBarVEmpty0, kBarVEmpty1, kBarSFull0, kBarSFull1, kBarPFull, kBarODone, kBarOFree, kBarDrain, kNumBarriers
+  kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarVFull0 = kBarKFull0 + 2, kBarSFull0 = kBarVFull0 + 2,
+  kBarPFull0 = kBarSFull0 + 2, kBarODone0 = kBarPFull0 + 2, kBarOFree = kBarODone0 + 2, kBarDrain, kNumBarriers
 };
 constexpr uint32_t kSmemTmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
@@ -141,6 +149,37 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// A full 128-column row block (4 x 32 columns) with a single wait.
+__device__ __forceinline__ void tmem_ld128(uint32_t taddr, float (&v)[128]) {
+  uint32_t r[128];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%128];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%129];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%64,%65,%66,%67,%68,%69,%70,%71,%72,%73,%74,%75,%76,%77,%78,%79,%80,%81,%82,%83,%84,%85,%86,%87,%88,%89,%90,%91,%92,%93,%94,%95}, [%130];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%96,%97,%98,%99,%100,%101,%102,%103,%104,%105,%106,%107,%108,%109,%110,%111,%112,%113,%114,%115,%116,%117,%118,%119,%120,%121,%122,%123,%124,%125,%126,%127}, [%131];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63]),
+        "=r"(r[64]), "=r"(r[65]), "=r"(r[66]), "=r"(r[67]), "=r"(r[68]), "=r"(r[69]), "=r"(r[70]), "=r"(r[71]),
+        "=r"(r[72]), "=r"(r[73]), "=r"(r[74]), "=r"(r[75]), "=r"(r[76]), "=r"(r[77]), "=r"(r[78]), "=r"(r[79]),
+        "=r"(r[80]), "=r"(r[81]), "=r"(r[82]), "=r"(r[83]), "=r"(r[84]), "=r"(r[85]), "=r"(r[86]), "=r"(r[87]),
+        "=r"(r[88]), "=r"(r[89]), "=r"(r[90]), "=r"(r[91]), "=r"(r[92]), "=r"(r[93]), "=r"(r[94]), "=r"(r[95]),
+        "=r"(r[96]), "=r"(r[97]), "=r"(r[98]), "=r"(r[99]), "=r"(r[100]), "=r"(r[101]), "=r"(r[102]), "=r"(r[103]),
+        "=r"(r[104]), "=r"(r[105]), "=r"(r[106]), "=r"(r[107]), "=r"(r[108]), "=r"(r[109]), "=r"(r[110]), "=r"(r[111]),
+        "=r"(r[112]), "=r"(r[113]), "=r"(r[114]), "=r"(r[115]), "=r"(r[116]), "=r"(r[117]), "=r"(r[118]), "=r"(r[119]),
+        "=r"(r[120]), "=r"(r[121]), "=r"(r[122]), "=r"(r[123]), "=r"(r[124]), "=r"(r[125]), "=r"(r[126]), "=r"(r[127])
+      : "r"(taddr), "r"(taddr + 32), "r"(taddr + 64), "r"(taddr + 96)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 128; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
@@ -202,43 +241,40 @@ __device__ __forceinline__ bool load_item(const int* it, int total_q, int total_
 }
 
 // ---------------------------------------------------------------- roles
-__device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUtensorMap* kmap,
-                                              const CUtensorMap* vmap, const int* items, int first, int last,
-                                              int total_q, int total_k, uint32_t sbase, uint32_t bars,
-                                              volatile int* abort_flag) {
+// kKeys: Q per tile + K per key block; otherwise V per key block.
+template <bool kKeys>
+__device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUtensorMap* kvmap, const int* items,
+                                              int first, int last, int total_q, int total_k, uint32_t sbase,
+                                              uint32_t bars, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
-  int gb = 0, it = 0;
-  int armed_q = 0, armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
+  // A K stage is free when the QK MMA that read it is done (kBarSFull), a V
+  // stage when its PV MMA is done (kBarODone): both pairs share the stage index.
+  constexpr int kStages = 2;
+  constexpr int kFull = kKeys ? kBarKFull0 : kBarVFull0;
+  constexpr int kEmpty = kKeys ? kBarSFull0 : kBarODone0;
+  constexpr uint32_t kRing = kKeys ? kSmemK : kSmemV;
+  int gb = 0, it = 0, armed_q = 0;
+  int armed[kStages] = {};
   bool ok = true;
   for (int idx = first; idx < last && ok; ++idx) {
     Item x;
     if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
     const int nb = x.key_blocks(), nctx = nb - 1;
-    if (!(ok = wait_or_abort(bar(kBarQEmpty), (it & 1) ^ 1, abort_flag))) break;
-    mbar_arrive_expect_tx(bar(kBarQFull), 32768);
-    tma_load_3d(sbase + kSmemQ, qmap, 0, 2 * x.head, x.q_row0, bar(kBarQFull));
-    tma_load_3d(sbase + kSmemQ + 16384, qmap, 64, 2 * x.head, x.q_row0, bar(kBarQFull));
-    ++armed_q;
-    // Consumption order is QK(0), QK(1), PV(0), QK(2), PV(1), ...: K runs one
-    // block ahead of V so a K stage is refilled as soon as its QK is done.
-    auto key_row = [&](int n) { return n < nctx ? x.k_base + n * kKeyBlock : x.blk_key0; };
-    for (int n = 0; n <= nb; ++n) {
-      if (n < nb) {
-        const int g = gb + n, st = g & 1;
-        if (!(ok = wait_or_abort(bar(kBarKEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
-        mbar_arrive_expect_tx(bar(kBarKFull0 + st), 32768);
-        tma_load_3d(sbase + kSmemK + st * 32768, kmap, 0, x.head, key_row(n), bar(kBarKFull0 + st));
-        tma_load_3d(sbase + kSmemK + st * 32768 + 16384, kmap, 64, x.head, key_row(n), bar(kBarKFull0 + st));
-        ++armed_k[st];
-      }
-      if (n >= 1) {
-        const int g = gb + n - 1, st = g & 1;
-        if (!(ok = wait_or_abort(bar(kBarVEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
-        mbar_arrive_expect_tx(bar(kBarVFull0 + st), 32768);
-        tma_load_3d(sbase + kSmemV + st * 32768, vmap, 0, x.head, key_row(n - 1), bar(kBarVFull0 + st));
-        tma_load_3d(sbase + kSmemV + st * 32768 + 16384, vmap, 64, x.head, key_row(n - 1), bar(kBarVFull0 + st));
-        ++armed_v[st];
-      }
+    if (kKeys) {
+      if (!(ok = wait_or_abort(bar(kBarQEmpty), (it & 1) ^ 1, abort_flag))) break;
+      mbar_arrive_expect_tx(bar(kBarQFull), 32768);
+      tma_load_3d(sbase + kSmemQ, qmap, 0, 2 * x.head, x.q_row0, bar(kBarQFull));
+      tma_load_3d(sbase + kSmemQ + 16384, qmap, 64, 2 * x.head, x.q_row0, bar(kBarQFull));
+      ++armed_q;
+    }
+    for (int n = 0; n < nb; ++n) {
+      const int g = gb + n, st = g % kStages;
+      const int row = n < nctx ? x.k_base + n * kKeyBlock : x.blk_key0;
+      if (!(ok = wait_or_abort(bar(kEmpty + st), ((g / kStages) & 1) ^ 1, abort_flag))) break;
+      mbar_arrive_expect_tx(bar(kFull + st), 32768);
+      tma_load_3d(sbase + kRing + st * 32768, kvmap, 0, x.head, row, bar(kFull + st));
+      tma_load_3d(sbase + kRing + st * 32768 + 16384, kvmap, 64, x.head, row, bar(kFull + st));
+      ++armed[st];
     }
     gb += nb;
     ++it;
@@ -247,70 +283,86 @@ __device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUt
   // Copies in flight land before the CTA can exit (a no-op when all were consumed).
   volatile int never = 0;
   if (armed_q) wait_or_abort(bar(kBarQFull), (armed_q - 1) & 1, &never);
-  for (int st = 0; st < 2; ++st) {
-    if (armed_k[st]) wait_or_abort(bar(kBarKFull0 + st), (armed_k[st] - 1) & 1, &never);
-    if (armed_v[st]) wait_or_abort(bar(kBarVFull0 + st), (armed_v[st] - 1) & 1, &never);
-  }
+  for (int st = 0; st < kStages; ++st)
+    if (armed[st]) wait_or_abort(bar(kFull + st), (armed[st] - 1) & 1, &never);
 }
 
-__device__ __forceinline__ void mma_role(const int* items, int first, int last, int total_q, int total_k,
-                                         uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
+// Two MMA issuers, one thread each: an MMA instruction is accepted only about
+// one ahead of the tensor pipe, so every mbarrier wait or commit on the issuing
+// thread leaves the pipe idle; with S = Q K^T and O += P V issued from
+// different warps, one issuer's waits overlap the other's MMAs. Their operands
+// are disjoint (S buffers vs O in TMEM; Q, K vs P, V in shared memory).
+//
+// QK issuer: S(g) = Q K(g)^T into S buffer g&1, 8 MMAs of K=16 over the head
+// dim; its commit on kBarSFull is also the "K stage free" signal.
+__device__ __forceinline__ void qk_role(const int* items, int first, int last, int total_q, int total_k,
+                                        uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
-  constexpr uint32_t kIdescQK = instr_desc(0);
-  constexpr uint32_t kIdescPV = instr_desc(1);
+  constexpr uint32_t kIdesc = instr_desc(0);
   int gb = 0, it = 0;
   bool ok = true;
-  // S(g) = Q K(g)^T: 8 MMAs of K=16 over the head dim (two 64-column halves).
-  auto issue_qk = [&](int g) -> bool {
-    const int st = g & 1;
-    if (!wait_or_abort(bar(kBarKFull0 + st), (g >> 1) & 1, abort_flag)) return false;
-    tc_fence_after();
-    const uint32_t kbase = sbase + kSmemK + st * 32768;
-#pragma unroll
-    for (int kk = 0; kk < 8; ++kk) {
-      const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-      umma_bf16(tmem + kTmemS + st * 128, smem_desc(sbase + kSmemQ + off, 16, 1024), smem_desc(kbase + off, 16, 1024),
-                kIdescQK, kk > 0);
-    }
-    umma_commit(bar(kBarSFull0 + st));
-    umma_commit(bar(kBarKEmpty0 + st));
-    return true;
-  };
   for (int idx = first; idx < last && ok; ++idx) {
     Item x;
     if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
     const int nb = x.key_blocks();
     if (!(ok = wait_or_abort(bar(kBarQFull), it & 1, abort_flag))) break;
-    tc_fence_after();
-    if (!(ok = issue_qk(gb))) break;
-    if (nb > 1 && !(ok = issue_qk(gb + 1))) break;
-    if (nb <= 2) umma_commit(bar(kBarQEmpty));
     for (int n = 0; n < nb; ++n) {
-      const int g = gb + n, st = g & 1;
-      if (!(ok = wait_or_abort(bar(kBarPFull), g & 1, abort_flag))) break;
-      if (n == 0 && !(ok = wait_or_abort(bar(kBarOFree), (it & 1) ^ 1, abort_flag))) break;
-      if (!(ok = wait_or_abort(bar(kBarVFull0 + st), (g >> 1) & 1, abort_flag))) break;
+      const int g = gb + n, sb = g & 1;
+      if (!(ok = wait_or_abort(bar(kBarKFull0 + sb), (g >> 1) & 1, abort_flag))) break;
+      // S buffer g&1 is free once the softmax has consumed S(g-2) (its P(g-2) is out).
+      if (g >= 2 && !(ok = wait_or_abort(bar(kBarPFull0 + sb), ((g - 2) >> 1) & 1, abort_flag))) break;
       tc_fence_after();
-      // O += P V(g): A = P (K-major over keys), B = V (N-major: d contiguous).
-      const uint32_t vbase = sbase + kSmemV + st * 32768;
+      const uint32_t kbase = sbase + kSmemK + sb * 32768;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-        umma_bf16(tmem + kTmemO, smem_desc(sbase + kSmemP + aoff, 16, 1024),
-                  smem_desc(vbase + kk * 2048, 16384, 1024), kIdescPV, (n > 0 || kk > 0) ? 1u : 0u);
+        const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+        umma_bf16(tmem + kTmemS + sb * 128, smem_desc(sbase + kSmemQ + off, 16, 1024),
+                  smem_desc(kbase + off, 16, 1024), kIdesc, kk > 0);
       }
-      umma_commit(bar(kBarODone));
-      umma_commit(bar(kBarVEmpty0 + st));
-      if (n + 2 < nb) {
-        if (!(ok = issue_qk(g + 2))) break;
-        if (n + 2 == nb - 1) umma_commit(bar(kBarQEmpty));
-      }
+      umma_commit(bar(kBarSFull0 + sb));
+      if (n == nb - 1) umma_commit(bar(kBarQEmpty));
     }
     gb += nb;
     ++it;
   }
   if (!ok) *abort_flag = 1;
   // Every MMA issued above completes before TMEM is released.
+  umma_commit(bar(kBarDrain));
+  volatile int never = 0;
+  wait_or_abort(bar(kBarDrain), 0, &never);
+}
+
+// PV issuer: O += P(g) V(g), A = P (K-major over keys), B = V (N-major: d
+// contiguous); its commit on kBarODone is also the "V stage free" signal.
+__device__ __forceinline__ void pv_role(const int* items, int first, int last, int total_q, int total_k,
+                                        uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
+  auto bar = [&](int i) { return bars + 8u * i; };
+  constexpr uint32_t kIdesc = instr_desc(1);
+  int gb = 0, it = 0;
+  bool ok = true;
+  for (int idx = first; idx < last && ok; ++idx) {
+    Item x;
+    if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
+    const int nb = x.key_blocks();
+    for (int n = 0; n < nb; ++n) {
+      const int g = gb + n, sb = g & 1;
+      if (!(ok = wait_or_abort(bar(kBarPFull0 + sb), (g >> 1) & 1, abort_flag))) break;
+      if (n == 0 && !(ok = wait_or_abort(bar(kBarOFree), (it & 1) ^ 1, abort_flag))) break;
+      if (!(ok = wait_or_abort(bar(kBarVFull0 + sb), (g >> 1) & 1, abort_flag))) break;
+      tc_fence_after();
+      const uint32_t vbase = sbase + kSmemV + sb * 32768;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
+        umma_bf16(tmem + kTmemO, smem_desc(sbase + kSmemP + sb * 32768 + aoff, 16, 1024),
+                  smem_desc(vbase + kk * 2048, 16384, 1024), kIdesc, (n > 0 || kk > 0) ? 1u : 0u);
+      }
+      umma_commit(bar(kBarODone0 + sb));
+    }
+    gb += nb;
+    ++it;
+  }
+  if (!ok) *abort_flag = 1;
   umma_commit(bar(kBarDrain));
   volatile int never = 0;
   wait_or_abort(bar(kBarDrain), 0, &never);
@@ -323,7 +375,7 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
   const int m = threadIdx.x;                       // S/O row == TMEM lane
   const int qi = m >> 1;                           // query row inside the tile
   const uint32_t lane_addr = static_cast<uint32_t>(m & ~31) << 16;
-  uint8_t* prow = smem + kSmemP + m * 128;
+  uint8_t* prow0 = smem + kSmemP + m * 128;
   const int swz = m & 7;
   int gb = 0;
   bool ok = true;
@@ -346,9 +398,7 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       float s[128];
-#pragma unroll
-      for (int c = 0; c < 4; ++c)
-        tmem_ld32(tmem + lane_addr + kTmemS + (g & 1) * 128 + c * 32, *reinterpret_cast<float(*)[32]>(&s[c * 32]));
+      tmem_ld128(tmem + lane_addr + kTmemS + (g & 1) * 128, s);
       int lo, hi;
       if (n < nctx) {
         lo = 0;
@@ -387,22 +437,26 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         pk[i] = pack_bf16x2(p0, p1);
       }
       l = l * alpha + sum;
-      if (n > 0) {
-        // PV(g-1) has finished: O may be rescaled and the P buffer rewritten.
-        ok = wait_or_abort(bar(kBarODone), (g - 1) & 1, abort_flag);
+      if (g >= 2) {
+        // PV(g-2) has finished reading this P buffer (within this item or the last).
+        ok = wait_or_abort(bar(kBarODone0 + (g & 1)), ((g - 2) >> 1) & 1, abort_flag);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      }
+      if (n > 0 && __any_sync(0xffffffffu, resc)) {
+        // A raised max rescales O once PV(g-1) has added into it.
+        ok = wait_or_abort(bar(kBarODone0 + ((g - 1) & 1)), ((g - 1) >> 1) & 1, abort_flag);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
-        if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            float o[32];
-            tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
+        for (int c = 0; c < 4; ++c) {
+          float o[32];
+          tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] *= alpha;
-            tmem_st32(tmem + lane_addr + kTmemO + c * 32, o);
-          }
+          for (int i = 0; i < 32; ++i) o[i] *= alpha;
+          tmem_st32(tmem + lane_addr + kTmemO + c * 32, o);
         }
       }
+      uint8_t* prow = prow0 + (g & 1) * 32768;
 #pragma unroll
       for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -413,11 +467,11 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         }
       fence_proxy_async_smem();
       tc_fence_before();
-      mbar_arrive(bar(kBarPFull));
+      mbar_arrive(bar(kBarPFull0 + (g & 1)));
     }
     if (!ok) break;
     gb += nb;
-    ok = wait_or_abort(bar(kBarODone), (gb - 1) & 1, abort_flag);
+    ok = wait_or_abort(bar(kBarODone0 + ((gb - 1) & 1)), ((gb - 1) >> 1) & 1, abort_flag);
     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
     tc_fence_after();
     const float inv_l = row_ok ? 1.f / l : 0.f;
@@ -472,15 +526,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBarriers; ++i)
-      mbar_init(bars + 8u * i, (i == kBarPFull || i == kBarOFree) ? 128u : 1u);
+      mbar_init(bars + 8u * i,
+                (i == kBarPFull0 || i == kBarPFull0 + 1 || i == kBarOFree) ? 128u : (i == kBarDrain ? 2u : 1u));
     *abort_flag = 0;
     fence_barrier_init();
   }
   if (warp == 5 && lane == 0) {
     prefetch_tmap(&qmap);
     prefetch_tmap(&kmap);
-    prefetch_tmap(&vmap);
   }
+  if (warp == 6 && lane == 0) prefetch_tmap(&vmap);
   if (warp == 4) tmem_alloc(sbase + kSmemTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -490,11 +545,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp < 4) {
     softmax_role(items, first, last, total_q, total_k, smem, bars, tmem, out, scale_log2, abort_flag);
   } else if (warp == 4) {
-    if (lane == 0) mma_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
+    if (lane == 0) qk_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
+    __syncwarp();
+  } else if (warp == 7) {
+    if (lane == 0) pv_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
+    __syncwarp();
+  } else if (warp == 5) {
+    if (lane == 0)
+      producer_role<true>(&qmap, &kmap, items, first, last, total_q, total_k, sbase, bars, abort_flag);
     __syncwarp();
   } else {
     if (lane == 0)
-      producer_role(&qmap, &kmap, &vmap, items, first, last, total_q, total_k, sbase, bars, abort_flag);
+      producer_role<false>(&qmap, &vmap, items, first, last, total_q, total_k, sbase, bars, abort_flag);
     __syncwarp();
   }
   tc_fence_before();
