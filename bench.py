@@ -15,6 +15,7 @@ over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank
 
 ``--case``/``--layers`` select a smaller workload (one path, fewer layers) for
 profiler captures; the default is the full round the metric is quoted on.
+``--case train`` measures config 4 (training-layout draft attention) alone.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -494,6 +495,20 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
+    if args.case == 'train':
+        # config 4 alone (profiling and standalone measurement); rank 0 reports
+        train = train_layout_leg(pkg, device, rank, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='cfg4 training-layout draft attention query-tok/s',
+                                          value=train['query_tok_per_s'], unit='query-tok/s', n_gpus=world,
+                                          steps=args.steps, warmup=args.warmup, ms_per_step=train['ms_per_launch'],
+                                          higher_is_better=True, dtype='bf16', data='synthetic',
+                                          train_layout=train, device_status=status))), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     dl = DRAFT['layers'] if args.case in ('round', 'draft') else 0
     vl = VERIFY['layers'] if args.case in ('round', 'verify') else 0
     if args.layers is not None:
@@ -597,7 +612,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()
