@@ -501,6 +501,8 @@ __device__ __forceinline__ void rope_new_rows_in_smem(const AttnParams& p, const
 
 // Epoch-tagged arrival counter of one cut item and head: returns this
 // arrival's ordinal (1-based), 0 if the bounded CAS loop never succeeded.
+// The last arrival clears it; the epoch tag also discounts a count left by an
+// aborted launch.
 __device__ __forceinline__ unsigned int count_arrival(unsigned long long* ctr, unsigned int epoch) {
   const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
   unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(ctr);
@@ -611,8 +613,12 @@ __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Ite
     int n = last - first + 1;
     if (total < p.grid)            // tiny launch: some ranges are empty and contribute nothing
       for (int c = first; c <= last; ++c) n -= range_empty(c, total, p.grid) ? 1 : 0;
-    merge = count_arrival(p.counters + static_cast<size_t>(first) * kKVHeads + h, p.epoch) ==
-            static_cast<unsigned int>(n);
+    unsigned long long* ctr = p.counters + static_cast<size_t>(first) * kKVHeads + h;
+    merge = count_arrival(ctr, p.epoch) == static_cast<unsigned int>(n);
+    // Every contributor has arrived: no one else touches this counter in this
+    // launch, and clearing it lets a replay of the same launch (a CUDA graph
+    // carries one epoch) start from zero.
+    if (merge) atomicExch(ctr, 0ull);
   }
   merge = __shfl_sync(0xffffffffu, merge, 0);
   if (merge) merge_split_item(p, it.q0, it.nrows, item_start, first, last, total, h, lane);

@@ -44,10 +44,19 @@ class Transaction:
     query_lengths: tuple
     meta: torch.Tensor          # int32 [4R+1]: cu_q | slot_row | ctx_len | slot_cap
     rope: dict = None           # inv_freq tensor -> [sum Q, 64] cos/sin table, built once per transaction
+    table: torch.Tensor = None  # fixed cos/sin buffer of a bound bucket (graph capture/replay)
+    capture: bool = False       # the placeholder transaction a CUDA graph is captured under
 
     @property
     def query_tokens(self):
         return sum(self.query_lengths)
+
+
+@dataclass
+class _BucketBuffers:
+    """Fixed-address per-bucket transaction state: what a captured verify program reads."""
+    meta: torch.Tensor          # int32 [4R+1]
+    table: torch.Tensor         # int32 [sum Q, 64] cos/sin of the new rows' positions
 
 
 def _upload(values, device):
@@ -100,6 +109,7 @@ class B200PersistentTargetKV:
         self._sequence = 0
         self._pending = None
         self._staged = set()
+        self._buckets = {}
         self.failed = False
 
     # -- views -----------------------------------------------------------------
@@ -184,6 +194,52 @@ class B200PersistentTargetKV:
             self.failed = True
             raise
 
+    # -- fixed-buffer buckets (graph capture; persistent_qwen_graph.py:198-275) ---
+    def bind_bucket(self, bucket):
+        """Give ``bucket`` (exact ordered ``query_lengths``) fixed-address metadata and
+        cos/sin buffers. ``begin(handles, bucket)`` then writes each transaction's
+        metadata into those buffers, so a verify program captured once under
+        ``capture_transaction(bucket)`` can be replayed for every transaction of the
+        bucket. Metadata is still built on the host (as the reference's graph does)."""
+        self._healthy()
+        qlens = tuple(bucket.query_lengths)
+        if (not qlens or any(type(q) is not int or q < 1 for q in qlens) or sum(qlens) > self.max_query_tokens
+                or len(qlens) > self.slot_capacity):
+            raise ValueError('Bucket query lengths must be positive and fit the store')
+        if bucket not in self._buckets:
+            r, n = len(qlens), sum(qlens)
+            self._buckets[bucket] = _BucketBuffers(
+                torch.zeros(4 * r + 1, dtype=torch.int32, device=self.device),
+                torch.zeros((n, HEAD_DIM // 2), dtype=torch.int32, device=self.device))
+        return self._buckets[bucket]
+
+    @torch.no_grad()
+    def capture_transaction(self, bucket):
+        """Placeholder transaction to capture a verify program under. Its metadata
+        is a valid empty-context layout (every request reads only its new rows), so
+        warm-up launches are well defined; a capture records launches without running
+        them. End it with ``abort``."""
+        self._idle()
+        buffers = self.bind_bucket(bucket)
+        qlens = tuple(bucket.query_lengths)
+        cu = [0]
+        for q in qlens:
+            cu.append(cu[-1] + q)
+        host = cu + [0] * len(qlens) + [0] * len(qlens) + [min(self.capacities)] * len(qlens)
+        buffers.meta.copy_(torch.tensor(host, dtype=torch.int32))
+        self._sequence += 1
+        tx = Transaction(self._sequence, (), (0,) * len(qlens), qlens, buffers.meta, {}, buffers.table, True)
+        self._pending, self._staged = tx, set()
+        return tx
+
+    def replayed(self, tx):
+        """Record that a captured program wrote every layer's scratch rows for ``tx``
+        (a transaction of a bound bucket); ``commit`` then accepts it."""
+        self._transaction(tx)
+        if tx.table is None or tx.capture:
+            raise ValueError('Only a bound-bucket transaction can be replayed')
+        self._staged = set(range(self.layers))
+
     # -- transactions -----------------------------------------------------------
     @torch.no_grad()
     def begin(self, handles, bucket=None, *, query_lengths=None):
@@ -214,9 +270,14 @@ class B200PersistentTargetKV:
         for q in query_lengths:
             cu.append(cu[-1] + q)
         host = cu + [self.slot_rows[i] for i in indices] + list(contexts) + [self.capacities[i] for i in indices]
-        meta = _upload(host, self.device)
+        buffers = self._buckets.get(bucket) if bucket is not None else None
+        if buffers is not None and query_lengths == tuple(bucket.query_lengths):
+            meta, table = buffers.meta, buffers.table
+            meta.copy_(torch.tensor(host, dtype=torch.int32).pin_memory(), non_blocking=True)
+        else:
+            meta, table = _upload(host, self.device), None
         self._sequence += 1
-        tx = Transaction(self._sequence, handles, contexts, query_lengths, meta, {})
+        tx = Transaction(self._sequence, handles, contexts, query_lengths, meta, {}, table)
         self._pending, self._staged = tx, set()
         return tx
 
@@ -230,7 +291,7 @@ class B200PersistentTargetKV:
 
     @staticmethod
     def _meta(tx):
-        r = len(tx.slots)
+        r = len(tx.query_lengths)
         m = tx.meta
         return m[:r + 1], m[r + 1:2 * r + 1], m[2 * r + 1:3 * r + 1], m[3 * r + 1:4 * r + 1]
 
@@ -268,16 +329,19 @@ class B200PersistentTargetKV:
         table = tx.rope.get(key)
         if table is None:
             # cos/sin of every new row's position, once for all layers of this transaction
-            table = torch.empty((n, HEAD_DIM // 2), dtype=torch.int32, device=self.device)
-            _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), cu_q.data_ptr(), ctx.data_ptr(), len(tx.slots), n,
-                                             table.data_ptr(), stream), 'dspark_rope_table')
+            table = tx.table if tx.table is not None else torch.empty((n, HEAD_DIM // 2), dtype=torch.int32,
+                                                                       device=self.device)
+            _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), cu_q.data_ptr(), ctx.data_ptr(),
+                                             len(tx.query_lengths), n, table.data_ptr(), stream),
+                       'dspark_rope_table')
             tx.rope.clear()
             tx.rope[key] = table
         ws = _lib.workspace(self.device, stream)
         _lib.check(lib.dspark_verify_fused(
             q_raw.data_ptr(), k_raw.data_ptr(), v_raw.data_ptr(), q_norm_weight.data_ptr(),
             k_norm_weight.data_ptr(), table.data_ptr(), float(eps), cu_q.data_ptr(), slot_row.data_ptr(),
-            ctx.data_ptr(), len(tx.slots), n, max(tx.query_lengths), self._keys.data_ptr(), self._values.data_ptr(),
+            ctx.data_ptr(), len(tx.query_lengths), n, max(tx.query_lengths), self._keys.data_ptr(),
+            self._values.data_ptr(),
             self.rows_per_layer, self.scratch_keys.data_ptr(), self.scratch_values.data_ptr(),
             self.max_query_tokens, self.layers, layer, float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(),
             stream), 'dspark_verify_fused')
@@ -347,6 +411,8 @@ class B200PersistentTargetKV:
     def commit(self, tx, committed_query_lengths: Mapping):
         """Commit caller-decided verified prefixes, anchor included (persistent_target_kv.py:463-491)."""
         self._transaction(tx)
+        if tx.capture:
+            raise ValueError('A capture placeholder transaction cannot commit')
         if set(committed_query_lengths) != set(tx.slots) or len(self._staged) != self.layers:
             raise ValueError('Complete layer scratch and one prefix count per active handle required')
         counts = []

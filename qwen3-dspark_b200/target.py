@@ -67,6 +67,7 @@ class B200Qwen3Target:
         self._pending = None
         self._captured = {}
         self._hooks = [model.model.layers[i].register_forward_hook(self._hook(i)) for i in self.layer_ids]
+        self._graphs = {}
         self._orig_forward = {}
         for layer in model.model.layers:
             att = layer.self_attn
@@ -166,6 +167,85 @@ class B200Qwen3Target:
             raise
         finally:
             self._tx, self._captured = None, {}
+
+    # -- captured verify program (persistent_qwen_graph.py:198-275) --------------------
+    def _forward(self, ids, pos):
+        out = self.model.model(input_ids=ids, position_ids=pos, attention_mask={'full_attention': None},
+                               use_cache=False, return_dict=True)
+        context = torch.cat([self._captured[i] for i in self.layer_ids], dim=-1) if self.layer_ids else None
+        return out.last_hidden_state, context
+
+    @torch.no_grad()
+    def capture(self, bucket):
+        """Capture one full-model verify forward for ``bucket`` (exact ordered
+        ``query_lengths``, e.g. the reference's ``Bucket``) into a CUDA graph. The
+        program reads fixed-address token ids, positions and store metadata and writes
+        fixed output buffers; ``verify_graph`` fills the inputs and replays it. As in
+        the reference, metadata construction, sampling and commit stay outside."""
+        if self._pending is not None:
+            raise RuntimeError('Finish the outstanding verification first')
+        if bucket in self._graphs:
+            raise ValueError('Bucket already captured')
+        n = sum(bucket.query_lengths)
+        ids = torch.zeros((1, n), dtype=torch.long, device=self.device)
+        pos = torch.zeros((1, n), dtype=torch.long, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):        # warm-up: library handles and allocator state
+            tx = self.pool.capture_transaction(bucket)
+            self._tx, self._captured = tx, {}
+            try:
+                self._forward(ids, pos)
+            finally:
+                self._tx, self._captured = None, {}
+                self.pool.abort(tx)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        tx = self.pool.capture_transaction(bucket)
+        self._tx, self._captured = tx, {}
+        try:
+            # captured on the warm-up stream, so the library workspace it binds is the
+            # one allocated eagerly during warm-up
+            with torch.cuda.graph(graph, stream=side):
+                last, context = self._forward(ids, pos)
+        finally:
+            self._tx, self._captured = None, {}
+            self.pool.abort(tx)
+        self._graphs[bucket] = dict(graph=graph, ids=ids, pos=pos, last=last, context=context)
+        return graph
+
+    @torch.no_grad()
+    def verify_graph(self, chunks, bucket):
+        """``verify`` through the program captured for ``bucket``: the chunks' lengths
+        must be the bucket's query lengths, in order. The returned features are views
+        of the program's fixed output buffers, valid until the next replay."""
+        if self._pending is not None:
+            raise RuntimeError('Finish the outstanding verification first')
+        ex = self._graphs.get(bucket)
+        if ex is None:
+            raise ValueError('Capture the bucket first')
+        for request, ids in chunks.items():
+            if request not in self._handles:
+                raise ValueError('Request not resident')
+            if (not isinstance(ids, torch.Tensor) or ids.ndim != 2 or ids.shape[0] != 1
+                    or ids.dtype != torch.long or ids.device != self.device):
+                raise ValueError('Each token chunk must be [1,Q] long on the target device')
+        qlens = tuple(ids.shape[1] for ids in chunks.values())
+        if qlens != tuple(bucket.query_lengths):
+            raise ValueError('Chunk lengths differ from the captured bucket')
+        tx = self.pool.begin(tuple(self._handles[r] for r in chunks), bucket)
+        spans, offset, positions = {}, 0, []
+        for request, c, q in zip(chunks, tx.context_lengths, qlens):
+            spans[request] = (offset, q, c)
+            positions.extend(range(c, c + q))
+            offset += q
+        ex['ids'].copy_(torch.cat(tuple(chunks.values()), dim=1))
+        ex['pos'].copy_(torch.tensor([positions], dtype=torch.long).pin_memory(), non_blocking=True)
+        ex['graph'].replay()
+        self.pool.replayed(tx)
+        features = TargetFeatures(ex['last'], ex['context'], spans, self.pool.work(tx))
+        self._pending = (features, tx)
+        return features
 
     @torch.no_grad()
     def commit(self, features, committed_query_lengths):
