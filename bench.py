@@ -15,7 +15,9 @@ over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank
 
 ``--case``/``--layers`` select a smaller workload (one path, fewer layers) for
 profiler captures; the default is the full round the metric is quoted on.
-``--case train`` measures config 4 (training-layout draft attention) alone.
+``--case train`` measures config 4 (training-layout draft attention) alone;
+``--case graph`` compares an eager and a CUDA-graph-replayed verify step at a small
+serving batch.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -387,6 +389,103 @@ def train_layout_leg(pkg, device, rank, warmup, iters=20):
         l2='256 MiB written before every launch', segment_path_ms=seg_ms)
 
 
+# --------------------------------------------------------------------------- graph replay
+GRAPH = dict(requests=8, ctx_lo=256, ctx_hi=2048, seed=5, layers=28, q=7)
+
+
+def graph_leg(pkg, device, rank, warmup, steps):
+    """Small serving batch (8 requests, context U[256,2048], 7 new rows, 28 layers):
+    one verify step = begin + cos/sin table + 28 fused verify layers + commit, run
+    eagerly (one host call per layer) and as a replay of the same 28 layers captured
+    once into a CUDA graph over the store's bucket-bound metadata buffers. Device
+    time per step, both ways, over the same rounds."""
+    import numpy as np
+    import torch
+    cfg = GRAPH
+    g = np.random.Generator(np.random.PCG64(cfg['seed'] * 1000 + rank))
+    ctx = [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
+    R, Q, L = cfg['requests'], cfg['q'], cfg['layers']
+    growth = Q * 2 * (warmup + steps + 2)
+    store = pkg.B200PersistentTargetKV(layers=L, slots=R, context_capacity=max(ctx) + growth,
+                                       max_query_tokens=R * Q, device=device)
+    handles = [store.add_request(f'g{i}') for i in range(R)]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(99 + rank)
+    store._keys.normal_(generator=gen)
+    store._values.normal_(generator=gen)
+    for h, c in zip(handles, ctx):
+        store._lengths[h.index] = c
+    bf = torch.bfloat16
+    vq = [torch.randn(R * Q, HQ, D, device=device, dtype=bf, generator=gen) for _ in range(L)]
+    vk = [torch.randn(R * Q, HKV, D, device=device, dtype=bf, generator=gen) for _ in range(L)]
+    vv = [torch.randn(R * Q, HKV, D, device=device, dtype=bf, generator=gen) for _ in range(L)]
+    w = torch.ones(D, dtype=bf, device=device)
+    inv = pkg.rope_inv_freq(1e6, device=device)
+    outs = [torch.empty(R * Q, HQ, D, dtype=bf, device=device) for _ in range(L)]
+    accept = np.random.Generator(np.random.PCG64(17 + rank))
+
+    class Bucket:
+        query_lengths = (Q,) * R
+
+    bucket = Bucket()
+    store.bind_bucket(bucket)
+
+    def layers(tx):
+        for layer in range(L):
+            store.verify_layer(tx, layer, vq[layer], vk[layer], vv[layer], w, w, inv_freq=inv, out=outs[layer])
+
+    def commit(tx):
+        store.commit(tx, {h: int(a) + 1 for h, a in zip(handles, accept.integers(0, Q, R))})
+
+    def eager_step():
+        tx = store.begin(handles, query_lengths=[Q] * R)
+        layers(tx)
+        commit(tx)
+
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        tx = store.capture_transaction(bucket)
+        layers(tx)
+        store.abort(tx)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    tx = store.capture_transaction(bucket)
+    with torch.cuda.graph(graph, stream=side):
+        layers(tx)
+    store.abort(tx)
+
+    def graph_step():
+        tx = store.begin(handles, bucket)
+        graph.replay()
+        store.replayed(tx)
+        commit(tx)
+
+    def timed(step):
+        for _ in range(warmup):
+            step()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0 = time.perf_counter()
+        a.record()
+        for _ in range(steps):
+            step()
+        b.record()
+        host_ms = (time.perf_counter() - t0) * 1e3 / steps
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / steps, host_ms
+
+    eager_ms, eager_host = timed(eager_step)
+    graph_ms, graph_host = timed(graph_step)
+    units = R * Q * L
+    return dict(workload=f'{R} requests, ctx U[{cfg["ctx_lo"]},{cfg["ctx_hi"]}], q {Q}, {L} fused verify layers '
+                         '+ cos/sin table + commit per step',
+                eager_ms_per_step=eager_ms, graph_ms_per_step=graph_ms, eager_host_ms_per_step=eager_host,
+                graph_host_ms_per_step=graph_host, eager_query_tok_per_s=units / (eager_ms / 1e3),
+                graph_query_tok_per_s=units / (graph_ms / 1e3), speedup=eager_ms / graph_ms,
+                graph_launches_per_step='1 graph (29 kernels) + commit')
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_sample(seconds=12.0, rank=0):
     """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
@@ -495,6 +594,19 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
+    if args.case == 'graph':
+        res = graph_leg(pkg, device, rank, args.warmup, args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='small-batch verify step, eager vs CUDA-graph replay',
+                                          value=res['graph_query_tok_per_s'], unit='query-tok/s', n_gpus=world,
+                                          steps=args.steps, warmup=args.warmup, ms_per_step=res['graph_ms_per_step'],
+                                          higher_is_better=True, dtype='bf16', data='synthetic', graph=res,
+                                          device_status=status))), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'train':
         # config 4 alone (profiling and standalone measurement); rank 0 reports
         train = train_layout_leg(pkg, device, rank, args.warmup, iters=args.steps)
@@ -612,7 +724,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

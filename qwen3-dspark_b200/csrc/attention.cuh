@@ -247,6 +247,16 @@ __device__ __forceinline__ bool range_empty(int c, long long total, long long gr
   return range_start(c, total, grid) == range_start(c + 1, total, grid);
 }
 
+// Ranges a launch of `total` tiles is split into: every CTA of the grid for large
+// launches, and about one range per kMinTilesPerRange tiles for small ones. A cut
+// item is merged by one warp, one contributor after another, so splitting a small
+// launch over all SMs makes the merges (not the streaming) the critical path.
+constexpr long long kMinTilesPerRange = 12;
+__device__ __forceinline__ long long sched_grid(long long total, long long grid) {
+  const long long g = total / kMinTilesPerRange;
+  return g < 1 ? 1 : (g < grid ? g : grid);
+}
+
 // Inclusive block-wide scan of v over all threads of the CTA.
 template <int kThreads>
 __device__ long long block_scan(long long v, long long* tmp, long long& total) {
@@ -320,8 +330,9 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
   if (p.num_requests <= kThreads) {
     const long long t = tid < p.num_requests ? request_tiles(p, tid) : 0;
     const long long incl = block_scan<kThreads>(t, s.scan_tmp, total);
-    start = range_start(blockIdx.x, total, p.grid);
-    end = range_start(blockIdx.x + 1, total, p.grid);
+    const long long g = sched_grid(total, p.grid);
+    start = blockIdx.x < g ? range_start(blockIdx.x, total, g) : total;
+    end = blockIdx.x < g ? range_start(blockIdx.x + 1, total, g) : total;
     if (tid < p.num_requests && start < end) {
       const long long excl = incl - t;
       if (excl <= start && start < incl) {
@@ -342,8 +353,9 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
       running += chunk_total;
     }
     total = running;
-    start = range_start(blockIdx.x, total, p.grid);
-    end = range_start(blockIdx.x + 1, total, p.grid);
+    const long long g = sched_grid(total, p.grid);
+    start = blockIdx.x < g ? range_start(blockIdx.x, total, g) : total;
+    end = blockIdx.x < g ? range_start(blockIdx.x + 1, total, g) : total;
     if (start < end) {
       running = 0;
       for (int base = 0; base < p.num_requests; base += kThreads) {
@@ -534,8 +546,9 @@ __device__ __forceinline__ void merge_split_item(const AttnParams& p, int q0, in
   __threadfence();
   __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
   const int d = lane * 4;
-  const bool dense = total >= p.grid;
-  const int slot_first = partial_slot(item_start, first, total, p.grid);
+  const long long grid = sched_grid(total, p.grid);
+  const bool dense = total >= grid;
+  const int slot_first = partial_slot(item_start, first, total, grid);
   const float sl2 = p.scale_log2;
 #pragma unroll 1
   for (int hh = 0; hh < 2; ++hh) {               // rows 8hh..8hh+7 = head 2h+hh
@@ -544,8 +557,8 @@ __device__ __forceinline__ void merge_split_item(const AttnParams& p, int q0, in
     for (int r = 0; r < 8; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
     float mrow = -INFINITY, lrow = 0.f;          // lane r < 8 tracks row r
     for (int c = first; c <= last; ++c) {
-      if (!dense && range_empty(c, total, p.grid)) continue;
-      const int sl = c == first ? slot_first : (dense ? 0 : partial_slot(item_start, c, total, p.grid));
+      if (!dense && range_empty(c, total, grid)) continue;
+      const int sl = c == first ? slot_first : (dense ? 0 : partial_slot(item_start, c, total, grid));
       const size_t bi = (static_cast<size_t>(c) * 2 + sl) * kKVHeads + h;
       const float* pml = p.part_ml + bi * 32 + 16 * hh;
       const float* po = p.part_o + (bi * 16 + 8 * hh) * kHeadDim + d;
@@ -606,13 +619,14 @@ __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Ite
   }
   __threadfence();
   __syncwarp();
-  const int first = cta_of_tile(item_start, total, p.grid);
-  const int last = cta_of_tile(item_end - 1, total, p.grid);
+  const long long grid = sched_grid(total, p.grid);
+  const int first = cta_of_tile(item_start, total, grid);
+  const int last = cta_of_tile(item_end - 1, total, grid);
   unsigned int merge = 0;
   if (lane == 0) {
     int n = last - first + 1;
-    if (total < p.grid)            // tiny launch: some ranges are empty and contribute nothing
-      for (int c = first; c <= last; ++c) n -= range_empty(c, total, p.grid) ? 1 : 0;
+    if (total < grid)              // tiny launch: some ranges are empty and contribute nothing
+      for (int c = first; c <= last; ++c) n -= range_empty(c, total, grid) ? 1 : 0;
     unsigned long long* ctr = p.counters + static_cast<size_t>(first) * kKVHeads + h;
     merge = count_arrival(ctr, p.epoch) == static_cast<unsigned int>(n);
     // Every contributor has arrived: no one else touches this counter in this
