@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 5
+#define DSPARK_ABI_VERSION 6
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -155,6 +155,30 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
                      const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, const int32_t* slot_cap,
                      const int32_t* n_commit, int num_requests, int num_layers, long long rows_per_layer,
                      int scratch_rows, int dtype, cudaStream_t stream);
+
+/*
+ * On-device greedy acceptance of a verify round (the rule of
+ * dspark_qwen/cached_decode.py:84-98; the reference applies it on the host).
+ *
+ * dspark_row_argmax: pred[r] = index of the maximum of logits row r (rows x vocab,
+ * row stride ld elements, bf16 or fp32); ties give the lowest index and NaN is
+ * larger than any number (torch.argmax).
+ *
+ * dspark_greedy_accept: request i verified the chunk tokens[cu_q[i]..cu_q[i+1]-1]
+ * (anchor, then its proposals) and pred holds the target's prediction after each
+ * of those rows. Proposals are accepted while they equal the prediction before
+ * them (stopping after an accepted EOS); the first mismatch commits the target's
+ * token instead and a full accept commits the bonus prediction. Committed tokens
+ * are cut after their first EOS and to budget[i] (if budget is not NULL). Outputs:
+ * accepted[i] proposals, n_commit[i] committed tokens (= verified rows to keep,
+ * the n_commit input of dspark_commit_kv) and emitted[cu_q[i] + k] the committed
+ * tokens (-1 after them). All pointers are device memory; int64 tokens.
+ */
+int dspark_row_argmax(const void* logits, long long ld, int rows, int vocab, int dtype, int32_t* pred,
+                      cudaStream_t stream);
+int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
+                         int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
+                         int32_t* n_commit, long long* emitted, cudaStream_t stream);
 
 /*
  * Training-layout block-draft attention (bf16, tcgen05 tensor cores).

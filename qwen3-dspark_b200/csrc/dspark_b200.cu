@@ -13,6 +13,7 @@
 #include <queue>
 #include <vector>
 
+#include "accept.cuh"
 #include "attention.cuh"
 #include "train.cuh"
 #include "verify.cuh"
@@ -397,6 +398,29 @@ int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, 
   cp.rows_per_layer = rows_per_layer;
   cp.scratch_rows = scratch_rows;
   commit_kernel<<<dim3(num_requests, num_layers), 256, 0, stream>>>(cp);
+  return launch_status();
+}
+
+int dspark_row_argmax(const void* logits, long long ld, int rows, int vocab, int dtype, int32_t* pred,
+                      cudaStream_t stream) {
+  if (!logits || !pred || rows < 1 || vocab < 1 || ld < vocab || (dtype != DSPARK_DTYPE_BF16 && dtype != DSPARK_DTYPE_F32))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (dtype == DSPARK_DTYPE_BF16)
+    row_argmax_kernel<__nv_bfloat16><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits),
+                                                                            ld, vocab, pred);
+  else
+    row_argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const float*>(logits), ld, vocab, pred);
+  return launch_status();
+}
+
+int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
+                         int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
+                         int32_t* n_commit, long long* emitted, cudaStream_t stream) {
+  if (!pred || !tokens || !cu_q || num_requests < 1 || total_rows < num_requests || n_eos < 0 ||
+      (n_eos > 0 && !eos) || !accepted || !n_commit || !emitted)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  AcceptParams p{pred, tokens, cu_q, eos, n_eos, budget, num_requests, total_rows, accepted, n_commit, emitted};
+  greedy_accept_kernel<<<(num_requests + 127) / 128, 128, 0, stream>>>(p);
   return launch_status();
 }
 

@@ -251,3 +251,38 @@ def segment_attention(query, cu_query, query_lengths, key_a, value_a, a_start, a
         max(query_lengths), int(bool(causal)), float(scale), _DTYPES[query.dtype], out.data_ptr(),
         ws.data_ptr(), ws.numel(), _stream(device)), 'dspark_segment_attn')
     return out
+
+
+def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
+    """Greedy acceptance of one verify round on the GPU (cached_decode.py:84-98).
+
+    ``logits`` [N, vocab] (bf16/fp32) are the target's logits of the N verified rows,
+    ``tokens`` [N] int64 the verified chunk tokens (per request: anchor, proposals),
+    ``cu_query`` int32 [R+1] the request boundaries. ``budget`` (optional, int32 [R])
+    caps each request's committed tokens. Returns device tensors
+    ``(pred [N] int32, accepted [R] int32, n_commit [R] int32, emitted [N] int64)``
+    with ``emitted[cu_query[i] + k]`` the committed tokens of request i (-1 after).
+    """
+    device = logits.device
+    if (logits.ndim != 2 or logits.dtype not in _DTYPES or logits.stride(1) != 1 or not logits.is_cuda
+            or tokens.shape != (logits.shape[0],) or tokens.dtype != torch.long or tokens.device != device
+            or cu_query.dtype != torch.int32 or cu_query.device != device or cu_query.ndim != 1
+            or cu_query.numel() < 2):
+        raise ValueError('logits [N,V] bf16/fp32 (unit column stride), tokens [N] int64 and int32 cu_query '
+                         'on one CUDA device required')
+    r = cu_query.numel() - 1
+    eos = torch.tensor(sorted(set(int(e) for e in eos_ids)), dtype=torch.long, device=device)
+    if budget is not None and (budget.shape != (r,) or budget.dtype != torch.int32 or budget.device != device):
+        raise ValueError('budget must be int32 [R] on the logits device')
+    n = logits.shape[0]
+    pred = torch.empty(n, dtype=torch.int32, device=device)
+    counts = torch.empty(2 * r, dtype=torch.int32, device=device)
+    emitted = torch.empty(n, dtype=torch.long, device=device)
+    lib, stream = _lib.load_library(), _stream(device)
+    _lib.check(lib.dspark_row_argmax(logits.data_ptr(), logits.stride(0), n, logits.shape[1], _DTYPES[logits.dtype],
+                                     pred.data_ptr(), stream), 'dspark_row_argmax')
+    _lib.check(lib.dspark_greedy_accept(pred.data_ptr(), tokens.data_ptr(), cu_query.contiguous().data_ptr(), r, n,
+                                        eos.data_ptr() if eos.numel() else None, eos.numel(),
+                                        budget.data_ptr() if budget is not None else None, counts.data_ptr(),
+                                        counts[r:].data_ptr(), emitted.data_ptr(), stream), 'dspark_greedy_accept')
+    return pred, counts[:r], counts[r:], emitted

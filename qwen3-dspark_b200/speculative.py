@@ -32,9 +32,37 @@ def accept_greedy(proposals, predictions, eos_ids=()):
     return accepted, committed
 
 
+def _accept_on_device(target, verified, chunks, proposals, output, max_new_tokens, eos_ids):
+    """One round's acceptance with the on-device argmax + accept kernels: the host
+    reads back one small int64 vector (counts and committed tokens) per round."""
+    from .kernels import greedy_accept
+    active = list(chunks)
+    logits = target.model.get_output_embeddings()(verified.last)[0]
+    tokens = torch.cat(tuple(chunks.values()), dim=1)[0]
+    cu = [0]
+    for r in active:
+        cu.append(cu[-1] + chunks[r].shape[1])
+    dev = logits.device
+    cu_q = torch.tensor(cu, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+    budget = torch.tensor([max_new_tokens - len(output[r]) for r in active], dtype=torch.int32)
+    budget = budget.pin_memory().to(dev, non_blocking=True)
+    _pred, accepted, n_commit, emitted = greedy_accept(logits, tokens, cu_q, eos_ids, budget)
+    host = torch.cat((accepted.long(), n_commit.long(), emitted)).cpu().tolist()
+    n = len(active)
+    result = {}
+    for i, r in enumerate(active):
+        k = host[n + i]
+        result[r] = (host[i], host[2 * n + cu[i]:2 * n + cu[i] + k])
+    return result
+
+
 @torch.no_grad()
-def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=()):
-    """prompts: {request: ids [1, P]} on the target device. Returns ({request: tokens}, rounds)."""
+def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), device_accept=True):
+    """prompts: {request: ids [1, P]} on the target device. Returns ({request: tokens}, rounds).
+
+    ``device_accept`` runs the argmax and the accept rule on the GPU (one small
+    read-back per round); otherwise each request's logits are read back and the rule
+    runs on the host. Both give the same tokens."""
     if type(max_new_tokens) is not int or max_new_tokens < 0:
         raise ValueError('max_new_tokens must be a nonnegative integer')
     eos_ids = set(eos_ids)
@@ -55,12 +83,17 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=()):
         chunks = {r: torch.tensor([[output[r][-1]] + proposals[r]], dtype=torch.long, device=target.device)
                   for r in active}
         verified = target.verify(chunks)
-        logits = target.predict(verified)
-        predictions = {r: v[0].argmax(-1).tolist() for r, v in logits.items()}
+        if device_accept:
+            decided = _accept_on_device(target, verified, chunks, proposals, output, max_new_tokens, eos_ids)
+        else:
+            logits = target.predict(verified)
+            decided = {}
+            for r, v in logits.items():
+                accepted, committed = accept_greedy(proposals[r], v[0].argmax(-1).tolist(), eos_ids)
+                decided[r] = (accepted, committed[:max_new_tokens - len(output[r])])
         commit, stats = {}, {}
         for r in active:
-            accepted, committed = accept_greedy(proposals[r], predictions[r], eos_ids)
-            committed = committed[:max_new_tokens - len(output[r])]
+            accepted, committed = decided[r]
             output[r].extend(committed)
             commit[r] = len(committed)          # old anchor .. newest-1 are now committed KV
             stats[r] = dict(accepted=accepted, committed=len(committed))
