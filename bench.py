@@ -17,7 +17,7 @@ over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank
 profiler captures; the default is the full round the metric is quoted on.
 ``--case train`` measures config 4 (training-layout draft attention) alone;
 ``--case graph`` compares an eager and a CUDA-graph-replayed verify step at a small
-serving batch.
+serving batch; ``--case accept`` times the on-device greedy acceptance of one round.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -486,6 +486,38 @@ def graph_leg(pkg, device, rank, warmup, steps):
                 graph_launches_per_step='1 graph (29 kernels) + commit')
 
 
+# --------------------------------------------------------------------------- accept
+def accept_leg(pkg, device, warmup, iters=20, vocab=151936):
+    """On-device greedy acceptance for one config-3 verify round: argmax over the
+    logits of 128 x 7 verified rows (Qwen3 vocab 151936, bf16: 272 MB, larger than
+    L2) + the accept rule. HBM roofline: the logits are read once."""
+    import torch
+    r, q = VERIFY['requests'], VERIFY['q']
+    n = r * q
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    logits = torch.randn(n, vocab, device=device, dtype=torch.bfloat16, generator=gen)
+    tokens = torch.randint(0, vocab, (n,), device=device, generator=gen)
+    cu = torch.arange(0, n + 1, q, dtype=torch.int32, device=device)
+    budget = torch.full((r,), 64, dtype=torch.int32, device=device)
+    for _ in range(warmup):
+        pkg.greedy_accept(logits, tokens, cu, (151645,), budget)
+    pairs = []
+    for _ in range(iters):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        pkg.greedy_accept(logits, tokens, cu, (151645,), budget)
+        b.record()
+        pairs.append((a, b))
+    torch.cuda.synchronize(device)
+    ms = statistics.median(a.elapsed_time(b) for a, b in pairs)
+    nbytes = n * vocab * 2
+    hbm, kind = peaks()
+    return dict(workload=f'{r} requests x {q} verified rows, vocab {vocab}, bf16 logits', ms=ms,
+                alg_bytes=nbytes, achieved_gbs=nbytes / (ms / 1e3) / 1e9,
+                frac=nbytes / (ms / 1e3) / 1e9 / hbm, peak_gbs=hbm, peak_source=kind)
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_sample(seconds=12.0, rank=0):
     """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
@@ -594,6 +626,19 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
+    if args.case == 'accept':
+        res = accept_leg(pkg, device, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='on-device greedy accept (argmax + accept rule) per verify round',
+                                          value=res['achieved_gbs'], unit='GB/s', n_gpus=world, steps=args.steps,
+                                          warmup=args.warmup, ms_per_step=res['ms'], higher_is_better=True,
+                                          dtype='bf16', data='synthetic', accept=res, device_status=status))),
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'graph':
         res = graph_leg(pkg, device, rank, args.warmup, args.steps)
         status = pkg.read_device_status(clear=True)
@@ -724,7 +769,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

@@ -40,25 +40,44 @@ __device__ __forceinline__ float to_f32<float>(float x) { return x; }
 template <>
 __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
 
-// One CTA per row; 16-byte loads when the row start is 16-byte aligned.
+// A thread visits its elements in increasing index order, so a strict '>'
+// keeps the first maximum; a NaN replaces any number and is kept thereafter.
+__device__ __forceinline__ void scan_one(ArgBest& best, float x, int idx) {
+  if (x > best.v || (x != x && best.v == best.v)) best = ArgBest{x, idx};
+}
+
+// One CTA per row; 4 independent 16-byte loads in flight per thread when the
+// row start is 16-byte aligned (the element tail and unaligned rows go scalar).
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads) row_argmax_kernel(const T* __restrict__ logits, long long ld,
                                                                     int vocab, int* __restrict__ pred) {
-  constexpr int kVec = 16 / sizeof(T);
+  constexpr int kVec = 16 / sizeof(T), kUnroll = 4;
   const T* row = logits + static_cast<long long>(blockIdx.x) * ld;
   ArgBest best{-INFINITY, 0x7fffffff};
   const bool vec = (reinterpret_cast<uintptr_t>(row) & 15) == 0;
   int i0 = 0;
   if (vec) {
     const int nvec = vocab / kVec;
-    for (int k = threadIdx.x; k < nvec; k += kArgmaxThreads) {
-      const uint4 raw = __ldg(reinterpret_cast<const uint4*>(row) + k);
+    const uint4* rv = reinterpret_cast<const uint4*>(row);
+    // vector base + j*kArgmaxThreads + t: coalesced loads, increasing index per thread
+    int base = 0;
+    for (; base + kArgmaxThreads * kUnroll <= nvec; base += kArgmaxThreads * kUnroll) {
+      uint4 raw[kUnroll];
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) raw[j] = __ldg(rv + base + j * kArgmaxThreads + threadIdx.x);
+#pragma unroll
+      for (int j = 0; j < kUnroll; ++j) {
+        const T* x = reinterpret_cast<const T*>(&raw[j]);
+        const int v0 = (base + j * kArgmaxThreads + threadIdx.x) * kVec;
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) scan_one(best, to_f32(x[e]), v0 + e);
+      }
+    }
+    for (int k = base + threadIdx.x; k < nvec; k += kArgmaxThreads) {
+      const uint4 raw = __ldg(rv + k);
       const T* x = reinterpret_cast<const T*>(&raw);
 #pragma unroll
-      for (int e = 0; e < kVec; ++e) {
-        const ArgBest c{to_f32(x[e]), k * kVec + e};
-        if (arg_better(c, best)) best = c;
-      }
+      for (int e = 0; e < kVec; ++e) scan_one(best, to_f32(x[e]), k * kVec + e);
     }
     i0 = nvec * kVec;
   }
