@@ -17,16 +17,16 @@
 //   warps 0-3  softmax: thread m owns S/O row m (TMEM lane m); online softmax
 //              with the running max raised only when it grows by more than
 //              2^8 (exact: the final O/l does not depend on the max used),
-//              P written to one of two shared-memory buffers as the A operand
-//              of the next PV MMA. Only a raised max (rare after the first
-//              blocks) waits for the previous PV to rescale O in TMEM, so the
-//              softmax of block n+1 overlaps the PV MMA of block n;
+//              P (bf16) written back over its own S buffer in TMEM, where the
+//              PV MMA reads it as its A operand. Only a raised max (rare after
+//              the first blocks) waits for the previous PV to rescale O in
+//              TMEM, so the softmax of block n+1 overlaps the PV MMA of block n;
 //   warp 4     TMEM owner and QK issuer (one thread): S = Q K^T into one of
 //              two S buffers;
 //   warp 7     PV issuer (one thread): O += P V into the O accumulator;
 //              completion is reported through tcgen05.commit on mbarriers;
-//   warp 5     TMA producer of Q (per tile) and K (2-stage ring), one thread;
-//   warp 6     TMA producer of V (2-stage ring), one thread. Separate K and V
+//   warp 5     TMA producer of Q (per tile) and K (3-stage ring), one thread;
+//   warp 6     TMA producer of V (3-stage ring), one thread. Separate K and V
 //              producers let a K stage refill as soon as its QK is done.
 // Every wait is bounded; a timed-out wait raises a CTA abort flag that ends all
 // roles, the MMA thread drains its MMAs, the producer waits for its copies in
@@ -68,23 +68,27 @@ __host__ __device__ constexpr int plan_items_at(int grid) { return ((kPlanHeader
 
 // Shared memory (offsets from a 1024-byte aligned base). Every operand tile is
 // two 16 KB halves of 128 rows x 64 bf16 in the 128-byte swizzle.
-// Key block g uses K/V stage, S buffer and P buffer g&1.
+// Key block g uses K and V stage g%3 and TMEM S/P buffer g&1.
+constexpr int kStages = 3;
 constexpr uint32_t kSmemQ = 0;
-constexpr uint32_t kSmemK = 32768;                       // 2 stages x 32 KB
-constexpr uint32_t kSmemV = kSmemK + 2 * 32768;          // 2 stages x 32 KB
-constexpr uint32_t kSmemP = kSmemV + 2 * 32768;          // 2 buffers x 32 KB
-constexpr uint32_t kSmemBar = kSmemP + 2 * 32768;
-// Per-block barriers come in pairs indexed by the block's parity, so no waiter
-// can ever be two phases behind its barrier.
+constexpr uint32_t kSmemK = 32768;                       // 3 stages x 32 KB
+constexpr uint32_t kSmemV = kSmemK + kStages * 32768;    // 3 stages x 32 KB
+constexpr uint32_t kSmemBar = kSmemV + kStages * 32768;
+// Per-block barriers of the S/P buffers come in pairs indexed by the block's
+// parity and the stage barriers one per stage, so no waiter can ever be two
+// phases behind its barrier.
 enum Barrier {
-  kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarVFull0 = kBarKFull0 + 2, kBarSFull0 = kBarVFull0 + 2,
-  kBarPFull0 = kBarSFull0 + 2, kBarODone0 = kBarPFull0 + 2, kBarOFree = kBarODone0 + 2, kBarDrain, kNumBarriers
+  kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarKEmpty0 = kBarKFull0 + kStages, kBarVFull0 = kBarKEmpty0 + kStages,
+  kBarVEmpty0 = kBarVFull0 + kStages, kBarSFull0 = kBarVEmpty0 + kStages, kBarPFull0 = kBarSFull0 + 2,
+  kBarODone0 = kBarPFull0 + 2, kBarOFree = kBarODone0 + 2, kBarDrain, kNumBarriers
 };
 constexpr uint32_t kSmemTmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
 constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 4;
 
-// TMEM columns: two S buffers and the O accumulator, 128 fp32 columns each.
+// TMEM columns: two S buffers and the O accumulator, 128 fp32 columns each. P
+// (bf16, two per column) overwrites the first 64 columns of its own S buffer
+// and is the A operand of the PV MMA straight from TMEM.
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0, kTmemO = 256;
 
@@ -110,6 +114,18 @@ __device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T: A is 128 rows (TMEM lanes) of K=16 bf16
+// packed two per 32-bit column (the lower key in the low half), 8 columns.
+__device__ __forceinline__ void umma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 
@@ -247,11 +263,8 @@ __device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUt
                                               int first, int last, int total_q, int total_k, uint32_t sbase,
                                               uint32_t bars, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
-  // A K stage is free when the QK MMA that read it is done (kBarSFull), a V
-  // stage when its PV MMA is done (kBarODone): both pairs share the stage index.
-  constexpr int kStages = 2;
   constexpr int kFull = kKeys ? kBarKFull0 : kBarVFull0;
-  constexpr int kEmpty = kKeys ? kBarSFull0 : kBarODone0;
+  constexpr int kEmpty = kKeys ? kBarKEmpty0 : kBarVEmpty0;
   constexpr uint32_t kRing = kKeys ? kSmemK : kSmemV;
   int gb = 0, it = 0, armed_q = 0;
   int armed[kStages] = {};
@@ -294,7 +307,7 @@ __device__ __forceinline__ void producer_role(const CUtensorMap* qmap, const CUt
 // are disjoint (S buffers vs O in TMEM; Q, K vs P, V in shared memory).
 //
 // QK issuer: S(g) = Q K(g)^T into S buffer g&1, 8 MMAs of K=16 over the head
-// dim; its commit on kBarSFull is also the "K stage free" signal.
+// dim.
 __device__ __forceinline__ void qk_role(const int* items, int first, int last, int total_q, int total_k,
                                         uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
@@ -307,12 +320,12 @@ __device__ __forceinline__ void qk_role(const int* items, int first, int last, i
     const int nb = x.key_blocks();
     if (!(ok = wait_or_abort(bar(kBarQFull), it & 1, abort_flag))) break;
     for (int n = 0; n < nb; ++n) {
-      const int g = gb + n, sb = g & 1;
-      if (!(ok = wait_or_abort(bar(kBarKFull0 + sb), (g >> 1) & 1, abort_flag))) break;
-      // S buffer g&1 is free once the softmax has consumed S(g-2) (its P(g-2) is out).
-      if (g >= 2 && !(ok = wait_or_abort(bar(kBarPFull0 + sb), ((g - 2) >> 1) & 1, abort_flag))) break;
+      const int g = gb + n, sb = g & 1, st = g % kStages;
+      if (!(ok = wait_or_abort(bar(kBarKFull0 + st), (g / kStages) & 1, abort_flag))) break;
+      // S buffer g&1 holds P(g-2) until PV(g-2) has read it.
+      if (g >= 2 && !(ok = wait_or_abort(bar(kBarODone0 + sb), ((g - 2) >> 1) & 1, abort_flag))) break;
       tc_fence_after();
-      const uint32_t kbase = sbase + kSmemK + sb * 32768;
+      const uint32_t kbase = sbase + kSmemK + st * 32768;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
@@ -320,6 +333,7 @@ __device__ __forceinline__ void qk_role(const int* items, int first, int last, i
                   smem_desc(kbase + off, 16, 1024), kIdesc, kk > 0);
       }
       umma_commit(bar(kBarSFull0 + sb));
+      umma_commit(bar(kBarKEmpty0 + st));
       if (n == nb - 1) umma_commit(bar(kBarQEmpty));
     }
     gb += nb;
@@ -332,8 +346,8 @@ __device__ __forceinline__ void qk_role(const int* items, int first, int last, i
   wait_or_abort(bar(kBarDrain), 0, &never);
 }
 
-// PV issuer: O += P(g) V(g), A = P (K-major over keys), B = V (N-major: d
-// contiguous); its commit on kBarODone is also the "V stage free" signal.
+// PV issuer: O += P(g) V(g), A = P from TMEM (K-major over keys), B = V
+// (N-major: d contiguous).
 __device__ __forceinline__ void pv_role(const int* items, int first, int last, int total_q, int total_k,
                                         uint32_t sbase, uint32_t bars, uint32_t tmem, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
@@ -345,19 +359,18 @@ __device__ __forceinline__ void pv_role(const int* items, int first, int last, i
     if (!load_item(items + static_cast<size_t>(idx) * kItemWords, total_q, total_k, x)) continue;
     const int nb = x.key_blocks();
     for (int n = 0; n < nb; ++n) {
-      const int g = gb + n, sb = g & 1;
+      const int g = gb + n, sb = g & 1, st = g % kStages;
       if (!(ok = wait_or_abort(bar(kBarPFull0 + sb), (g >> 1) & 1, abort_flag))) break;
       if (n == 0 && !(ok = wait_or_abort(bar(kBarOFree), (it & 1) ^ 1, abort_flag))) break;
-      if (!(ok = wait_or_abort(bar(kBarVFull0 + sb), (g >> 1) & 1, abort_flag))) break;
+      if (!(ok = wait_or_abort(bar(kBarVFull0 + st), (g / kStages) & 1, abort_flag))) break;
       tc_fence_after();
-      const uint32_t vbase = sbase + kSmemV + sb * 32768;
+      const uint32_t vbase = sbase + kSmemV + st * 32768;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const uint32_t aoff = (kk >> 2) * 16384 + (kk & 3) * 32;
-        umma_bf16(tmem + kTmemO, smem_desc(sbase + kSmemP + sb * 32768 + aoff, 16, 1024),
-                  smem_desc(vbase + kk * 2048, 16384, 1024), kIdesc, (n > 0 || kk > 0) ? 1u : 0u);
-      }
+      for (int kk = 0; kk < 8; ++kk)
+        umma_bf16_ts(tmem + kTmemO, tmem + kTmemS + sb * 128 + kk * 8, smem_desc(vbase + kk * 2048, 16384, 1024),
+                     kIdesc, (n > 0 || kk > 0) ? 1u : 0u);
       umma_commit(bar(kBarODone0 + sb));
+      umma_commit(bar(kBarVEmpty0 + st));
     }
     gb += nb;
     ++it;
@@ -375,8 +388,6 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
   const int m = threadIdx.x;                       // S/O row == TMEM lane
   const int qi = m >> 1;                           // query row inside the tile
   const uint32_t lane_addr = static_cast<uint32_t>(m & ~31) << 16;
-  uint8_t* prow0 = smem + kSmemP + m * 128;
-  const int swz = m & 7;
   int gb = 0;
   bool ok = true;
   for (int idx = first; idx < last && ok; ++idx) {
@@ -437,11 +448,6 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         pk[i] = pack_bf16x2(p0, p1);
       }
       l = l * alpha + sum;
-      if (g >= 2) {
-        // PV(g-2) has finished reading this P buffer (within this item or the last).
-        ok = wait_or_abort(bar(kBarODone0 + (g & 1)), ((g - 2) >> 1) & 1, abort_flag);
-        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      }
       if (n > 0 && __any_sync(0xffffffffu, resc)) {
         // A raised max rescales O once PV(g-1) has added into it.
         ok = wait_or_abort(bar(kBarODone0 + ((g - 1) & 1)), ((g - 1) >> 1) & 1, abort_flag);
@@ -456,16 +462,11 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
           tmem_st32(tmem + lane_addr + kTmemO + c * 32, o);
         }
       }
-      uint8_t* prow = prow0 + (g & 1) * 32768;
+      // P over the first 64 columns of its own S buffer (S is already in registers)
 #pragma unroll
-      for (int h = 0; h < 2; ++h)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const uint4 v = make_uint4(pk[h * 32 + 4 * j], pk[h * 32 + 4 * j + 1], pk[h * 32 + 4 * j + 2],
-                                     pk[h * 32 + 4 * j + 3]);
-          *reinterpret_cast<uint4*>(prow + h * 16384 + ((j ^ swz) << 4)) = v;
-        }
-      fence_proxy_async_smem();
+      for (int c = 0; c < 2; ++c)
+        tmem_st32(tmem + lane_addr + kTmemS + (g & 1) * 128 + c * 32,
+                  *reinterpret_cast<const float(*)[32]>(&pk[c * 32]));
       tc_fence_before();
       mbar_arrive(bar(kBarPFull0 + (g & 1)));
     }
