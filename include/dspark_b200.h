@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 6
+#define DSPARK_ABI_VERSION 7
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -179,6 +179,29 @@ int dspark_row_argmax(const void* logits, long long ld, int rows, int vocab, int
 int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
                          int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
                          int32_t* n_commit, long long* emitted, cudaStream_t stream);
+
+/*
+ * One step of the draft's greedy Markov proposal (DSparkDraft._sample_greedy,
+ * dspark_qwen/model.py:210-221), bf16, for up to 128 requests:
+ *   emb = emb_table[prev[r * prev_stride]]                        (rank wide)
+ *   conf[r * tok_stride + k] = sigmoid(hidden_row . conf_w[:H] + emb . conf_w[H:] + conf_b)
+ *   tokens[r * tok_stride + k] = argmax_v(base_row[v] + emb . proj_weight[v])
+ * where base_row / hidden_row are rows r * base_stride_r + k of base [*, vocab]
+ * (the LM head logits of the block rows) and hidden [*, hidden_dim], with the
+ * reference's bf16 rounding (projection output, then the sum) and ties to the
+ * lowest index. proj_weight / emb_table are [vocab, rank] (vocab a multiple of 8,
+ * rank a multiple of 64 up to 256). The [R, vocab] logits are never written:
+ * a tcgen05 GEMM keeps each tile in TMEM and the argmax is folded in. scratch
+ * (dspark_markov_scratch_bytes(), 16-byte aligned device memory) must be zero
+ * before the first call and is left zero by every call. Run the block's steps k
+ * = 0 .. S-1 in order, passing prev = the anchors for k = 0 and
+ * prev = tokens + (k - 1) (stride tok_stride) afterwards.
+ */
+size_t dspark_markov_scratch_bytes(void);
+int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                       long long base_stride_r, int k, const long long* prev, long long prev_stride,
+                       const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,
+                       float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream);
 
 /*
  * Training-layout block-draft attention (bf16, tcgen05 tensor cores).

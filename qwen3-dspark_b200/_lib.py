@@ -33,6 +33,9 @@ SIGNATURES = {
     'dspark_commit_kv': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _vp]),
     'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
     'dspark_row_argmax': (_i, [_vp, _ll, _i, _i, _i, _vp, _vp]),
+    'dspark_markov_scratch_bytes': (_sz, []),
+    'dspark_markov_step': (_i, [_vp, _vp, _i, _i, _vp, _ll, _i, _vp, _ll, _vp, _i, _vp, _f, _vp, _vp, _ll, _i,
+                                _vp, _vp]),
     'dspark_greedy_accept': (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
     'dspark_train_attn': (_i, [_vp, _vp, _vp, _i, _ll, _vp, _i, _f, _vp, _vp]),
 }
@@ -55,7 +58,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 6:
+        if lib.dspark_abi_version() != 7:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

@@ -15,6 +15,7 @@
 
 #include "accept.cuh"
 #include "attention.cuh"
+#include "markov.cuh"
 #include "train.cuh"
 #include "verify.cuh"
 #include "../../include/dspark_b200.h"
@@ -74,7 +75,9 @@ int device_info(int dev, DeviceInfo* out) {
         cudaFuncSetAttribute(attn_bf16_kernel<true, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(kAttnSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(train::train_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(train::kSmemBytes)) != cudaSuccess)
+                             static_cast<int>(train::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(markov::markov_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(markov::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
@@ -421,6 +424,55 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
     return DSPARK_ERR_INVALID_ARGUMENT;
   AcceptParams p{pred, tokens, cu_q, eos, n_eos, budget, num_requests, total_rows, accepted, n_commit, emitted};
   greedy_accept_kernel<<<(num_requests + 127) / 128, 128, 0, stream>>>(p);
+  return launch_status();
+}
+
+size_t dspark_markov_scratch_bytes(void) { return markov::kRows * sizeof(unsigned long long) + 16; }
+
+int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                       long long base_stride_r, int k, const long long* prev, long long prev_stride,
+                       const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,
+                       float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream) {
+  if (!proj_weight || !emb_table || !base || !prev || !hidden || !conf_w || !tokens || !conf || !scratch ||
+      vocab < 8 || vocab % 8 != 0 || rank < 64 || rank > markov::kMaxRank || rank % 64 != 0 || hidden_dim < 1 ||
+      num_requests < 1 || num_requests > markov::kRows || k < 0 || k >= base_stride_r || base_stride_r < 1 ||
+      prev_stride < 0 || tok_stride <= k || !aligned(proj_weight, 16) || !aligned(emb_table, 16) ||
+      !aligned(base, 16) || !aligned(scratch, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  CUtensorMap wm;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(rank), static_cast<cuuint64_t>(vocab)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(rank) * 2};
+  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(markov::kVocabTile)};
+  cuuint32_t estr[2] = {1, 1};
+  if (g_encode(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(proj_weight), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return DSPARK_ERR_CUDA;
+  markov::Params p{};
+  p.emb_table = static_cast<const __nv_bfloat16*>(emb_table);
+  p.base = static_cast<const __nv_bfloat16*>(base);
+  p.base_stride_r = base_stride_r;
+  p.k = k;
+  p.prev = prev;
+  p.prev_stride = prev_stride;
+  p.hidden = static_cast<const __nv_bfloat16*>(hidden);
+  p.hidden_dim = hidden_dim;
+  p.conf_w = static_cast<const __nv_bfloat16*>(conf_w);
+  p.conf_b = conf_b;
+  p.tokens = tokens;
+  p.tok_stride = tok_stride;
+  p.conf = conf;
+  p.best = static_cast<unsigned long long*>(scratch);
+  p.arrivals = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(scratch) + markov::kRows * 8);
+  p.num_requests = num_requests;
+  p.vocab = vocab;
+  p.rank = rank;
+  p.tiles = (vocab + markov::kVocabTile - 1) / markov::kVocabTile;
+  const int grid = p.tiles < dev.sms ? p.tiles : dev.sms;
+  markov::markov_step_kernel<<<grid, markov::kThreads, markov::kSmemBytes, stream>>>(wm, p);
   return launch_status();
 }
 

@@ -25,7 +25,7 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import HEAD_DIM, HKV, HQ, segment_attention
+from .kernels import HEAD_DIM, HKV, HQ, markov_greedy, segment_attention
 from .kv_store import _upload
 
 
@@ -270,6 +270,14 @@ class B200PackedDraft:
         return DraftFeatures(hidden, requests, size, tuple(self._lengths[q] for q in requests), work)
 
     @torch.no_grad()
+    def _confidence_bias(self):
+        """confidence.bias as a host float, read once per parameter version."""
+        b = self.draft.confidence.bias
+        key = (b.data_ptr(), b._version)
+        if getattr(self, '_bias_key', None) != key:
+            self._bias_value, self._bias_key = float(b.float().item()), key
+        return self._bias_value
+
     def propose_greedy(self, anchors):
         """Greedy block proposal per request: serial Markov argmax over the block rows
         (DSparkDraft._sample_greedy, dspark_qwen/model.py:210-221), batched over requests.
@@ -277,9 +285,20 @@ class B200PackedDraft:
         feats = self.backbone(anchors)
         d, size = self.draft, feats.block_size
         r = len(feats.requests)
+        prev = torch.cat([anchors[q].view(1) for q in feats.requests])
+        rank = d.markov_projection.weight.shape[1]
+        if (d.markov_projection.weight.dtype == torch.bfloat16 and feats.hidden.dtype == torch.bfloat16
+                and rank % 64 == 0 and rank <= 256 and d.markov_projection.weight.shape[0] % 8 == 0):
+            # fused on-device Markov loop: one tcgen05 launch per block position
+            hidden = feats.hidden.reshape(r * size, -1).contiguous()
+            base = d.lm_head(hidden).contiguous()
+            bias = self._confidence_bias()
+            toks, confs = markov_greedy(d.markov_projection.weight, d.markov_embedding.weight,
+                                        d.confidence.weight.reshape(-1), bias, hidden, base, prev, size)
+            toks, confs = toks.tolist(), confs.tolist()
+            return {q: (toks[i], confs[i]) for i, q in enumerate(feats.requests)}
         hidden = feats.hidden.view(r, size, -1)
         base = d.lm_head(hidden.to(d.lm_head.weight.dtype))
-        prev = torch.cat([anchors[q].view(1) for q in feats.requests])
         tokens, conf = [], []
         for k in range(size):
             emb = d.markov_embedding(prev)

@@ -286,3 +286,49 @@ def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
                                         budget.data_ptr() if budget is not None else None, counts.data_ptr(),
                                         counts[r:].data_ptr(), emitted.data_ptr(), stream), 'dspark_greedy_accept')
     return pred, counts[:r], counts[r:], emitted
+
+
+_markov_scratch = {}
+
+
+def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, anchors, block_size):
+    """Serial greedy Markov proposal of one draft block for every request on the
+    GPU (DSparkDraft._sample_greedy, dspark_qwen/model.py:210-221), one fused
+    tcgen05 launch per block position (``dspark_markov_step``).
+
+    ``proj_weight``/``emb_table`` [V, rank] bf16 (markov_projection.weight /
+    markov_embedding.weight), ``conf_weight`` [H + rank] bf16, ``conf_bias`` a float,
+    ``hidden`` [R * block_size, H] bf16, ``base`` = lm_head(hidden) [R * block_size, V]
+    bf16, ``anchors`` [R] int64. Returns device tensors ``tokens`` [R, block_size]
+    int64 and ``conf`` [R, block_size] float32.
+    """
+    device = hidden.device
+    v, rank = proj_weight.shape
+    r = anchors.numel()
+    h = hidden.shape[1]
+    for x in (proj_weight, emb_table, conf_weight, hidden, base):
+        if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.device != device:
+            raise ValueError('Markov proposal operands must be contiguous bf16 on one device')
+    if (emb_table.shape != (v, rank) or conf_weight.shape != (h + rank,) or hidden.shape != (r * block_size, h)
+            or base.shape != (r * block_size, v) or anchors.dtype != torch.long or anchors.device != device):
+        raise ValueError('Markov proposal shapes do not match')
+    key = device.index
+    if key not in _markov_scratch:
+        _markov_scratch[key] = torch.zeros(int(_lib.load_library().dspark_markov_scratch_bytes()),
+                                           dtype=torch.uint8, device=device)
+    scratch = _markov_scratch[key]
+    tokens = torch.empty((r, block_size), dtype=torch.long, device=device)
+    conf = torch.empty((r, block_size), dtype=torch.float32, device=device)
+    anchors = anchors.contiguous()
+    lib, stream = _lib.load_library(), _stream(device)
+    for r0 in range(0, r, 128):
+        n = min(128, r - r0)
+        for k in range(block_size):
+            prev, prev_stride = ((anchors[r0:].data_ptr(), 1) if k == 0
+                                 else (tokens[r0:, k - 1:].data_ptr(), block_size))
+            _lib.check(lib.dspark_markov_step(
+                proj_weight.data_ptr(), emb_table.data_ptr(), v, rank, base[r0 * block_size:].data_ptr(), block_size,
+                k, prev, prev_stride, hidden[r0 * block_size:].data_ptr(), h, conf_weight.data_ptr(),
+                float(conf_bias), tokens[r0:].data_ptr(), conf[r0:].data_ptr(), block_size, n, scratch.data_ptr(),
+                stream), 'dspark_markov_step')
+    return tokens, conf

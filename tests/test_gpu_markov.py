@@ -1,0 +1,106 @@
+"""Fused greedy Markov proposal (tcgen05 GEMM + in-TMEM argmax) vs the reference's
+torch formula (DSparkDraft._sample_greedy, dspark_qwen/model.py:210-221) in bf16.
+
+Each step is compared given the same previous token. The kernel's fp32 dot is
+accumulated in a different order than a library GEMM, so after the reference's
+bf16 rounding two logits can land one bf16 ulp apart the other way: a token may
+differ only where the reference's own top logits are within one ulp, and at
+least 98% of tokens must be identical.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import dev, status_clean
+
+pytestmark = pytest.mark.gpu
+
+
+def make(seed, r, vocab, rank, hdim, block=7):
+    g = torch.Generator(device='cpu').manual_seed(seed)
+    bf = torch.bfloat16
+    w = (torch.randn(vocab, rank, generator=g) * 0.05).to(bf)
+    e = (torch.randn(vocab, rank, generator=g) * 0.5).to(bf)
+    cw = (torch.randn(hdim + rank, generator=g) * 0.05).to(bf)
+    cb = 0.1
+    hidden = torch.randn(r * block, hdim, generator=g).to(bf)
+    base = (torch.randn(r * block, vocab, generator=g) * 0.5).to(bf)
+    anchors = torch.randint(0, vocab, (r,), generator=g)
+    return [x.to(dev()) for x in (w, e, cw, hidden, base, anchors)] + [cb]
+
+
+def ref_step(w, e, cw, cb, hidden_k, base_k, prev):
+    emb = e[prev]                                                     # bf16 [R, rank]
+    lin = torch.nn.functional.linear(torch.cat((hidden_k, emb), -1), cw[None], torch.tensor([cb], dtype=cw.dtype,
+                                                                                             device=cw.device))
+    conf = lin.sigmoid().flatten().float()
+    logits = base_k + torch.nn.functional.linear(emb, w)             # bf16 projection, bf16 sum
+    return logits, conf
+
+
+@pytest.mark.parametrize('r,vocab,rank', [(64, 32768, 256), (5, 1024, 64), (128, 4096, 128), (130, 2048, 192)])
+def test_markov_steps_match_reference(pkg, r, vocab, rank):
+    hdim, block = 1024, 7
+    w, e, cw, hidden, base, anchors, cb = make(r + vocab, r, vocab, rank, hdim, block)
+    toks, conf = pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+    torch.cuda.synchronize()
+    toks_h = toks.cpu()
+    same = total = 0
+    for k in range(block):
+        prev = anchors if k == 0 else toks[:, k - 1]
+        rows = torch.arange(r, device=dev()) * block + k
+        logits, rconf = ref_step(w, e, cw, cb, hidden[rows], base[rows], prev)
+        ref = logits.float().argmax(-1).cpu()
+        got = toks_h[:, k]
+        lf = logits.float().cpu()
+        for i in range(r):
+            total += 1
+            if got[i] == ref[i]:
+                same += 1
+                continue
+            top, mine = lf[i, ref[i]].item(), lf[i, got[i]].item()
+            ulp = 2.0 ** (np.floor(np.log2(max(abs(top), 1e-30))) - 7)
+            assert top - mine <= ulp, (k, i, top, mine)
+        np.testing.assert_allclose(conf[:, k].cpu().numpy(), rconf.cpu().numpy(), atol=1e-2)
+    assert same / total >= 0.98, same / total
+    status_clean(pkg)
+
+
+def test_packed_draft_uses_fused_markov(pkg):
+    """propose_greedy of a bf16 draft with rank 64 goes through markov_greedy and gives
+    the tokens of the torch loop on the same backbone output (near-tie rule)."""
+    import inputs as I
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(**I.TINY_TARGET)
+    model = Qwen3ForCausalLM(cfg).eval()
+    shapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(shapes, 1).items()})
+    model = model.to(dev(), torch.bfloat16)
+    spec = pkg.DraftSpec(**dict(I.TINY_DRAFT, markov_rank=64))
+    draft = pkg.DSparkDraftModel(model, spec).eval()
+    dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items() if not k.startswith(('embedding.', 'lm_head.'))}
+    draft.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(dshapes, 2).items()}, strict=False)
+    draft = draft.to(dev(), torch.bfloat16)
+    pd = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=300)
+    g = np.random.Generator(np.random.PCG64(9))
+    for i in range(4):
+        pd.add_request(f'q{i}')
+        ctx = torch.from_numpy(g.standard_normal((1, 20 + 30 * i, 256 * len(spec.layer_ids))).astype(np.float32))
+        pd.append_committed({f'q{i}': ctx.to(dev(), torch.bfloat16)})
+    anchors = {f'q{i}': torch.tensor([[int(g.integers(0, 1000))]], device=dev()) for i in range(4)}
+    proposed = pd.propose_greedy(anchors)
+    feats = pd.backbone(anchors)
+    hidden = feats.hidden.reshape(4 * 7, -1)
+    base = draft.lm_head(hidden)
+    d = draft
+    for i, q in enumerate(feats.requests):
+        prev = anchors[q].view(1)
+        toks = proposed[q][0]
+        for k in range(7):
+            emb = d.markov_embedding(prev)
+            logits = (base[i * 7 + k] + d.markov_projection(emb)[0]).float()
+            ref = int(logits.argmax())
+            if toks[k] != ref:
+                assert logits[ref] - logits[toks[k]] <= 2.0 ** (np.floor(np.log2(abs(float(logits[ref])))) - 7)
+            prev = torch.tensor([toks[k]], device=dev())
+    status_clean(pkg)
