@@ -17,7 +17,8 @@ over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank
 profiler captures; the default is the full round the metric is quoted on.
 ``--case train`` measures config 4 (training-layout draft attention) alone;
 ``--case graph`` compares an eager and a CUDA-graph-replayed verify step at a small
-serving batch; ``--case accept`` times the on-device greedy acceptance of one round.
+serving batch; ``--case accept`` times the on-device greedy acceptance of one round;
+``--case markov`` the fused greedy Markov proposal of one draft block.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -518,6 +519,67 @@ def accept_leg(pkg, device, warmup, iters=20, vocab=151936):
                 frac=nbytes / (ms / 1e3) / 1e9 / hbm, peak_gbs=hbm, peak_source=kind)
 
 
+# --------------------------------------------------------------------------- markov
+def markov_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, hdim=1024):
+    """Greedy Markov proposal of one draft block (config 2's 64 requests, Qwen3 vocab,
+    markov_rank 256 of the 0.6B draft config, block 7): the fused kernel (one launch
+    per position, logits never written) vs the reference's torch loop on the same
+    inputs. HBM roofline per block: 7 x (projection weight + one LM-head logits row
+    per request)."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(11)
+    bf = torch.bfloat16
+    w = torch.randn(vocab, rank, device=device, dtype=bf, generator=gen) * 0.05
+    e = torch.randn(vocab, rank, device=device, dtype=bf, generator=gen) * 0.5
+    cw = torch.randn(hdim + rank, device=device, dtype=bf, generator=gen) * 0.05
+    hidden = torch.randn(r * BLOCK, hdim, device=device, dtype=bf, generator=gen)
+    base = torch.randn(r * BLOCK, vocab, device=device, dtype=bf, generator=gen)
+    anchors = torch.randint(0, vocab, (r,), device=device, generator=gen)
+    proj = torch.nn.Linear(rank, vocab, bias=False, device=device, dtype=bf)
+    proj.weight.data.copy_(w)
+    conf_lin = torch.nn.Linear(hdim + rank, 1, device=device, dtype=bf)
+    conf_lin.weight.data.copy_(cw[None])
+    conf_lin.bias.data.fill_(0.1)
+    emb = torch.nn.Embedding(vocab, rank, device=device, dtype=bf)
+    emb.weight.data.copy_(e)
+    hv = hidden.view(r, BLOCK, hdim)
+    bv = base.view(r, BLOCK, vocab)
+
+    def fused():
+        return pkg.markov_greedy(w, e, cw, 0.1, hidden, base, anchors, BLOCK)
+
+    def torch_loop():                       # DSparkDraft._sample_greedy, batched over requests
+        prev, toks, confs = anchors, [], []
+        for k in range(BLOCK):
+            em = emb(prev)
+            confs.append(conf_lin(torch.cat((hv[:, k], em), -1)).sigmoid().flatten())
+            prev = (bv[:, k] + proj(em)).argmax(-1)
+            toks.append(prev)
+        return torch.stack(toks, 1), torch.stack(confs, 1)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        pairs = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+    ms, torch_ms = timed(fused), timed(torch_loop)
+    nbytes = BLOCK * (vocab * rank * 2 + r * vocab * 2)
+    hbm, kind = peaks()
+    return dict(workload=f'{r} requests x block {BLOCK}, vocab {vocab}, markov_rank {rank}, bf16',
+                ms_per_block=ms, torch_loop_ms_per_block=torch_ms, speedup=torch_ms / ms, alg_bytes=nbytes,
+                achieved_gbs=nbytes / (ms / 1e3) / 1e9, frac=nbytes / (ms / 1e3) / 1e9 / hbm, peak_gbs=hbm,
+                peak_source=kind)
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_sample(seconds=12.0, rank=0):
     """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
@@ -626,6 +688,19 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
+    if args.case == 'markov':
+        res = markov_leg(pkg, device, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='fused greedy Markov proposal per draft block',
+                                          value=res['achieved_gbs'], unit='GB/s', n_gpus=world, steps=args.steps,
+                                          warmup=args.warmup, ms_per_step=res['ms_per_block'], higher_is_better=True,
+                                          dtype='bf16', data='synthetic', markov=res, device_status=status))),
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'accept':
         res = accept_leg(pkg, device, args.warmup, iters=args.steps)
         status = pkg.read_device_status(clear=True)
@@ -769,7 +844,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

@@ -17,8 +17,9 @@
 // lowest index); the last CTA to finish writes the tokens and clears the scratch.
 //
 // Roles (192 threads, persistent CTAs over the vocabulary tiles):
-//   warps 0-3  gather emb rows into shared memory (A operand), confidence (CTA
-//              0), epilogue (thread r = request r = TMEM lane r);
+//   warps 0-3  gather emb rows into shared memory (A operand), confidence (one
+//              warp per request, spread over the CTAs), epilogue (thread r =
+//              request r = TMEM lane r);
 //   warp 4     TMEM owner and MMA issuer (one thread);
 //   warp 5     TMA producer of the projection-weight tiles (two stages).
 #pragma once
@@ -130,17 +131,25 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     fence_proxy_async_smem();
     mbar_arrive(bar(kBarAReady));
-    // ---- confidence (before the token; one CTA) ---------------------------------
-    if (blockIdx.x == 0 && live) {
-      const __nv_bfloat16* h = p.hidden + (static_cast<long long>(r) * p.base_stride_r + p.k) * p.hidden_dim;
+    // ---- confidence (before the token): request r on CTA r % grid, one warp ------
+    for (int rr = static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) * warp; rr < p.num_requests;
+         rr += 4 * static_cast<int>(gridDim.x)) {
+      long long t = p.prev[rr * p.prev_stride];
+      t = (t < 0 || t >= p.vocab) ? 0 : t;
+      const __nv_bfloat16* h = p.hidden + (static_cast<long long>(rr) * p.base_stride_r + p.k) * p.hidden_dim;
+      const __nv_bfloat16* em = p.emb_table + t * p.rank;
       float acc = 0.f;
-      for (int i = 0; i < p.hidden_dim; ++i) acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
-      for (int i = 0; i < p.rank; ++i)
-        acc = fmaf(__bfloat162float(p.emb_table[tok * p.rank + i]), __bfloat162float(p.conf_w[p.hidden_dim + i]),
-                   acc);
-      // bf16 Linear output (fp32 dot + bias, rounded once), then a bf16 sigmoid
-      const float logit = bf16_round(acc + p.conf_b);
-      p.conf[r * p.tok_stride + p.k] = bf16_round(1.f / (1.f + expf(-logit)));
+      for (int i = lane; i < p.hidden_dim; i += 32)
+        acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
+      for (int i = lane; i < p.rank; i += 32)
+        acc = fmaf(__bfloat162float(em[i]), __bfloat162float(p.conf_w[p.hidden_dim + i]), acc);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) {
+        // bf16 Linear output (fp32 dot + bias, rounded once), then a bf16 sigmoid
+        const float logit = bf16_round(acc + p.conf_b);
+        p.conf[rr * p.tok_stride + p.k] = bf16_round(1.f / (1.f + expf(-logit)));
+      }
     }
     // ---- epilogue: running first-maximum over this CTA's tiles --------------------
     float best_v = -INFINITY;
@@ -151,6 +160,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < n_mine; ++t) {
       const int b = t & 1;
       const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+      // this request's 128 base logits of the tile, loaded before the MMA result is
+      // waited for so their latency overlaps it
+      uint4 braw[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        braw[q] = (live && v0 + q * 8 < p.vocab) ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8))
+                                                 : make_uint4(0, 0, 0, 0);
       ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -163,8 +179,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 4; ++q) {
             const int v = v0 + c * 32 + q * 8;
             if (v >= p.vocab) break;
-            const uint4 raw = __ldg(reinterpret_cast<const uint4*>(brow + v));
-            const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+            const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(&braw[c * 4 + q]);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
               const float x = bf16_round(bf16_round(d[q * 8 + e]) + __bfloat162float(bv[e]));
