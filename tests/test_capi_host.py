@@ -46,6 +46,18 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert st == 1
     size = ctypes.c_size_t(0)
     assert lib.dspark_attention_workspace_size(0, None) == 1
+    # training layout, acceptance and Markov entries refuse before touching the device
+    assert lib.dspark_train_attn(None, None, None, 1, 1, None, 1, 128 ** -0.5, None, None) == 1
+    assert lib.dspark_row_argmax(None, 16, 1, 16, 0, None, None) == 1
+    assert lib.dspark_row_argmax(ctypes.c_void_p(16), 8, 1, 16, 0, ctypes.c_void_p(16), None) == 1   # ld < vocab
+    assert lib.dspark_greedy_accept(None, None, None, 1, 1, None, 0, None, None, None, None, None) == 1
+    assert lib.dspark_markov_step(None, None, 1024, 256, None, 7, 0, None, 1, None, 1024, None, 0.0, None, None, 7, 1,
+                                  None, None) == 1
+    fake = ctypes.c_void_p(256)
+    for vocab, rank, r in ((1001, 256, 4), (1024, 96, 4), (1024, 320, 4), (1024, 256, 129)):   # refused shapes
+        assert lib.dspark_markov_step(fake, fake, vocab, rank, fake, 7, 0, fake, 1, fake, 1024, fake, 0.0, fake,
+                                      fake, 7, r, fake, None) == 1
+    assert lib.dspark_markov_scratch_bytes() >= 128 * 8
 
 
 def _fixture(pkg):
