@@ -18,7 +18,8 @@ profiler captures; the default is the full round the metric is quoted on.
 ``--case train`` measures config 4 (training-layout draft attention) alone;
 ``--case graph`` compares an eager and a CUDA-graph-replayed verify step at a small
 serving batch; ``--case accept`` times the on-device greedy acceptance of one round;
-``--case markov`` the fused greedy Markov proposal of one draft block.
+``--case markov`` the fused greedy Markov proposal of one draft block; ``--case round5``
+the full greedy speculative loop of config 5 on a Qwen3-0.6B-shaped model.
 
 Multi-GPU: launched by torchrun, one rank per GPU; ranks share nothing on the data
 path; one NCCL all_gather of per-rank stats after timing.
@@ -580,6 +581,92 @@ def markov_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, hdim
                 peak_source=kind)
 
 
+# --------------------------------------------------------------------------- config 5
+ROUND5 = dict(requests=32, prompts=(64, 256, 2048), new_tokens=128, seed=5)
+
+
+def round5_leg(pkg, device, rank, warmup):
+    """Config 5: a full greedy speculative round loop on a Qwen3-0.6B-shaped target (28
+    layers, hidden 1024, FFN 3072, vocab 151936, tied embeddings) and the 5-layer DSpark
+    draft of the 0.6B config (layers 1/7/14/21/26, block 7, markov_rank 256), random
+    weights (seeded), bf16, 32 requests with prompts cycling 64/256/2048 tokens, 128 new
+    tokens each. Everything the round needs runs on this library: fused verify layers,
+    commit/rollback, draft attention over the paged pool, the fused Markov proposal and
+    on-device acceptance; the GEMMs are the library GEMMs of torch."""
+    import numpy as np
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    cfg = Qwen3Config(vocab_size=151936, hidden_size=1024, intermediate_size=3072, num_hidden_layers=28,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
+                      rms_norm_eps=1e-6, tie_word_embeddings=True,
+                      rope_parameters={'rope_type': 'default', 'rope_theta': 1e6})
+    cfg._attn_implementation = 'sdpa'
+    torch.manual_seed(ROUND5['seed'] * 1000 + rank)
+    with torch.device(device):
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+        spec = pkg.DraftSpec()
+        draft = pkg.DSparkDraftModel(model, spec).to(torch.bfloat16).eval()
+    g = np.random.Generator(np.random.PCG64(ROUND5['seed'] * 1000 + rank))
+    lens = [ROUND5['prompts'][i % len(ROUND5['prompts'])] for i in range(ROUND5['requests'])]
+    cap = max(lens) + ROUND5['new_tokens'] + 16
+    target = pkg.B200Qwen3Target(model, spec.layer_ids, slots=ROUND5['requests'], context_capacity=cap,
+                                 max_query_tokens=sum(lens), slot_capacities=[n + ROUND5['new_tokens'] + 16 for n in lens])
+    pdraft = pkg.B200PackedDraft(draft, max_requests=ROUND5['requests'], context_capacity=cap)
+
+    def prompts(tag):
+        return {f'{tag}{i}': torch.from_numpy(g.integers(0, 151643, (1, n))).to(device) for i, n in enumerate(lens)}
+
+    def release(ps):
+        for r in ps:
+            target.remove_request(r)
+            pdraft.remove_request(r)
+
+    for w in range(max(1, warmup // 3)):                  # warm-up: library handles, allocator
+        ps = prompts(f'w{w}_')
+        pkg.speculative_greedy(target, pdraft, ps, 4)
+        release(ps)
+    def timed_loop(tag, graph):
+        ps = prompts(tag)
+        torch.cuda.synchronize(device)
+        t0 = time.perf_counter()
+        out, rounds = pkg.speculative_greedy(target, pdraft, ps, ROUND5['new_tokens'], graph=graph)
+        torch.cuda.synchronize(device)
+        dt = time.perf_counter() - t0
+        release(ps)
+        return out, rounds, dt
+
+    out, rounds, total_s = timed_loop('m', False)
+    pkg.speculative_greedy(target, pdraft, prompts('gw'), 4, graph=True)   # capture + warm the replayed path
+    release([f'gw{i}' for i in range(len(lens))])
+    out_g, rounds_g, total_g = timed_loop('g', True)
+    # prefill alone (same prompts, fresh requests), to split the time
+    ps = prompts('p')
+    for r in ps:
+        target.add_request(r)
+        pdraft.add_request(r)
+    torch.cuda.synchronize(device)
+    t1 = time.perf_counter()
+    feats = target.prefill(ps)
+    pdraft.append_committed({r: feats.context_for(r) for r in ps})
+    torch.cuda.synchronize(device)
+    prefill_s = time.perf_counter() - t1
+    release(ps)
+    generated = sum(len(v) for v in out.values())
+    accepted = [s['accepted'] for rd in rounds for s in rd.values()]
+    decode_s = max(total_s - prefill_s, 1e-9)
+    decode_g = max(total_g - prefill_s, 1e-9)
+    return dict(workload=f'Qwen3-0.6B-shaped target + 5-layer DSpark draft (random weights, bf16), '
+                         f'{ROUND5["requests"]} requests, prompts {ROUND5["prompts"]} cycling, '
+                         f'{ROUND5["new_tokens"]} new tokens each',
+                generated_tokens=generated, rounds=len(rounds), total_s=total_s, prefill_s=prefill_s,
+                decode_tok_per_s=(generated - len(out)) / decode_s, total_tok_per_s=generated / total_s,
+                graph_total_s=total_g, graph_decode_tok_per_s=(generated - len(out)) / decode_g,
+                mean_accepted_per_round=float(np.mean(accepted)) if accepted else 0.0,
+                note='random draft weights: acceptance is ~0, so every round emits one token per request; '
+                     'eager and graph loops run different random prompts of the same lengths '
+                     '(graph and eager tokens are compared on equal prompts in the GPU tests)')
+
+
 # --------------------------------------------------------------------------- CPU legs
 def cpu_sample(seconds=12.0, rank=0):
     """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
@@ -688,6 +775,19 @@ def run_b200(args):
     torch.cuda.set_device(device)
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
+    if args.case == 'round5':
+        res = round5_leg(pkg, device, rank, args.warmup)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='config-5 greedy speculative decode tokens/s per GPU',
+                                          value=max(res['decode_tok_per_s'], res['graph_decode_tok_per_s']), unit='tok/s', n_gpus=world, steps=1,
+                                          warmup=args.warmup, ms_per_step=res['total_s'] * 1e3 / max(res['rounds'], 1),
+                                          higher_is_better=True, dtype='bf16', data='synthetic (random weights)',
+                                          round5=res, device_status=status))), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'markov':
         res = markov_leg(pkg, device, args.warmup, iters=args.steps)
         status = pkg.read_device_status(clear=True)
@@ -844,7 +944,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'round5'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

@@ -10,7 +10,15 @@ and the draft projects the committed features. Here all active requests share on
 draft backbone call and one target verify forward per round.
 Greedy acceptance makes the output equal to the target's own greedy decode.
 """
+from dataclasses import dataclass
+
 import torch
+
+
+@dataclass(frozen=True)
+class QueryBucket:
+    """Exact ordered query lengths of a verify round: the key of a captured graph."""
+    query_lengths: tuple
 
 
 def accept_greedy(proposals, predictions, eos_ids=()):
@@ -57,12 +65,14 @@ def _accept_on_device(target, verified, chunks, proposals, output, max_new_token
 
 
 @torch.no_grad()
-def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), device_accept=True):
+def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), device_accept=True, graph=False):
     """prompts: {request: ids [1, P]} on the target device. Returns ({request: tokens}, rounds).
 
     ``device_accept`` runs the argmax and the accept rule on the GPU (one small
     read-back per round); otherwise each request's logits are read back and the rule
-    runs on the host. Both give the same tokens."""
+    runs on the host. Both give the same tokens. ``graph`` replays the target's verify
+    forward from a CUDA graph captured once per set of chunk lengths (``QueryBucket``)
+    instead of running it eagerly; the tokens are the same."""
     if type(max_new_tokens) is not int or max_new_tokens < 0:
         raise ValueError('max_new_tokens must be a nonnegative integer')
     eos_ids = set(eos_ids)
@@ -82,7 +92,13 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
         proposals = {r: toks for r, (toks, _conf) in draft.propose_greedy(anchors).items()}
         chunks = {r: torch.tensor([[output[r][-1]] + proposals[r]], dtype=torch.long, device=target.device)
                   for r in active}
-        verified = target.verify(chunks)
+        if graph:
+            bucket = QueryBucket(tuple(c.shape[1] for c in chunks.values()))
+            if bucket not in target._graphs:
+                target.capture(bucket)
+            verified = target.verify_graph(chunks, bucket)
+        else:
+            verified = target.verify(chunks)
         if device_accept:
             decided = _accept_on_device(target, verified, chunks, proposals, output, max_new_tokens, eos_ids)
         else:

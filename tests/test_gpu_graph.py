@@ -122,3 +122,26 @@ def test_graph_refusals(pkg):
     t.abort(f)
     assert t.lengths == {'a': 0, 'b': 0}
     status_clean(pkg)
+
+
+def test_speculative_loop_with_graph_replay_gives_the_same_tokens(pkg):
+    """speculative_greedy(graph=True) (target verify replayed per query bucket) emits the
+    tokens of the eager loop on the same bf16 model and prompts."""
+    model = tiny_bf16_model()
+    spec = pkg.DraftSpec(**dict(I.TINY_DRAFT, markov_rank=64))
+    outs = []
+    for graph in (False, True):
+        draft = pkg.DSparkDraftModel(model, spec).eval()
+        dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items()
+                   if not k.startswith(('embedding.', 'lm_head.'))}
+        draft.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(dshapes, 2).items()},
+                              strict=False)
+        draft = draft.to(dev(), torch.bfloat16)
+        target = pkg.B200Qwen3Target(model, spec.layer_ids, slots=4, context_capacity=400, max_query_tokens=700)
+        pdraft = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=400)
+        prompts = {f'r{i}': torch.from_numpy(ids)[None].to(dev()) for i, ids in enumerate(I.greedy_prompts()[3:6])}
+        out, rounds = pkg.speculative_greedy(target, pdraft, prompts, 24, graph=graph)
+        outs.append(out)
+        target.close()
+    assert outs[0] == outs[1]
+    status_clean(pkg)
