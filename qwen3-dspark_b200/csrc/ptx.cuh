@@ -83,7 +83,7 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
 
-// 3-D tiled TMA load (no multicast) completing on an mbarrier.
+// 3-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* m, int c0, int c1, int c2,
                                             uint32_t bar) {
   asm volatile(
@@ -93,7 +93,7 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* m, 
       : "memory");
 }
 
-// 2-D tiled TMA load (no multicast) completing on an mbarrier.
+// 2-D tiled TMA load into this CTA's shared memory, completing on an mbarrier.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, int c0, int c1, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
@@ -102,7 +102,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* m, 
       : "memory");
 }
 
-// 1-D bulk copy global -> shared (no multicast) completing on an mbarrier.
+// 1-D bulk copy global -> this CTA's shared memory, completing on an mbarrier.
 // Both addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
