@@ -269,6 +269,91 @@ class B200PackedDraft:
                     context_block_concatenation_kv_bytes=0, gathered_kv_bytes=0)
         return DraftFeatures(hidden, requests, size, tuple(self._lengths[q] for q in requests), work)
 
+    # -- captured proposal (fixed buffers, one CUDA graph per request count) ----------
+    def _propose_body(self, anchor_buf, pos_buf, meta, r):
+        """Backbone + LM head + greedy Markov loop over fixed-address inputs (bf16 drafts
+        whose Markov head runs on the fused kernel)."""
+        d, size = self.draft, self.draft.spec.block_size
+        cu_q, a_start, a_len, b_len = meta[:r + 1], meta[r + 1:2 * r + 1], meta[2 * r + 1:3 * r + 1], meta[3 * r + 1:]
+        b_start = cu_q[:r]
+        block = torch.full((r, size), d.spec.mask_token_id, dtype=torch.long, device=self.device)
+        block[:, 0] = anchor_buf
+        z = d.embedding(block.reshape(1, r * size)).to(d.fc.weight.dtype)
+        cos, sin = d.rotary(z, pos_buf[None])
+        qlens = [size] * r
+        for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
+            att = layer.attention
+            x = layer.input_norm(z)
+            q = att.project_q(x, cos, sin).to(self.kv_dtype).contiguous()
+            kb, vb = att.project_kv(x, cos, sin)
+            out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
+                                    vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
+            z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
+            z = z + layer.mlp(layer.post_norm(z))
+        hidden = d.norm(z)[0].contiguous()
+        base = d.lm_head(hidden).contiguous()
+        return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),
+                             self._confidence_bias(), hidden, base, anchor_buf, size)
+
+    def _graph_ready(self):
+        d = self.draft
+        rank = d.markov_projection.weight.shape[1]
+        return (d.markov_projection.weight.dtype == torch.bfloat16 and self.kv_dtype == torch.bfloat16
+                and rank % 64 == 0 and rank <= 256 and d.markov_projection.weight.shape[0] % 8 == 0)
+
+    @torch.no_grad()
+    def capture_propose(self, num_requests):
+        """Capture ``propose_greedy`` for ``num_requests`` requests into a CUDA graph:
+        anchors, block positions and the attention metadata live in fixed buffers that
+        ``propose_greedy_graph`` fills each round (bf16 drafts with the fused Markov
+        head)."""
+        if not self._graph_ready():
+            raise ValueError('Graph proposal needs a bf16 draft whose Markov head runs on the fused kernel')
+        graphs = self.__dict__.setdefault('_graphs', {})
+        if num_requests in graphs:
+            raise ValueError('Request count already captured')
+        r, size = num_requests, self.draft.spec.block_size
+        anchor_buf = torch.zeros(r, dtype=torch.long, device=self.device)
+        pos_buf = torch.arange(r * size, dtype=torch.long, device=self.device) % size
+        meta = torch.tensor([size * i for i in range(r + 1)] + [self.slot_rows[0]] * r + [0] * r + [size] * r,
+                            dtype=torch.int32, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):                       # warm-up: handles, allocator, workspace
+            self._propose_body(anchor_buf, pos_buf, meta, r)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            toks, conf = self._propose_body(anchor_buf, pos_buf, meta, r)
+        graphs[r] = dict(graph=graph, anchors=anchor_buf, pos=pos_buf, meta=meta, tokens=toks, conf=conf)
+        return graph
+
+    @torch.no_grad()
+    def propose_greedy_graph(self, anchors):
+        """``propose_greedy`` through the program captured for ``len(anchors)`` requests."""
+        ex = self.__dict__.get('_graphs', {}).get(len(anchors))
+        if ex is None:
+            raise ValueError('Capture the request count first')
+        size = self.draft.spec.block_size
+        requests = tuple(anchors)
+        positions = []
+        for request, anchor in anchors.items():
+            self._request(request)
+            if (not isinstance(anchor, torch.Tensor) or anchor.shape != (1, 1) or anchor.dtype != torch.long
+                    or anchor.device != self.device):
+                raise ValueError('Require one [1,1] long anchor per active request')
+            start = self._lengths[request]
+            positions.extend(range(start, start + size))
+        r = len(requests)
+        host = ([size * i for i in range(r + 1)] + [self.slot_rows[self._slots[q]] for q in requests]
+                + [self._lengths[q] for q in requests] + [size] * r)
+        ex['meta'].copy_(torch.tensor(host, dtype=torch.int32).pin_memory(), non_blocking=True)
+        ex['pos'].copy_(torch.tensor(positions, dtype=torch.long).pin_memory(), non_blocking=True)
+        ex['anchors'].copy_(torch.cat([anchors[q].view(1) for q in requests]))
+        ex['graph'].replay()
+        toks, confs = ex['tokens'].tolist(), ex['conf'].tolist()
+        return {q: (toks[i], confs[i]) for i, q in enumerate(requests)}
+
     @torch.no_grad()
     def _confidence_bias(self):
         """confidence.bias as a host float, read once per parameter version."""

@@ -72,7 +72,9 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
     read-back per round); otherwise each request's logits are read back and the rule
     runs on the host. Both give the same tokens. ``graph`` replays the target's verify
     forward from a CUDA graph captured once per set of chunk lengths (``QueryBucket``)
-    instead of running it eagerly; the tokens are the same."""
+    and, for bf16 drafts with the fused Markov head, the draft proposal from a graph
+    captured once per request count, instead of running them eagerly; the tokens are
+    the same."""
     if type(max_new_tokens) is not int or max_new_tokens < 0:
         raise ValueError('max_new_tokens must be a nonnegative integer')
     eos_ids = set(eos_ids)
@@ -89,7 +91,13 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
     rounds = []
     while active:
         anchors = {r: torch.tensor([[output[r][-1]]], dtype=torch.long, device=target.device) for r in active}
-        proposals = {r: toks for r, (toks, _conf) in draft.propose_greedy(anchors).items()}
+        if graph and getattr(draft, '_graph_ready', lambda: False)():
+            if len(anchors) not in draft.__dict__.get('_graphs', {}):
+                draft.capture_propose(len(anchors))
+            proposed = draft.propose_greedy_graph(anchors)
+        else:
+            proposed = draft.propose_greedy(anchors)
+        proposals = {r: toks for r, (toks, _conf) in proposed.items()}
         chunks = {r: torch.tensor([[output[r][-1]] + proposals[r]], dtype=torch.long, device=target.device)
                   for r in active}
         if graph:
