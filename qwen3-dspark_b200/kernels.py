@@ -312,7 +312,9 @@ def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, 
     if (emb_table.shape != (v, rank) or conf_weight.shape != (h + rank,) or hidden.shape != (r * block_size, h)
             or base.shape != (r * block_size, v) or anchors.dtype != torch.long or anchors.device != device):
         raise ValueError('Markov proposal shapes do not match')
-    key = device.index
+    # the packed maxima / arrival counter are shared by the calls on one stream (they
+    # run in order); another stream gets its own, so concurrent calls cannot race
+    key = (device.index, _stream(device))
     if key not in _markov_scratch:
         _markov_scratch[key] = torch.zeros(int(_lib.load_library().dspark_markov_scratch_bytes()),
                                            dtype=torch.uint8, device=device)

@@ -283,6 +283,8 @@ class B200Qwen3Target:
                 for r, (off, q, _) in features.spans.items()}
 
     def close(self):
+        """Restore the model's attention forwards and release captured programs."""
+        self._graphs.clear()
         for hook in self._hooks:
             hook.remove()
         for att, fwd in self._orig_forward.items():
