@@ -393,9 +393,12 @@ def train_layout_leg(pkg, device, rank, warmup, iters=20):
 
 # --------------------------------------------------------------------------- graph replay
 GRAPH = dict(requests=8, ctx_lo=256, ctx_hi=2048, seed=5, layers=28, q=7)
+# config 5's decode rounds: 32 requests, prompts 64/256/2048 cycling, 64 tokens into the
+# 128-token generation, 1 + block 7 verified rows
+GRAPH5 = dict(requests=32, prompts=(64, 256, 2048), generated=64, seed=5, layers=28, q=8)
 
 
-def graph_leg(pkg, device, rank, warmup, steps):
+def graph_leg(pkg, device, rank, warmup, steps, cfg=GRAPH):
     """Small serving batch (8 requests, context U[256,2048], 7 new rows, 28 layers):
     one verify step = begin + cos/sin table + 28 fused verify layers + commit, run
     eagerly (one host call per layer) and as a replay of the same 28 layers captured
@@ -403,13 +406,16 @@ def graph_leg(pkg, device, rank, warmup, steps):
     time per step, both ways, over the same rounds."""
     import numpy as np
     import torch
-    cfg = GRAPH
     g = np.random.Generator(np.random.PCG64(cfg['seed'] * 1000 + rank))
-    ctx = [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
+    if 'prompts' in cfg:
+        ctx = [cfg['prompts'][i % len(cfg['prompts'])] + cfg['generated'] for i in range(cfg['requests'])]
+    else:
+        ctx = [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
     R, Q, L = cfg['requests'], cfg['q'], cfg['layers']
     growth = Q * 2 * (warmup + steps + 2)
     store = pkg.B200PersistentTargetKV(layers=L, slots=R, context_capacity=max(ctx) + growth,
-                                       max_query_tokens=R * Q, device=device)
+                                       max_query_tokens=R * Q, device=device,
+                                       slot_capacities=[c + growth for c in ctx])
     handles = [store.add_request(f'g{i}') for i in range(R)]
     gen = torch.Generator(device=device)
     gen.manual_seed(99 + rank)
@@ -480,8 +486,14 @@ def graph_leg(pkg, device, rank, warmup, steps):
     eager_ms, eager_host = timed(eager_step)
     graph_ms, graph_host = timed(graph_step)
     units = R * Q * L
-    return dict(workload=f'{R} requests, ctx U[{cfg["ctx_lo"]},{cfg["ctx_hi"]}], q {Q}, {L} fused verify layers '
-                         '+ cos/sin table + commit per step',
+    # algorithmic bytes of one layer: resident + new K/V rows read once, q read, out written
+    layer_bytes = sum(c + Q for c in ctx) * HKV * D * 2 * 2 + 2 * R * Q * HQ * D * 2
+    span = (f'prompts {cfg["prompts"]} + {cfg["generated"]}' if 'prompts' in cfg
+            else f'ctx U[{cfg["ctx_lo"]},{cfg["ctx_hi"]}]')
+    hbm, kind = peaks()
+    return dict(workload=f'{R} requests, {span}, q {Q}, {L} fused verify layers + cos/sin table + commit per step',
+                layer_alg_bytes=layer_bytes, graph_gbs=layer_bytes * L / (graph_ms / 1e3) / 1e9,
+                graph_frac=layer_bytes * L / (graph_ms / 1e3) / 1e9 / hbm, peak_gbs=hbm, peak_source=kind,
                 eager_ms_per_step=eager_ms, graph_ms_per_step=graph_ms, eager_host_ms_per_step=eager_host,
                 graph_host_ms_per_step=graph_host, eager_query_tok_per_s=units / (eager_ms / 1e3),
                 graph_query_tok_per_s=units / (graph_ms / 1e3), speedup=eager_ms / graph_ms,
@@ -579,6 +591,98 @@ def markov_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, hdim
                 ms_per_block=ms, torch_loop_ms_per_block=torch_ms, speedup=torch_ms / ms, alg_bytes=nbytes,
                 achieved_gbs=nbytes / (ms / 1e3) / 1e9, frac=nbytes / (ms / 1e3) / 1e9 / hbm, peak_gbs=hbm,
                 peak_source=kind)
+
+
+def append_leg(pkg, device, warmup, iters=10):
+    """Draft-context append at the 0.6B draft geometry (hidden 1024, five draft layers,
+    five captured target layers of features; random weights, bf16): every layer's
+    k = RoPE(k_norm(k_proj(c))) and v = v_proj(c) of the context rows c = context_norm(
+    fc(features)) written into the paged pool. Two workloads of config 5: the prefill
+    append (32 requests, prompts cycling 64/256/2048 = 24,000 rows) and one round's
+    fixed-shape append (32 requests x 8 verified rows, random commit counts). Compared:
+    the fused tcgen05 append (rope table + one GEMM-with-epilogue launch) and the
+    reference's per-layer torch formula on the same pool. Tensor-core roofline of the
+    fused kernel: 2 x rows x (layers x 2048) x hidden FLOPs."""
+    import numpy as np
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    hidden, layers, nfeat = 1024, 5, 5
+    torch.manual_seed(21)
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=hidden, intermediate_size=3072, num_hidden_layers=nfeat + 2,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
+                      rms_norm_eps=1e-6, tie_word_embeddings=False,
+                      rope_parameters={'rope_type': 'default', 'rope_theta': 1e6})
+    with torch.device(device), torch.no_grad():
+        model = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+        spec = pkg.DraftSpec(layer_ids=tuple(range(1, nfeat + 1)), num_layers=layers, mask_token_id=1000)
+        draft = pkg.DSparkDraftModel(model, spec).to(torch.bfloat16).eval()
+    lens = [(64, 256, 2048)[i % 3] for i in range(32)]
+    fused = pkg.B200PackedDraft(draft, max_requests=32, slot_capacities=[n + 64 for n in lens],
+                                context_capacity=0)
+    plain = pkg.B200PackedDraft(draft, max_requests=32, slot_capacities=[n + 64 for n in lens],
+                                context_capacity=0)
+    plain._fused_append_ready = lambda: False
+    g = np.random.Generator(np.random.PCG64(22))
+
+    def feats(n):
+        return torch.from_numpy(g.standard_normal((1, n, nfeat * hidden)).astype(np.float32)).to(device, torch.bfloat16)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        pairs = []
+        for _ in range(iters):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+    tflops_peak, kind = tensor_peak()
+    out = {}
+    cases = (('prefill', lens, lens), ('round', [8] * 32, [int(c) for c in g.integers(1, 9, 32)]))
+    for name, widths, counts in cases:
+        r, n = len(widths), sum(widths)
+        cu = [0]
+        for w in widths:
+            cu.append(cu[-1] + w)
+        meta = torch.tensor(cu + list(fused.slot_rows) + [0] * r + counts, dtype=torch.int32, device=device)
+        x = feats(n)
+        with torch.no_grad():
+            ctx = draft.context_norm(draft.fc(x))[0].contiguous()
+        kv_w, kn_w, inv_freq = fused._append_operands()
+        eps = draft.layers[0].attention.k_norm.variance_epsilon
+
+        def kernel():
+            pkg.kernels.draft_append(ctx, kv_w, kn_w, inv_freq, meta, r, fused.pool_k, fused.pool_v,
+                                     fused.trash_row, eps)
+
+        with torch.no_grad():
+            fused_ms = timed(lambda: fused._append_rows(x, meta, r, n))
+            torch_ms = timed(lambda: plain._append_rows(x, meta, r, n))
+        kernel_ms = timed(kernel)
+        flops = 2.0 * n * layers * 2048 * hidden
+        out[name] = dict(rows=n, requests=r, fused_ms=fused_ms, torch_formula_ms=torch_ms,
+                         speedup=torch_ms / fused_ms, append_kernel_ms=kernel_ms,
+                         kernel_tflops=flops / (kernel_ms / 1e3) / 1e12,
+                         kernel_frac=flops / (kernel_ms / 1e3) / 1e12 / tflops_peak)
+    if hasattr(fused, 'capture_append'):
+        reqs = tuple(f'g{i}' for i in range(32))
+        for q in reqs:
+            fused.add_request(q)
+        fused.capture_append(32, 8)
+        x = feats(256)
+        counts = [0] * 32
+
+        def replay():
+            fused.append_verified_graph(x, reqs, counts)
+        with torch.no_grad():
+            out['round']['graph_replay_ms'] = timed(replay)
+    out.update(workload='0.6B draft geometry: hidden 1024, 5 draft layers, 5 x 1024 features, bf16',
+               peak_tflops=tflops_peak, peak_source=kind)
+    return out
 
 
 # --------------------------------------------------------------------------- config 5
@@ -788,6 +892,20 @@ def run_b200(args):
             dist.barrier()
             dist.destroy_process_group()
         return
+    if args.case == 'append':
+        res = append_leg(pkg, device, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='fused draft-context append (prefill of config 5)',
+                                          value=res['prefill']['kernel_tflops'], unit='TFLOP/s', n_gpus=world,
+                                          steps=args.steps, warmup=args.warmup,
+                                          ms_per_step=res['prefill']['fused_ms'], higher_is_better=True,
+                                          dtype='bf16', data='synthetic', append=res, device_status=status))),
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'markov':
         res = markov_leg(pkg, device, args.warmup, iters=args.steps)
         status = pkg.read_device_status(clear=True)
@@ -814,8 +932,11 @@ def run_b200(args):
             dist.barrier()
             dist.destroy_process_group()
         return
-    if args.case == 'graph':
-        res = graph_leg(pkg, device, rank, args.warmup, args.steps)
+    if args.case in ('graph', 'graph5'):
+        cfg = dict(GRAPH if args.case == 'graph' else GRAPH5)
+        if args.layers:
+            cfg['layers'] = min(cfg['layers'], args.layers)
+        res = graph_leg(pkg, device, rank, args.warmup, args.steps, cfg)
         status = pkg.read_device_status(clear=True)
         if rank == 0:
             print(json.dumps(_finite(dict(metric='small-batch verify step, eager vs CUDA-graph replay',
@@ -944,7 +1065,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'round5'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'append', 'round5', 'graph5'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 7
+#define DSPARK_ABI_VERSION 9
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -49,9 +49,11 @@ const char* dspark_status_string(int status);
 unsigned long long dspark_launch_count(void);
 
 /* Bytes of workspace the bf16 attention entry points need on `device`
- * (fp32 partials of items split between CTAs plus per-item arrival counters;
- * scales with the SM count, ~19 MB on a B200). Its contents never need
- * clearing: counters are tagged with a per-launch epoch. */
+ * (fp32 partials of items split between CTAs plus one merge record per CTA and
+ * KV head; scales with the SM count, ~19 MB on a B200). Its contents never need
+ * clearing: every launch rewrites the records it reads. Each bf16 attention
+ * call launches the attention kernel and then the merge of its split items on
+ * the same stream. */
 int dspark_attention_workspace_size(int device, size_t* bytes);
 
 /* Copies the device status word of the current device (synchronising), and
@@ -117,16 +119,22 @@ int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t*
                       int total_q, void* table, cudaStream_t stream);
 
 /*
- * Fused verify layer for a persistent KV store (bf16), one kernel launch:
+ * Verify layer for a persistent KV store (bf16):
  *  1. Qwen3 q_norm/k_norm (RMSNorm over the head dim, eps) and rotate-half RoPE
  *     (cos/sin from dspark_rope_table) of the new tokens' raw projections, at
- *     position ctx_len[i] + r for new row r of request i (q in registers, k in
- *     shared memory after its TMA load);
+ *     position ctx_len[i] + r for new row r of request i;
  *  2. KV append: roped k and raw v into scratch rows layer*scratch_rows + cu_q[i] + r;
  *  3. bottom-right causal attention over the resident prefix rows
  *     layer*rows_per_layer + slot_row[i] + [0, ctx_len[i]) followed by the
- *     request's new rows, read in place (no workspace gather).
- * Resident K/V: [num_layers * rows_per_layer, 8, 128]; scratch K/V:
+ *     request's new rows, read in place (no workspace gather);
+ *  4. the merge of requests split between CTAs.
+ * `path` DSPARK_VERIFY_FUSED does 1-3 in one attention kernel (q normalised in
+ * registers, new k in shared memory after its TMA load); DSPARK_VERIFY_PREP runs
+ * 1-2 as a small kernel once per new row (q written to `out`, which the
+ * attention kernel then reads in place) and the attention as its programmatic
+ * dependent, which pays off for small launches where every CTA would repeat
+ * the q prologue; DSPARK_VERIFY_AUTO takes PREP below 512 new rows. Resident
+ * K/V: [num_layers * rows_per_layer, 8, 128]; scratch K/V:
  * [num_layers * scratch_rows, 8, 128]; k_raw/v_raw: [total_q, 8, 128].
  * Replaces, per decoder layer, transformers Qwen3Attention.forward's
  * q_norm/k_norm/apply_rotary_pos_emb (modeling_qwen3.py:263-268) plus
@@ -134,12 +142,15 @@ int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t*
  * PersistentTargetKV.stage_layer + prepare_attention, persistent_target_kv.py:427-460)
  * plus persistent_attention_forward -> _native_attention (persistent_qwen_target.py:45-60,223-234).
  */
+#define DSPARK_VERIFY_AUTO (-1)
+#define DSPARK_VERIFY_FUSED 0
+#define DSPARK_VERIFY_PREP 1
 int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
                         const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
                         const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
                         void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
-                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* out,
-                        void* workspace, size_t workspace_bytes, cudaStream_t stream);
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, int path,
+                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Commit / rollback for all layers in one launch: for every request copy
@@ -204,6 +215,31 @@ int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab
                        float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream);
 
 /*
+ * Fused draft-context append (bf16, tcgen05 tensor cores): for every draft layer
+ * l < num_layers, k = RoPE(k_norm_l(context @ k_proj_l^T)) and
+ * v = context @ v_proj_l^T of each input row, written into the layer's K/V pool.
+ * context: [rows, hidden] (the output of the draft's fc + context_norm; hidden a
+ * multiple of 64); kv_weight: [num_layers * 2048, hidden], layer l's k_proj
+ * weight rows then its v_proj weight rows; k_norm_weight: [num_layers, 128];
+ * rope_table: [rows, 64] from dspark_rope_table over the same cu_rows / ctx_len.
+ * Input row g of request i (cu_rows[i] <= g < cu_rows[i + 1], j = g - cu_rows[i])
+ * is at position ctx_len[i] + j and lands in pool row slot_row[i] + ctx_len[i] + j
+ * when j < count[i], else in trash_row (so whole verified chunks can be appended
+ * with fixed shapes and only the committed rows become visible). pool_k / pool_v:
+ * host arrays of num_layers (<= 8) device pointers, each [pool_rows, 8, 128];
+ * destination rows outside [0, pool_rows) are skipped and flagged in the device
+ * status. Arithmetic follows the reference's bf16 ops (projection output, RMSNorm,
+ * weight product, each RoPE product and the sum rounded to bf16).
+ * Replaces PackedDraft.append_committed's per-layer project_kv and cache
+ * concatenation (dspark_qwen/packed_draft.py:146-158; model.py:41-45).
+ */
+int dspark_draft_append(const void* context, int rows, int hidden, const void* kv_weight, int num_layers,
+                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_rows,
+                        const int32_t* slot_row, const int32_t* ctx_len, const int32_t* count, int num_requests,
+                        void* const* pool_k, void* const* pool_v, long long pool_rows, long long trash_row,
+                        cudaStream_t stream);
+
+/*
  * Training-layout block-draft attention (bf16, tcgen05 tensor cores).
  * Replaces DraftAttention.forward's masked SDPA with block_mask
  * (dspark_qwen/model.py:12-19,47-61) for several sequences packed back to back.
@@ -240,7 +276,7 @@ int dspark_train_attn(const void* q, const void* k, const void* v, int total_q, 
  * where an extra cudaMalloc would fail and a cudaMalloc/cudaFree would stall the
  * device mid-step. The split-item scratch is a static device array of
  * dspark_varlen_attn_noalloc_scratch_bytes() bytes (18.8 MiB: partials and
- * counters of at most 148 CTAs) that every GPU loading the library holds until exit; the
+ * merge records of at most 148 CTAs) that every GPU loading the library holds until exit; the
  * requirement does not grow with the inputs, and the call returns
  * DSPARK_ERR_UNSUPPORTED if a launch would ever need more. The first call on a
  * device looks up that device's address of the array (make it before any

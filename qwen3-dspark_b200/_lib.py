@@ -13,6 +13,7 @@ from .build import LIB_PATH
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_CUDA = 0, 1, 2, 3
 DTYPE_BF16, DTYPE_F32 = 0, 1
 DEVICE_WAIT_TIMEOUT, DEVICE_BAD_SCHEDULE, DEVICE_BAD_ARGUMENT = 1, 2, 4
+VERIFY_PATHS = {'auto': -1, 'fused': 0, 'prep': 1}
 
 _vp, _i, _ll, _f, _sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_float, ctypes.c_size_t
 
@@ -28,7 +29,7 @@ SIGNATURES = {
     'dspark_segment_attn': (_i, [_vp, _vp, _vp, _ll, _vp, _vp, _ll, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
                                  _i, _f, _i, _vp, _vp, _sz, _vp]),
     'dspark_verify_fused': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _vp, _vp, _ll, _vp,
-                                 _vp, _i, _i, _i, _f, _vp, _vp, _sz, _vp]),
+                                 _vp, _i, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
     'dspark_rope_table': (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
     'dspark_commit_kv': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _vp]),
     'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
@@ -38,6 +39,8 @@ SIGNATURES = {
                                 _vp, _vp]),
     'dspark_greedy_accept': (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
     'dspark_train_attn': (_i, [_vp, _vp, _vp, _i, _ll, _vp, _i, _f, _vp, _vp]),
+    'dspark_draft_append': (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp, _ll, _ll,
+                                 _vp]),
 }
 
 _lock = threading.Lock()
@@ -58,7 +61,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 7:
+        if lib.dspark_abi_version() != 9:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

@@ -1,0 +1,269 @@
+// Fused draft-context append: every draft layer's k/v projection of the
+// committed context rows, Qwen3 k_norm and rotate-half RoPE of k, and the write
+// of both into the request-contiguous K/V pool, in one launch.
+//
+// The reference appends committed target features with
+//   context = context_norm(fc(features))                  (packed_draft.py:129-168)
+//   k, v    = project_kv(context, cos, sin) per layer     (model.py:41-45)
+//           = rope(k_norm(k_proj(context))), v_proj(context)
+// and concatenates them onto the cache. Here fc and context_norm stay library
+// GEMM + elementwise work; this kernel does the rest: a tcgen05 GEMM of the
+// context [rows, hidden] against the stacked projection weights
+// [layers * 2 * 8 * 128, hidden] (layer l: k_proj rows then v_proj rows), whose
+// N tiles of 128 are exactly one head of one layer's K or V. The accumulator of
+// a tile stays in TMEM; thread m of the epilogue owns row m of the tile (TMEM
+// lane m) and the head's 128 values, so k_norm (a 128-wide RMSNorm) and the
+// rotate-half partner d +- 64 are thread-local. Rounding follows the
+// reference's bf16 arithmetic: projection output to bf16, RMSNorm in fp32 then
+// bf16, times the bf16 weight then bf16, RoPE products and sum each to bf16.
+//
+// Input row g belongs to request i with cu_rows[i] <= g < cu_rows[i + 1]; its
+// position is ctx_len[i] + (g - cu_rows[i]) and it lands in pool row
+// slot_row[i] + position when g - cu_rows[i] < count[i], else in trash_row
+// (a row no request owns): a fixed-shape append of whole verified chunks then
+// writes only the committed rows, with no host-side slicing.
+//
+// Roles (192 threads, persistent CTAs over (row tile, head tile) pairs):
+//   warps 0-3  epilogue (thread m = tile row m = TMEM lane m);
+//   warp 4     TMEM owner and MMA issuer (one thread), two 128-column
+//              accumulators so one tile's epilogue overlaps the next one's MMAs;
+//   warp 5     TMA producer: context and weight 64-wide K chunks, six stages.
+#pragma once
+#include "train.cuh"
+#include "verify.cuh"
+
+namespace dspark {
+namespace append {
+
+using train::instr_desc;
+using train::smem_desc;
+using train::tc_fence_after;
+using train::tc_fence_before;
+using train::tmem_alloc;
+using train::tmem_dealloc;
+using train::tmem_ld32;
+using train::umma_bf16;
+using train::umma_commit;
+using train::wait_or_abort;
+
+constexpr int kThreads = 192;
+constexpr int kTileRows = 128;        // context rows per tile (MMA M)
+constexpr int kHeadCols = 128;        // one head (MMA N)
+constexpr int kStages = 6;
+constexpr int kMaxLayers = 8;
+constexpr uint32_t kStageBytes = 32768;            // context chunk 16 KB + weight chunk 16 KB
+constexpr uint32_t kSmemBar = kStages * kStageBytes;
+enum Barrier { kBarFull0 = 0, kBarEmpty0 = kStages, kBarDFull0 = 2 * kStages, kBarDFull1, kBarDFree0, kBarDFree1,
+               kBarDrain, kNumBarriers };
+constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
+constexpr uint32_t kSmemAbort = kSmemSlot + 4;
+constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 4;
+constexpr uint32_t kTmemCols = 256;
+
+struct Params {
+  const __nv_bfloat16* k_norm_w;      // [layers, 128] k_norm.weight of each layer
+  const uint32_t* rope;               // [rows, 64]: bf16 cos | bf16 sin << 16 of row g's position
+  const int* cu_rows;                 // [R + 1]
+  const int* slot_row;                // [R] first pool row of the request's slot
+  const int* ctx_len;                 // [R] position of the request's first input row
+  const int* count;                   // [R] rows of the request that are written
+  __nv_bfloat16* pool_k[kMaxLayers];  // [pool rows, 8, 128] per layer
+  __nv_bfloat16* pool_v[kMaxLayers];
+  long long trash_row;
+  long long pool_rows;                // rows of every pool tensor (destinations are checked)
+  int num_requests;
+  int rows;                           // input rows
+  int k_chunks;                       // hidden / 64
+  int head_tiles;                     // layers * 16
+  int row_tiles;
+  float eps;
+};
+
+__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* x) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q)
+    d[q] = make_uint4(pack_bf16x2(x[8 * q], x[8 * q + 1]), pack_bf16x2(x[8 * q + 2], x[8 * q + 3]),
+                      pack_bf16x2(x[8 * q + 4], x[8 * q + 5]), pack_bf16x2(x[8 * q + 6], x[8 * q + 7]));
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    draft_append_kernel(const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap wmap,
+                        Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + kSmemBar;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kNumBarriers; ++i) mbar_init(bar(i), (i == kBarDFree0 || i == kBarDFree1) ? 128u : 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5 && lane == 0) {
+    prefetch_tmap(&cmap);
+    prefetch_tmap(&wmap);
+  }
+  if (warp == 4) tmem_alloc(sbase + kSmemSlot, kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kSmemSlot);
+  const int tiles = p.row_tiles * p.head_tiles;
+  const int n_mine = tiles > static_cast<int>(blockIdx.x)
+                         ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
+
+  if (warp < 4) {
+    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    bool ok = true;
+    int cur_rt = -1;
+    long long dest = -1;
+    int g = 0;
+    for (int t = 0; t < n_mine; ++t) {
+      const int b = t & 1;
+      const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+      const int rt = tile / p.head_tiles, ht = tile - rt * p.head_tiles;
+      const int layer = ht >> 4, is_v = (ht >> 3) & 1, head = ht & 7;
+      if (rt != cur_rt) {                       // destination row of this thread's input row
+        cur_rt = rt;
+        g = rt * kTileRows + static_cast<int>(threadIdx.x);
+        dest = -1;
+        if (g < p.rows) {
+          const int i = min(find_request(p.cu_rows, p.num_requests + 1, g), p.num_requests - 1);
+          const int j = g - p.cu_rows[i];
+          dest = j < p.count[i] ? static_cast<long long>(p.slot_row[i]) + p.ctx_len[i] + j : p.trash_row;
+          if (dest < 0 || dest >= p.pool_rows) {
+            atomicOr(&g_device_status, kStatusBadArgument);
+            dest = -1;
+          }
+        }
+      }
+      ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      const uint32_t acc = tmem + lane_addr + b * kHeadCols;
+      __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) + (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) +
+                           head * kHeadDim;
+      if (is_v) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float d[32];
+          tmem_ld32(acc + c * 32, d);
+          if (dest >= 0) store_row32(out + c * 32, d);
+        }
+      } else {
+        // k_norm over the head's 128 values of the bf16 projection output
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          float d[32];
+          tmem_ld32(acc + c * 32, d);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float x = bf16r(d[e]);
+            ss = fmaf(x, x, ss);
+          }
+        }
+        const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+        const __nv_bfloat16* w = p.k_norm_w + layer * kHeadDim;
+        const uint32_t* cs = p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {           // d in [32c, 32c + 32) and its partners d + 64
+          float lo[32], hi[32];
+          tmem_ld32(acc + c * 32, lo);
+          tmem_ld32(acc + 64 + c * 32, hi);
+          if (dest >= 0) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              const int d = c * 32 + e;
+              const float a = bf16r(__bfloat162float(w[d]) * bf16r(bf16r(lo[e]) * rs));
+              const float bb = bf16r(__bfloat162float(w[d + 64]) * bf16r(bf16r(hi[e]) * rs));
+              const float2 r = unpack_bf16x2(__ldg(cs + d));   // .x cos, .y sin
+              lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
+              hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
+            }
+            store_row32(out + c * 32, lo);
+            store_row32(out + 64 + c * 32, hi);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kBarDFree0 + b));
+    }
+    if (!ok) *abort_flag = 1;
+  } else if (warp == 4) {
+    if (lane == 0) {
+      constexpr uint32_t kIdesc = instr_desc(0);
+      bool ok = true;
+      int st = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < n_mine && ok; ++t) {
+        const int b = t & 1;
+        if (!(ok = wait_or_abort(bar(kBarDFree0 + b), ((t >> 1) & 1) ^ 1, abort_flag))) break;
+        tc_fence_after();
+        for (int c = 0; c < p.k_chunks; ++c) {
+          if (!(ok = wait_or_abort(bar(kBarFull0 + st), ph, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + st * kStageBytes, w = a + 16384;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_bf16(tmem + b * kHeadCols, smem_desc(a + kk * 32, 16, 1024), smem_desc(w + kk * 32, 16, 1024),
+                      kIdesc, (c | kk) != 0);
+          umma_commit(bar(kBarEmpty0 + st));
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(bar(kBarDFull0 + b));
+      }
+      if (!ok) *abort_flag = 1;
+      umma_commit(bar(kBarDrain));
+      volatile int never = 0;
+      wait_or_abort(bar(kBarDrain), 0, &never);
+    }
+    __syncwarp();
+  } else {
+    if (lane == 0) {
+      int armed[kStages] = {};
+      bool ok = true;
+      int st = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < n_mine && ok; ++t) {
+        const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
+        const int rt = tile / p.head_tiles, ht = tile - rt * p.head_tiles;
+        for (int c = 0; c < p.k_chunks; ++c) {
+          if (!(ok = wait_or_abort(bar(kBarEmpty0 + st), ph ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(bar(kBarFull0 + st), kStageBytes);
+          const uint32_t dst = sbase + st * kStageBytes;
+          tma_load_2d(dst, &cmap, c * 64, rt * kTileRows, bar(kBarFull0 + st));
+          tma_load_2d(dst + 16384, &wmap, c * 64, ht * kHeadCols, bar(kBarFull0 + st));
+          ++armed[st];
+          if (++st == kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      volatile int never = 0;
+      for (int s = 0; s < kStages; ++s)
+        if (armed[s]) wait_or_abort(bar(kBarFull0 + s), (armed[s] - 1) & 1, &never);
+    }
+    __syncwarp();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+}
+
+}  // namespace append
+}  // namespace dspark

@@ -18,9 +18,12 @@
 // ranges, one per CTA (one CTA per SM). A CTA streams its range through a
 // 3-stage TMA pipeline: warp 8 issues the loads, warps 0-7 (one per KV head)
 // consume them. Items that lie wholly inside one range are normalised and
-// written directly. An item cut by range boundaries leaves fp32 partials; the
-// warp that contributes last (an epoch-tagged counter per item and head, no
-// waiting) merges them with a log-sum-exp combine and writes the output.
+// written directly. An item cut by range boundaries leaves fp32 partials, and
+// the CTA holding its first tile records it; split_merge_kernel, launched
+// right after (programmatic dependent launch), combines the partials of every
+// cut item with a log-sum-exp merge and writes the output. No CTA ever waits
+// for another one, and the merges run in parallel on many SMs instead of
+// trailing the contributor that arrives last.
 //
 // Fused verify mode (kFused): q holds the layer's raw q projections and source
 // B is the raw k/v projections of the new tokens. Consumer warps apply Qwen3
@@ -96,9 +99,20 @@ struct AttnParams {
   // workspace (split items)
   float* part_o;             // [grid][2][8][16][128]
   float* part_ml;            // [grid][2][8][16][2]
-  unsigned long long* counters;  // [grid][8]: (epoch << 32) | arrivals, per item and head
-  unsigned int epoch;        // unique per launch; stale counters never match it
+  struct MergeEntry* merges; // [grid][8]: the cut item CTA c starts, per KV head
   int grid;
+};
+
+// A cut item (one whose tiles span several CTAs) and KV head, recorded by the
+// CTA holding its first tile for the merge kernel. Every launch rewrites the
+// entries of all its CTAs, so stale entries are never read.
+struct MergeEntry {
+  long long item_start;      // global index of the item's first tile
+  long long total;           // tiles of the launch
+  int first, last;           // contributing CTAs
+  int q0, nrows;             // output rows of the item
+  int valid;
+  int pad[3];
 };
 
 // ---------------------------------------------------------------------------
@@ -511,23 +525,6 @@ __device__ __forceinline__ void rope_new_rows_in_smem(const AttnParams& p, const
   }
 }
 
-// Epoch-tagged arrival counter of one cut item and head: returns this
-// arrival's ordinal (1-based), 0 if the bounded CAS loop never succeeded.
-// The last arrival clears it; the epoch tag also discounts a count left by an
-// aborted launch.
-__device__ __forceinline__ unsigned int count_arrival(unsigned long long* ctr, unsigned int epoch) {
-  const unsigned long long tag = static_cast<unsigned long long>(epoch) << 32;
-  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(ctr);
-  for (int i = 0; i < (1 << 20); ++i) {
-    const unsigned int cnt = static_cast<unsigned int>(cur >> 32) == epoch ? static_cast<unsigned int>(cur) : 0u;
-    const unsigned long long prev = atomicCAS(ctr, cur, tag | (cnt + 1u));
-    if (prev == cur) return cnt + 1u;
-    cur = prev;
-  }
-  atomicOr(&g_device_status, kStatusBadSchedule);
-  return 0u;
-}
-
 // Partial slot of contributor c for an item starting at tile item_start: slot
 // 1 only when the item began before c's range (c is then the item's first
 // contributor and the item is its last one).
@@ -535,69 +532,10 @@ __device__ __forceinline__ int partial_slot(long long item_start, int c, long lo
   return item_start <= range_start(c, total, grid) ? 0 : 1;
 }
 
-// The last-arriving warp of a cut item merges all contributors' partials of
-// KV head h and writes the item's output rows. Rows are merged 8 at a time
-// (one head of the GQA pair) with an online log-sum-exp rescale, so each
-// contributor costs one round of independent loads. With at least as many
-// tiles as CTAs no range is empty and only the first contributor can hold the
-// item in slot 1, so the loop needs no division.
-__device__ __forceinline__ void merge_split_item(const AttnParams& p, int q0, int nrows, long long item_start,
-                                                 int first, int last, long long total, int h, int lane) {
-  __threadfence();
-  __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
-  const int d = lane * 4;
-  const long long grid = sched_grid(total, p.grid);
-  const bool dense = total >= grid;
-  const int slot_first = partial_slot(item_start, first, total, grid);
-  const float sl2 = p.scale_log2;
-#pragma unroll 1
-  for (int hh = 0; hh < 2; ++hh) {               // rows 8hh..8hh+7 = head 2h+hh
-    float4 acc[8];
-#pragma unroll
-    for (int r = 0; r < 8; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float mrow = -INFINITY, lrow = 0.f;          // lane r < 8 tracks row r
-    for (int c = first; c <= last; ++c) {
-      if (!dense && range_empty(c, total, grid)) continue;
-      const int sl = c == first ? slot_first : (dense ? 0 : partial_slot(item_start, c, total, grid));
-      const size_t bi = (static_cast<size_t>(c) * 2 + sl) * kKVHeads + h;
-      const float* pml = p.part_ml + bi * 32 + 16 * hh;
-      const float* po = p.part_o + (bi * 16 + 8 * hh) * kHeadDim + d;
-      const float2 ml = __ldcg(reinterpret_cast<const float2*>(pml + 2 * (lane & 7)));
-      float4 v[8];
-#pragma unroll
-      for (int r = 0; r < 8; ++r) v[r] = __ldcg(reinterpret_cast<const float4*>(po + r * kHeadDim));
-      const float mnew = fmaxf(mrow, ml.x);
-      const float mu = mnew == -INFINITY ? 0.f : mnew;
-      const float a_old = ex2((mrow - mu) * sl2), w = ex2((ml.x - mu) * sl2);
-      lrow = lrow * a_old + w * ml.y;
-      mrow = mnew;
-#pragma unroll
-      for (int r = 0; r < 8; ++r) {
-        const float ar = __shfl_sync(0xffffffffu, a_old, r), wr = __shfl_sync(0xffffffffu, w, r);
-        acc[r].x = acc[r].x * ar + wr * v[r].x;
-        acc[r].y = acc[r].y * ar + wr * v[r].y;
-        acc[r].z = acc[r].z * ar + wr * v[r].z;
-        acc[r].w = acc[r].w * ar + wr * v[r].w;
-      }
-    }
-    const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
-#pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const float ir = __shfl_sync(0xffffffffu, inv, r);
-      const int row = q0 + r;
-      if (r >= nrows || row < 0 || row >= p.total_q) continue;
-      __nv_bfloat16* dst = og + (static_cast<size_t>(row) * kQHeads + 2 * h + hh) * kHeadDim + d;
-      uint2 res;
-      res.x = pack_bf16x2(acc[r].x * ir, acc[r].y * ir);
-      res.y = pack_bf16x2(acc[r].z * ir, acc[r].w * ir);
-      *reinterpret_cast<uint2*>(dst) = res;
-    }
-  }
-}
-
 // A cut item's contribution from this CTA (warp of KV head h): store the fp32
-// partial O (unnormalised), row max m and row sum l; the warp that arrives
-// last over all contributing CTAs merges every partial and writes the output.
+// partial O (unnormalised), row max m and row sum l. The CTA holding the
+// item's first tile records the item for split_merge_kernel, which combines
+// the partials after this kernel; no CTA waits on another one here.
 __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Item& it, long long item_start,
                                                   long long item_end, long long start, long long total, int h,
                                                   int lane, const float (&o)[16][4], float m_a, float m_b, float l_a,
@@ -617,25 +555,110 @@ __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Ite
     __stcg(reinterpret_cast<float2*>(pml + 2 * g), make_float2(m_a, l_a));
     __stcg(reinterpret_cast<float2*>(pml + 2 * (g + 8)), make_float2(m_b, l_b));
   }
-  __threadfence();
-  __syncwarp();
-  const long long grid = sched_grid(total, p.grid);
-  const int first = cta_of_tile(item_start, total, grid);
-  const int last = cta_of_tile(item_end - 1, total, grid);
-  unsigned int merge = 0;
-  if (lane == 0) {
-    int n = last - first + 1;
-    if (total < grid)              // tiny launch: some ranges are empty and contribute nothing
-      for (int c = first; c <= last; ++c) n -= range_empty(c, total, grid) ? 1 : 0;
-    unsigned long long* ctr = p.counters + static_cast<size_t>(first) * kKVHeads + h;
-    merge = count_arrival(ctr, p.epoch) == static_cast<unsigned int>(n);
-    // Every contributor has arrived: no one else touches this counter in this
-    // launch, and clearing it lets a replay of the same launch (a CUDA graph
-    // carries one epoch) start from zero.
-    if (merge) atomicExch(ctr, 0ull);
+  if (item_start >= start && lane == 0) {
+    const long long grid = sched_grid(total, p.grid);
+    MergeEntry e;
+    e.item_start = item_start;
+    e.total = total;
+    e.first = static_cast<int>(blockIdx.x);
+    e.last = cta_of_tile(item_end - 1, total, grid);
+    e.q0 = it.q0;
+    e.nrows = it.nrows;
+    e.valid = 1;
+    e.pad[0] = e.pad[1] = e.pad[2] = 0;
+    p.merges[static_cast<size_t>(blockIdx.x) * kKVHeads + h] = e;
   }
-  merge = __shfl_sync(0xffffffffu, merge, 0);
-  if (merge) merge_split_item(p, it.q0, it.nrows, item_start, first, last, total, h, lane);
+}
+
+// Merge of the cut items, launched right after the attention kernel (as a
+// programmatic dependent launch where available, so its CTAs are resident
+// before the attention kernel ends). CTA (c, h) merges the item CTA c
+// recorded for KV head h, if any: warp w owns rows 4w..4w+3 of the head pair
+// (row r: head 2h + r / 8, query row q0 + r % 8), lane l owns d = 4l..4l+3.
+// Two passes over the contributors, four contributors' loads per round: the
+// row maximum M and sum L = sum_c l_c 2^((m_c - M) s), then
+// out = sum_c 2^((m_c - M) s) O_c / L. With at least as many tiles as CTAs no
+// range is empty and only the first contributor can hold the item in slot 1.
+constexpr int kMergeThreads = 128;
+__global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(const AttnParams p) {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  const int c0 = static_cast<int>(blockIdx.x) / kKVHeads, h = static_cast<int>(blockIdx.x) % kKVHeads;
+  if (c0 >= p.grid) return;
+  const MergeEntry e = p.merges[blockIdx.x];
+  if (!e.valid) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long grid = sched_grid(e.total, p.grid);
+  const bool dense = e.total >= grid;
+  const int slot_first = partial_slot(e.item_start, e.first, e.total, grid);
+  const float sl2 = p.scale_log2;
+  const int my_row = 4 * warp + (lane & 3);   // row whose statistics this lane tracks
+  const int d = lane * 4;
+  auto block = [&](int c) -> long long {
+    if (c > e.last || (!dense && range_empty(c, e.total, grid))) return -1;
+    const int sl = c == e.first ? slot_first : (dense ? 0 : partial_slot(e.item_start, c, e.total, grid));
+    return (static_cast<long long>(c) * 2 + sl) * kKVHeads + h;
+  };
+  float mrow = -INFINITY, lrow = 0.f;
+#pragma unroll 1
+  for (int c = e.first; c <= e.last; c += 4) {
+    float2 ml[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long bi = block(c + u);
+      ml[u] = bi >= 0 ? __ldcg(reinterpret_cast<const float2*>(p.part_ml + bi * 32 + 2 * my_row))
+                      : make_float2(-INFINITY, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float mnew = fmaxf(mrow, ml[u].x);
+      const float mu = mnew == -INFINITY ? 0.f : mnew;
+      lrow = lrow * ex2((mrow - mu) * sl2) + ml[u].y * ex2((ml[u].x - mu) * sl2);
+      mrow = mnew;
+    }
+  }
+  const float mu = mrow == -INFINITY ? 0.f : mrow;
+  const float inv = lrow > 0.f ? 1.f / lrow : 0.f;
+  float4 acc[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 1
+  for (int c = e.first; c <= e.last; c += 4) {
+    float4 v[4][4];
+    float wl[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const long long bi = block(c + u);
+      const float* po = p.part_o + (bi * 16 + 4 * warp) * kHeadDim + d;
+      const float2 ml = bi >= 0 ? __ldcg(reinterpret_cast<const float2*>(p.part_ml + bi * 32 + 2 * my_row))
+                                : make_float2(-INFINITY, 0.f);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        v[u][r] = bi >= 0 ? __ldcg(reinterpret_cast<const float4*>(po + r * kHeadDim))
+                          : make_float4(0.f, 0.f, 0.f, 0.f);
+      wl[u] = ex2((ml.x - mu) * sl2) * inv;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        const float wr = __shfl_sync(0xffffffffu, wl[u], r);
+        acc[r].x = fmaf(wr, v[u][r].x, acc[r].x);
+        acc[r].y = fmaf(wr, v[u][r].y, acc[r].y);
+        acc[r].z = fmaf(wr, v[u][r].z, acc[r].z);
+        acc[r].w = fmaf(wr, v[u][r].w, acc[r].w);
+      }
+  }
+  __nv_bfloat16* og = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {
+    const int rr = 4 * warp + r, qr = rr & 7, row = e.q0 + qr;
+    if (qr >= e.nrows || row < 0 || row >= p.total_q) continue;
+    __nv_bfloat16* dst = og + (static_cast<size_t>(row) * kQHeads + 2 * h + (rr >> 3)) * kHeadDim + d;
+    uint2 res;
+    res.x = pack_bf16x2(acc[r].x, acc[r].y);
+    res.y = pack_bf16x2(acc[r].z, acc[r].w);
+    *reinterpret_cast<uint2*>(dst) = res;
+  }
 }
 
 // Q fragments of heads 2h (MMA rows 0-7) and 2h+1 (rows 8-15) for query row
@@ -674,19 +697,26 @@ __device__ __forceinline__ void load_q_fragments(const AttnParams& p, const Item
         sn[ks][e] = cv.y;
       }
     }
+    // One head at a time through the same code: this prologue runs once per item
+    // and CTA, and an unrolled copy per head mostly costs instruction fetches.
     uint32_t lo[8], hi[8];
-#pragma unroll
+#pragma unroll 1
     for (int hh = 0; hh < 2; ++hh) {
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        lo[ks] = qf[ks][hh];
-        hi[ks] = qf[ks][hh + 2];
+        lo[ks] = hh ? qf[ks][1] : qf[ks][0];
+        hi[ks] = hh ? qf[ks][3] : qf[ks][2];
       }
       norm_rope_fragment(lo, hi, p, qw_smem, cs, sn, t4);
 #pragma unroll
       for (int ks = 0; ks < 8; ++ks) {
-        qf[ks][hh] = rv ? lo[ks] : 0u;
-        qf[ks][hh + 2] = rv ? hi[ks] : 0u;
+        if (hh) {
+          qf[ks][1] = rv ? lo[ks] : 0u;
+          qf[ks][3] = rv ? hi[ks] : 0u;
+        } else {
+          qf[ks][0] = rv ? lo[ks] : 0u;
+          qf[ks][2] = rv ? hi[ks] : 0u;
+        }
       }
     }
   }
@@ -724,6 +754,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     }
     fence_barrier_init();
   }
+  asm volatile("griddepcontrol.launch_dependents;");
+  // every CTA of the launch rewrites its merge entries (valid ones later)
+  if (warp < kConsumerWarps && lane == 0) p.merges[static_cast<size_t>(blockIdx.x) * kKVHeads + warp].valid = 0;
   locate_range<kAttnThreads>(p, sched);   // contains __syncthreads
   const long long start = sched.start, end = sched.end, total = sched.total;
   if (start >= end) return;
@@ -737,6 +770,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       prefetch_tmap(&tm_vb);
       int issued[kStages] = {};
       int kl = 0;
+      bool prep_done = false;
       const bool reorder = kReorderWalk && sched.reorder;
       const long long last_start = end - 1 - sched.t_l;
       bool ok = true;
@@ -760,6 +794,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             break;
           }
           const Tile ti = tile_of(w.it, w.t);
+          if (ti.src_b && !prep_done) {
+            // launched as a dependent of the verify prep kernel: the source-B
+            // (scratch) rows are complete past this point; resident rows
+            // before it stream while the prep runs (a no-op otherwise)
+            asm volatile("griddepcontrol.wait;" ::: "memory");
+            prep_done = true;
+          }
           const uint32_t bar = smem_u32(&full[stage]);
           const CUtensorMap* mk = ti.src_b ? &tm_kb : &tm_ka;
           const CUtensorMap* mv = ti.src_b ? &tm_vb : &tm_va;
@@ -807,6 +848,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       hi = reorder ? last_start : end;
     }
     long long item_start = lo - w.t;
+    if (seg == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
     load_q_fragments<kFused>(p, w.it, h, lane, qw_smem, qf);
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;

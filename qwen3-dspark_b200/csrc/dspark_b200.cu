@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "accept.cuh"
+#include "append.cuh"
 #include "attention.cuh"
 #include "markov.cuh"
 #include "train.cuh"
@@ -36,17 +37,13 @@ struct DeviceInfo {
 std::mutex g_mu;
 DeviceInfo g_dev[kMaxDevices];
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
-// Launch counter: tags the split-item arrival counters of each launch so that
-// counters left by an earlier launch never need clearing.
-std::atomic<unsigned int> g_epoch{1};
+// Verify launches with fewer new rows take the prep-kernel path (measured on
+// B200: 28-layer decode steps of 8 and 32 requests 30-40% faster; at 128
+// requests x 7 rows over 0.5 M resident rows the fused kernel is ~1.5% faster,
+// its in-register q prologue being amortised over long CTA ranges).
+constexpr int kVerifyPrepMaxRows = 512;
 // Kernels launched by this library since load (all devices, all streams).
 std::atomic<unsigned long long> g_launches{0};
-
-unsigned int next_epoch() {
-  unsigned int e = g_epoch.fetch_add(1);
-  if (e == 0) e = g_epoch.fetch_add(1);
-  return e;
-}
 
 constexpr size_t kAttnSmemBytes = 1024 + static_cast<size_t>(kSmemBarOff) + 2 * kStages * sizeof(uint64_t) +
                                   sizeof(SchedShared);
@@ -77,7 +74,9 @@ int device_info(int dev, DeviceInfo* out) {
         cudaFuncSetAttribute(train::train_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(train::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(markov::markov_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(markov::kSmemBytes)) != cudaSuccess)
+                             static_cast<int>(markov::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(append::draft_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(append::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
@@ -99,22 +98,22 @@ int current_device_info(DeviceInfo* out) {
   return device_info(dev, out);
 }
 
-// Workspace: fp32 partials of up to two cut items per CTA, then one
-// epoch-tagged arrival counter per (CTA, KV head).
+// Workspace: fp32 partials of up to two cut items per CTA, then one merge
+// entry per (CTA, KV head). Every launch rewrites what it reads.
 constexpr size_t workspace_for_grid(int grid) {
   return static_cast<size_t>(grid) * (2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float) +
-                                      kKVHeads * sizeof(unsigned long long));
+                                      kKVHeads * sizeof(MergeEntry));
 }
 
 void bind_workspace(AttnParams& p, void* workspace, int grid) {
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   p.part_o = reinterpret_cast<float*>(ws);
   p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
-  p.counters = reinterpret_cast<unsigned long long*>(
+  p.merges = reinterpret_cast<MergeEntry*>(
       ws + static_cast<size_t>(grid) * 2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
   p.grid = grid;
-  p.epoch = next_epoch();
 }
+
 
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
@@ -141,6 +140,29 @@ int launch_status() {
   return DSPARK_OK;
 }
 
+// The cut-item merge after an attention launch on the same stream, as a
+// programmatic dependent launch (its CTAs wait in griddepcontrol.wait for the
+// attention kernel's completion and memory); a plain launch where the
+// attribute is refused.
+int launch_merge(const AttnParams& p, cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(p.grid * kKVHeads));
+  cfg.blockDim = dim3(kMergeThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, split_merge_kernel, p) != cudaSuccess) {
+    cudaGetLastError();
+    cfg.numAttrs = 0;
+    if (cudaLaunchKernelEx(&cfg, split_merge_kernel, p) != cudaSuccess) return DSPARK_ERR_CUDA;
+  }
+  return launch_status();
+}
+
 struct KeySources {
   const void* ka;
   const void* va;
@@ -153,7 +175,7 @@ struct KeySources {
 // Shared launch path of every attention entry point; `fused` selects the
 // verify kernel that normalises/rotates q and produces the source-B rows.
 int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, void* workspace,
-                  size_t workspace_bytes, cudaStream_t stream, bool fused = false) {
+                  size_t workspace_bytes, cudaStream_t stream, bool fused = false, bool dependent = false) {
   DeviceInfo dev;
   int st = current_device_info(&dev);
   if (st != DSPARK_OK) return st;
@@ -186,13 +208,33 @@ int run_attention(AttnParams p, const KeySources& src, int dtype, int max_q, voi
     kb = ka;
     vb = va;
   }
-  if (fused)
+  if (dependent && p.causal && !fused) {
+    // programmatic dependent launch after the verify prep kernel: the schedule
+    // and the first loads of resident rows overlap the prep's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(grid));
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = kAttnSmemBytes;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaLaunchKernelEx(&cfg, attn_bf16_kernel<true, false>, ka, va, kb, vb, p) != cudaSuccess) {
+      cudaGetLastError();
+      cfg.numAttrs = 0;
+      if (cudaLaunchKernelEx(&cfg, attn_bf16_kernel<true, false>, ka, va, kb, vb, p) != cudaSuccess)
+        return DSPARK_ERR_CUDA;
+    }
+  } else if (fused)
     attn_bf16_kernel<true, true><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
   else if (p.causal)
     attn_bf16_kernel<true, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
   else
     attn_bf16_kernel<false, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, kb, vb, p);
-  return launch_status();
+  if ((st = launch_status()) != DSPARK_OK) return st;
+  return launch_merge(p, stream);
 }
 
 bool common_ok(const void* q, const void* out, const int32_t* cu_q, int num_requests, int total_q, float scale,
@@ -333,8 +375,10 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
                         const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
                         const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
                         void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
-                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, void* out,
-                        void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, int path,
+                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  if (path != DSPARK_VERIFY_AUTO && path != DSPARK_VERIFY_FUSED && path != DSPARK_VERIFY_PREP)
+    return DSPARK_ERR_INVALID_ARGUMENT;
   if (!common_ok(q_raw, out, cu_q, num_requests, total_q, scale, DSPARK_DTYPE_BF16) || !k_raw || !v_raw ||
       !q_norm_weight || !k_norm_weight || !rope_table || !aligned(rope_table, 16) || !slot_row || !ctx_len ||
       !resident_k || !resident_v ||
@@ -370,6 +414,26 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
   p.scratch_rows = scratch_rows;
   const uint8_t* rk = static_cast<const uint8_t*>(resident_k) + res_row0 * row_bytes;
   const uint8_t* rv = static_cast<const uint8_t*>(resident_v) + res_row0 * row_bytes;
+  const bool prep = path == DSPARK_VERIFY_PREP || (path == DSPARK_VERIFY_AUTO && total_q < kVerifyPrepMaxRows);
+  if (prep) {
+    // q_norm/k_norm + RoPE + KV append once per new row, then the plain causal
+    // kernel over [resident prefix ; scratch rows] with q read from `out` in
+    // place (an item's q rows are read only by its own contributors, and its
+    // output rows are written by its single CTA or by the merge kernel after
+    // every contributor has finished).
+    VerifyPrepParams vp{static_cast<const __nv_bfloat16*>(q_raw), static_cast<const __nv_bfloat16*>(k_raw),
+                        static_cast<const __nv_bfloat16*>(v_raw), static_cast<const __nv_bfloat16*>(q_norm_weight),
+                        static_cast<const __nv_bfloat16*>(k_norm_weight), static_cast<const uint32_t*>(rope_table),
+                        static_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(sk),
+                        reinterpret_cast<__nv_bfloat16*>(sv), total_q, eps};
+    const long long warps = static_cast<long long>(total_q) * 32;
+    verify_prep_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(vp);
+    int st = launch_status();
+    if (st != DSPARK_OK) return st;
+    p.q = out;
+    KeySources src{rk, rv, rows_per_layer, sk, sv, scratch_rows};
+    return run_attention(p, src, DSPARK_DTYPE_BF16, max_q, workspace, workspace_bytes, stream, false, true);
+  }
   // Source B = the raw new-row projections; the kernel normalises/rotates them
   // in shared memory and writes the scratch rows itself.
   KeySources src{rk, rv, rows_per_layer, k_raw, v_raw, total_q};
@@ -473,6 +537,62 @@ int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab
   p.tiles = (vocab + markov::kVocabTile - 1) / markov::kVocabTile;
   const int grid = p.tiles < dev.sms ? p.tiles : dev.sms;
   markov::markov_step_kernel<<<grid, markov::kThreads, markov::kSmemBytes, stream>>>(wm, p);
+  return launch_status();
+}
+
+int dspark_draft_append(const void* context, int rows, int hidden, const void* kv_weight, int num_layers,
+                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_rows,
+                        const int32_t* slot_row, const int32_t* ctx_len, const int32_t* count, int num_requests,
+                        void* const* pool_k, void* const* pool_v, long long pool_rows, long long trash_row,
+                        cudaStream_t stream) {
+  if (!context || !kv_weight || !k_norm_weight || !rope_table || !cu_rows || !slot_row || !ctx_len || !count ||
+      !pool_k || !pool_v || rows < 1 || hidden < 64 || hidden % 64 != 0 || num_layers < 1 ||
+      num_layers > append::kMaxLayers || num_requests < 1 || !(eps > 0.f) || pool_rows < 1 ||
+      pool_rows >= (1ll << 40) || trash_row < 0 || trash_row >= pool_rows || !aligned(context, 16) ||
+      !aligned(kv_weight, 16) || !aligned(rope_table, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  for (int l = 0; l < num_layers; ++l)
+    if (!pool_k[l] || !pool_v[l] || !aligned(pool_k[l], 16) || !aligned(pool_v[l], 16))
+      return DSPARK_ERR_INVALID_ARGUMENT;
+  DeviceInfo dev;
+  int st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  CUtensorMap cm, wm;
+  cuuint32_t box[2] = {64, 128};
+  cuuint32_t estr[2] = {1, 1};
+  cuuint64_t cdims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(rows)};
+  cuuint64_t wdims[2] = {static_cast<cuuint64_t>(hidden), static_cast<cuuint64_t>(num_layers) * 2 * 1024};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(hidden) * 2};
+  if (g_encode(&cm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(context), cdims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS ||
+      g_encode(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(kv_weight), wdims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return DSPARK_ERR_CUDA;
+  append::Params p{};
+  p.k_norm_w = static_cast<const __nv_bfloat16*>(k_norm_weight);
+  p.rope = static_cast<const uint32_t*>(rope_table);
+  p.cu_rows = cu_rows;
+  p.slot_row = slot_row;
+  p.ctx_len = ctx_len;
+  p.count = count;
+  for (int l = 0; l < num_layers; ++l) {
+    p.pool_k[l] = static_cast<__nv_bfloat16*>(pool_k[l]);
+    p.pool_v[l] = static_cast<__nv_bfloat16*>(pool_v[l]);
+  }
+  p.trash_row = trash_row;
+  p.pool_rows = pool_rows;
+  p.num_requests = num_requests;
+  p.rows = rows;
+  p.k_chunks = hidden / 64;
+  p.head_tiles = num_layers * 16;
+  p.row_tiles = (rows + append::kTileRows - 1) / append::kTileRows;
+  p.eps = eps;
+  const long long tiles = static_cast<long long>(p.row_tiles) * p.head_tiles;
+  if (tiles >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
+  const int grid = tiles < dev.sms ? static_cast<int>(tiles) : dev.sms;
+  append::draft_append_kernel<<<grid, append::kThreads, append::kSmemBytes, stream>>>(cm, wm, p);
   return launch_status();
 }
 
@@ -599,7 +719,7 @@ namespace {
 constexpr int kNoAllocMaxCtas = 148;
 constexpr size_t kNoAllocScratchBytes = workspace_for_grid(kNoAllocMaxCtas);
 
-// 148 CTAs x (2 x 66 KB of fp32 partials + 64 B of counters) = 18.8 MiB. Every
+// 148 CTAs x (2 x 66 KB of fp32 partials + 384 B of merge entries) = 18.8 MiB. Every
 // GPU that loads this library holds it until the process exits.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
@@ -645,5 +765,6 @@ extern "C" int dspark_varlen_attn_noalloc(const void* q, const void* k, const vo
   if ((st = encode_kv_map(&ka, k, key_rows)) != DSPARK_OK) return st;
   if ((st = encode_kv_map(&va, v, key_rows)) != DSPARK_OK) return st;
   attn_bf16_kernel<true, false><<<grid, kAttnThreads, kAttnSmemBytes, stream>>>(ka, va, ka, va, p);
-  return launch_status();
+  if ((st = launch_status()) != DSPARK_OK) return st;
+  return launch_merge(p, stream);
 }

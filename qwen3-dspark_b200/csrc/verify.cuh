@@ -34,6 +34,81 @@ __global__ void __launch_bounds__(256) rope_table_kernel(const float* __restrict
   table[static_cast<size_t>(row) * 64 + f] = pack_bf16x2(cs, sn);
 }
 
+// Verify-layer preparation of the new rows, shared by every tile that reads
+// them: q_norm + RoPE of the raw q projections (written to q_out, which the
+// attention kernel then reads), k_norm + RoPE of the raw k and a copy of the
+// raw v into this layer's scratch rows (the KV append). transformers' order of
+// bf16 roundings (modeling_qwen3.py:59-64,136-156): RMSNorm in fp32, cast to
+// bf16, times the bf16 weight; each RoPE product and the sum rounded to bf16.
+// One warp per (row, vector) with 32 vectors per row (16 q heads, 8 k, 8 v);
+// lane l holds d = 4l..4l+3 and its rotate-half partner d +- 64 is lane l ^ 16.
+struct VerifyPrepParams {
+  const __nv_bfloat16* q_raw;   // [total_q, 16, 128]
+  const __nv_bfloat16* k_raw;   // [total_q, 8, 128]
+  const __nv_bfloat16* v_raw;
+  const __nv_bfloat16* q_w;     // [128]
+  const __nv_bfloat16* k_w;
+  const uint32_t* rope;         // [total_q, 64] bf16 cos | bf16 sin << 16
+  __nv_bfloat16* q_out;         // [total_q, 16, 128]
+  __nv_bfloat16* scratch_k;     // this layer's scratch, row r = new row r
+  __nv_bfloat16* scratch_v;
+  int total_q;
+  float eps;
+};
+
+__global__ void __launch_bounds__(256) verify_prep_kernel(const VerifyPrepParams p) {
+  asm volatile("griddepcontrol.launch_dependents;");
+  const int wid = static_cast<int>(blockIdx.x) * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  const int row = wid >> 5, vec = wid & 31;
+  if (row >= p.total_q) return;
+  const int d0 = lane * 4;
+  const __nv_bfloat16* src;
+  __nv_bfloat16* dst;
+  const __nv_bfloat16* w = nullptr;
+  if (vec < kQHeads) {
+    src = p.q_raw + (static_cast<size_t>(row) * kQHeads + vec) * kHeadDim;
+    dst = p.q_out + (static_cast<size_t>(row) * kQHeads + vec) * kHeadDim;
+    w = p.q_w;
+  } else if (vec < kQHeads + kKVHeads) {
+    src = p.k_raw + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads) * kHeadDim;
+    dst = p.scratch_k + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads) * kHeadDim;
+    w = p.k_w;
+  } else {
+    src = p.v_raw + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads - kKVHeads) * kHeadDim;
+    dst = p.scratch_v + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads - kKVHeads) * kHeadDim;
+  }
+  const uint2 raw = *reinterpret_cast<const uint2*>(src + d0);
+  if (w == nullptr) {                       // warp-uniform: v rows are copied as they are
+    *reinterpret_cast<uint2*>(dst + d0) = raw;
+    return;
+  }
+  const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
+  float x[4] = {a.x, a.y, b.x, b.y};
+  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+  const uint2 wr = *reinterpret_cast<const uint2*>(w + d0);
+  const float2 wa = unpack_bf16x2(wr.x), wb = unpack_bf16x2(wr.y);
+  const float wv[4] = {wa.x, wa.y, wb.x, wb.y};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = bf16r(wv[i] * bf16r(x[i] * rs));
+  const uint4 cs = *reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(row) * 64 + (d0 & 63));
+  const uint32_t cw[4] = {cs.x, cs.y, cs.z, cs.w};
+  const bool lower = lane < 16;             // d < 64: partner d + 64 is lane + 16
+  float y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float partner = __shfl_xor_sync(0xffffffffu, x[i], 16);
+    const float2 c = unpack_bf16x2(cw[i]);  // .x cos, .y sin
+    y[i] = lower ? bf16r(bf16r(x[i] * c.x) + bf16r(-partner * c.y)) : bf16r(bf16r(x[i] * c.x) + bf16r(partner * c.y));
+  }
+  uint2 res;
+  res.x = pack_bf16x2(y[0], y[1]);
+  res.y = pack_bf16x2(y[2], y[3]);
+  *reinterpret_cast<uint2*>(dst + d0) = res;
+}
+
 struct CommitParams {
   uint4* resident_k;             // [layers * rows_per_layer, 8, 128] of bf16 or fp32
   uint4* resident_v;

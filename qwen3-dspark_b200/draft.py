@@ -25,7 +25,7 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import HEAD_DIM, HKV, HQ, markov_greedy, segment_attention
+from .kernels import HEAD_DIM, HKV, HQ, draft_append, markov_greedy, segment_attention
 from .kv_store import _upload
 
 
@@ -148,7 +148,9 @@ class B200PackedDraft:
         if rows[-1] >= 2 ** 31:
             raise ValueError('Draft pool rows exceed the int32 row index')
         self.capacities, self.slot_rows = tuple(caps), tuple(rows[:-1])
-        shape = (rows[-1], HKV, HEAD_DIM)
+        # one extra row no slot owns: the fixed-shape append writes its unused rows there
+        self.trash_row = rows[-1]
+        shape = (rows[-1] + 1, HKV, HEAD_DIM)
         self.pool_k = [torch.zeros(shape, dtype=self.kv_dtype, device=self.device) for _ in draft.layers]
         self.pool_v = [torch.zeros(shape, dtype=self.kv_dtype, device=self.device) for _ in draft.layers]
         self._slots = {}          # request -> slot index
@@ -192,13 +194,62 @@ class B200PackedDraft:
         return tuple((k[r0:r0 + n].clone(), v[r0:r0 + n].clone()) for k, v in zip(self.pool_k, self.pool_v))
 
     # -- context append (packed_draft.py:129-168) ---------------------------------
+    def _fused_append_ready(self):
+        d = self.draft
+        att = d.layers[0].attention
+        return (self.kv_dtype == torch.bfloat16 and d.fc.weight.dtype == torch.bfloat16
+                and att.k_proj.bias is None and att.v_proj.bias is None and len(d.layers) <= 8
+                and d.fc.out_features % 64 == 0 and float(getattr(d.rotary, 'attention_scaling', 1.0)) == 1.0)
+
+    def _append_operands(self):
+        """Stacked [k_proj; v_proj] weights of every layer, the stacked k_norm weights and
+        the float32 rotary frequencies for the fused append, rebuilt when one changes. A captured append reads
+        the stacks made when it was captured."""
+        d = self.draft
+        params = [t for layer in d.layers for t in (layer.attention.k_proj.weight, layer.attention.v_proj.weight,
+                                                    layer.attention.k_norm.weight)] + [d.rotary.inv_freq]
+        key = tuple((t.data_ptr(), t._version) for t in params)
+        if getattr(self, '_append_key', None) != key:
+            self._kv_weight = torch.cat([torch.cat((layer.attention.k_proj.weight, layer.attention.v_proj.weight))
+                                         for layer in d.layers]).contiguous()
+            self._k_norm_w = torch.stack([layer.attention.k_norm.weight for layer in d.layers]).contiguous()
+            # the rotary module's frequencies in float32, as its forward uses them
+            self._inv_freq = d.rotary.inv_freq.float().contiguous()
+            self._append_key = key
+        return self._kv_weight, self._k_norm_w, self._inv_freq
+
+    def _append_rows(self, feat, meta, r, n):
+        """Project n feature rows [1, n, F] and write them into the pool. ``meta`` is an
+        int32 device vector [4r + 1]: cu_rows (r + 1), slot_row, ctx_len, count (r each);
+        row j of request i sits at position ctx_len[i] + j and is written to its slot
+        when j < count[i], else to the trash row. No host reads: capturable."""
+        d = self.draft
+        context = d.context_norm(d.fc(feat.to(d.fc.weight.dtype)))
+        if self._fused_append_ready():
+            kv_weight, k_norm_w, inv_freq = self._append_operands()
+            draft_append(context[0], kv_weight, k_norm_w, inv_freq, meta, r, self.pool_k, self.pool_v,
+                         self.trash_row, d.layers[0].attention.k_norm.variance_epsilon)
+            return
+        cu, slot, ctx, cnt = (meta[:r + 1].long(), meta[r + 1:2 * r + 1].long(), meta[2 * r + 1:3 * r + 1].long(),
+                              meta[3 * r + 1:].long())
+        g = torch.arange(n, device=self.device)
+        i = torch.searchsorted(cu[1:].contiguous(), g, right=True)
+        j = g - cu[i]
+        pos = ctx[i] + j
+        cos, sin = d.rotary(context, pos[None])
+        idx = torch.where(j < cnt[i], slot[i] + pos, torch.full_like(pos, self.trash_row))
+        for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
+            k, v = layer.attention.project_kv(context, cos, sin)
+            pk.index_copy_(0, idx, k.to(self.kv_dtype))
+            pv.index_copy_(0, idx, v.to(self.kv_dtype))
+
     @torch.no_grad()
     def append_committed(self, chunks):
         """Project committed target features [1, n, F] once and write K/V rows in place."""
         if not chunks:
             raise ValueError('Require at least one committed feature chunk')
         d = self.draft
-        features, positions, rows, new_lengths = [], [], [], {}
+        features, cu, slots, starts, counts = [], [0], [], [], []
         for request, value in chunks.items():
             self._request(request)
             if (not isinstance(value, torch.Tensor) or value.ndim != 3 or value.shape[0] != 1 or value.shape[1] < 1
@@ -210,21 +261,86 @@ class B200PackedDraft:
             if start + n > self.capacities[slot]:
                 raise ValueError('Draft context exceeds the request slot capacity')
             features.append(value)
-            positions.extend(range(start, start + n))
-            rows.extend(range(self.slot_rows[slot] + start, self.slot_rows[slot] + start + n))
-            new_lengths[request] = start + n
-        context = d.context_norm(d.fc(torch.cat(features, dim=1).to(d.fc.weight.dtype)))
-        pos = torch.tensor(positions, dtype=torch.long, device=self.device)
-        cos, sin = d.rotary(context, pos[None])
-        idx = torch.tensor(rows, dtype=torch.long, device=self.device)
-        for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
-            k, v = layer.attention.project_kv(context, cos, sin)
-            pk.index_copy_(0, idx, k.to(self.kv_dtype))
-            pv.index_copy_(0, idx, v.to(self.kv_dtype))
-        self._lengths.update(new_lengths)
-        self.last_projection_work = dict(requests=len(chunks), new_context_tokens=len(positions),
-                                         context_projection_calls=1, kv_projection_calls=len(d.layers),
+            cu.append(cu[-1] + n)
+            slots.append(self.slot_rows[slot])
+            starts.append(start)
+            counts.append(n)
+        r = len(chunks)
+        meta = _upload(cu + slots + starts + counts, self.device)
+        self._append_rows(torch.cat(features, dim=1), meta, r, cu[-1])
+        for request, n in zip(chunks, counts):
+            self._lengths[request] += n
+        self.last_projection_work = dict(requests=r, new_context_tokens=cu[-1], context_projection_calls=1,
+                                         kv_projection_calls=1 if self._fused_append_ready() else len(d.layers),
                                          cache_concatenation_kv_bytes=0)
+
+    # -- fixed-shape append of whole verified chunks (capturable) -------------------
+    def _verified_meta(self, requests, counts, q):
+        for request in requests:
+            self._request(request)
+        n = [int(c) for c in counts]
+        if len(n) != len(requests) or any(not 0 <= c <= q for c in n) or any(
+                self._lengths[x] + c > self.capacities[self._slots[x]] for x, c in zip(requests, n)):
+            raise ValueError('Committed counts must lie in [0, q] and fit the slot capacity')
+        r = len(requests)
+        host = ([q * i for i in range(r + 1)] + [self.slot_rows[self._slots[x]] for x in requests]
+                + [self._lengths[x] for x in requests] + n)
+        return host, n
+
+    @torch.no_grad()
+    def append_verified(self, features, requests, counts):
+        """``append_committed`` of a round whose verified chunks all have q rows:
+        ``features`` [1, len(requests) * q, F] in request order, of which the first
+        ``counts[i]`` rows of request i are committed. Fixed shapes and no host-side
+        slicing: every row is projected, uncommitted rows go to the trash row."""
+        r = len(requests)
+        if (features.ndim != 3 or r < 1 or features.shape[1] % r or features.shape[1] == 0
+                or features.shape[2] != self.draft.fc.in_features or features.device != self.device):
+            raise ValueError('Expected [1, requests * q, target_features] verified features')
+        q = features.shape[1] // r
+        host, n = self._verified_meta(requests, counts, q)
+        self._append_rows(features, _upload(host, self.device), r, r * q)
+        for request, c in zip(requests, n):
+            self._lengths[request] += c
+
+    @torch.no_grad()
+    def capture_append(self, num_requests, width):
+        """Capture ``append_verified`` for ``num_requests`` chunks of ``width`` rows
+        into a CUDA graph reading fixed feature and metadata buffers."""
+        graphs = self.__dict__.setdefault('_append_graphs', {})
+        key = (num_requests, width)
+        if key in graphs:
+            raise ValueError('Append shape already captured')
+        r, q = num_requests, width
+        feat = torch.zeros((1, r * q, self.draft.fc.in_features), dtype=self.draft.fc.weight.dtype,
+                           device=self.device)
+        host = [q * i for i in range(r + 1)] + [self.trash_row] * r + [0] * r + [0] * r
+        meta = torch.tensor(host, dtype=torch.int32, device=self.device)   # warm-up writes only the trash row
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):
+            self._append_rows(feat, meta, r, r * q)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            self._append_rows(feat, meta, r, r * q)
+        graphs[key] = dict(graph=graph, feat=feat, meta=meta)
+        return graph
+
+    @torch.no_grad()
+    def append_verified_graph(self, features, requests, counts):
+        """``append_verified`` through the program captured for its shape."""
+        r = len(requests)
+        q = features.shape[1] // max(r, 1)
+        ex = self.__dict__.get('_append_graphs', {}).get((r, q))
+        if ex is None or features.shape != ex['feat'].shape:
+            raise ValueError('Capture the append shape first')
+        host, n = self._verified_meta(requests, counts, q)
+        ex['feat'].copy_(features)
+        ex['meta'].copy_(torch.tensor(host, dtype=torch.int32).pin_memory(), non_blocking=True)
+        ex['graph'].replay()
+        for request, c in zip(requests, n):
+            self._lengths[request] += c
 
     # -- backbone (packed_draft.py:186-252) -----------------------------------------
     @torch.no_grad()
@@ -329,8 +445,11 @@ class B200PackedDraft:
         return graph
 
     @torch.no_grad()
-    def propose_greedy_graph(self, anchors):
-        """``propose_greedy`` through the program captured for ``len(anchors)`` requests."""
+    def propose_greedy_graph(self, anchors, on_device=False):
+        """``propose_greedy`` through the program captured for ``len(anchors)`` requests.
+        ``on_device`` returns the program's output buffers (tokens [R, block] int64,
+        confidences [R, block] float32, valid until the next replay) without a host
+        read."""
         ex = self.__dict__.get('_graphs', {}).get(len(anchors))
         if ex is None:
             raise ValueError('Capture the request count first')
@@ -351,6 +470,8 @@ class B200PackedDraft:
         ex['pos'].copy_(torch.tensor(positions, dtype=torch.long).pin_memory(), non_blocking=True)
         ex['anchors'].copy_(torch.cat([anchors[q].view(1) for q in requests]))
         ex['graph'].replay()
+        if on_device:
+            return ex['tokens'], ex['conf']
         toks, confs = ex['tokens'].tolist(), ex['conf'].tolist()
         return {q: (toks[i], confs[i]) for i, q in enumerate(requests)}
 

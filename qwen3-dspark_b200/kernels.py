@@ -334,3 +334,43 @@ def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, 
                 float(conf_bias), tokens[r0:].data_ptr(), conf[r0:].data_ptr(), block_size, n, scratch.data_ptr(),
                 stream), 'dspark_markov_step')
     return tokens, conf
+
+
+def draft_append(context, kv_weight, k_norm_weight, inv_freq, meta, num_requests, pool_k, pool_v, trash_row, eps):
+    """Fused draft-context append (``dspark_rope_table`` + ``dspark_draft_append``):
+    every layer's k = RoPE(k_norm(k_proj(context))) and v = v_proj(context) of the
+    context rows, written into the layer's pool (PackedDraft.append_committed's
+    project_kv + cache concatenation, dspark_qwen/packed_draft.py:146-158).
+
+    ``context`` [n, hidden] bf16 (fc + context_norm output), ``kv_weight``
+    [layers * 2048, hidden] bf16 (per layer k_proj then v_proj weight rows),
+    ``k_norm_weight`` [layers, 128] bf16, ``inv_freq`` [64] float32, ``meta`` int32
+    [4R + 1] on the device: cu_rows (R + 1), slot_row, ctx_len, count (R each).
+    ``pool_k``/``pool_v``: per-layer [pool_rows, 8, 128] bf16 pools; row j of request
+    i lands in slot_row[i] + ctx_len[i] + j when j < count[i], else in ``trash_row``.
+    """
+    import ctypes
+    device = context.device
+    n, hidden = context.shape
+    layers = len(pool_k)
+    for x in (context, kv_weight, k_norm_weight, *pool_k, *pool_v):
+        if x.dtype != torch.bfloat16 or not x.is_contiguous() or x.device != device:
+            raise ValueError('Draft append operands must be contiguous bf16 on one device')
+    rows = pool_k[0].shape[0]
+    if (kv_weight.shape != (layers * 2 * HKV * HEAD_DIM, hidden) or k_norm_weight.shape != (layers, HEAD_DIM)
+            or len(pool_v) != layers or any(t.shape != (rows, HKV, HEAD_DIM) for t in (*pool_k, *pool_v))
+            or meta.dtype != torch.int32 or meta.shape != (4 * num_requests + 1,) or meta.device != device
+            or inv_freq.dtype != torch.float32 or inv_freq.shape != (HEAD_DIM // 2,) or inv_freq.device != device):
+        raise ValueError('Draft append shapes do not match')
+    table = torch.empty((n, HEAD_DIM // 2), dtype=torch.int32, device=device)
+    r = num_requests
+    lib, stream = _lib.load_library(), _stream(device)
+    _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), meta.data_ptr(), meta[2 * r + 1:].data_ptr(), r, n,
+                                     table.data_ptr(), stream), 'dspark_rope_table')
+    pk = (ctypes.c_void_p * layers)(*[t.data_ptr() for t in pool_k])
+    pv = (ctypes.c_void_p * layers)(*[t.data_ptr() for t in pool_v])
+    _lib.check(lib.dspark_draft_append(context.data_ptr(), n, hidden, kv_weight.data_ptr(), layers,
+                                       k_norm_weight.data_ptr(), table.data_ptr(), float(eps), meta.data_ptr(),
+                                       meta[r + 1:].data_ptr(), meta[2 * r + 1:].data_ptr(),
+                                       meta[3 * r + 1:].data_ptr(), r, pk, pv, rows, int(trash_row), stream),
+               'dspark_draft_append')

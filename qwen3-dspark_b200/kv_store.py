@@ -297,12 +297,15 @@ class B200PersistentTargetKV:
 
     @torch.no_grad()
     def verify_layer(self, tx, layer, q_raw, k_raw, v_raw, q_norm_weight, k_norm_weight, *, inv_freq,
-                     eps=1e-6, scale=SCALE, out=None):
+                     eps=1e-6, scale=SCALE, out=None, path='auto'):
         """Fused verify for one decoder layer; returns attention output [sum Q, 16, 128].
 
         ``q_raw``/``k_raw``/``v_raw`` are the layer's q/k/v projections of the new
         tokens before q_norm/k_norm/RoPE ([sum Q, 16|8, 128] bf16); norm weights [128]
         bf16; ``inv_freq`` [64] float32 on this device (see ``rope_inv_freq``).
+        ``path``: 'fused' (norm/RoPE/append inside the attention kernel), 'prep' (a
+        prep kernel per layer, then the attention kernel) or 'auto' (prep below 512
+        new rows); all give the same values.
         """
         self._transaction(tx)
         if type(layer) is not int or not 0 <= layer < self.layers or layer in self._staged:
@@ -343,8 +346,8 @@ class B200PersistentTargetKV:
             ctx.data_ptr(), len(tx.query_lengths), n, max(tx.query_lengths), self._keys.data_ptr(),
             self._values.data_ptr(),
             self.rows_per_layer, self.scratch_keys.data_ptr(), self.scratch_values.data_ptr(),
-            self.max_query_tokens, self.layers, layer, float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(),
-            stream), 'dspark_verify_fused')
+            self.max_query_tokens, self.layers, layer, float(scale), _lib.VERIFY_PATHS[path], out.data_ptr(),
+            ws.data_ptr(), ws.numel(), stream), 'dspark_verify_fused')
         self._staged.add(layer)
         return out
 

@@ -40,20 +40,22 @@ def accept_greedy(proposals, predictions, eos_ids=()):
     return accepted, committed
 
 
-def _accept_on_device(target, verified, chunks, proposals, output, max_new_tokens, eos_ids):
+def _pinned(values, dtype, device):
+    """Host list -> device tensor through pinned memory, without a host wait."""
+    return torch.tensor(values, dtype=dtype).pin_memory().to(device, non_blocking=True)
+
+
+def _accept_on_device(target, verified, ids, active, width, output, max_new_tokens, eos_ids):
     """One round's acceptance with the on-device argmax + accept kernels: the host
-    reads back one small int64 vector (counts and committed tokens) per round."""
+    reads back one small int64 vector (counts and committed tokens) per round.
+    ``ids`` [R, width] are the verified chunks (anchor, proposals) in ``active`` order."""
     from .kernels import greedy_accept
-    active = list(chunks)
     logits = target.model.get_output_embeddings()(verified.last)[0]
-    tokens = torch.cat(tuple(chunks.values()), dim=1)[0]
-    cu = [0]
-    for r in active:
-        cu.append(cu[-1] + chunks[r].shape[1])
+    tokens = ids.reshape(-1)
+    cu = [width * i for i in range(len(active) + 1)]
     dev = logits.device
-    cu_q = torch.tensor(cu, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-    budget = torch.tensor([max_new_tokens - len(output[r]) for r in active], dtype=torch.int32)
-    budget = budget.pin_memory().to(dev, non_blocking=True)
+    cu_q = _pinned(cu, torch.int32, dev)
+    budget = _pinned([max_new_tokens - len(output[r]) for r in active], torch.int32, dev)
     _pred, accepted, n_commit, emitted = greedy_accept(logits, tokens, cu_q, eos_ids, budget)
     host = torch.cat((accepted.long(), n_commit.long(), emitted)).cpu().tolist()
     n = len(active)
@@ -89,31 +91,35 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
     draft.append_committed({r: features.context_for(r) for r in prompts})
     active = [r for r in prompts if output[r][-1] not in eos_ids and max_new_tokens > 1]
     rounds = []
+    width = draft.draft.spec.block_size + 1
     while active:
-        anchors = {r: torch.tensor([[output[r][-1]]], dtype=torch.long, device=target.device) for r in active}
+        # one upload of the anchors; the chunks are rows of one device tensor
+        anchor_ids = _pinned([output[r][-1] for r in active], torch.long, target.device)
+        anchors = {r: anchor_ids[i].view(1, 1) for i, r in enumerate(active)}
         if graph and getattr(draft, '_graph_ready', lambda: False)():
             if len(anchors) not in draft.__dict__.get('_graphs', {}):
                 draft.capture_propose(len(anchors))
-            proposed = draft.propose_greedy_graph(anchors)
+            proposed, _conf = draft.propose_greedy_graph(anchors, on_device=True)
+            ids = torch.cat((anchor_ids[:, None], proposed), dim=1)        # no host read of the proposals
         else:
             proposed = draft.propose_greedy(anchors)
-        proposals = {r: toks for r, (toks, _conf) in proposed.items()}
-        chunks = {r: torch.tensor([[output[r][-1]] + proposals[r]], dtype=torch.long, device=target.device)
-                  for r in active}
+            ids = _pinned([[output[r][-1]] + proposed[r][0] for r in active], torch.long, target.device)
+        chunks = {r: ids[i:i + 1] for i, r in enumerate(active)}
         if graph:
-            bucket = QueryBucket(tuple(c.shape[1] for c in chunks.values()))
+            bucket = QueryBucket((width,) * len(active))
             if bucket not in target._graphs:
                 target.capture(bucket)
             verified = target.verify_graph(chunks, bucket)
         else:
             verified = target.verify(chunks)
         if device_accept:
-            decided = _accept_on_device(target, verified, chunks, proposals, output, max_new_tokens, eos_ids)
+            decided = _accept_on_device(target, verified, ids, active, width, output, max_new_tokens, eos_ids)
         else:
             logits = target.predict(verified)
+            host_ids = ids.tolist()
             decided = {}
-            for r, v in logits.items():
-                accepted, committed = accept_greedy(proposals[r], v[0].argmax(-1).tolist(), eos_ids)
+            for i, (r, v) in enumerate(logits.items()):
+                accepted, committed = accept_greedy(host_ids[i][1:], v[0].argmax(-1).tolist(), eos_ids)
                 decided[r] = (accepted, committed[:max_new_tokens - len(output[r])])
         commit, stats = {}, {}
         for r in active:
@@ -122,7 +128,14 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
             commit[r] = len(committed)          # old anchor .. newest-1 are now committed KV
             stats[r] = dict(accepted=accepted, committed=len(committed))
         target.commit(verified, commit)
-        draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
+        counts = [commit[r] for r in active]
+        if graph and hasattr(draft, 'capture_append'):
+            # whole verified chunks through the captured fixed-shape append
+            if (len(active), width) not in draft.__dict__.get('_append_graphs', {}):
+                draft.capture_append(len(active), width)
+            draft.append_verified_graph(verified.context, tuple(active), counts)
+        else:
+            draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
         rounds.append(stats)
         active = [r for r in active if len(output[r]) < max_new_tokens and output[r][-1] not in eos_ids]
     return output, rounds

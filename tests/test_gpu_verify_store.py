@@ -1,4 +1,5 @@
-"""GPU parity of the fused verify layer (QK-norm + RoPE + KV append + attention) and commit/rollback.
+"""GPU parity of the verify layer (QK-norm + RoPE + KV append + attention) and commit/rollback,
+through both the fused kernel and the prep-kernel path.
 
 Checked against the oracle: ``qk_norm_rope_bf16`` for the appended K (bf16, at
 most one bf16 ulp from transformers' float32 transcendental rounding), the
@@ -39,8 +40,9 @@ def make_store(pkg, layers, caps, max_q, g):
     return store, oracle
 
 
+@pytest.mark.parametrize('path', ['fused', 'prep'])
 @pytest.mark.parametrize('weights', ['ones', 'random'])
-def test_fused_verify_commit_rollback(pkg, weights):
+def test_fused_verify_commit_rollback(pkg, weights, path):
     g = I.rng(7 if weights == 'ones' else 8)
     layers = 3
     contexts = [0, 1, 300, 2047, 64]
@@ -70,7 +72,7 @@ def test_fused_verify_commit_rollback(pkg, weights):
             qw = f32_to_bf16_bits(1 + 0.1 * I.normal(g, (128,)))
             kw = f32_to_bf16_bits(1 + 0.1 * I.normal(g, (128,)))
         out = store.verify_layer(tx, layer, bits_to_dev(qr), bits_to_dev(kr), bits_to_dev(vr), bits_to_dev(qw),
-                                 bits_to_dev(kw), inv_freq=inv, eps=I.RMS_EPS)
+                                 bits_to_dev(kw), inv_freq=inv, eps=I.RMS_EPS, path=path)
         torch.cuda.synchronize()
         q_o, k_o = qk_norm_rope_bf16(qr, kr, qw, kw, positions, I.ROPE_THETA, I.RMS_EPS)
         # KV append: scratch rows hold roped k and raw v of this layer.
