@@ -133,7 +133,8 @@ int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t*
  * 1-2 as a small kernel once per new row (q written to `out`, which the
  * attention kernel then reads in place) and the attention as its programmatic
  * dependent, which pays off for small launches where every CTA would repeat
- * the q prologue; DSPARK_VERIFY_AUTO takes PREP below 512 new rows. Resident
+ * the q prologue; DSPARK_VERIFY_AUTO takes PREP below 512 new rows or when a
+ * request has more than 16 (prefill chunks). Resident
  * K/V: [num_layers * rows_per_layer, 8, 128]; scratch K/V:
  * [num_layers * scratch_rows, 8, 128]; k_raw/v_raw: [total_q, 8, 128].
  * Replaces, per decoder layer, transformers Qwen3Attention.forward's

@@ -23,11 +23,15 @@
 // (a row no request owns): a fixed-shape append of whole verified chunks then
 // writes only the committed rows, with no host-side slicing.
 //
-// Roles (192 threads, persistent CTAs over (row tile, head tile) pairs):
-//   warps 0-3  epilogue (thread m = tile row m = TMEM lane m);
-//   warp 4     TMEM owner and MMA issuer (one thread), two 128-column
+// Roles (320 threads, persistent CTAs over (row tile, head tile) pairs):
+//   warps 0-7  epilogue: warp w reads TMEM lanes 32(w%4).. (tile rows) and writes
+//              half w/4 of the head: d in [32h, 32h+32) and the rotate partners
+//              d + 64, so each RoPE pair is thread-local; for k_norm's sum of
+//              squares it also reads the row's other 64 values (TMEM reads are
+//              cheap, and the two warps never wait on each other);
+//   warp 8     TMEM owner and MMA issuer (one thread), two 128-column
 //              accumulators so one tile's epilogue overlaps the next one's MMAs;
-//   warp 5     TMA producer: context and weight 64-wide K chunks, six stages.
+//   warp 9     TMA producer: context and weight 64-wide K chunks, six stages.
 #pragma once
 #include "train.cuh"
 #include "verify.cuh"
@@ -46,7 +50,9 @@ using train::umma_bf16;
 using train::umma_commit;
 using train::wait_or_abort;
 
-constexpr int kThreads = 192;
+constexpr int kEpilogueWarps = 8;
+constexpr int kMmaWarp = kEpilogueWarps, kTmaWarp = kEpilogueWarps + 1;
+constexpr int kThreads = (kEpilogueWarps + 2) * 32;
 constexpr int kTileRows = 128;        // context rows per tile (MMA M)
 constexpr int kHeadCols = 128;        // one head (MMA N)
 constexpr int kStages = 6;
@@ -57,7 +63,8 @@ enum Barrier { kBarFull0 = 0, kBarEmpty0 = kStages, kBarDFull0 = 2 * kStages, kB
                kBarDrain, kNumBarriers };
 constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemSlot + 4;
-constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 4;
+constexpr uint32_t kSmemNormW = kSmemAbort + 12;                    // float [kMaxLayers][128]
+constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
 constexpr uint32_t kTmemCols = 256;
 
 struct Params {
@@ -76,6 +83,7 @@ struct Params {
   int k_chunks;                       // hidden / 64
   int head_tiles;                     // layers * 16
   int row_tiles;
+  int layers;
   float eps;
 };
 
@@ -100,16 +108,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  constexpr uint32_t kEpiThreads = kEpilogueWarps * 32;
+  float* norm_w = reinterpret_cast<float*>(smem + kSmemNormW);
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBarriers; ++i) mbar_init(bar(i), (i == kBarDFree0 || i == kBarDFree1) ? 128u : 1u);
+    for (int i = 0; i < kNumBarriers; ++i)
+      mbar_init(bar(i), (i == kBarDFree0 || i == kBarDFree1) ? kEpiThreads : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5 && lane == 0) {
+  for (int i = threadIdx.x; i < p.layers * 128; i += kThreads) norm_w[i] = __bfloat162float(p.k_norm_w[i]);
+  if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&cmap);
     prefetch_tmap(&wmap);
   }
-  if (warp == 4) tmem_alloc(sbase + kSmemSlot, kTmemCols);
+  if (warp == kMmaWarp) tmem_alloc(sbase + kSmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -118,8 +130,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int n_mine = tiles > static_cast<int>(blockIdx.x)
                          ? (tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
 
-  if (warp < 4) {
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+  if (warp < kEpilogueWarps) {
+    const int quarter = warp & 3, half = warp >> 2;
+    const int m = quarter * 32 + lane;                  // tile row of this thread
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
     bool ok = true;
     int cur_rt = -1;
     long long dest = -1;
@@ -131,7 +145,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int layer = ht >> 4, is_v = (ht >> 3) & 1, head = ht & 7;
       if (rt != cur_rt) {                       // destination row of this thread's input row
         cur_rt = rt;
-        g = rt * kTileRows + static_cast<int>(threadIdx.x);
+        g = rt * kTileRows + m;
         dest = -1;
         if (g < p.rows) {
           const int i = min(find_request(p.cu_rows, p.num_requests + 1, g), p.num_requests - 1);
@@ -143,6 +157,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      // this row's cos/sin for d in [32 half, 32 half + 32), fetched before the wait
+      uint4 cs4[8];
+      if (!is_v) {
+        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64 +
+                                                         half * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) cs4[q] = __ldg(cs + q);
+      }
       ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
@@ -151,52 +173,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                            head * kHeadDim;
       if (is_v) {
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float d[32];
-          tmem_ld32(acc + c * 32, d);
-          if (dest >= 0) store_row32(out + c * 32, d);
+          tmem_ld32(acc + half * 64 + c * 32, d);
+          if (dest >= 0) store_row32(out + half * 64 + c * 32, d);
         }
       } else {
-        // k_norm over the head's 128 values of the bf16 projection output
+        // k_proj output (bf16) of d in [32 half, +32) and of the partners d + 64;
+        // the row's other 64 values (the other warp's) are read too, for the sum
+        float lo[32], hi[32];
         float ss = 0.f;
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          float d[32];
-          tmem_ld32(acc + c * 32, d);
+        {
+          float o1[32], o2[32];
+          tmem_ld32(acc + (half ^ 1) * 32, o1);
+          tmem_ld32(acc + 64 + (half ^ 1) * 32, o2);
 #pragma unroll
           for (int e = 0; e < 32; ++e) {
-            const float x = bf16r(d[e]);
-            ss = fmaf(x, x, ss);
+            const float x1 = bf16r(o1[e]), x2 = bf16r(o2[e]);
+            ss = fmaf(x1, x1, ss);
+            ss = fmaf(x2, x2, ss);
           }
         }
-        const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
-        const __nv_bfloat16* w = p.k_norm_w + layer * kHeadDim;
-        const uint32_t* cs = p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {           // d in [32c, 32c + 32) and its partners d + 64
-          float lo[32], hi[32];
-          tmem_ld32(acc + c * 32, lo);
-          tmem_ld32(acc + 64 + c * 32, hi);
-          if (dest >= 0) {
+        tmem_ld32(acc + half * 32, lo);
+        tmem_ld32(acc + 64 + half * 32, hi);
 #pragma unroll
-            for (int e = 0; e < 32; ++e) {
-              const int d = c * 32 + e;
-              const float a = bf16r(__bfloat162float(w[d]) * bf16r(bf16r(lo[e]) * rs));
-              const float bb = bf16r(__bfloat162float(w[d + 64]) * bf16r(bf16r(hi[e]) * rs));
-              const float2 r = unpack_bf16x2(__ldg(cs + d));   // .x cos, .y sin
-              lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
-              hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
-            }
-            store_row32(out + c * 32, lo);
-            store_row32(out + 64 + c * 32, hi);
+        for (int e = 0; e < 32; ++e) {
+          lo[e] = bf16r(lo[e]);
+          hi[e] = bf16r(hi[e]);
+          ss = fmaf(lo[e], lo[e], ss);
+          ss = fmaf(hi[e], hi[e], ss);
+        }
+        const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+        const float* w = norm_w + layer * kHeadDim + half * 32;
+        if (dest >= 0) {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            const float a = bf16r(w[e] * bf16r(lo[e] * rs));
+            const float bb = bf16r(w[e + 64] * bf16r(hi[e] * rs));
+            const uint32_t cw = e % 4 == 0 ? cs4[e / 4].x : e % 4 == 1 ? cs4[e / 4].y : e % 4 == 2 ? cs4[e / 4].z
+                                                                                                   : cs4[e / 4].w;
+            const float2 r = unpack_bf16x2(cw);   // .x cos, .y sin
+            lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
+            hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
           }
+          store_row32(out + half * 32, lo);
+          store_row32(out + 64 + half * 32, hi);
         }
       }
       tc_fence_before();
       mbar_arrive(bar(kBarDFree0 + b));
     }
     if (!ok) *abort_flag = 1;
-  } else if (warp == 4) {
+  } else if (warp == kMmaWarp) {
     if (lane == 0) {
       constexpr uint32_t kIdesc = instr_desc(0);
       bool ok = true;
@@ -262,7 +290,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace append

@@ -42,6 +42,10 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 // requests x 7 rows over 0.5 M resident rows the fused kernel is ~1.5% faster,
 // its in-register q prologue being amortised over long CTA ranges).
 constexpr int kVerifyPrepMaxRows = 512;
+// Chunks longer than this (prefill) also take the prep path: the fused kernel
+// normalises and rotates a new-row tile in every item that reads it, which for a
+// 2048-row prompt is 256 q-blocks redoing the same tiles.
+constexpr int kVerifyFusedMaxQ = 16;
 // Kernels launched by this library since load (all devices, all streams).
 std::atomic<unsigned long long> g_launches{0};
 
@@ -414,7 +418,8 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
   p.scratch_rows = scratch_rows;
   const uint8_t* rk = static_cast<const uint8_t*>(resident_k) + res_row0 * row_bytes;
   const uint8_t* rv = static_cast<const uint8_t*>(resident_v) + res_row0 * row_bytes;
-  const bool prep = path == DSPARK_VERIFY_PREP || (path == DSPARK_VERIFY_AUTO && total_q < kVerifyPrepMaxRows);
+  const bool prep = path == DSPARK_VERIFY_PREP ||
+                    (path == DSPARK_VERIFY_AUTO && (total_q < kVerifyPrepMaxRows || max_q > kVerifyFusedMaxQ));
   if (prep) {
     // q_norm/k_norm + RoPE + KV append once per new row, then the plain causal
     // kernel over [resident prefix ; scratch rows] with q read from `out` in
@@ -587,6 +592,7 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
   p.rows = rows;
   p.k_chunks = hidden / 64;
   p.head_tiles = num_layers * 16;
+  p.layers = num_layers;
   p.row_tiles = (rows + append::kTileRows - 1) / append::kTileRows;
   p.eps = eps;
   const long long tiles = static_cast<long long>(p.row_tiles) * p.head_tiles;

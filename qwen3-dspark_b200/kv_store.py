@@ -305,7 +305,7 @@ class B200PersistentTargetKV:
         bf16; ``inv_freq`` [64] float32 on this device (see ``rope_inv_freq``).
         ``path``: 'fused' (norm/RoPE/append inside the attention kernel), 'prep' (a
         prep kernel per layer, then the attention kernel) or 'auto' (prep below 512
-        new rows); all give the same values.
+        new rows or for chunks longer than 16 rows); all give the same values.
         """
         self._transaction(tx)
         if type(layer) is not int or not 0 <= layer < self.layers or layer in self._staged:
