@@ -102,3 +102,44 @@ def deterministic_state(named_shapes, seed):
 def greedy_prompts(seed=55):
     g = rng(seed)
     return [g.integers(0, TINY_TARGET['vocab_size'] - 1, n).astype(np.int64) for n in GREEDY_PROMPTS]
+
+
+# Stochastic acceptance (tensor_sampling.verify_proposal): seeded cases over a small
+# vocabulary and, every fifth case, the Qwen3 vocabulary.
+STOCH_SEED = 777
+STOCH_CASES = 30
+STOCH_SMALL_VOCAB = 1000
+QWEN3_VOCAB = 151936
+
+
+def softmax64(x):
+    """float64 softmax normalised twice (a valid law within 1e-12 of sum one)."""
+    x = np.asarray(x, dtype=np.float64)
+    e = np.exp(x - x.max(axis=-1, keepdims=True))
+    w = e / e.sum(axis=-1, keepdims=True)
+    return w / w.sum(axis=-1, keepdims=True)
+
+
+def stochastic_case(idx):
+    """One verify_proposal case. Draft laws q [n, V] are float64 softmaxes of seeded
+    logits at temperature T; proposals are sampled from q; target logits [n + 1, V]
+    (float32 values exact in bf16) are the draft logits plus a case-dependent amount of
+    noise; ``uniforms`` holds n + 1 draws (the most a round consumes); ``budget`` is the
+    round's max_new_tokens and ``eos`` the stop tokens."""
+    from oracle.bf16 import round_bf16
+    g = rng(STOCH_SEED + idx)
+    vocab = QWEN3_VOCAB if idx % 5 == 4 else STOCH_SMALL_VOCAB
+    n = idx % 8
+    temperature = (0.6, 1.0, 1.7)[idx % 3]
+    draft_logits = g.standard_normal((n, vocab), dtype=np.float32) * 2
+    q = softmax64(draft_logits.astype(np.float64) / temperature)
+    tokens = np.array([int(min(np.searchsorted(np.cumsum(q[j]), g.random(), side='right'), vocab - 1))
+                       for j in range(n)], dtype=np.int64)
+    mix = (0.0, 0.05, 0.3, 1.0, 3.0)[idx % 5]
+    base = np.concatenate([draft_logits, g.standard_normal((1, vocab), dtype=np.float32) * 2], axis=0)
+    target_logits = round_bf16((base + mix * g.standard_normal(base.shape, dtype=np.float32)).astype(np.float32))
+    uniforms = g.random(n + 1)
+    budget = (100, 100, 3, 1, 0, 100, 2)[idx % 7]
+    eos = (int(tokens[1]),) if idx % 6 == 1 and n > 1 else ((5,) if idx % 6 == 3 else ())
+    return dict(tokens=tokens, q=q, target_logits=target_logits, temperature=temperature, uniforms=uniforms,
+                budget=budget, eos=eos, vocab=vocab)

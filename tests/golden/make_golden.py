@@ -254,9 +254,47 @@ def greedy_fixtures(out):
                                first_proposals=np.array(proposals))
 
 
+def stochastic_fixtures(out):
+    """Reference tensor_sampling.verify_proposal on the seeded cases of
+    inputs.stochastic_case, its target laws from logits_to_probabilities, and a
+    scripted generator that hands out the case's uniforms in order."""
+    import torch
+    from dspark_qwen.tensor_sampling import TensorProposal, logits_to_probabilities, verify_proposal
+
+    class Scripted:
+        def __init__(self, values):
+            self.values, self.used = list(values), 0
+
+        def uniform(self, reference):
+            v = torch.tensor(self.values[self.used], dtype=torch.float64, device=reference.device)
+            self.used += 1
+            return v
+
+    rec = {}
+    for idx in range(I.STOCH_CASES):
+        c = I.stochastic_case(idx)
+        p = logits_to_probabilities(t(c['target_logits']), c['temperature'])
+        n = c['tokens'].size
+        proposal = TensorProposal(t(c['tokens']), t(c['q']), torch.zeros(n, dtype=torch.float32))
+        rng = Scripted(c['uniforms'])
+        r = verify_proposal(proposal, p, rng, max_new_tokens=c['budget'], eos_ids=c['eos'])
+        extra = {None: 0, 'residual': 1, 'bonus': 2}[r.extra_token_kind]
+        reason = {'round_complete': 0, 'eos': 1, 'budget': 2}[r.stop_reason]
+        pn = p.numpy()
+        probe = np.concatenate([np.arange(min(8, c['vocab'])), c['tokens']])
+        rec[f'case{idx}_tokens'] = r.tokens.numpy()
+        rec[f'case{idx}_decision'] = np.array([r.accepted_draft_tokens,
+                                               -1 if r.rejected_index is None else r.rejected_index,
+                                               extra, reason, rng.used])
+        rec[f'case{idx}_p_probe'] = pn[:, probe]
+        rec[f'case{idx}_p_rowsum'] = pn.sum(axis=1)
+    out['stochastic_accept'] = rec
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True, help='path of a qwen3-dspark checkout')
+    ap.add_argument('--only', nargs='*', default=None, help='fixture functions to run (default: all)')
     args = ap.parse_args()
     os.environ.setdefault('PYTHONDONTWRITEBYTECODE', '1')
     sys.dont_write_bytecode = True
@@ -266,8 +304,9 @@ def main():
     torch.set_num_threads(4)
     out = {}
     for fn in (draft_fixtures, varlen_fixtures, training_fixtures, layout_fixtures, rope_fixtures,
-               kv_store_fixtures, greedy_fixtures):
-        fn(out)
+               kv_store_fixtures, greedy_fixtures, stochastic_fixtures):
+        if args.only is None or fn.__name__ in args.only:
+            fn(out)
     for name, rec in out.items():
         np.savez_compressed(os.path.join(HERE, f'{name}.npz'), **{k: np.asarray(v) for k, v in rec.items()})
         print(name, {k: np.asarray(v).shape for k, v in rec.items()})
