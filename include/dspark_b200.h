@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 9
+#define DSPARK_ABI_VERSION 10
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -239,6 +239,32 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
                         const int32_t* slot_row, const int32_t* ctx_len, const int32_t* count, int num_requests,
                         void* const* pool_k, void* const* pool_v, long long pool_rows, long long trash_row,
                         cudaStream_t stream);
+
+/*
+ * Stochastic acceptance of a verify round under the reference's float64 law
+ * (dspark_qwen/tensor_sampling.py:38-162): for request i with n_i = cu_n[i+1] - cu_n[i]
+ * proposals tokens[cu_n[i] ..] drawn from the draft laws q[cu_n[i] ..] ([draft_rows,
+ * vocab] float64), the target laws are softmax(logits / temperature) in float64,
+ * normalised once more, of target rows cu_n[i] + i .. + n_i (n_i + 1 rows of `logits`,
+ * bf16 or f32, row stride ld). Proposal j is accepted while u < min(p[t] / q[t], 1); the
+ * first rejection samples the residual law relu(p - q) / mass, a full accept samples the
+ * last target row (strict CDF rule, last positive index past the end); an accepted EOS
+ * stops the round, and so does reaching budget[i] tokens. Uniforms are consumed from
+ * uniforms[i * u_stride ..] in the reference's draw order (u_stride >= n_i + 1).
+ * Outputs: emitted[i * u_stride ..] (committed tokens, -1 after) and result[i * 8 ..] =
+ * {count, accepted, rejected index or -1, extra (0 none, 1 residual, 2 bonus),
+ *  reason (0 round complete, 1 EOS, 2 budget), uniforms used, status, 0}; status 0 or a
+ * refusal of the reference's checks (1 non-finite logits, 2 draft row not a law, 3 token
+ * out of range, 4 proposal with zero draft mass, 5 zero residual mass, 6 uniform outside
+ * [0, 1), 7 inconsistent offsets), in which case count is 0. scratch: device memory of
+ * dspark_stochastic_scratch_bytes(target_rows + draft_rows) bytes. Two launches.
+ */
+size_t dspark_stochastic_scratch_bytes(int rows);
+int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vocab, double temperature,
+                             int target_rows, const double* q, int draft_rows, const long long* tokens,
+                             const int32_t* cu_n, int num_requests, const double* uniforms, int u_stride,
+                             const long long* eos, int n_eos, const int32_t* budget, long long* emitted,
+                             int32_t* result, void* scratch, size_t scratch_bytes, cudaStream_t stream);
 
 /*
  * Training-layout block-draft attention (bf16, tcgen05 tensor cores).

@@ -39,6 +39,9 @@ SIGNATURES = {
                                 _vp, _vp]),
     'dspark_greedy_accept': (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
     'dspark_train_attn': (_i, [_vp, _vp, _vp, _i, _ll, _vp, _i, _f, _vp, _vp]),
+    'dspark_stochastic_scratch_bytes': (_sz, [_i]),
+    'dspark_stochastic_accept': (_i, [_vp, _ll, _i, _i, ctypes.c_double, _i, _vp, _i, _vp, _vp, _i, _vp, _i, _vp, _i,
+                                      _vp, _vp, _vp, _vp, _sz, _vp]),
     'dspark_draft_append': (_i, [_vp, _i, _i, _vp, _i, _vp, _vp, _f, _vp, _vp, _vp, _vp, _i, _vp, _vp, _ll, _ll,
                                  _vp]),
 }
@@ -61,7 +64,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 9:
+        if lib.dspark_abi_version() != 10:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

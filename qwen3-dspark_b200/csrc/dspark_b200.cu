@@ -6,6 +6,7 @@
 #include <cudaTypedefs.h>
 #include <algorithm>
 #include <atomic>
+#include <cmath>
 #include <cstdint>
 #include <cstdio>
 #include <mutex>
@@ -17,6 +18,7 @@
 #include "append.cuh"
 #include "attention.cuh"
 #include "markov.cuh"
+#include "sampling.cuh"
 #include "train.cuh"
 #include "verify.cuh"
 #include "../../include/dspark_b200.h"
@@ -599,6 +601,48 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
   if (tiles >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
   const int grid = tiles < dev.sms ? static_cast<int>(tiles) : dev.sms;
   append::draft_append_kernel<<<grid, append::kThreads, append::kSmemBytes, stream>>>(cm, wm, p);
+  return launch_status();
+}
+
+size_t dspark_stochastic_scratch_bytes(int rows) {
+  return rows > 0 ? static_cast<size_t>(rows) * sizeof(sampling::RowStats) : 0;
+}
+
+int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vocab, double temperature,
+                             int target_rows, const double* q, int draft_rows, const long long* tokens,
+                             const int32_t* cu_n, int num_requests, const double* uniforms, int u_stride,
+                             const long long* eos, int n_eos, const int32_t* budget, long long* emitted,
+                             int32_t* result, void* scratch, size_t scratch_bytes, cudaStream_t stream) {
+  if (!logits || !cu_n || !uniforms || !budget || !emitted || !result || !scratch || vocab < 1 || ld < vocab ||
+      (dtype != DSPARK_DTYPE_BF16 && dtype != DSPARK_DTYPE_F32) || !(temperature > 0.0) ||
+      !std::isfinite(temperature) || num_requests < 1 || target_rows != draft_rows + num_requests ||
+      draft_rows < 0 || (draft_rows > 0 && (!q || !tokens)) || u_stride < 1 || n_eos < 0 || (n_eos > 0 && !eos) ||
+      scratch_bytes < dspark_stochastic_scratch_bytes(target_rows + draft_rows) || !aligned(scratch, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  sampling::Params p{};
+  p.logits = logits;
+  p.ld = ld;
+  p.dtype = dtype == DSPARK_DTYPE_BF16 ? 0 : 1;
+  p.vocab = vocab;
+  p.temperature = temperature;
+  p.target_rows = target_rows;
+  p.q = q;
+  p.draft_rows = draft_rows;
+  p.stats = static_cast<sampling::RowStats*>(scratch);
+  p.tokens = tokens;
+  p.cu_n = cu_n;
+  p.num_requests = num_requests;
+  p.uniforms = uniforms;
+  p.u_stride = u_stride;
+  p.eos = eos;
+  p.n_eos = n_eos;
+  p.budget = budget;
+  p.emitted = emitted;
+  p.result = result;
+  sampling::law_stats_kernel<<<target_rows + draft_rows, sampling::kThreads, 0, stream>>>(p);
+  int st = launch_status();
+  if (st != DSPARK_OK) return st;
+  sampling::stochastic_accept_kernel<<<num_requests, sampling::kThreads, 0, stream>>>(p);
   return launch_status();
 }
 

@@ -1,0 +1,308 @@
+// Stochastic acceptance of a verify round under the reference's float64 law
+// (dspark_qwen/tensor_sampling.py): the target law p = softmax(logits / T)
+// normalised once more (logits_to_probabilities, :38-51), the acceptance test
+// u < min(p[t] / q[t], 1) per proposal, the residual law relu(p - q) / mass at the
+// first rejection (residual_distribution, :87-96) or the bonus draw from the last
+// target row, each sampled by the strict CDF rule with the last positive index
+// past the end (sample_categorical, :77-84), and the stop rules of
+// verify_proposal (:114-162).
+//
+// Two launches. law_stats_kernel: one CTA per target row (max of x / T, the sum of
+// exp(x / T - max) and the sum of the normalised weights) and one per draft row
+// (a law: finite, in [0, 1], sum within 1e-12 of one). stochastic_accept_kernel:
+// one CTA per request; thread 0 walks the proposals with the request's uniforms
+// in the reference's draw order; a residual or bonus sample is a CTA-wide pass
+// (mass, then a chunked CDF scan). All arithmetic is float64.
+#pragma once
+#include "ptx.cuh"
+
+namespace dspark {
+namespace sampling {
+
+constexpr int kThreads = 512;
+
+enum Status {
+  kOk = 0,
+  kBadLogits = 1,        // non-finite logits or scaled logits
+  kBadDraftLaw = 2,      // a draft row is not a float64 law
+  kTokenRange = 3,       // proposal outside the vocabulary
+  kZeroDraftMass = 4,    // proposal with zero mass under its own law
+  kZeroResidual = 5,     // rejection with zero residual mass
+  kBadUniform = 6,       // a uniform outside [0, 1)
+  kBadLayout = 7,        // proposal offsets inconsistent with the buffers
+};
+enum Extra { kExtraNone = 0, kExtraResidual = 1, kExtraBonus = 2 };
+enum Reason { kRoundComplete = 0, kEos = 1, kBudget = 2 };
+
+struct RowStats {
+  double m;    // max of x / T
+  double s;    // sum of exp(x / T - m)
+  double s2;   // sum of exp(x / T - m) / s
+  int bad;     // status of the row (kOk, kBadLogits or kBadDraftLaw)
+  int pad;
+};
+
+struct Params {
+  const void* logits;        // target rows, [rows, ld] bf16 or f32
+  long long ld;
+  int dtype;                 // 0 bf16, 1 f32
+  int vocab;
+  double temperature;
+  int target_rows;
+  const double* q;           // draft laws [draft_rows, vocab]
+  int draft_rows;
+  RowStats* stats;           // [target_rows + draft_rows]
+  const long long* tokens;   // [draft_rows] proposals
+  const int* cu_n;           // [R + 1] proposals of request i: rows cu_n[i] .. cu_n[i + 1]
+  int num_requests;
+  const double* uniforms;    // [R, u_stride]
+  int u_stride;
+  const long long* eos;
+  int n_eos;
+  const int* budget;         // [R] max new tokens of the round
+  long long* emitted;        // [R, u_stride] committed tokens, -1 after
+  int* result;               // [R, 8]: count, accepted, rejected, extra, reason, draws, status, 0
+};
+
+__device__ __forceinline__ double load_logit(const Params& p, long long row, int i) {
+  if (p.dtype == 0)
+    return static_cast<double>(
+        __bfloat162float(static_cast<const __nv_bfloat16*>(p.logits)[row * p.ld + i]));
+  return static_cast<double>(static_cast<const float*>(p.logits)[row * p.ld + i]);
+}
+
+template <typename T, typename Op>
+__device__ __forceinline__ T block_reduce(T v, T* scratch, Op op) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();                                   // scratch reuse across calls
+  if (lane == 0) scratch[warp] = v;
+  __syncthreads();
+  v = scratch[0];
+  for (int w = 1; w < kThreads / 32; ++w) v = op(v, scratch[w]);
+  return v;
+}
+
+struct MaxOp {
+  __device__ double operator()(double a, double b) const { return a > b || b != b ? a : b; }
+};
+struct SumOp {
+  __device__ double operator()(double a, double b) const { return a + b; }
+};
+struct OrOp {
+  __device__ int operator()(int a, int b) const { return a | b; }
+};
+struct MinIntOp {
+  __device__ int operator()(int a, int b) const { return a < b ? a : b; }
+};
+struct MaxIntOp {
+  __device__ int operator()(int a, int b) const { return a > b ? a : b; }
+};
+
+// Row statistics of the target laws and validation of the draft laws.
+__global__ void __launch_bounds__(kThreads) law_stats_kernel(const Params p) {
+  __shared__ double dscr[kThreads / 32];
+  __shared__ int iscr[kThreads / 32];
+  const int row = blockIdx.x;
+  if (row < p.target_rows) {
+    int bad = 0;
+    double m = -INFINITY;
+    for (int i = threadIdx.x; i < p.vocab; i += kThreads) {
+      const double x = load_logit(p, row, i);
+      const double s = x / p.temperature;
+      if (!isfinite(x) || !isfinite(s)) bad = 1;
+      m = s > m ? s : m;
+    }
+    bad = block_reduce(bad, iscr, OrOp());
+    m = block_reduce(m, dscr, MaxOp());
+    double sum = 0.0;
+    for (int i = threadIdx.x; i < p.vocab; i += kThreads) sum += exp(load_logit(p, row, i) / p.temperature - m);
+    sum = block_reduce(sum, dscr, SumOp());
+    double sum2 = 0.0;
+    for (int i = threadIdx.x; i < p.vocab; i += kThreads)
+      sum2 += exp(load_logit(p, row, i) / p.temperature - m) / sum;
+    sum2 = block_reduce(sum2, dscr, SumOp());
+    if (threadIdx.x == 0) p.stats[row] = RowStats{m, sum, sum2, bad ? kBadLogits : kOk, 0};
+  } else if (row < p.target_rows + p.draft_rows) {
+    const int r = row - p.target_rows;
+    const double* q = p.q + static_cast<long long>(r) * p.vocab;
+    int bad = 0;
+    double sum = 0.0;
+    for (int i = threadIdx.x; i < p.vocab; i += kThreads) {
+      const double v = q[i];
+      if (!(v >= 0.0 && v <= 1.0)) bad = 1;            // NaN fails too
+      sum += v;
+    }
+    bad = block_reduce(bad, iscr, OrOp());
+    sum = block_reduce(sum, dscr, SumOp());
+    if (threadIdx.x == 0) {
+      const bool law = !bad && isfinite(sum) && fabs(sum - 1.0) <= 1e-12;
+      p.stats[row] = RowStats{0.0, sum, 0.0, law ? kOk : kBadDraftLaw, 0};
+    }
+  }
+}
+
+// Target law value at (row, i).
+__device__ __forceinline__ double law_at(const Params& p, const RowStats& st, long long row, int i) {
+  return exp(load_logit(p, row, i) / p.temperature - st.m) / st.s / st.s2;
+}
+
+__global__ void __launch_bounds__(kThreads) stochastic_accept_kernel(const Params p) {
+  __shared__ double dscr[kThreads / 32];
+  __shared__ int iscr[kThreads / 32];
+  __shared__ double sh_u;
+  __shared__ int sh_action, sh_row, sh_qrow;
+  const int r = blockIdx.x;
+  if (r >= p.num_requests) return;
+  const int q0 = p.cu_n[r], n = p.cu_n[r + 1] - q0;
+  const long long t0 = static_cast<long long>(q0) + r;     // target rows of request r: t0 .. t0 + n
+  long long* out = p.emitted + static_cast<long long>(r) * p.u_stride;
+  const double* u = p.uniforms + static_cast<long long>(r) * p.u_stride;
+  int count = 0, accepted = 0, rejected = -1, extra = kExtraNone, reason = kRoundComplete, draws = 0,
+      status = kOk;
+  const bool layout_ok = n >= 0 && n + 1 <= p.u_stride && q0 >= 0 && q0 + n <= p.draft_rows &&
+                         t0 + n < p.target_rows;
+  if (threadIdx.x == 0) {
+    sh_action = 0;
+    if (!layout_ok) status = kBadLayout;
+    for (int j = 0; j <= n && status == kOk; ++j)
+      if (p.stats[t0 + j].bad) status = p.stats[t0 + j].bad;
+    for (int j = 0; j < n && status == kOk; ++j) {
+      const long long t = p.tokens[q0 + j];
+      if (p.stats[p.target_rows + q0 + j].bad) status = kBadDraftLaw;
+      else if (t < 0 || t >= p.vocab) status = kTokenRange;
+      else if (!(p.q[static_cast<long long>(q0 + j) * p.vocab + t] > 0.0)) status = kZeroDraftMass;
+    }
+    const int budget = p.budget[r];
+    auto is_eos = [&](long long t) {
+      for (int e = 0; e < p.n_eos; ++e)
+        if (p.eos[e] == t) return true;
+      return false;
+    };
+    auto next_uniform = [&](double& v) {
+      v = u[draws++];
+      if (!(v >= 0.0 && v < 1.0)) status = kBadUniform;
+      return status == kOk;
+    };
+    if (status == kOk) {
+      if (budget <= 0) {
+        reason = kBudget;
+      } else {
+        bool stopped = false;
+        for (int j = 0; j < n; ++j) {
+          const long long t = p.tokens[q0 + j];
+          const double pj = law_at(p, p.stats[t0 + j], t0 + j, static_cast<int>(t));
+          const double qj = p.q[static_cast<long long>(q0 + j) * p.vocab + t];
+          const double alpha = fmin(pj / qj, 1.0);
+          double v;
+          if (!next_uniform(v)) break;
+          if (v >= alpha) {
+            double v2;
+            if (!next_uniform(v2)) break;
+            accepted = j;
+            rejected = j;
+            extra = kExtraResidual;
+            sh_action = 1;
+            sh_row = j;
+            sh_qrow = q0 + j;
+            sh_u = v2;
+            stopped = true;
+            break;
+          }
+          out[count++] = t;
+          accepted = j + 1;
+          if (is_eos(t) || count == budget) {
+            reason = is_eos(t) ? kEos : kBudget;
+            stopped = true;
+            break;
+          }
+        }
+        if (!stopped && status == kOk) {
+          double v2;
+          if (next_uniform(v2)) {
+            accepted = n;
+            extra = kExtraBonus;
+            sh_action = 2;
+            sh_row = n;
+            sh_qrow = -1;
+            sh_u = v2;
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const int action = sh_action;
+  if (action != 0) {
+    // the sampled law: relu(p - q) / mass (residual) or p (bonus); chunked CDF scan
+    const long long trow = t0 + sh_row;
+    const RowStats st = p.stats[trow];
+    const double* q = sh_qrow >= 0 ? p.q + static_cast<long long>(sh_qrow) * p.vocab : nullptr;
+    auto value = [&](int i) {
+      const double pv = law_at(p, st, trow, i);
+      return q ? fmax(pv - q[i], 0.0) : pv;
+    };
+    double mass = 1.0;
+    if (q) {
+      double sum = 0.0;
+      for (int i = threadIdx.x; i < p.vocab; i += kThreads) sum += value(i);
+      mass = block_reduce(sum, dscr, SumOp());
+    }
+    const int chunk = (p.vocab + kThreads - 1) / kThreads;
+    const int lo = min(p.vocab, static_cast<int>(threadIdx.x) * chunk), hi = min(p.vocab, lo + chunk);
+    double local = 0.0;
+    int last_pos = -1;
+    for (int i = lo; i < hi; ++i) {
+      const double e = q ? value(i) / mass : value(i);
+      local += e;
+      if (e > 0.0) last_pos = i;
+    }
+    // exclusive prefix of the chunk sums (ordered by thread, i.e. by index)
+    __shared__ double chunk_sum[kThreads];
+    chunk_sum[threadIdx.x] = local;
+    __syncthreads();
+    double prefix = 0.0;
+    for (int k = 0; k < static_cast<int>(threadIdx.x); ++k) prefix += chunk_sum[k];
+    int found = p.vocab;
+    const double uu = sh_u;
+    double cdf = prefix;
+    for (int i = lo; i < hi; ++i) {
+      cdf += q ? value(i) / mass : value(i);
+      if (cdf > uu) {
+        found = i;
+        break;
+      }
+    }
+    found = block_reduce(found, iscr, MinIntOp());
+    last_pos = block_reduce(last_pos, iscr, MaxIntOp());
+    if (threadIdx.x == 0) {
+      if (q && !(mass > 0.0)) {
+        status = kZeroResidual;
+      } else {
+        const long long tok = found < p.vocab ? found : last_pos;
+        out[count++] = tok;
+        const int budget = p.budget[r];
+        bool eos = false;
+        for (int e = 0; e < p.n_eos; ++e) eos = eos || p.eos[e] == tok;
+        reason = eos ? kEos : (count == budget ? kBudget : kRoundComplete);
+      }
+    }
+  }
+  if (threadIdx.x == 0) {
+    if (status != kOk) count = 0;
+    for (int k = count; k < p.u_stride; ++k) out[k] = -1;
+    int* res = p.result + static_cast<long long>(r) * 8;
+    res[0] = count;
+    res[1] = accepted;
+    res[2] = rejected;
+    res[3] = extra;
+    res[4] = reason;
+    res[5] = draws;
+    res[6] = status;
+    res[7] = 0;
+  }
+}
+
+}  // namespace sampling
+}  // namespace dspark

@@ -374,3 +374,58 @@ def draft_append(context, kv_weight, k_norm_weight, inv_freq, meta, num_requests
                                        meta[r + 1:].data_ptr(), meta[2 * r + 1:].data_ptr(),
                                        meta[3 * r + 1:].data_ptr(), r, pk, pv, rows, int(trash_row), stream),
                'dspark_draft_append')
+
+
+STOCHASTIC_STATUS = {0: 'ok', 1: 'non-finite target logits', 2: 'draft row is not a float64 law',
+                     3: 'proposal outside the vocabulary', 4: 'proposal with zero draft mass',
+                     5: 'zero residual mass', 6: 'uniform outside [0, 1)', 7: 'inconsistent proposal offsets'}
+
+
+def stochastic_accept(target_logits, tokens, draft_probs, cu_proposals, temperature, uniforms, budget, eos_ids=()):
+    """Stochastic acceptance of one verify round on the GPU under the reference's
+    float64 law (dspark_qwen/tensor_sampling.py:38-162, ``verify_proposal`` per request).
+
+    ``target_logits`` [sum(n_i + 1), V] bf16/fp32 (request i's n_i + 1 verified rows,
+    unit column stride), ``tokens`` [sum n_i] int64 proposals, ``draft_probs``
+    [sum n_i, V] float64 (the draft laws they were sampled from), ``cu_proposals``
+    int32 [R + 1], ``uniforms`` float64 [R, S] (S >= max n_i + 1; request i consumes
+    them in the reference's draw order), ``budget`` int32 [R] (max new tokens).
+    Returns device tensors ``emitted`` [R, S] int64 (-1 after the committed tokens)
+    and ``result`` [R, 8] int32: count, accepted, rejected index (-1 none), extra
+    (0 none, 1 residual, 2 bonus), stop reason (0 round complete, 1 EOS, 2 budget),
+    uniforms used, status (0 ok, else the reference's refusal; see
+    ``STOCHASTIC_STATUS``), 0.
+    """
+    device = target_logits.device
+    r = cu_proposals.numel() - 1
+    if (target_logits.ndim != 2 or target_logits.dtype not in _DTYPES or target_logits.stride(1) != 1
+            or not target_logits.is_cuda or draft_probs.dtype != torch.float64 or draft_probs.ndim != 2
+            or not draft_probs.is_contiguous() or draft_probs.shape[1] != target_logits.shape[1]
+            or tokens.dtype != torch.long or tokens.shape != (draft_probs.shape[0],)
+            or cu_proposals.dtype != torch.int32 or r < 1 or uniforms.dtype != torch.float64
+            or uniforms.ndim != 2 or uniforms.shape[0] != r or not uniforms.is_contiguous()
+            or budget.dtype != torch.int32 or budget.shape != (r,)
+            or target_logits.shape[0] != draft_probs.shape[0] + r
+            or any(t.device != device for t in (tokens, draft_probs, cu_proposals, uniforms, budget))):
+        raise ValueError('stochastic_accept: [sum(n+1), V] logits, [sum n] int64 tokens, [sum n, V] float64 '
+                         'draft laws, int32 [R+1] offsets, float64 [R, S] uniforms and int32 [R] budgets on '
+                         'one CUDA device required')
+    temperature = float(temperature)
+    if not math.isfinite(temperature) or temperature <= 0:
+        raise ValueError('temperature must be finite and strictly positive')
+    eos = torch.tensor(sorted(set(int(e) for e in eos_ids)), dtype=torch.long, device=device)
+    s = uniforms.shape[1]
+    emitted = torch.empty((r, s), dtype=torch.long, device=device)
+    result = torch.empty((r, 8), dtype=torch.int32, device=device)
+    lib = _lib.load_library()
+    rows = target_logits.shape[0] + draft_probs.shape[0]
+    nbytes = int(lib.dspark_stochastic_scratch_bytes(rows))
+    scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=device)
+    _lib.check(lib.dspark_stochastic_accept(
+        target_logits.data_ptr(), target_logits.stride(0), _DTYPES[target_logits.dtype], target_logits.shape[1],
+        temperature, target_logits.shape[0], draft_probs.data_ptr() if draft_probs.numel() else None,
+        draft_probs.shape[0], tokens.data_ptr() if tokens.numel() else None, cu_proposals.contiguous().data_ptr(),
+        r, uniforms.data_ptr(), s, eos.data_ptr() if eos.numel() else None, eos.numel(), budget.data_ptr(),
+        emitted.data_ptr(), result.data_ptr(), scratch.data_ptr(), scratch.numel(), _stream(device)),
+        'dspark_stochastic_accept')
+    return emitted, result

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 9
+    assert lib.dspark_abi_version() == 10
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -58,6 +58,13 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
         assert lib.dspark_markov_step(fake, fake, vocab, rank, fake, 7, 0, fake, 1, fake, 1024, fake, 0.0, fake,
                                       fake, 7, r, fake, None) == 1
     assert lib.dspark_markov_scratch_bytes() >= 128 * 8
+    # stochastic acceptance: target rows must be draft rows + requests, temperature > 0
+    for rows, temp in ((4, 1.0), (3, 0.0), (3, float('nan'))):
+        assert lib.dspark_stochastic_accept(fake, 1000, 1, 1000, temp, rows, fake, 1, fake, fake, 2, fake, 2, None, 0,
+                                            fake, fake, fake, fake, 1 << 20, None) == 1
+    assert lib.dspark_stochastic_accept(None, 1000, 1, 1000, 1.0, 3, fake, 1, fake, fake, 2, fake, 2, None, 0, fake,
+                                        fake, fake, fake, 1 << 20, None) == 1
+    assert lib.dspark_stochastic_scratch_bytes(4) >= 4 * 24
     ptrs = (ctypes.c_void_p * 1)(256)
     assert lib.dspark_draft_append(None, 8, 1024, fake, 1, fake, fake, 1e-6, fake, fake, fake, fake, 1, ptrs, ptrs,
                                    16, 15, None) == 1
