@@ -685,6 +685,76 @@ def append_leg(pkg, device, warmup, iters=10):
     return out
 
 
+def stochastic_leg(pkg, device, warmup, iters=10, r=128, n=6, vocab=151936, temperature=0.8):
+    """Stochastic acceptance of one verify round at config 3's shape (128 requests,
+    6 proposals + 1 row each, Qwen3 vocabulary): target logits bf16 [R * 7, V], draft
+    laws float64 [R * 6, V] (the reference's TensorProposal.draft_probs), float64
+    uniforms. The on-device law statistics + acceptance (two launches) against the
+    reference's verify_proposal formula run per request with torch float64 ops on the
+    same GPU (logits_to_probabilities + the sequential accept loop)."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(31)
+    logits = (torch.randn(r * (n + 1), vocab, device=device, generator=gen) * 2).to(torch.bfloat16)
+    draft_logits = logits[:0].float()
+    rows = []
+    for i in range(r):
+        rows.append(logits[i * (n + 1):i * (n + 1) + n].float() + 0.3 * torch.randn(n, vocab, device=device,
+                                                                                      generator=gen))
+    q = torch.softmax(torch.cat(rows).double() / temperature, -1)
+    q = q / q.sum(-1, keepdim=True)
+    tokens = torch.multinomial(q.float(), 1, generator=gen).flatten()
+    cu = torch.arange(0, r * n + 1, n, dtype=torch.int32, device=device)
+    u = torch.rand(r, n + 1, dtype=torch.float64, device=device, generator=gen)
+    budget = torch.full((r,), 1000, dtype=torch.int32, device=device)
+    del draft_logits, rows
+
+    def fused():
+        return pkg.stochastic_accept(logits, tokens, q, cu, temperature, u, budget)
+
+    def torch_formula():                     # the reference's per-request float64 loop (tensor_sampling.py)
+        out = []
+        for i in range(r):
+            p = torch.softmax(logits[i * (n + 1):(i + 1) * (n + 1)].double() / temperature, -1)
+            p = p / p.sum(-1, keepdim=True)
+            qi, ti = q[i * n:(i + 1) * n], tokens[i * n:(i + 1) * n]
+            alpha = torch.minimum(p[:n].gather(1, ti[:, None]).flatten() / qi.gather(1, ti[:, None]).flatten(),
+                                  torch.ones(n, dtype=torch.float64, device=device))
+            rej = (u[i, :n] >= alpha).nonzero()
+            if rej.numel():
+                j = int(rej[0, 0])
+                res = (p[j] - qi[j]).relu()
+                res = res / res.sum()
+                out.append(torch.searchsorted(res.cumsum(-1), u[i, n:n + 1], right=True))
+            else:
+                out.append(torch.searchsorted(p[n].cumsum(-1), u[i, n:n + 1], right=True))
+        return out
+
+    def timed(fn, k):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize(device)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(k):
+            fn()
+        b.record()
+        torch.cuda.synchronize(device)
+        return a.elapsed_time(b) / k
+
+    ms = timed(fused, iters)
+    torch_ms = timed(torch_formula, 2)
+    _, res = fused()
+    res = res.cpu()
+    nbytes = q.numel() * 8 + logits.numel() * 2
+    hbm, kind = peaks()
+    return dict(workload=f'{r} requests x {n} proposals, vocab {vocab}, bf16 target logits, float64 draft laws',
+                ms=ms, torch_formula_ms=torch_ms, speedup=torch_ms / ms,
+                mean_accepted=float(res[:, 1].float().mean()), status_ok=bool((res[:, 6] == 0).all()),
+                alg_bytes=nbytes, achieved_gbs=nbytes / (ms / 1e3) / 1e9, frac=nbytes / (ms / 1e3) / 1e9 / hbm,
+                peak_gbs=hbm, peak_source=kind)
+
+
 # --------------------------------------------------------------------------- config 5
 ROUND5 = dict(requests=32, prompts=(64, 256, 2048), new_tokens=128, seed=5)
 
@@ -892,6 +962,19 @@ def run_b200(args):
             dist.barrier()
             dist.destroy_process_group()
         return
+    if args.case == 'stochastic':
+        res = stochastic_leg(pkg, device, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='on-device stochastic acceptance per verify round',
+                                          value=res['achieved_gbs'], unit='GB/s', n_gpus=world, steps=args.steps,
+                                          warmup=args.warmup, ms_per_step=res['ms'], higher_is_better=True,
+                                          dtype='f64', data='synthetic', stochastic=res, device_status=status))),
+                  flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'append':
         res = append_leg(pkg, device, args.warmup, iters=args.steps)
         status = pkg.read_device_status(clear=True)
@@ -1065,7 +1148,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'append', 'round5', 'graph5'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'append', 'round5', 'graph5', 'stochastic'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

@@ -25,7 +25,7 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import HEAD_DIM, HKV, HQ, draft_append, markov_greedy, segment_attention
+from .kernels import HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, sample_rows, segment_attention
 from .kv_store import _upload
 
 
@@ -474,6 +474,45 @@ class B200PackedDraft:
             return ex['tokens'], ex['conf']
         toks, confs = ex['tokens'].tolist(), ex['conf'].tolist()
         return {q: (toks[i], confs[i]) for i, q in enumerate(requests)}
+
+    @torch.no_grad()
+    def propose_stochastic(self, anchors, limits, uniforms, temperature):
+        """Stochastic block proposal (DSparkDraft._sample_stochastic, dspark_qwen/model.py:
+        193-208, batched over requests as propose_packed, packed_sampling.py:73-94): one
+        backbone + LM head for all requests, then per position k < limits[r] the float64
+        law q = softmax((base_k + markov_projection(emb(prev))) / T) (normalised twice)
+        and a token drawn by the strict CDF rule with ``uniforms[i, k]`` (request i of
+        ``anchors``' order). Returns ({request: tokens [n] long}, {request: laws [n, V]
+        float64}) on the device; the raw confidence logits are not part of acceptance
+        and are not computed."""
+        d = self.draft
+        requests = tuple(anchors)
+        n = [int(limits[r]) for r in requests]
+        size = d.spec.block_size
+        if any(not 0 <= x <= size for x in n) or uniforms.shape != (len(requests), size):
+            raise ValueError('limits in [0, block_size] and [R, block_size] uniforms required')
+        feats = self.backbone(anchors)
+        r = len(requests)
+        hidden = feats.hidden.reshape(r, size, -1)
+        base = d.lm_head(hidden.to(d.lm_head.weight.dtype))
+        prev = torch.cat([anchors[q].view(1) for q in requests])
+        tokens = [[] for _ in requests]
+        laws = [[] for _ in requests]
+        for k in range(max(n) if n else 0):
+            rows = [i for i in range(r) if k < n[i]]
+            idx = torch.tensor(rows, dtype=torch.long, device=self.device)
+            emb = d.markov_embedding(prev[idx])
+            logits = base[idx, k] + d.markov_projection(emb)
+            law = float64_law(logits, temperature)
+            tok = sample_rows(law, uniforms[idx, k])
+            prev = prev.index_copy(0, idx, tok)
+            for j, i in enumerate(rows):
+                tokens[i].append(tok[j:j + 1])
+                laws[i].append(law[j])
+        empty_t = torch.empty(0, dtype=torch.long, device=self.device)
+        empty_l = torch.empty((0, base.shape[-1]), dtype=torch.float64, device=self.device)
+        return ({q: torch.cat(tokens[i]) if tokens[i] else empty_t for i, q in enumerate(requests)},
+                {q: torch.stack(laws[i]) if laws[i] else empty_l for i, q in enumerate(requests)})
 
     @torch.no_grad()
     def _confidence_bias(self):

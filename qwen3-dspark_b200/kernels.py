@@ -429,3 +429,20 @@ def stochastic_accept(target_logits, tokens, draft_probs, cu_proposals, temperat
         emitted.data_ptr(), result.data_ptr(), scratch.data_ptr(), scratch.numel(), _stream(device)),
         'dspark_stochastic_accept')
     return emitted, result
+
+
+def float64_law(logits, temperature):
+    """The reference's sampling law of logits rows (tensor_sampling.py:38-51): float64
+    softmax of logits / T, normalised once more. Torch ops on the logits' device."""
+    scaled = logits.to(torch.float64) / float(temperature)
+    weights = scaled.softmax(-1)
+    return weights / weights.sum(-1, keepdim=True)
+
+
+def sample_rows(laws, uniforms):
+    """One token per law row by the strict CDF rule (tensor_sampling.py:77-84):
+    searchsorted(cumsum(law), u, right=True), past the end -> last positive index."""
+    vocab = laws.shape[-1]
+    index = torch.searchsorted(laws.cumsum(-1), uniforms.reshape(-1, 1).to(torch.float64), right=True).flatten()
+    last_positive = vocab - 1 - (laws.flip(-1) > 0).to(torch.int8).argmax(-1)
+    return torch.where(index < vocab, index, last_positive)

@@ -139,3 +139,89 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
         rounds.append(stats)
         active = [r for r in active if len(output[r]) < max_new_tokens and output[r][-1] not in eos_ids]
     return output, rounds
+
+
+@torch.no_grad()
+def speculative_sample(target, draft, prompts, max_new_tokens, generators, temperature=1.0, eos_ids=()):
+    """Batched stochastic speculative decoding; per request the rule of
+    ``cached_speculative_sample`` (dspark_qwen/cached_sampling.py:80-175) under the
+    reference's float64 law. ``generators``: {request: CPU torch.Generator}. Each
+    request's uniforms come from its generator in the reference's draw order (the
+    first token, then per round the proposal draws and the acceptance draws), and
+    after each round the generator is left exactly where the reference's would be,
+    so a request's tokens equal the reference's single-request run with the same
+    seed. Acceptance runs on the GPU (``stochastic_accept``); the host reads back one
+    small result per round. Returns ({request: tokens}, rounds)."""
+    from .kernels import STOCHASTIC_STATUS, float64_law, sample_rows, stochastic_accept
+    import math
+    if type(max_new_tokens) is not int or max_new_tokens < 0:
+        raise ValueError('max_new_tokens must be a nonnegative integer')
+    temperature = float(temperature)
+    if not math.isfinite(temperature) or temperature <= 0:
+        raise ValueError('temperature must be finite and strictly positive')
+    if set(generators) != set(prompts):
+        raise ValueError('One generator per request required')
+    eos_ids = set(int(e) for e in eos_ids)
+    dev = target.device
+    f64 = torch.float64
+    for r in prompts:
+        target.add_request(r)
+        draft.add_request(r)
+    if max_new_tokens == 0:
+        return {r: [] for r in prompts}, []
+    features = target.prefill(prompts)
+    last = target.predict(features, last_only=True)
+    requests = list(prompts)
+    first_u = torch.stack([torch.rand((), dtype=f64, generator=generators[r]) for r in requests]).to(dev)
+    law = float64_law(torch.cat([last[r].reshape(1, -1) for r in requests]), temperature)
+    first = sample_rows(law, first_u).tolist()
+    output = {r: [first[i]] for i, r in enumerate(requests)}
+    draft.append_committed({r: features.context_for(r) for r in prompts})
+    active = [r for r in requests if output[r][-1] not in eos_ids and max_new_tokens > 1]
+    size = draft.draft.spec.block_size
+    rounds = []
+    while active:
+        remaining = {r: max_new_tokens - len(output[r]) for r in active}
+        n = {r: min(size, remaining[r]) for r in active}
+        states = {r: generators[r].get_state() for r in active}
+        drawn = {r: torch.rand(2 * n[r] + 1, dtype=f64, generator=generators[r]) for r in active}
+        u_prop = torch.zeros((len(active), size), dtype=f64)
+        u_acc = torch.zeros((len(active), size + 1), dtype=f64)
+        for i, r in enumerate(active):
+            u_prop[i, :n[r]] = drawn[r][:n[r]]
+            u_acc[i, :n[r] + 1] = drawn[r][n[r]:]
+        u_prop = u_prop.pin_memory().to(dev, non_blocking=True)
+        u_acc = u_acc.pin_memory().to(dev, non_blocking=True)
+        anchors = {r: torch.tensor([[output[r][-1]]], dtype=torch.long, device=dev) for r in active}
+        tokens, laws = draft.propose_stochastic(anchors, n, u_prop, temperature)
+        chunks = {r: torch.cat((anchors[r][0], tokens[r]))[None] for r in active}
+        verified = target.verify(chunks)
+        logits = target.model.get_output_embeddings()(verified.last)[0]
+        cu = [0]
+        for r in active:
+            cu.append(cu[-1] + n[r])
+        emitted, result = stochastic_accept(
+            logits, torch.cat([tokens[r] for r in active]), torch.cat([laws[r] for r in active]),
+            torch.tensor(cu, dtype=torch.int32).pin_memory().to(dev, non_blocking=True), temperature, u_acc,
+            torch.tensor([remaining[r] for r in active], dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
+            eos_ids)
+        res = result.cpu().tolist()
+        em = emitted.cpu().tolist()
+        commit, stats = {}, {}
+        for i, r in enumerate(active):
+            count, accepted, rejected, extra, reason, used, status, _ = res[i]
+            if status:
+                target.abort(verified)
+                raise ValueError(f'stochastic acceptance refused request {r}: {STOCHASTIC_STATUS[status]}')
+            generators[r].set_state(states[r])
+            torch.rand(n[r] + used, dtype=f64, generator=generators[r])   # consume exactly the used draws
+            output[r].extend(em[i][:count])
+            commit[r] = count
+            stats[r] = dict(accepted=accepted, committed=count, rejected_index=None if rejected < 0 else rejected,
+                            extra_token_kind={0: None, 1: 'residual', 2: 'bonus'}[extra],
+                            stop_reason=('round_complete', 'eos', 'budget')[reason])
+        target.commit(verified, commit)
+        draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
+        rounds.append(stats)
+        active = [r for r in active if len(output[r]) < max_new_tokens and stats[r]['stop_reason'] != 'eos']
+    return output, rounds

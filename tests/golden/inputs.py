@@ -80,6 +80,9 @@ TINY_TARGET = dict(vocab_size=1024, hidden_size=256, intermediate_size=512, num_
 TINY_DRAFT = dict(layer_ids=(1, 2), num_layers=2, block_size=7, markov_rank=16, mask_token_id=1023)
 GREEDY_PROMPTS = (64, 256, 2048, 64, 256, 100)
 GREEDY_NEW_TOKENS = 48
+# stochastic speculative decode on the same model: one seeded generator per prompt
+STOCH_ROUND_SEED = 4242
+STOCH_ROUND_TEMPERATURE = 0.9
 
 
 def deterministic_state(named_shapes, seed):

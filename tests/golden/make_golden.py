@@ -291,6 +291,42 @@ def stochastic_fixtures(out):
     out['stochastic_accept'] = rec
 
 
+def stochastic_round_fixtures(out):
+    """The reference's stochastic speculative decode (cached_speculative_sample) on the
+    tiny fp32 model of the greedy case, one seeded CPU generator per prompt."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from dspark_qwen.cached_sampling import cached_speculative_sample
+    from dspark_qwen.cached_target import CachedTarget
+    from dspark_qwen.config import DraftConfig
+    from dspark_qwen.model import DSparkDraft
+    from dspark_qwen.tensor_sampling import TensorRandom
+    cfg = Qwen3Config(**I.TINY_TARGET)
+    cfg._attn_implementation = 'sdpa'
+    model = Qwen3ForCausalLM(cfg).eval()
+    tshapes = {k: tuple(v.shape) for k, v in model.state_dict().items()}
+    model.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(tshapes, 1).items()})
+    spec = DraftConfig(**I.TINY_DRAFT)
+    draft = DSparkDraft(model, spec).eval()
+    dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items()
+               if not k.startswith(('embedding.', 'lm_head.'))}
+    draft.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(dshapes, 2).items()}, strict=False)
+    target = CachedTarget(model, spec.layer_ids)
+    tokens, accepted, residual, bonus = [], [], [], []
+    with torch.no_grad():
+        for i, ids in enumerate(I.greedy_prompts()):
+            rng = TensorRandom(torch.Generator().manual_seed(I.STOCH_ROUND_SEED + i))
+            x = torch.from_numpy(ids)[None]
+            o, rounds = cached_speculative_sample(target, draft, x, I.GREEDY_NEW_TOKENS,
+                                                  temperature=I.STOCH_ROUND_TEMPERATURE, rng=rng)
+            tokens.append(o + [-1] * (I.GREEDY_NEW_TOKENS - len(o)))
+            accepted.append(sum(r['accepted'] for r in rounds))
+            residual.append(sum(r['extra_token_kind'] == 'residual' for r in rounds))
+            bonus.append(sum(r['extra_token_kind'] == 'bonus' for r in rounds))
+    out['stochastic_round'] = dict(tokens=np.array(tokens), accepted=np.array(accepted),
+                                   residual_rounds=np.array(residual), bonus_rounds=np.array(bonus))
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument('--reference', required=True, help='path of a qwen3-dspark checkout')
@@ -304,7 +340,8 @@ def main():
     torch.set_num_threads(4)
     out = {}
     for fn in (draft_fixtures, varlen_fixtures, training_fixtures, layout_fixtures, rope_fixtures,
-               kv_store_fixtures, greedy_fixtures, stochastic_fixtures):
+               kv_store_fixtures, greedy_fixtures, stochastic_fixtures,
+               stochastic_round_fixtures):
         if args.only is None or fn.__name__ in args.only:
             fn(out)
     for name, rec in out.items():
