@@ -306,7 +306,6 @@ struct SchedShared {
   long long req_prefix, last_prefix;
   int req0, qb0, t0;        // item and tile offset of this CTA's first tile
   int req_l, qb_l, t_l;     // item and tile offset of this CTA's last tile
-  int reorder;              // process the last item's part first (see locate_range)
   int issued[kStages];
 };
 
@@ -327,12 +326,6 @@ __device__ __forceinline__ void locate_in_request(const AttnParams& p, int req, 
 // Finds the total tile count and the items holding this CTA's first and last
 // tiles. All threads of the CTA must call it. With at most one request per
 // thread the tile counts are scanned once; otherwise twice (total, then place).
-//
-// Walk order: if the CTA's last item began inside the range and continues into
-// the next CTA's range, the CTA processes that item's part first and then the
-// rest of its range. Its contribution to that cut item then arrives early and
-// the merge of the item (done by whichever contributor arrives last) overlaps
-// with streaming instead of trailing the kernel.
 template <int kThreads>
 __device__ void locate_range(const AttnParams& p, SchedShared& s) {
   const int tid = threadIdx.x;
@@ -393,7 +386,6 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
     s.total = total;
     s.start = start;
     s.end = end;
-    s.reorder = 0;
     if (start < end) {
       if (s.req0 < 0 || s.req_l < 0) {
         atomicOr(&g_device_status, kStatusBadSchedule);
@@ -402,8 +394,6 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
         Item it;
         locate_in_request(p, s.req0, start - s.req_prefix, s.qb0, s.t0, it);
         locate_in_request(p, s.req_l, end - 1 - s.last_prefix, s.qb_l, s.t_l, it);
-        const long long last_start = end - 1 - s.t_l;
-        s.reorder = last_start > start && last_start + it.tiles > end;
       }
     }
   }
@@ -738,9 +728,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   __nv_bfloat16* qw_smem = reinterpret_cast<__nv_bfloat16*>(smem + kSmemWeightOff);
   __nv_bfloat16* kw_smem = qw_smem + kHeadDim;
 
-  // Measured: the two-segment walk helps the plain kernels (cut-item merges no
-  // longer trail the kernel) but slows the fused one, which walks in order.
-  constexpr bool kReorderWalk = !kFused;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (kFused && threadIdx.x < kHeadDim) {
     qw_smem[threadIdx.x] = p.q_w[threadIdx.x];
@@ -771,28 +758,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       int issued[kStages] = {};
       int kl = 0;
       bool prep_done = false;
-      const bool reorder = kReorderWalk && sched.reorder;
-      const long long last_start = end - 1 - sched.t_l;
-      bool ok = true;
-      for (int seg = 0; seg < (reorder ? 2 : 1) && ok; ++seg) {
-        Walker w;
-        long long lo, hi;
-        if (reorder && seg == 0) {
-          w.begin(p, sched.req_l, sched.qb_l, 0);
-          lo = last_start;
-          hi = end;
-        } else {
-          w.begin(p, sched.req0, sched.qb0, sched.t0);
-          lo = start;
-          hi = reorder ? last_start : end;
-        }
-        for (long long gk = lo; gk < hi; ++gk, ++kl) {
+      Walker w;
+      w.begin(p, sched.req0, sched.qb0, sched.t0);
+      {
+        for (long long gk = start; gk < end; ++gk, ++kl) {
           const int stage = kl % kStages;
           const uint32_t parity = ((kl / kStages) & 1) ^ 1;
-          if (!mbar_wait(smem_u32(&empty[stage]), parity)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(smem_u32(&empty[stage]), parity)) break;
           const Tile ti = tile_of(w.it, w.t);
           if (ti.src_b && !prep_done) {
             // launched as a dependent of the verify prep kernel: the source-B
@@ -832,37 +804,23 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     float o[16][4];
     float m_a = -INFINITY, m_b = -INFINITY, l_a = 0.f, l_b = 0.f;
     int kl = 0;
-    const bool reorder = kReorderWalk && sched.reorder;
-    const long long last_start = end - 1 - sched.t_l;
-    bool ok = true;
-    for (int seg = 0; seg < (reorder ? 2 : 1) && ok; ++seg) {
     Walker w;
-    long long lo, hi;
-    if (reorder && seg == 0) {
-      w.begin(p, sched.req_l, sched.qb_l, 0);
-      lo = last_start;
-      hi = end;
-    } else {
-      w.begin(p, sched.req0, sched.qb0, sched.t0);
-      lo = start;
-      hi = reorder ? last_start : end;
-    }
-    long long item_start = lo - w.t;
-    if (seg == 0) asm volatile("griddepcontrol.wait;" ::: "memory");
+    w.begin(p, sched.req0, sched.qb0, sched.t0);
+    long long item_start = start - w.t;
+    // launched as a dependent of the verify prep kernel: q is complete past this
+    // point (a no-op for an ordinary launch)
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     load_q_fragments<kFused>(p, w.it, h, lane, qw_smem, qf);
 #pragma unroll
     for (int j = 0; j < 16; ++j) o[j][0] = o[j][1] = o[j][2] = o[j][3] = 0.f;
     m_a = m_b = -INFINITY;
     l_a = l_b = 0.f;
 
-    for (long long gk = lo; gk < hi; ++gk, ++kl) {
+    for (long long gk = start; gk < end; ++gk, ++kl) {
       const int stage = kl % kStages;
       const uint32_t parity = (kl / kStages) & 1;
       const Item& it = w.it;
-      if (!mbar_wait(smem_u32(&full[stage]), parity)) {
-        ok = false;
-        break;
-      }
+      if (!mbar_wait(smem_u32(&full[stage]), parity)) break;
       const Tile ti = tile_of(it, w.t);
       const bool self_filled = kFused && ti.src_b;
       if (self_filled) {
@@ -970,7 +928,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&empty[stage]));
 
       const bool last_tile = w.t + 1 >= it.tiles;
-      if (last_tile || gk + 1 == hi) {
+      if (last_tile || gk + 1 == end) {
         const float la = quad_sum(l_a), lb = quad_sum(l_b);
         const long long item_end = item_start + it.tiles;
         if (item_start >= start && item_end <= end) {
@@ -988,10 +946,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         } else {
           finish_split_item(p, it, item_start, item_end, start, total, h, lane, o, m_a, m_b, la, lb);
         }
-        if (!last_tile || gk + 1 == hi) {            // this segment ends here
-          ++kl;
-          break;
-        }
+        if (gk + 1 == end) break;                    // the range ends here
         // Next item: its Q replaces qf and its accumulators restart.
         w.advance(p);
         item_start = gk + 1;
@@ -1003,7 +958,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       w.advance(p);
-    }
     }
   }
   // Never leave the CTA with a TMA write still in flight (only possible after
