@@ -100,6 +100,7 @@ struct AttnParams {
   float* part_o;             // [grid][2][8][16][128]
   float* part_ml;            // [grid][2][8][16][2]
   struct MergeEntry* merges; // [grid][8]: the cut item CTA c starts, per KV head
+  long long* ranges;         // [grid][2]: tile range [start, end) of CTA c in this launch
   int grid;
 };
 
@@ -108,8 +109,9 @@ struct AttnParams {
 // entries of all its CTAs, so stale entries are never read.
 struct MergeEntry {
   long long item_start;      // global index of the item's first tile
-  long long total;           // tiles of the launch
-  int first, last;           // contributing CTAs
+  long long item_end;        // one past its last tile
+  int first;                 // CTA holding the first tile (contributors: first, first + 1, ...)
+  int slot_first;            // partial slot of the first contributor
   int q0, nrows;             // output rows of the item
   int valid;
   int pad[3];
@@ -247,24 +249,21 @@ struct Walker {
   }
 };
 
-// CTA c owns global tiles [c*T/G, (c+1)*T/G).
-__device__ __forceinline__ long long range_start(long long c, long long total, long long grid) {
-  return (c * total) / grid;
-}
-
-// The CTA whose range holds global tile x (largest c with range_start(c) <= x).
-__device__ __forceinline__ int cta_of_tile(long long x, long long total, long long grid) {
-  return static_cast<int>(((x + 1) * grid - 1) / total);
-}
-
-__device__ __forceinline__ bool range_empty(int c, long long total, long long grid) {
-  return range_start(c, total, grid) == range_start(c + 1, total, grid);
-}
+// CTA ranges are equal shares of *work*, not of tiles: an item costs its tiles
+// plus kItemCost tiles' worth of switching (the q prologue, the partial write of
+// a cut item and the pipeline refill; per-CTA traces put an item switch at about
+// four tiles of streaming time). The tiles of all items are numbered in request
+// order and each item is preceded by a kItemCost-unit overhead zone in work
+// units; CTA c owns the tiles of work units [c W / G, (c + 1) W / G), a work
+// position inside an overhead zone meaning the item's first tile. Ranges stay
+// contiguous and ordered in tile space, so a CTA that would otherwise take on
+// two or three item switches gets correspondingly fewer tiles.
+constexpr long long kItemCost = 4;
 
 // Ranges a launch of `total` tiles is split into: every CTA of the grid for large
-// launches, and about one range per kMinTilesPerRange tiles for small ones. A cut
-// item is merged by one warp, one contributor after another, so splitting a small
-// launch over all SMs makes the merges (not the streaming) the critical path.
+// launches, and about one range per kMinTilesPerRange tiles for small ones, where
+// the per-CTA fixed costs would otherwise dominate. Every range then holds more
+// than kItemCost work units, so none is empty.
 constexpr long long kMinTilesPerRange = 12;
 __device__ __forceinline__ long long sched_grid(long long total, long long grid) {
   const long long g = total / kMinTilesPerRange;
@@ -309,6 +308,28 @@ struct SchedShared {
   int issued[kStages];
 };
 
+// Tile offset inside request `req` of work offset `off` (its items laid out as
+// [kItemCost overhead units][tiles] each; an offset inside an overhead zone maps
+// to that item's first tile).
+__device__ long long tile_in_request(const AttnParams& p, int req, long long off) {
+  const int nqb = request_qblocks(p, req);
+  long long before = 0;
+  Item it;
+  for (int qb = 0; qb < nqb; ++qb) {
+    if (off < kItemCost) return before;
+    off -= kItemCost;
+    load_item(p, req, qb, it);
+    if (off < it.tiles) return before + off;
+    off -= it.tiles;
+    before += it.tiles;
+  }
+  return before;
+}
+
+__device__ __forceinline__ long long request_work(const AttnParams& p, int req, long long tiles) {
+  return tiles + kItemCost * request_qblocks(p, req);
+}
+
 // (q-block, tile offset) of the tile `off` tiles into request `req`.
 __device__ __forceinline__ void locate_in_request(const AttnParams& p, int req, long long off, int& qb_out,
                                                   int& t_out, Item& it) {
@@ -333,13 +354,28 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
     s.req0 = -1;
     s.req_l = -1;
   }
-  long long total, start, end, chunk_total;
+  long long total, start, end, chunk_total, work;
   if (p.num_requests <= kThreads) {
     const long long t = tid < p.num_requests ? request_tiles(p, tid) : 0;
+    const long long wk = tid < p.num_requests ? request_work(p, tid, t) : 0;
     const long long incl = block_scan<kThreads>(t, s.scan_tmp, total);
+    const long long incl_w = block_scan<kThreads>(wk, s.scan_tmp, work);
     const long long g = sched_grid(total, p.grid);
-    start = blockIdx.x < g ? range_start(blockIdx.x, total, g) : total;
-    end = blockIdx.x < g ? range_start(blockIdx.x + 1, total, g) : total;
+    const long long ws = blockIdx.x < g ? (blockIdx.x * work) / g : work;
+    const long long we = blockIdx.x < g ? ((blockIdx.x + 1) * work) / g : work;
+    if (tid == 0) {
+      s.start = total;
+      s.end = total;
+    }
+    __syncthreads();
+    if (tid < p.num_requests) {
+      const long long ew = incl_w - wk, et = incl - t;
+      if (ew <= ws && ws < incl_w) s.start = et + tile_in_request(p, tid, ws - ew);
+      if (ew <= we && we < incl_w) s.end = et + tile_in_request(p, tid, we - ew);
+    }
+    __syncthreads();
+    start = s.start;
+    end = s.end;
     if (tid < p.num_requests && start < end) {
       const long long excl = incl - t;
       if (excl <= start && start < incl) {
@@ -352,17 +388,45 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
       }
     }
   } else {
-    long long running = 0;
+    long long running = 0, running_w = 0, chunk_w;
     for (int base = 0; base < p.num_requests; base += kThreads) {
       const int i = base + tid;
       const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+      const long long wk = i < p.num_requests ? request_work(p, i, t) : 0;
       block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+      block_scan<kThreads>(wk, s.scan_tmp, chunk_w);
       running += chunk_total;
+      running_w += chunk_w;
     }
     total = running;
+    work = running_w;
     const long long g = sched_grid(total, p.grid);
-    start = blockIdx.x < g ? range_start(blockIdx.x, total, g) : total;
-    end = blockIdx.x < g ? range_start(blockIdx.x + 1, total, g) : total;
+    const long long ws = blockIdx.x < g ? (blockIdx.x * work) / g : work;
+    const long long we = blockIdx.x < g ? ((blockIdx.x + 1) * work) / g : work;
+    if (tid == 0) {
+      s.start = total;
+      s.end = total;
+    }
+    __syncthreads();
+    running = 0;
+    running_w = 0;
+    for (int base = 0; base < p.num_requests; base += kThreads) {
+      const int i = base + tid;
+      const long long t = i < p.num_requests ? request_tiles(p, i) : 0;
+      const long long wk = i < p.num_requests ? request_work(p, i, t) : 0;
+      const long long incl = running + block_scan<kThreads>(t, s.scan_tmp, chunk_total);
+      const long long incl_w = running_w + block_scan<kThreads>(wk, s.scan_tmp, chunk_w);
+      if (i < p.num_requests) {
+        const long long ew = incl_w - wk, et = incl - t;
+        if (ew <= ws && ws < incl_w) s.start = et + tile_in_request(p, i, ws - ew);
+        if (ew <= we && we < incl_w) s.end = et + tile_in_request(p, i, we - ew);
+      }
+      running += chunk_total;
+      running_w += chunk_w;
+    }
+    __syncthreads();
+    start = s.start;
+    end = s.end;
     if (start < end) {
       running = 0;
       for (int base = 0; base < p.num_requests; base += kThreads) {
@@ -386,6 +450,8 @@ __device__ void locate_range(const AttnParams& p, SchedShared& s) {
     s.total = total;
     s.start = start;
     s.end = end;
+    p.ranges[2 * blockIdx.x] = start;                // read by the merge kernel
+    p.ranges[2 * blockIdx.x + 1] = end;
     if (start < end) {
       if (s.req0 < 0 || s.req_l < 0) {
         atomicOr(&g_device_status, kStatusBadSchedule);
@@ -515,13 +581,6 @@ __device__ __forceinline__ void rope_new_rows_in_smem(const AttnParams& p, const
   }
 }
 
-// Partial slot of contributor c for an item starting at tile item_start: slot
-// 1 only when the item began before c's range (c is then the item's first
-// contributor and the item is its last one).
-__device__ __forceinline__ int partial_slot(long long item_start, int c, long long total, long long grid) {
-  return item_start <= range_start(c, total, grid) ? 0 : 1;
-}
-
 // A cut item's contribution from this CTA (warp of KV head h): store the fp32
 // partial O (unnormalised), row max m and row sum l. The CTA holding the
 // item's first tile records the item for split_merge_kernel, which combines
@@ -546,12 +605,14 @@ __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Ite
     __stcg(reinterpret_cast<float2*>(pml + 2 * (g + 8)), make_float2(m_b, l_b));
   }
   if (item_start >= start && lane == 0) {
-    const long long grid = sched_grid(total, p.grid);
+    // Partial slot 1 holds an item that began after the range start (a CTA's
+    // last item), slot 0 one that began at or before it (its first item); every
+    // later contributor holds this item as its first one, in slot 0.
     MergeEntry e;
     e.item_start = item_start;
-    e.total = total;
+    e.item_end = item_end;
     e.first = static_cast<int>(blockIdx.x);
-    e.last = cta_of_tile(item_end - 1, total, grid);
+    e.slot_first = slot;
     e.q0 = it.q0;
     e.nrows = it.nrows;
     e.valid = 1;
@@ -567,8 +628,9 @@ __device__ __forceinline__ void finish_split_item(const AttnParams& p, const Ite
 // (row r: head 2h + r / 8, query row q0 + r % 8), lane l owns d = 4l..4l+3.
 // Two passes over the contributors, four contributors' loads per round: the
 // row maximum M and sum L = sum_c l_c 2^((m_c - M) s), then
-// out = sum_c 2^((m_c - M) s) O_c / L. With at least as many tiles as CTAs no
-// range is empty and only the first contributor can hold the item in slot 1.
+// out = sum_c 2^((m_c - M) s) O_c / L. The contributors are the CTAs from the
+// recorded first one whose ranges (written by every CTA of the launch) start
+// before the item's end; ranges are never empty.
 constexpr int kMergeThreads = 128;
 __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(const AttnParams p) {
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -577,20 +639,26 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(const AttnPa
   const MergeEntry e = p.merges[blockIdx.x];
   if (!e.valid) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long grid = sched_grid(e.total, p.grid);
-  const bool dense = e.total >= grid;
-  const int slot_first = partial_slot(e.item_start, e.first, e.total, grid);
+  // last contributor: ranges are ordered, so the contributors after the first are
+  // the CTAs c > first with range start < item end (counted kMergeThreads at a time)
+  int last = e.first;
+  for (int base = e.first + 1; base < p.grid; base += kMergeThreads) {
+    const int c = base + static_cast<int>(threadIdx.x);
+    const int n = __syncthreads_count(c < p.grid && p.ranges[2 * c] < e.item_end);
+    last += n;
+    if (n < kMergeThreads) break;
+  }
   const float sl2 = p.scale_log2;
   const int my_row = 4 * warp + (lane & 3);   // row whose statistics this lane tracks
   const int d = lane * 4;
   auto block = [&](int c) -> long long {
-    if (c > e.last || (!dense && range_empty(c, e.total, grid))) return -1;
-    const int sl = c == e.first ? slot_first : (dense ? 0 : partial_slot(e.item_start, c, e.total, grid));
+    if (c > last) return -1;
+    const int sl = c == e.first ? e.slot_first : 0;
     return (static_cast<long long>(c) * 2 + sl) * kKVHeads + h;
   };
   float mrow = -INFINITY, lrow = 0.f;
 #pragma unroll 1
-  for (int c = e.first; c <= e.last; c += 4) {
+  for (int c = e.first; c <= last; c += 4) {
     float2 ml[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -612,7 +680,7 @@ __global__ void __launch_bounds__(kMergeThreads) split_merge_kernel(const AttnPa
 #pragma unroll
   for (int r = 0; r < 4; ++r) acc[r] = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll 1
-  for (int c = e.first; c <= e.last; c += 4) {
+  for (int c = e.first; c <= last; c += 4) {
     float4 v[4][4];
     float wl[4];
 #pragma unroll

@@ -104,11 +104,11 @@ int current_device_info(DeviceInfo* out) {
   return device_info(dev, out);
 }
 
-// Workspace: fp32 partials of up to two cut items per CTA, then one merge
-// entry per (CTA, KV head). Every launch rewrites what it reads.
+// Workspace: fp32 partials of up to two cut items per CTA, one merge entry per
+// (CTA, KV head) and each CTA's tile range. Every launch rewrites what it reads.
 constexpr size_t workspace_for_grid(int grid) {
   return static_cast<size_t>(grid) * (2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float) +
-                                      kKVHeads * sizeof(MergeEntry));
+                                      kKVHeads * sizeof(MergeEntry) + 2 * sizeof(long long));
 }
 
 void bind_workspace(AttnParams& p, void* workspace, int grid) {
@@ -117,6 +117,7 @@ void bind_workspace(AttnParams& p, void* workspace, int grid) {
   p.part_ml = reinterpret_cast<float*>(ws + static_cast<size_t>(grid) * 2 * kPartFloatsPerSlot * sizeof(float));
   p.merges = reinterpret_cast<MergeEntry*>(
       ws + static_cast<size_t>(grid) * 2 * (kPartFloatsPerSlot + kPartMlPerSlot) * sizeof(float));
+  p.ranges = reinterpret_cast<long long*>(p.merges + static_cast<size_t>(grid) * kKVHeads);
   p.grid = grid;
 }
 
