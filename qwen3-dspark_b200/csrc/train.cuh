@@ -13,20 +13,24 @@
 // are the context prefix up to the tile's largest anchor, in 128-row blocks,
 // then one 128-row block starting at the tile's first block row.
 //
-// Roles (256 threads, one CTA per SM):
-//   warps 0-3  softmax: thread m owns S/O row m (TMEM lane m); online softmax
-//              with the running max raised only when it grows by more than
-//              2^8 (exact: the final O/l does not depend on the max used),
-//              P (bf16) written back over its own S buffer in TMEM, where the
-//              PV MMA reads it as its A operand. Only a raised max (rare after
-//              the first blocks) waits for the previous PV to rescale O in
-//              TMEM, so the softmax of block n+1 overlaps the PV MMA of block n;
-//   warp 4     TMEM owner and QK issuer (one thread): S = Q K^T into one of
+// Roles (384 threads, one CTA per SM):
+//   warps 0-7  softmax: warps w and w + 4 share S/O rows 32w.. (TMEM lanes of
+//              quarter w) and split each row's columns in halves; online
+//              softmax with the running max raised only when it grows by more
+//              than 2^8 (exact: the final O/l does not depend on the max used),
+//              the row maximum of each block and the final row sum exchanged
+//              between the two halves through TMEM and a bounded mbarrier
+//              wait; P (bf16) written back over its own S buffer in TMEM,
+//              where the PV MMA reads it as its A operand. Only a raised max
+//              (rare after the first blocks) waits for the previous PV to
+//              rescale O in TMEM, so the softmax of block n+1 overlaps the PV
+//              MMA of block n;
+//   warp 8     TMEM owner and QK issuer (one thread): S = Q K^T into one of
 //              two S buffers;
-//   warp 7     PV issuer (one thread): O += P V into the O accumulator;
+//   warp 11    PV issuer (one thread): O += P V into the O accumulator;
 //              completion is reported through tcgen05.commit on mbarriers;
-//   warp 5     TMA producer of Q (per tile) and K (3-stage ring), one thread;
-//   warp 6     TMA producer of V (3-stage ring), one thread. Separate K and V
+//   warp 9     TMA producer of Q (per tile) and K (3-stage ring), one thread;
+//   warp 10    TMA producer of V (3-stage ring), one thread. Separate K and V
 //              producers let a K stage refill as soon as its QK is done.
 // Every wait is bounded; a timed-out wait raises a CTA abort flag that ends all
 // roles, the MMA thread drains its MMAs, the producer waits for its copies in
@@ -37,7 +41,9 @@
 namespace dspark {
 namespace train {
 
-constexpr int kThreads = 256;
+constexpr int kSoftmaxWarps = 8;     // two per TMEM lane quarter: column halves of each row
+constexpr int kQkWarp = 8, kQkProducerWarp = 9, kVProducerWarp = 10, kPvWarp = 11;
+constexpr int kThreads = 12 * 32;
 constexpr int kTileQ = 64;          // query rows per tile (x2 heads = 128 MMA rows)
 constexpr int kKeyBlock = 128;      // keys per S tile
 constexpr int kMaxTileBlocks = 12;  // anchor slots per tile
@@ -80,7 +86,7 @@ constexpr uint32_t kSmemBar = kSmemV + kStages * 32768;
 enum Barrier {
   kBarQFull = 0, kBarQEmpty, kBarKFull0, kBarKEmpty0 = kBarKFull0 + kStages, kBarVFull0 = kBarKEmpty0 + kStages,
   kBarVEmpty0 = kBarVFull0 + kStages, kBarSFull0 = kBarVEmpty0 + kStages, kBarPFull0 = kBarSFull0 + 2,
-  kBarODone0 = kBarPFull0 + 2, kBarOFree = kBarODone0 + 2, kBarDrain, kNumBarriers
+  kBarODone0 = kBarPFull0 + 2, kBarOFree = kBarODone0 + 2, kBarDrain, kBarX0, kNumBarriers = kBarX0 + 4
 };
 constexpr uint32_t kSmemTmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemTmemSlot + 4;
@@ -88,9 +94,11 @@ constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 4;
 
 // TMEM columns: two S buffers and the O accumulator, 128 fp32 columns each. P
 // (bf16, two per column) overwrites the first 64 columns of its own S buffer
-// and is the A operand of the PV MMA straight from TMEM.
+// and is the A operand of the PV MMA straight from TMEM. Columns from kTmemX
+// carry the row maxima and sums the two softmax warps of a lane quarter
+// exchange (each warp owns half of every row's columns).
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemS = 0, kTmemO = 256;
+constexpr uint32_t kTmemS = 0, kTmemO = 256, kTmemX = 384;
 
 // ---------------------------------------------------------------- tcgen05 PTX
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
@@ -213,6 +221,26 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const float (&v)[32]) 
       "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
       "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
       : "memory");
+}
+
+// One fp32 column per lane (32 lanes x 1 column), completed in the statement.
+__device__ __forceinline__ void tmem_st1(uint32_t taddr, float v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x1.b32 [%0], {%1};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v))
+      : "memory");
+}
+
+__device__ __forceinline__ float tmem_ld1(uint32_t taddr) {
+  uint32_t r;
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x1.b32 {%0}, [%1];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r)
+      : "r"(taddr)
+      : "memory");
+  return __uint_as_float(r);
 }
 
 // Bounded wait that also gives up as soon as another role has raised the CTA
@@ -385,16 +413,36 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
                                              uint8_t* smem, uint32_t bars, uint32_t tmem, __nv_bfloat16* out,
                                              float scale_log2, volatile int* abort_flag) {
   auto bar = [&](int i) { return bars + 8u * i; };
-  const int m = threadIdx.x;                       // S/O row == TMEM lane
+  // warp w handles TMEM lanes 32 (w % 4) .. (rows) and column half w / 4 of every
+  // row: keys [64 h, 64 h + 64) of S, their packed P columns [32 h, 32 h + 32) and
+  // O columns (d) [64 h, 64 h + 64); the row maximum of each block and the final
+  // row sum are exchanged with warp w ^ 4 through TMEM columns kTmemX.. and the
+  // quarter's mbarrier (both warps arrive, each waits with a bound).
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int half = warp >> 2, quarter = warp & 3;
+  const int m = quarter * 32 + lane;               // S/O row == TMEM lane
   const int qi = m >> 1;                           // query row inside the tile
-  const uint32_t lane_addr = static_cast<uint32_t>(m & ~31) << 16;
+  const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+  const uint32_t xbar = bar(kBarX0 + quarter);
+  uint32_t xcount = 0;                             // exchanges done (barrier phase)
   int gb = 0;
   bool ok = true;
+  auto exchange = [&](uint32_t col0, float mine, float& theirs) {
+    tmem_st1(tmem + lane_addr + col0 + half, mine);
+    tc_fence_before();
+    mbar_arrive(xbar);
+    const bool w = wait_or_abort(xbar, xcount & 1, abort_flag);
+    ++xcount;
+    if (!__all_sync(0xffffffffu, w)) return false;
+    tc_fence_after();
+    theirs = tmem_ld1(tmem + lane_addr + col0 + (half ^ 1));
+    return true;
+  };
   for (int idx = first; idx < last && ok; ++idx) {
     const int* ip = items + static_cast<size_t>(idx) * kItemWords;
     Item x;
     if (!load_item(ip, total_q, total_k, x)) {
-      if (m == 0) atomicOr(&g_device_status, kStatusBadArgument);
+      if (threadIdx.x == 0) atomicOr(&g_device_status, kStatusBadArgument);
       continue;
     }
     const int nb = x.key_blocks(), nctx = nb - 1;
@@ -408,8 +456,9 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
       ok = wait_or_abort(bar(kBarSFull0 + (g & 1)), (g >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      float s[128];
-      tmem_ld128(tmem + lane_addr + kTmemS + (g & 1) * 128, s);
+      float s[64];
+      tmem_ld32(tmem + lane_addr + kTmemS + (g & 1) * 128 + half * 64, *reinterpret_cast<float(*)[32]>(&s[0]));
+      tmem_ld32(tmem + lane_addr + kTmemS + (g & 1) * 128 + half * 64 + 32, *reinterpret_cast<float(*)[32]>(&s[32]));
       int lo, hi;
       if (n < nctx) {
         lo = 0;
@@ -419,18 +468,23 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         hi = min(lo + x.bs, kKeyBlock);
       }
       if (!row_ok) hi = lo;
+      lo -= half * 64;                             // into this half's key index
+      hi -= half * 64;
       float mb = -INFINITY;
-      if (lo == 0 && hi == kKeyBlock) {
+      if (lo <= 0 && hi >= 64) {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) mb = fmaxf(mb, s[i]);
+        for (int i = 0; i < 64; ++i) mb = fmaxf(mb, s[i]);
       } else {
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
+        for (int i = 0; i < 64; ++i) {
           const bool vis = i >= lo && i < hi;
           s[i] = vis ? s[i] : -INFINITY;
           mb = fmaxf(mb, s[i]);
         }
       }
+      float mo;
+      if (!(ok = exchange(kTmemX + (xcount & 1) * 2, mb, mo))) break;
+      mb = fmaxf(mb, mo);
       const float m_new = fmaxf(m_run, mb * scale_log2);
       const bool resc = m_new > m_run + 8.f;
       float alpha = 1.f;
@@ -439,9 +493,9 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         m_run = m_new;
       }
       float sum = 0.f;
-      uint32_t pk[64];
+      uint32_t pk[32];
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
+      for (int i = 0; i < 32; ++i) {
         const float p0 = ex2(fmaf(s[2 * i], scale_log2, -m_run));
         const float p1 = ex2(fmaf(s[2 * i + 1], scale_log2, -m_run));
         sum += p0 + p1;
@@ -454,33 +508,35 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        for (int c = 0; c < 2; ++c) {
           float o[32];
-          tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
+          tmem_ld32(tmem + lane_addr + kTmemO + half * 64 + c * 32, o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] *= alpha;
-          tmem_st32(tmem + lane_addr + kTmemO + c * 32, o);
+          tmem_st32(tmem + lane_addr + kTmemO + half * 64 + c * 32, o);
         }
       }
-      // P over the first 64 columns of its own S buffer (S is already in registers)
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-        tmem_st32(tmem + lane_addr + kTmemS + (g & 1) * 128 + c * 32,
-                  *reinterpret_cast<const float(*)[32]>(&pk[c * 32]));
+      // P of this half's 64 keys: packed columns [32 half, +32) of its own S buffer
+      // (the other warp has read its S columns: it arrived at the exchange after)
+      tmem_st32(tmem + lane_addr + kTmemS + (g & 1) * 128 + half * 32, *reinterpret_cast<const float(*)[32]>(pk));
       tc_fence_before();
       mbar_arrive(bar(kBarPFull0 + (g & 1)));
     }
     if (!ok) break;
     gb += nb;
+    float lo_other;
+    if (!(ok = exchange(kTmemX + 4, l, lo_other))) break;
+    l += lo_other;
     ok = wait_or_abort(bar(kBarODone0 + ((gb - 1) & 1)), ((gb - 1) >> 1) & 1, abort_flag);
     if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
     tc_fence_after();
     const float inv_l = row_ok ? 1.f / l : 0.f;
-    __nv_bfloat16* orow = out + (static_cast<size_t>(x.q_row0 + (row_ok ? qi : 0)) * 16 + 2 * x.head + (m & 1)) * 128;
+    __nv_bfloat16* orow = out + (static_cast<size_t>(x.q_row0 + (row_ok ? qi : 0)) * 16 + 2 * x.head + (m & 1)) * 128 +
+                          half * 64;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
+    for (int c = 0; c < 2; ++c) {
       float o[32];
-      tmem_ld32(tmem + lane_addr + kTmemO + c * 32, o);
+      tmem_ld32(tmem + lane_addr + kTmemO + half * 64 + c * 32, o);
       if (row_ok) {
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -527,31 +583,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBarriers; ++i)
-      mbar_init(bars + 8u * i,
-                (i == kBarPFull0 || i == kBarPFull0 + 1 || i == kBarOFree) ? 128u : (i == kBarDrain ? 2u : 1u));
+      mbar_init(bars + 8u * i, (i == kBarPFull0 || i == kBarPFull0 + 1 || i == kBarOFree)
+                                   ? 32u * kSoftmaxWarps
+                                   : (i >= kBarX0 ? 64u : (i == kBarDrain ? 2u : 1u)));
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5 && lane == 0) {
+  if (warp == kQkProducerWarp && lane == 0) {
     prefetch_tmap(&qmap);
     prefetch_tmap(&kmap);
   }
-  if (warp == 6 && lane == 0) prefetch_tmap(&vmap);
-  if (warp == 4) tmem_alloc(sbase + kSmemTmemSlot, kTmemCols);
+  if (warp == kVProducerWarp && lane == 0) prefetch_tmap(&vmap);
+  if (warp == kQkWarp) tmem_alloc(sbase + kSmemTmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + kSmemTmemSlot);
 
-  if (warp < 4) {
+  if (warp < kSoftmaxWarps) {
     softmax_role(items, first, last, total_q, total_k, smem, bars, tmem, out, scale_log2, abort_flag);
-  } else if (warp == 4) {
+  } else if (warp == kQkWarp) {
     if (lane == 0) qk_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
     __syncwarp();
-  } else if (warp == 7) {
+  } else if (warp == kPvWarp) {
     if (lane == 0) pv_role(items, first, last, total_q, total_k, sbase, bars, tmem, abort_flag);
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kQkProducerWarp) {
     if (lane == 0)
       producer_role<true>(&qmap, &kmap, items, first, last, total_q, total_k, sbase, bars, abort_flag);
     __syncwarp();
@@ -563,7 +620,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+  if (warp == kQkWarp) tmem_dealloc(tmem, kTmemCols);
 }
 
 }  // namespace train
