@@ -207,12 +207,18 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
             eos_ids)
         res = result.cpu().tolist()
         em = emitted.cpu().tolist()
+        bad = [(r, res[i][6]) for i, r in enumerate(active) if res[i][6]]
+        if bad:
+            # nothing of this round is kept: the caches roll back and the generators
+            # return to where the round started
+            target.abort(verified)
+            for r in active:
+                generators[r].set_state(states[r])
+            r, status = bad[0]
+            raise ValueError(f'stochastic acceptance refused request {r}: {STOCHASTIC_STATUS[status]}')
         commit, stats = {}, {}
         for i, r in enumerate(active):
-            count, accepted, rejected, extra, reason, used, status, _ = res[i]
-            if status:
-                target.abort(verified)
-                raise ValueError(f'stochastic acceptance refused request {r}: {STOCHASTIC_STATUS[status]}')
+            count, accepted, rejected, extra, reason, used, _status, _ = res[i]
             generators[r].set_state(states[r])
             torch.rand(n[r] + used, dtype=f64, generator=generators[r])   # consume exactly the used draws
             output[r].extend(em[i][:count])
