@@ -803,7 +803,10 @@ def round5_leg(pkg, device, rank, warmup):
         ps = prompts(tag)
         torch.cuda.synchronize(device)
         t0 = time.perf_counter()
-        out, rounds = pkg.speculative_greedy(target, pdraft, ps, ROUND5['new_tokens'], graph=graph)
+        if graph == 'pipelined':
+            out, rounds = pkg.speculative_greedy_pipelined(target, pdraft, ps, ROUND5['new_tokens'])
+        else:
+            out, rounds = pkg.speculative_greedy(target, pdraft, ps, ROUND5['new_tokens'], graph=graph)
         torch.cuda.synchronize(device)
         dt = time.perf_counter() - t0
         release(ps)
@@ -813,6 +816,9 @@ def round5_leg(pkg, device, rank, warmup):
     pkg.speculative_greedy(target, pdraft, prompts('gw'), 4, graph=True)   # capture + warm the replayed path
     release([f'gw{i}' for i in range(len(lens))])
     out_g, rounds_g, total_g = timed_loop('g', True)
+    pkg.speculative_greedy_pipelined(target, pdraft, prompts('pw'), 4)   # warm the pipelined path
+    release([f'pw{i}' for i in range(len(lens))])
+    out_p, rounds_p, total_p = timed_loop('q', 'pipelined')
     # prefill alone (same prompts, fresh requests), to split the time
     ps = prompts('p')
     for r in ps:
@@ -835,6 +841,9 @@ def round5_leg(pkg, device, rank, warmup):
                 generated_tokens=generated, rounds=len(rounds), total_s=total_s, prefill_s=prefill_s,
                 decode_tok_per_s=(generated - len(out)) / decode_s, total_tok_per_s=generated / total_s,
                 graph_total_s=total_g, graph_decode_tok_per_s=(generated - len(out)) / decode_g,
+                pipelined_total_s=total_p,
+                pipelined_decode_tok_per_s=(generated - len(out)) / max(total_p - prefill_s, 1e-9),
+                pipelined_total_tok_per_s=generated / total_p, graph_total_tok_per_s=generated / total_g,
                 mean_accepted_per_round=float(np.mean(accepted)) if accepted else 0.0,
                 note='random draft weights: acceptance is ~0, so every round emits one token per request; '
                      'eager and graph loops run different random prompts of the same lengths '
@@ -954,7 +963,8 @@ def run_b200(args):
         status = pkg.read_device_status(clear=True)
         if rank == 0:
             print(json.dumps(_finite(dict(metric='config-5 greedy speculative decode tokens/s per GPU',
-                                          value=max(res['decode_tok_per_s'], res['graph_decode_tok_per_s']), unit='tok/s', n_gpus=world, steps=1,
+                                          value=max(res['decode_tok_per_s'], res['graph_decode_tok_per_s'],
+                                                    res['pipelined_decode_tok_per_s']), unit='tok/s', n_gpus=world, steps=1,
                                           warmup=args.warmup, ms_per_step=res['total_s'] * 1e3 / max(res['rounds'], 1),
                                           higher_is_better=True, dtype='bf16', data='synthetic (random weights)',
                                           round5=res, device_status=status))), flush=True)

@@ -30,7 +30,7 @@ def __getattr__(name):
     if name == 'B200Qwen3Target':
         from .target import B200Qwen3Target
         return B200Qwen3Target
-    if name in ('speculative_greedy', 'speculative_sample', 'accept_greedy'):
+    if name in ('speculative_greedy', 'speculative_greedy_pipelined', 'speculative_sample', 'accept_greedy'):
         from . import speculative
         return getattr(speculative, name)
     raise AttributeError(name)
@@ -43,6 +43,6 @@ launch_count = _lib.launch_count
 __all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'TRAIN_BACKEND', 'B200CapacityKernel',
            'B200DraftKernel', 'B200TrainingLayoutKernel', 'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH',
            'PackedLayout', 'PersistentAttentionLayout', 'TrainingLayout', 'Slot', 'Transaction', 'B200PackedDraft',
-           'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target', 'speculative_greedy', 'speculative_sample', 'accept_greedy', 'build',
+           'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target', 'speculative_greedy', 'speculative_greedy_pipelined', 'speculative_sample', 'accept_greedy', 'build',
            'draft_append', 'float64_law', 'greedy_accept', 'markov_greedy', 'sample_rows', 'stochastic_accept', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
            'segment_attention']

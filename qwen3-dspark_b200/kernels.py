@@ -258,6 +258,8 @@ def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
 
     ``logits`` [N, vocab] (bf16/fp32) are the target's logits of the N verified rows,
     ``tokens`` [N] int64 the verified chunk tokens (per request: anchor, proposals),
+    ``eos_ids`` the stop tokens (an iterable, or an int64 device tensor, which avoids a
+    host-to-device copy per call),
     ``cu_query`` int32 [R+1] the request boundaries. ``budget`` (optional, int32 [R])
     caps each request's committed tokens. Returns device tensors
     ``(pred [N] int32, accepted [R] int32, n_commit [R] int32, emitted [N] int64)``
@@ -271,7 +273,12 @@ def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
         raise ValueError('logits [N,V] bf16/fp32 (unit column stride), tokens [N] int64 and int32 cu_query '
                          'on one CUDA device required')
     r = cu_query.numel() - 1
-    eos = torch.tensor(sorted(set(int(e) for e in eos_ids)), dtype=torch.long, device=device)
+    if isinstance(eos_ids, torch.Tensor):
+        if eos_ids.dtype != torch.long or eos_ids.device != device or eos_ids.ndim != 1:
+            raise ValueError('eos_ids tensor must be int64 [n] on the logits device')
+        eos = eos_ids.contiguous()
+    else:
+        eos = torch.tensor(sorted(set(int(e) for e in eos_ids)), dtype=torch.long, device=device)
     if budget is not None and (budget.shape != (r,) or budget.dtype != torch.int32 or budget.device != device):
         raise ValueError('budget must be int32 [R] on the logits device')
     n = logits.shape[0]

@@ -231,3 +231,151 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
         rounds.append(stats)
         active = [r for r in active if len(output[r]) < max_new_tokens and stats[r]['stop_reason'] != 'eos']
     return output, rounds
+
+
+@torch.no_grad()
+def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids=()):
+    """``speculative_greedy(graph=True)`` with the round state kept on the GPU, so the
+    host never sits between two rounds (the device-side transaction metadata and
+    accept-to-commit path of the reference's captured verify,
+    persistent_qwen_graph.py:198-275 and persistent_target_kv.py:369-415).
+
+    Every round runs the captured draft proposal, the captured target verify, the
+    on-device greedy accept, the commit kernel and the captured fixed-shape draft
+    append; between them, device ops derive the next round's inputs from this
+    round's results: anchors (the last committed token), the target's context lengths
+    and positions, the draft's lengths and positions, and each request's remaining
+    budget (zeroed by an EOS). The host enqueues round k + 1 before it reads round k's
+    small result vector, so the GPU never waits for it. A finished request stays in
+    the fixed-shape batch and commits nothing. The same tokens as ``speculative_greedy``;
+    needs a bf16 draft whose Markov head runs on the fused kernel. Returns
+    ({request: tokens}, rounds)."""
+    from .kernels import greedy_accept
+    from . import _lib
+    if type(max_new_tokens) is not int or max_new_tokens < 0:
+        raise ValueError('max_new_tokens must be a nonnegative integer')
+    if not draft._graph_ready():
+        raise ValueError('The pipelined loop needs a bf16 draft whose Markov head runs on the fused kernel')
+    eos_ids = sorted(set(int(e) for e in eos_ids))
+    dev = target.device
+    for r in prompts:
+        target.add_request(r)
+        draft.add_request(r)
+    if max_new_tokens == 0:
+        return {r: [] for r in prompts}, []
+    features = target.prefill(prompts)
+    last = target.predict(features, last_only=True)
+    requests = list(prompts)
+    output = {r: [int(last[r].argmax(-1).item())] for r in requests}
+    draft.append_committed({r: features.context_for(r) for r in requests})
+    if max_new_tokens == 1 or all(output[r][-1] in eos_ids for r in requests):
+        return output, []
+    R, size = len(requests), draft.draft.spec.block_size
+    width = size + 1
+    store = target.pool
+    handles = [target._handles[r] for r in requests]
+    slots = [h.index for h in handles]
+    # -- fixed buffers of the three captured programs -----------------------------------
+    bucket = QueryBucket((width,) * R)
+    if bucket not in target._graphs:
+        target.capture(bucket)
+    tg = target._graphs[bucket]
+    tmeta = store.bind_bucket(bucket).meta
+    if R not in draft.__dict__.get('_graphs', {}):
+        draft.capture_propose(R)
+    pg = draft._graphs[R]
+    if (R, width) not in draft.__dict__.get('_append_graphs', {}):
+        draft.capture_append(R, width)
+    ag = draft._append_graphs[(R, width)]
+    i32 = torch.int32
+    cu_t = [width * i for i in range(R + 1)]
+    ctx0 = [store._lengths[s] for s in slots]
+    dlen0 = [draft._lengths[r] for r in requests]
+    if any(c + max_new_tokens + width > store.capacities[s] for c, s in zip(ctx0, slots)):
+        raise ValueError('Request slots cannot hold max_new_tokens plus one verify chunk')
+    tmeta.copy_(torch.tensor(cu_t + [store.slot_rows[s] for s in slots] + ctx0
+                             + [store.capacities[s] for s in slots], dtype=i32))
+    pg['meta'].copy_(torch.tensor([size * i for i in range(R + 1)]
+                                  + [draft.slot_rows[draft._slots[r]] for r in requests] + dlen0 + [size] * R,
+                                  dtype=i32))
+    ag['meta'].copy_(torch.tensor(cu_t + [draft.slot_rows[draft._slots[r]] for r in requests] + dlen0 + [0] * R,
+                                  dtype=i32))
+    ctx = tmeta[2 * R + 1:3 * R + 1]                  # target context lengths (device state)
+    dlen = pg['meta'][2 * R + 1:3 * R + 1]            # draft context lengths (device state)
+    anchors = torch.tensor([output[r][-1] for r in requests], dtype=torch.long, device=dev)
+    budget = torch.tensor([max_new_tokens - 1 if output[r][-1] not in eos_ids else 0 for r in requests],
+                          dtype=i32, device=dev)
+    cu_dev = torch.tensor(cu_t, dtype=i32, device=dev)
+    rep_t = torch.arange(R, device=dev).repeat_interleave(width)
+    off_t = torch.arange(width, device=dev).repeat(R)
+    rep_d = torch.arange(R, device=dev).repeat_interleave(size)
+    off_d = torch.arange(size, device=dev).repeat(R)
+    lm_head = target.model.get_output_embeddings()
+    eos_dev = torch.tensor(eos_ids, dtype=torch.long, device=dev)
+    lib = _lib.load_library()
+    stream = torch.cuda.current_stream(dev)
+    res_host = [torch.empty(2 * R + R * width, dtype=torch.long).pin_memory() for _ in range(2)]
+    events = [torch.cuda.Event() for _ in range(2)]
+
+    def launch_round(k):
+        pg['anchors'].copy_(anchors)
+        pg['pos'].copy_((dlen.long()[rep_d] + off_d))
+        pg['graph'].replay()
+        tg['ids'][0].copy_(torch.cat((anchors[:, None], pg['tokens']), dim=1).reshape(-1))
+        tg['pos'][0].copy_(ctx.long()[rep_t] + off_t)
+        tg['graph'].replay()
+        logits = lm_head(tg['last'])[0]
+        _pred, accepted, n_commit, emitted = greedy_accept(logits, tg['ids'][0], cu_dev, eos_dev, budget)
+        # commit the verified prefixes (rollback of the rest), all layers, one launch
+        _lib.check(lib.dspark_commit_kv(
+            store._keys.data_ptr(), store._values.data_ptr(), store.scratch_keys.data_ptr(),
+            store.scratch_values.data_ptr(), tmeta.data_ptr(), tmeta[R + 1:].data_ptr(), ctx.data_ptr(),
+            tmeta[3 * R + 1:].data_ptr(), n_commit.data_ptr(), R, store.layers, store.rows_per_layer,
+            store.max_query_tokens, _lib.DTYPE_F32 if store.dtype == torch.float32 else _lib.DTYPE_BF16,
+            stream.cuda_stream), 'dspark_commit_kv')
+        ctx.add_(n_commit)
+        # the draft projects the committed rows of every verified chunk
+        ag['feat'].copy_(tg['context'])
+        ag['meta'][2 * R + 1:3 * R + 1].copy_(dlen)
+        ag['meta'][3 * R + 1:].copy_(n_commit)
+        ag['graph'].replay()
+        dlen.add_(n_commit)
+        last_idx = cu_dev[:-1].long() + (n_commit.long() - 1).clamp(min=0)
+        last_tok = emitted[last_idx]
+        anchors.copy_(torch.where(n_commit > 0, last_tok, anchors))
+        hit = (n_commit > 0) & torch.isin(last_tok, eos_dev) if eos_ids else torch.zeros_like(n_commit, dtype=torch.bool)
+        budget.copy_(torch.where(hit, torch.zeros_like(budget), budget - n_commit))
+        buf = res_host[k & 1]
+        buf.copy_(torch.cat((accepted.long(), n_commit.long(), emitted)), non_blocking=True)
+        events[k & 1].record(stream)
+
+    rounds = []
+    done = {r: output[r][-1] in eos_ids for r in requests}
+    launch_round(0)
+    k = 0
+    while True:
+        if not all(done.values()):
+            launch_round(k + 1)                        # enqueued before round k is read
+        events[k & 1].synchronize()
+        host = res_host[k & 1].tolist()
+        stats = {}
+        for i, r in enumerate(requests):
+            if done[r]:
+                continue
+            n = host[R + i]
+            committed = host[2 * R + width * i:2 * R + width * i + n]
+            output[r].extend(committed)
+            stats[r] = dict(accepted=host[i], committed=n)
+            if len(output[r]) >= max_new_tokens or (committed and committed[-1] in eos_ids):
+                done[r] = True
+        rounds.append(stats)
+        if all(done.values()):
+            break
+        k += 1
+    torch.cuda.synchronize(dev)
+    # the host mirrors of the committed lengths follow the device state
+    for s, r, c in zip(slots, requests, ctx.tolist()):
+        store._lengths[s] = c
+    for r, d in zip(requests, dlen.tolist()):
+        draft._lengths[r] = d
+    return output, rounds

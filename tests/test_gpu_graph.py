@@ -125,12 +125,14 @@ def test_graph_refusals(pkg):
 
 
 def test_speculative_loop_with_graph_replay_gives_the_same_tokens(pkg):
-    """speculative_greedy(graph=True) (target verify replayed per query bucket) emits the
-    tokens of the eager loop on the same bf16 model and prompts."""
+    """speculative_greedy(graph=True) (target verify, draft proposal and draft append
+    replayed) and speculative_greedy_pipelined (the round state kept on the GPU, the
+    host one round behind) emit the tokens of the eager loop on the same bf16 model and
+    prompts."""
     model = tiny_bf16_model()
     spec = pkg.DraftSpec(**dict(I.TINY_DRAFT, markov_rank=64))
     outs = []
-    for graph in (False, True):
+    for graph in (False, True, 'pipelined'):
         draft = pkg.DSparkDraftModel(model, spec).eval()
         dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items()
                    if not k.startswith(('embedding.', 'lm_head.'))}
@@ -140,8 +142,14 @@ def test_speculative_loop_with_graph_replay_gives_the_same_tokens(pkg):
         target = pkg.B200Qwen3Target(model, spec.layer_ids, slots=4, context_capacity=400, max_query_tokens=700)
         pdraft = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=400)
         prompts = {f'r{i}': torch.from_numpy(ids)[None].to(dev()) for i, ids in enumerate(I.greedy_prompts()[3:6])}
-        out, rounds = pkg.speculative_greedy(target, pdraft, prompts, 24, graph=graph)
+        if graph == 'pipelined':
+            out, rounds = pkg.speculative_greedy_pipelined(target, pdraft, prompts, 24, eos_ids=(7,))
+            # the host mirrors of the committed lengths follow the device state
+            assert all(target.lengths[r] == prompts[r].shape[1] + len(out[r]) - 1 for r in prompts)
+            assert all(pdraft.lengths[r] == target.lengths[r] for r in prompts)
+        else:
+            out, rounds = pkg.speculative_greedy(target, pdraft, prompts, 24, eos_ids=(7,), graph=graph)
         outs.append(out)
         target.close()
-    assert outs[0] == outs[1]
+    assert outs[0] == outs[1] == outs[2]
     status_clean(pkg)
