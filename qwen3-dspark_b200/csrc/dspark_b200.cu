@@ -532,6 +532,7 @@ int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab
   p.prev_stride = prev_stride;
   p.hidden = static_cast<const __nv_bfloat16*>(hidden);
   p.hidden_dim = hidden_dim;
+  p.conf_vec = hidden_dim % 8 == 0 && aligned(hidden, 16) && aligned(conf_w, 16);
   p.conf_w = static_cast<const __nv_bfloat16*>(conf_w);
   p.conf_b = conf_b;
   p.tokens = tokens;

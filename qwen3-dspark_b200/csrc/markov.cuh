@@ -12,14 +12,18 @@
 // weight per tile and K = rank puts each logits tile in TMEM, where thread r
 // (TMEM lane r) adds its base row, rounds like the reference's bf16 arithmetic
 // (projection output to bf16, then the sum to bf16) and keeps a running
-// first-maximum. Each CTA publishes one packed 64-bit atomicMax per request
-// (order-preserving value bits high, inverted index low, so ties resolve to the
-// lowest index); the last CTA to finish writes the tokens and clears the scratch.
+// first-maximum: each bf16 logit becomes an order-preserving 16-bit key (-0
+// folded onto +0, NaN above everything, as torch.argmax orders them) packed
+// above its inverted column, so one unsigned max per value keeps the largest
+// value at its lowest index. Each CTA publishes one packed 64-bit atomicMax per
+// request (key high, inverted index low); the last CTA to finish writes the
+// tokens and clears the scratch.
 //
 // Roles (192 threads, persistent CTAs over the vocabulary tiles):
-//   warps 0-3  gather emb rows into shared memory (A operand), confidence (one
-//              warp per request, spread over the CTAs), epilogue (thread r =
-//              request r = TMEM lane r);
+//   warps 0-3  gather emb rows into shared memory (A operand), epilogue
+//              (thread r = request r = TMEM lane r; the base row of the next
+//              tile is loaded while the current tile is reduced), then the
+//              confidence (one warp per request, spread over the CTAs);
 //   warp 4     TMEM owner and MMA issuer (one thread);
 //   warp 5     TMA producer of the projection-weight tiles (two stages).
 #pragma once
@@ -63,6 +67,7 @@ struct Params {
   long long prev_stride;
   const __nv_bfloat16* hidden;      // [R * base_stride_r, H] backbone output (confidence input)
   int hidden_dim;
+  int conf_vec;                     // hidden rows, conf_w and hidden_dim allow 16-byte loads
   const __nv_bfloat16* conf_w;      // [H + rank] confidence.weight
   float conf_b;
   long long* tokens;                // tokens[r * tok_stride + k] = next token
@@ -76,13 +81,46 @@ struct Params {
   int tiles;                        // ceil(V / 128)
 };
 
-// Unsigned key ordered like the float (for non-NaN values).
-__device__ __forceinline__ unsigned int order_key(float f) {
-  const unsigned int b = __float_as_uint(f);
-  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// Two bf16 values (lo, hi halves) -> two 16-bit keys ordered like the values:
+// -0 is first turned into +0 (they compare equal), then negative values map to
+// ~b and others to b | 0x8000. A canonical NaN (0x7fff, what the conversions
+// produce) gets the largest key; no value gets key 0.
+__device__ __forceinline__ uint32_t bf16x2_order_keys(uint32_t b) {
+  const uint32_t nonzero = ((b & 0x7fff7fffu) + 0x7fff7fffu) & 0x80008000u;   // bit 15: magnitude != 0
+  b &= nonzero | 0x7fff7fffu;
+  const uint32_t neg = (b >> 15) & 0x00010001u;
+  return b ^ ((neg * 0x7fffu) | 0x80008000u);
 }
 
-__device__ __forceinline__ float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+// 32 lanes x 64 fp32 columns from TMEM (two loads, one wait).
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  float (&a)[32] = *reinterpret_cast<float(*)[32]>(&v[0]);
+  float (&b)[32] = *reinterpret_cast<float(*)[32]>(&v[32]);
+  uint32_t ra[32], rb[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%64];\n\t"
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,"
+      "%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%65];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(ra[0]), "=r"(ra[1]), "=r"(ra[2]), "=r"(ra[3]), "=r"(ra[4]), "=r"(ra[5]), "=r"(ra[6]), "=r"(ra[7]),
+        "=r"(ra[8]), "=r"(ra[9]), "=r"(ra[10]), "=r"(ra[11]), "=r"(ra[12]), "=r"(ra[13]), "=r"(ra[14]), "=r"(ra[15]),
+        "=r"(ra[16]), "=r"(ra[17]), "=r"(ra[18]), "=r"(ra[19]), "=r"(ra[20]), "=r"(ra[21]), "=r"(ra[22]), "=r"(ra[23]),
+        "=r"(ra[24]), "=r"(ra[25]), "=r"(ra[26]), "=r"(ra[27]), "=r"(ra[28]), "=r"(ra[29]), "=r"(ra[30]), "=r"(ra[31]),
+        "=r"(rb[0]), "=r"(rb[1]), "=r"(rb[2]), "=r"(rb[3]), "=r"(rb[4]), "=r"(rb[5]), "=r"(rb[6]), "=r"(rb[7]),
+        "=r"(rb[8]), "=r"(rb[9]), "=r"(rb[10]), "=r"(rb[11]), "=r"(rb[12]), "=r"(rb[13]), "=r"(rb[14]), "=r"(rb[15]),
+        "=r"(rb[16]), "=r"(rb[17]), "=r"(rb[18]), "=r"(rb[19]), "=r"(rb[20]), "=r"(rb[21]), "=r"(rb[22]), "=r"(rb[23]),
+        "=r"(rb[24]), "=r"(rb[25]), "=r"(rb[26]), "=r"(rb[27]), "=r"(rb[28]), "=r"(rb[29]), "=r"(rb[30]), "=r"(rb[31])
+      : "r"(taddr), "r"(taddr + 32)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    a[i] = __uint_as_float(ra[i]);
+    b[i] = __uint_as_float(rb[i]);
+  }
+}
 
 __global__ void __launch_bounds__(kThreads, 1)
     markov_step_kernel(const __grid_constant__ CUtensorMap wmap, Params p) {
@@ -131,6 +169,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     fence_proxy_async_smem();
     mbar_arrive(bar(kBarAReady));
+    // ---- epilogue: running first-maximum over this CTA's tiles --------------------
+    // best_key: 16-bit order key of the best bf16 logit so far (0: none yet),
+    // best_idx its vocabulary index (tiles come in increasing vocabulary order,
+    // so a later tile replaces it only with a strictly larger key).
+    uint32_t best_key = 0;
+    int best_idx = 0x7fffffff;
+    const __nv_bfloat16* brow = p.base + (static_cast<long long>(r) * p.base_stride_r + p.k) * p.vocab;
+    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+    bool ok = true;
+    // this request's 128 base logits of a tile, one tile ahead of the MMA result
+    // they are added to, so their DRAM latency overlaps the previous tile's work
+    auto load_base = [&](int t, uint4 (&raw)[16]) {
+      const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        raw[q] = (live && t < n_mine && v0 + q * 8 < p.vocab)
+                     ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8)) : make_uint4(0, 0, 0, 0);
+    };
+    uint4 bnext[16];
+    load_base(0, bnext);
+    for (int t = 0; t < n_mine; ++t) {
+      const int b = t & 1;
+      const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+      const int nvalid = min(kVocabTile, p.vocab - v0);   // the last tile may be partial
+      uint4 braw[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q) braw[q] = bnext[q];
+      load_base(t + 1, bnext);
+      ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+      // one running max per 32-column chunk of packed (key << 16 | 127 - column)
+      uint32_t chain[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float d[64];
+        tmem_ld64(tmem + lane_addr + b * 128 + h * 64, d);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int col = h * 64 + 2 * i;
+          // projection output to bf16, plus the bf16 base logit, sum to bf16
+          const uint32_t r1 = pack_bf16x2(d[2 * i], d[2 * i + 1]);
+          const uint4& bq = braw[col >> 3];
+          const uint32_t bb = ((col & 7) >> 1) == 0 ? bq.x : ((col & 7) >> 1) == 1 ? bq.y
+                            : ((col & 7) >> 1) == 2 ? bq.z : bq.w;
+          const float s0 = __uint_as_float(r1 << 16) + __uint_as_float(bb << 16);
+          const float s1 = __uint_as_float(r1 & 0xffff0000u) + __uint_as_float(bb & 0xffff0000u);
+          const uint32_t k = bf16x2_order_keys(pack_bf16x2(s0, s1));
+          uint32_t p0 = (k << 16) | static_cast<uint32_t>(127 - col);
+          uint32_t p1 = (k & 0xffff0000u) | static_cast<uint32_t>(126 - col);
+          if (nvalid < kVocabTile) {
+            p0 = col < nvalid ? p0 : 0u;
+            p1 = col + 1 < nvalid ? p1 : 0u;
+          }
+          chain[col >> 5] = max(chain[col >> 5], max(p0, p1));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(bar(kBarDFree0 + b));
+      const uint32_t tb = max(max(chain[0], chain[1]), max(chain[2], chain[3]));
+      if (live && (tb >> 16) > best_key) {
+        best_key = tb >> 16;
+        best_idx = v0 + 127 - static_cast<int>(tb & 0xffffu);
+      }
+    }
+    if (!ok) *abort_flag = 1;
     // ---- confidence (before the token): request r on CTA r % grid, one warp ------
     for (int rr = static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) * warp; rr < p.num_requests;
          rr += 4 * static_cast<int>(gridDim.x)) {
@@ -139,10 +243,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const __nv_bfloat16* h = p.hidden + (static_cast<long long>(rr) * p.base_stride_r + p.k) * p.hidden_dim;
       const __nv_bfloat16* em = p.emb_table + t * p.rank;
       float acc = 0.f;
-      for (int i = lane; i < p.hidden_dim; i += 32)
-        acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
-      for (int i = lane; i < p.rank; i += 32)
-        acc = fmaf(__bfloat162float(em[i]), __bfloat162float(p.conf_w[p.hidden_dim + i]), acc);
+      if (p.conf_vec) {
+        // 8 bf16 per 16-byte load, all of a lane's loads in flight together
+        auto dot8 = [](uint4 a, uint4 b, float acc) {
+          const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&a);
+          const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc = fmaf(__bfloat162float(x[e]), __bfloat162float(y[e]), acc);
+          return acc;
+        };
+#pragma unroll 4
+        for (int i = lane * 8; i < p.hidden_dim; i += 256)
+          acc = dot8(__ldg(reinterpret_cast<const uint4*>(h + i)), __ldg(reinterpret_cast<const uint4*>(p.conf_w + i)),
+                     acc);
+#pragma unroll 2
+        for (int i = lane * 8; i < p.rank; i += 256)
+          acc = dot8(__ldg(reinterpret_cast<const uint4*>(em + i)),
+                     __ldg(reinterpret_cast<const uint4*>(p.conf_w + p.hidden_dim + i)), acc);
+      } else {
+        for (int i = lane; i < p.hidden_dim; i += 32)
+          acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
+        for (int i = lane; i < p.rank; i += 32)
+          acc = fmaf(__bfloat162float(em[i]), __bfloat162float(p.conf_w[p.hidden_dim + i]), acc);
+      }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
       if (lane == 0) {
@@ -151,53 +274,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         p.conf[rr * p.tok_stride + p.k] = bf16_round(1.f / (1.f + expf(-logit)));
       }
     }
-    // ---- epilogue: running first-maximum over this CTA's tiles --------------------
-    float best_v = -INFINITY;
-    int best_i = 0x7fffffff;
-    const __nv_bfloat16* brow = p.base + (static_cast<long long>(r) * p.base_stride_r + p.k) * p.vocab;
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    bool ok = true;
-    for (int t = 0; t < n_mine; ++t) {
-      const int b = t & 1;
-      const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
-      // this request's 128 base logits of the tile, loaded before the MMA result is
-      // waited for so their latency overlaps it
-      uint4 braw[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        braw[q] = (live && v0 + q * 8 < p.vocab) ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8))
-                                                 : make_uint4(0, 0, 0, 0);
-      ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        float d[32];
-        tmem_ld32(tmem + lane_addr + b * 128 + c * 32, d);
-        if (live) {
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const int v = v0 + c * 32 + q * 8;
-            if (v >= p.vocab) break;
-            const __nv_bfloat16* bv = reinterpret_cast<const __nv_bfloat16*>(&braw[c * 4 + q]);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              const float x = bf16_round(bf16_round(d[q * 8 + e]) + __bfloat162float(bv[e]));
-              if (x > best_v || (x != x && best_v == best_v)) {
-                best_v = x;
-                best_i = v + e;
-              }
-            }
-          }
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bar(kBarDFree0 + b));
-    }
-    if (!ok) *abort_flag = 1;
-    if (live && best_i != 0x7fffffff)
-      atomicMax(p.best + r, (static_cast<unsigned long long>(order_key(best_v)) << 32) |
-                                static_cast<unsigned long long>(0xffffffffu - static_cast<unsigned int>(best_i)));
+    if (live && best_idx != 0x7fffffff)
+      atomicMax(p.best + r, (static_cast<unsigned long long>(best_key) << 32) |
+                                static_cast<unsigned long long>(0xffffffffu - static_cast<unsigned int>(best_idx)));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t kIdesc = instr_desc(0);
