@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 10
+#define DSPARK_ABI_VERSION 11
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -205,15 +205,26 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
  * rank a multiple of 64 up to 256). The [R, vocab] logits are never written:
  * a tcgen05 GEMM keeps each tile in TMEM and the argmax is folded in. scratch
  * (dspark_markov_scratch_bytes(), 16-byte aligned device memory) must be zero
- * before the first call and is left zero by every call. Run the block's steps k
- * = 0 .. S-1 in order, passing prev = the anchors for k = 0 and
- * prev = tokens + (k - 1) (stride tok_stride) afterwards.
+ * before the first call and is kept usable by every call (one scratch per
+ * stream). Run the block's steps k = 0 .. S-1 in order, passing prev = the
+ * anchors for k = 0 and prev = tokens + (k - 1) (stride tok_stride) afterwards.
+ *
+ * dspark_markov_block runs all block_size (<= 64) steps of a block in one
+ * cooperative launch (the same results as dspark_markov_step for k = 0 ..
+ * block_size-1 with base_stride_r = tok_stride = block_size and prev = anchors
+ * [num_requests]): the projection weight streams on across steps and the CTAs
+ * meet at a bounded grid barrier between steps. If the cooperative launch is
+ * refused (not every CTA could be resident), it launches the steps one by one.
  */
 size_t dspark_markov_scratch_bytes(void);
 int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
                        long long base_stride_r, int k, const long long* prev, long long prev_stride,
                        const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,
                        float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream);
+int dspark_markov_block(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                        int block_size, const long long* anchors, const void* hidden, int hidden_dim,
+                        const void* conf_w, float conf_b, long long* tokens, float* conf, int num_requests,
+                        void* scratch, cudaStream_t stream);
 
 /*
  * Fused draft-context append (bf16, tcgen05 tensor cores): for every draft layer

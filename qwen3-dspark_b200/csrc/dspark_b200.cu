@@ -81,6 +81,8 @@ int device_info(int dev, DeviceInfo* out) {
                              static_cast<int>(train::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(markov::markov_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(markov::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(markov::markov_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(markov::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(append::draft_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(append::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
@@ -499,37 +501,36 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
   return launch_status();
 }
 
-size_t dspark_markov_scratch_bytes(void) { return markov::kRows * sizeof(unsigned long long) + 16; }
+size_t dspark_markov_scratch_bytes(void) { return markov::kScratchBytes; }
 
-int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
-                       long long base_stride_r, int k, const long long* prev, long long prev_stride,
-                       const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,
-                       float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream) {
-  if (!proj_weight || !emb_table || !base || !prev || !hidden || !conf_w || !tokens || !conf || !scratch ||
-      vocab < 8 || vocab % 8 != 0 || rank < 64 || rank > markov::kMaxRank || rank % 64 != 0 || hidden_dim < 1 ||
-      num_requests < 1 || num_requests > markov::kRows || k < 0 || k >= base_stride_r || base_stride_r < 1 ||
-      prev_stride < 0 || tok_stride <= k || !aligned(proj_weight, 16) || !aligned(emb_table, 16) ||
-      !aligned(base, 16) || !aligned(scratch, 16))
+namespace {
+
+// Shared argument checks and parameter block of the Markov entries.
+int markov_setup(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                 long long base_stride_r, const void* hidden, int hidden_dim, const void* conf_w, float conf_b,
+                 long long* tokens, float* conf, long long tok_stride, int num_requests, void* scratch,
+                 CUtensorMap* wm, markov::Params* pp, int* grid) {
+  if (!proj_weight || !emb_table || !base || !hidden || !conf_w || !tokens || !conf || !scratch || vocab < 8 ||
+      vocab % 8 != 0 || rank < 64 || rank > markov::kMaxRank || rank % 64 != 0 || hidden_dim < 1 ||
+      num_requests < 1 || num_requests > markov::kRows || base_stride_r < 1 || !aligned(proj_weight, 16) ||
+      !aligned(emb_table, 16) || !aligned(base, 16) || !aligned(scratch, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
   DeviceInfo dev;
   int st = current_device_info(&dev);
   if (st != DSPARK_OK) return st;
-  CUtensorMap wm;
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(rank), static_cast<cuuint64_t>(vocab)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(rank) * 2};
   cuuint32_t box[2] = {64, static_cast<cuuint32_t>(markov::kVocabTile)};
   cuuint32_t estr[2] = {1, 1};
-  if (g_encode(&wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(proj_weight), dims, strides, box, estr,
+  if (g_encode(wm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(proj_weight), dims, strides, box, estr,
                CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return DSPARK_ERR_CUDA;
-  markov::Params p{};
+  markov::Params& p = *pp;
+  p = markov::Params{};
   p.emb_table = static_cast<const __nv_bfloat16*>(emb_table);
   p.base = static_cast<const __nv_bfloat16*>(base);
   p.base_stride_r = base_stride_r;
-  p.k = k;
-  p.prev = prev;
-  p.prev_stride = prev_stride;
   p.hidden = static_cast<const __nv_bfloat16*>(hidden);
   p.hidden_dim = hidden_dim;
   p.conf_vec = hidden_dim % 8 == 0 && aligned(hidden, 16) && aligned(conf_w, 16);
@@ -539,14 +540,75 @@ int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab
   p.tok_stride = tok_stride;
   p.conf = conf;
   p.best = static_cast<unsigned long long*>(scratch);
-  p.arrivals = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(scratch) + markov::kRows * 8);
+  p.arrivals = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(scratch) + 3 * markov::kRows * 8);
+  p.generation = p.arrivals + 1;
   p.num_requests = num_requests;
   p.vocab = vocab;
   p.rank = rank;
   p.tiles = (vocab + markov::kVocabTile - 1) / markov::kVocabTile;
-  const int grid = p.tiles < dev.sms ? p.tiles : dev.sms;
+  *grid = p.tiles < dev.sms ? p.tiles : dev.sms;
+  return DSPARK_OK;
+}
+
+}  // namespace
+
+int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                       long long base_stride_r, int k, const long long* prev, long long prev_stride,
+                       const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,
+                       float* conf, long long tok_stride, int num_requests, void* scratch, cudaStream_t stream) {
+  if (!prev || k < 0 || k >= base_stride_r || prev_stride < 0 || tok_stride <= k) return DSPARK_ERR_INVALID_ARGUMENT;
+  CUtensorMap wm;
+  markov::Params p;
+  int grid = 0;
+  int st = markov_setup(proj_weight, emb_table, vocab, rank, base, base_stride_r, hidden, hidden_dim, conf_w, conf_b,
+                        tokens, conf, tok_stride, num_requests, scratch, &wm, &p, &grid);
+  if (st != DSPARK_OK) return st;
+  p.k = k;
+  p.steps = 1;
+  p.prev = prev;
+  p.prev_stride = prev_stride;
   markov::markov_step_kernel<<<grid, markov::kThreads, markov::kSmemBytes, stream>>>(wm, p);
   return launch_status();
+}
+
+int dspark_markov_block(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
+                        int block_size, const long long* anchors, const void* hidden, int hidden_dim,
+                        const void* conf_w, float conf_b, long long* tokens, float* conf, int num_requests,
+                        void* scratch, cudaStream_t stream) {
+  if (!anchors || block_size < 1 || block_size > markov::kMaxSteps) return DSPARK_ERR_INVALID_ARGUMENT;
+  CUtensorMap wm;
+  markov::Params p;
+  int grid = 0;
+  int st = markov_setup(proj_weight, emb_table, vocab, rank, base, block_size, hidden, hidden_dim, conf_w, conf_b,
+                        tokens, conf, block_size, num_requests, scratch, &wm, &p, &grid);
+  if (st != DSPARK_OK) return st;
+  p.steps = block_size;
+  p.prev = anchors;
+  p.prev_stride = 1;
+  // Cooperative: the runtime refuses the launch unless every CTA can be
+  // resident at once, which the grid barrier between steps relies on.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(markov::kThreads);
+  cfg.dynamicSmemBytes = markov::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, markov::markov_block_kernel, wm, p) == cudaSuccess) return launch_status();
+  (void)cudaGetLastError();
+  // Refused (other work holds SMs): one launch per position, same results.
+  for (int k = 0; k < block_size; ++k) {
+    p.k = k;
+    p.steps = 1;
+    p.prev = k == 0 ? anchors : tokens + (k - 1);
+    p.prev_stride = k == 0 ? 1 : block_size;
+    markov::markov_step_kernel<<<grid, markov::kThreads, markov::kSmemBytes, stream>>>(wm, p);
+    if ((st = launch_status()) != DSPARK_OK) return st;
+  }
+  return DSPARK_OK;
 }
 
 int dspark_draft_append(const void* context, int rows, int hidden, const void* kv_weight, int num_layers,

@@ -1,10 +1,10 @@
-// One step of the draft's serial Markov proposal (DSparkDraft._sample_greedy,
-// dspark_qwen/model.py:210-221; batched as in packed_sampling.py:73-94):
+// The draft's serial Markov proposal (DSparkDraft._sample_greedy,
+// dspark_qwen/model.py:210-221; batched as in packed_sampling.py:73-94). Step k:
 //
 //   emb      = markov_embedding[prev]                       [R, rank]
 //   conf     = sigmoid(confidence(cat(hidden_k, emb)))     [R]   (before the token)
 //   logits   = base_k + markov_projection(emb)             [R, V]
-//   next     = argmax(logits)                               [R]
+//   next     = argmax(logits)                               [R]   (prev of step k+1)
 //
 // with base_k = lm_head(hidden)[:, k] computed once per block by the caller. The
 // [R, V] logits never reach HBM: a tcgen05 GEMM with M = requests (the gathered
@@ -16,14 +16,27 @@
 // folded onto +0, NaN above everything, as torch.argmax orders them) packed
 // above its inverted column, so one unsigned max per value keeps the largest
 // value at its lowest index. Each CTA publishes one packed 64-bit atomicMax per
-// request (key high, inverted index low); the last CTA to finish writes the
-// tokens and clears the scratch.
+// request (key high, inverted index low).
+//
+// Two kernels share this body:
+//   markov_step_kernel   one step per launch; the last CTA to finish writes the
+//                        tokens and clears the scratch;
+//   markov_block_kernel  all steps of a block in one cooperative launch (every
+//                        CTA resident): the projection-weight stream runs on
+//                        across steps (it does not depend on the tokens), and
+//                        between steps the CTAs meet at a grid barrier (a
+//                        generation counter with a bounded wait) after which
+//                        every CTA reads the step's argmax for its next gather.
+//                        Step s publishes into best buffer s % 3; CTA 0 writes
+//                        the tokens and clears the buffer of step s - 2 during
+//                        step s (all CTAs finished reading it before the
+//                        barrier of step s - 1).
 //
 // Roles (192 threads, persistent CTAs over the vocabulary tiles):
-//   warps 0-3  gather emb rows into shared memory (A operand), epilogue
-//              (thread r = request r = TMEM lane r; the base row of the next
-//              tile is loaded while the current tile is reduced), then the
-//              confidence (one warp per request, spread over the CTAs);
+//   warps 0-3  per step: gather emb rows into shared memory (A operand),
+//              confidence (one warp per request, spread over the CTAs),
+//              epilogue (thread r = request r = TMEM lane r; the base row of
+//              the next tile is loaded while the current tile is reduced);
 //   warp 4     TMEM owner and MMA issuer (one thread);
 //   warp 5     TMA producer of the projection-weight tiles (two stages).
 #pragma once
@@ -47,23 +60,29 @@ constexpr int kThreads = 192;
 constexpr int kRows = 128;        // padded request rows (MMA M)
 constexpr int kVocabTile = 128;   // vocabulary rows per tile (MMA N)
 constexpr int kMaxRank = 256;
+constexpr int kMaxSteps = 64;     // block positions per fused launch
 constexpr uint32_t kSmemA = 0;                           // 128 x rank bf16 (<= 64 KB)
 constexpr uint32_t kSmemW = 65536;                       // 2 stages x 64 KB
 constexpr uint32_t kSmemBar = kSmemW + 2 * 65536;
-enum Barrier { kBarAReady = 0, kBarWFull0, kBarWFull1, kBarWEmpty0, kBarWEmpty1, kBarDFull0, kBarDFull1,
+enum Barrier { kBarAReady = 0, kBarAFree, kBarWFull0, kBarWFull1, kBarWEmpty0, kBarWEmpty1, kBarDFull0, kBarDFull1,
                kBarDFree0, kBarDFree1, kBarDrain, kNumBarriers };
 constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemSlot + 4;
 constexpr uint32_t kSmemLast = kSmemAbort + 4;
 constexpr uint32_t kSmemBytes = 1024 + kSmemLast + 4;
 constexpr uint32_t kTmemCols = 256;                      // two 128-column D buffers
+// Scratch (zero between calls): three best buffers of kRows packed maxima, the
+// CTA arrival counter, the grid-barrier generation (the only word that is not
+// returned to zero: it only ever advances).
+constexpr size_t kScratchBytes = 3 * kRows * sizeof(unsigned long long) + 16;
 
 struct Params {
   const __nv_bfloat16* emb_table;   // [V, rank] markov_embedding.weight
   const __nv_bfloat16* base;        // row (r * base_stride_r + k): lm_head logits of block row k, V wide
   long long base_stride_r;          // rows between requests in base (the block size)
-  int k;                            // block position of this step
-  const long long* prev;            // previous token of request r at prev[r * prev_stride]
+  int k;                            // block position of this step (step kernel)
+  int steps;                        // block positions 0 .. steps-1 (block kernel)
+  const long long* prev;            // previous token of request r at prev[r * prev_stride] (step k / step 0)
   long long prev_stride;
   const __nv_bfloat16* hidden;      // [R * base_stride_r, H] backbone output (confidence input)
   int hidden_dim;
@@ -73,8 +92,9 @@ struct Params {
   long long* tokens;                // tokens[r * tok_stride + k] = next token
   long long tok_stride;
   float* conf;                      // conf[r * tok_stride + k] = sigmoid(confidence logit)
-  unsigned long long* best;         // [kRows] packed maxima (zero between steps)
-  unsigned int* arrivals;           // CTA arrival counter (zero between steps)
+  unsigned long long* best;         // 3 x [kRows] packed maxima (zero between calls)
+  unsigned int* arrivals;           // CTA arrival counter (zero between calls)
+  unsigned int* generation;         // grid-barrier generation
   int num_requests;                 // R <= 128
   int vocab;                        // V, multiple of 8
   int rank;                         // multiple of 64, <= 256
@@ -122,8 +142,192 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
   }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
-    markov_step_kernel(const __grid_constant__ CUtensorMap wmap, Params p) {
+// Token of a packed maximum.
+__device__ __forceinline__ long long packed_token(unsigned long long v) {
+  return static_cast<long long>(0xffffffffu - static_cast<unsigned int>(v));
+}
+
+__device__ __forceinline__ long long checked_token(const Params& p, long long t) {
+  if (t < 0 || t >= p.vocab) {
+    atomicOr(&g_device_status, kStatusBadArgument);
+    return 0;
+  }
+  return t;
+}
+
+// Row r of the A operand (K-major, 128-byte swizzle): the embedding of `tok`,
+// or zeros for a padding row.
+__device__ __forceinline__ void gather_row(const Params& p, uint8_t* smem, int r, long long tok, bool live) {
+  const uint4* src = reinterpret_cast<const uint4*>(p.emb_table + tok * p.rank);
+  const int chunks = p.rank / 64;
+  uint4 v[kMaxRank / 8];                           // every load in flight before the first store
+#pragma unroll
+  for (int i = 0; i < kMaxRank / 8; ++i) v[i] = live && i < chunks * 8 ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int i = 0; i < kMaxRank / 8; ++i)
+    if (i < chunks * 8)
+      *reinterpret_cast<uint4*>(smem + kSmemA + (i >> 3) * 16384 + r * 128 + (((i & 7) ^ (r & 7)) << 4)) = v[i];
+}
+
+// Confidence of block position k (before its token) for the requests of this
+// CTA (request r on CTA grid - 1 - r % grid, one warp each: the last CTAs own
+// the fewest vocabulary tiles); prev_of(rr) is request rr's previous token.
+template <class PrevFn>
+__device__ __forceinline__ void confidence_rows(const Params& p, int k, int warp, int lane, PrevFn prev_of) {
+  const int from_end = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);
+  for (int rr = from_end + static_cast<int>(gridDim.x) * warp; rr < p.num_requests;
+       rr += 4 * static_cast<int>(gridDim.x)) {
+    const long long t = prev_of(rr);
+    const __nv_bfloat16* h = p.hidden + (static_cast<long long>(rr) * p.base_stride_r + k) * p.hidden_dim;
+    const __nv_bfloat16* em = p.emb_table + t * p.rank;
+    float acc = 0.f;
+    if (p.conf_vec) {
+      // 8 bf16 per 16-byte load, all of a lane's loads in flight together
+      auto dot8 = [](uint4 a, uint4 b, float acc) {
+        const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&a);
+        const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&b);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc = fmaf(__bfloat162float(x[e]), __bfloat162float(y[e]), acc);
+        return acc;
+      };
+#pragma unroll 4
+      for (int i = lane * 8; i < p.hidden_dim; i += 256)
+        acc = dot8(__ldg(reinterpret_cast<const uint4*>(h + i)), __ldg(reinterpret_cast<const uint4*>(p.conf_w + i)),
+                   acc);
+#pragma unroll 2
+      for (int i = lane * 8; i < p.rank; i += 256)
+        acc = dot8(__ldg(reinterpret_cast<const uint4*>(em + i)),
+                   __ldg(reinterpret_cast<const uint4*>(p.conf_w + p.hidden_dim + i)), acc);
+    } else {
+      for (int i = lane; i < p.hidden_dim; i += 32)
+        acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
+      for (int i = lane; i < p.rank; i += 32)
+        acc = fmaf(__bfloat162float(em[i]), __bfloat162float(p.conf_w[p.hidden_dim + i]), acc);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) {
+      // bf16 Linear output (fp32 dot + bias, rounded once), then a bf16 sigmoid
+      const float logit = bf16_round(acc + p.conf_b);
+      p.conf[rr * p.tok_stride + k] = bf16_round(1.f / (1.f + expf(-logit)));
+    }
+  }
+}
+
+// Request r's 128 base logits of tile t at block position k (zeros past the
+// vocabulary or for padding rows).
+__device__ __forceinline__ void load_base(const Params& p, int k, int t, int n_mine, int r, bool live,
+                                          uint4 (&raw)[16]) {
+  const __nv_bfloat16* brow = p.base + (static_cast<long long>(r) * p.base_stride_r + k) * p.vocab;
+  const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+#pragma unroll
+  for (int q = 0; q < 16; ++q)
+    raw[q] = (live && t < n_mine && v0 + q * 8 < p.vocab)
+                 ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8)) : make_uint4(0, 0, 0, 0);
+}
+
+// Epilogue of one step over this CTA's n_mine tiles (global tile counter g0 ..):
+// the first maximum of request r's logits (best_key / best_idx, key 0 = none).
+// bnext holds the base logits of the step's first tile on entry; each tile's are
+// loaded one tile ahead of the MMA result they are added to, and the last tile
+// loads the first tile of block position k_next (if >= 0), so their DRAM latency
+// overlaps other work.
+__device__ __forceinline__ bool epilogue_step(const Params& p, int k, int k_next, int g0, int n_mine, int r,
+                                              bool live, uint32_t tmem, uint32_t bars, volatile int* abort_flag,
+                                              uint4 (&bnext)[16], uint32_t& best_key, int& best_idx) {
+  auto bar = [&](int i) { return bars + 8u * i; };
+  const int warp = threadIdx.x >> 5;
+  best_key = 0;
+  best_idx = 0x7fffffff;
+  const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
+  for (int t = 0; t < n_mine; ++t) {
+    const int g = g0 + t, b = g & 1;
+    const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+    const int nvalid = min(kVocabTile, p.vocab - v0);   // the last tile may be partial
+    uint4 braw[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) braw[q] = bnext[q];
+    if (t + 1 < n_mine)
+      load_base(p, k, t + 1, n_mine, r, live, bnext);
+    else if (k_next >= 0)
+      load_base(p, k_next, 0, n_mine, r, live, bnext);
+    const bool ok = wait_or_abort(bar(kBarDFull0 + b), (g >> 1) & 1, abort_flag);
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    tc_fence_after();
+    // one running max per 32-column chunk of packed (key << 16 | 127 - column)
+    uint32_t chain[4] = {0u, 0u, 0u, 0u};
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float d[64];
+      tmem_ld64(tmem + lane_addr + b * 128 + h * 64, d);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const int col = h * 64 + 2 * i;
+        // projection output to bf16, plus the bf16 base logit, sum to bf16
+        const uint32_t r1 = pack_bf16x2(d[2 * i], d[2 * i + 1]);
+        const uint4& bq = braw[col >> 3];
+        const uint32_t bb = ((col & 7) >> 1) == 0 ? bq.x : ((col & 7) >> 1) == 1 ? bq.y
+                          : ((col & 7) >> 1) == 2 ? bq.z : bq.w;
+        const float s0 = __uint_as_float(r1 << 16) + __uint_as_float(bb << 16);
+        const float s1 = __uint_as_float(r1 & 0xffff0000u) + __uint_as_float(bb & 0xffff0000u);
+        const uint32_t key = bf16x2_order_keys(pack_bf16x2(s0, s1));
+        uint32_t p0 = (key << 16) | static_cast<uint32_t>(127 - col);
+        uint32_t p1 = (key & 0xffff0000u) | static_cast<uint32_t>(126 - col);
+        if (nvalid < kVocabTile) {
+          p0 = col < nvalid ? p0 : 0u;
+          p1 = col + 1 < nvalid ? p1 : 0u;
+        }
+        chain[col >> 5] = max(chain[col >> 5], max(p0, p1));
+      }
+    }
+    tc_fence_before();
+    mbar_arrive(bar(kBarDFree0 + b));
+    const uint32_t tb = max(max(chain[0], chain[1]), max(chain[2], chain[3]));
+    if (live && (tb >> 16) > best_key) {
+      best_key = tb >> 16;
+      best_idx = v0 + 127 - static_cast<int>(tb & 0xffffu);
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void publish(const Params& p, unsigned long long* best, int r, bool live,
+                                        uint32_t best_key, int best_idx) {
+  if (live && best_idx != 0x7fffffff)
+    atomicMax(best + r, (static_cast<unsigned long long>(best_key) << 32) |
+                            static_cast<unsigned long long>(0xffffffffu - static_cast<unsigned int>(best_idx)));
+}
+
+// The four epilogue warps meet (a named barrier they all reach on every path).
+__device__ __forceinline__ void epilogue_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// Grid barrier of the cooperative block kernel, run by thread 0 of each CTA:
+// the last CTA to arrive resets the counter and advances the generation; the
+// others wait (bounded) for the generation to change.
+__device__ __forceinline__ void grid_barrier(const Params& p, volatile int* abort_flag) {
+  if (*abort_flag) return;                         // the other CTAs' waits run out and report it
+  volatile unsigned int* gen = p.generation;
+  const unsigned int g = *gen;
+  __threadfence();
+  if (atomicAdd(p.arrivals, 1u) == gridDim.x - 1) {
+    atomicExch(p.arrivals, 0u);
+    __threadfence();
+    atomicAdd(p.generation, 1u);
+    return;
+  }
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t it = 1; *gen == g; ++it) {
+    if ((it & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+      atomicOr(&g_device_status, kStatusWaitTimeout);
+      *abort_flag = 1;
+      return;
+    }
+  }
+  __threadfence();
+}
+
+template <bool kBlock>
+__device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Params& p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -133,13 +337,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int chunks = p.rank / 64;                       // 64-wide K chunks (one 128-byte swizzle row each)
   const uint32_t tile_bytes = static_cast<uint32_t>(chunks) * 16384u;
+  const int steps = kBlock ? p.steps : 1;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kNumBarriers; ++i) mbar_init(bar(i), (i == kBarAReady || i == kBarDFree0 || i == kBarDFree1) ? 128u : 1u);
+    for (int i = 0; i < kNumBarriers; ++i)
+      mbar_init(bar(i), (i == kBarAReady || i == kBarDFree0 || i == kBarDFree1) ? 128u : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 5 && lane == 0) prefetch_tmap(&wmap);
+  if (warp == 5 && lane == 0) prefetch_tmap(wmap);
   if (warp == 4) tmem_alloc(sbase + kSmemSlot, kTmemCols);
   tc_fence_before();
   __syncthreads();
@@ -149,152 +355,82 @@ __global__ void __launch_bounds__(kThreads, 1)
                          ? (p.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
 
   if (warp < 4) {
-    // ---- gather emb rows (K-major, 128-byte swizzle) ---------------------------
     const int r = threadIdx.x;
     const bool live = r < p.num_requests;
-    long long tok = 0;
-    if (live) {
-      tok = p.prev[r * p.prev_stride];
-      if (tok < 0 || tok >= p.vocab) {
-        atomicOr(&g_device_status, kStatusBadArgument);
-        tok = 0;
+    uint4 bnext[16];                               // base logits of the next tile to reduce
+    load_base(p, kBlock ? 0 : p.k, 0, n_mine, r, live, bnext);
+    for (int s = 0; s < steps; ++s) {
+      const int k = kBlock ? s : p.k;
+      unsigned long long* const best_now = p.best + (kBlock ? (s % 3) * kRows : 0);
+      const unsigned long long* const best_prev = p.best + ((s + 2) % 3) * kRows;
+      // previous token of request rr: the given one, or (block kernel, s > 0)
+      // the argmax of step s - 1, read past L1 (other CTAs wrote it)
+      auto prev_of = [&](int rr) -> long long {
+        if (!kBlock || s == 0) return checked_token(p, p.prev[rr * p.prev_stride]);
+        return checked_token(p, packed_token(__ldcg(best_prev + rr)));
+      };
+      const long long tok = live ? prev_of(r) : 0;
+      // the A tile is free once the previous step's MMAs are done (decisions are
+      // warp-uniform: the confidence and the TMEM loads are warp-collective)
+      bool ok = __all_sync(0xffffffffu, !*abort_flag);
+      if (ok && s > 0) ok = __all_sync(0xffffffffu, wait_or_abort(bar(kBarAFree), (s - 1) & 1, abort_flag));
+      if (ok) {
+        gather_row(p, smem, r, tok, live);
+        fence_proxy_async_smem();
+      }
+      mbar_arrive(bar(kBarAReady));
+      if (kBlock && blockIdx.x == 0) {
+        if (s > 0 && live) p.tokens[r * p.tok_stride + s - 1] = tok;
+        // the buffer of step s - 2 (read by every CTA before the last barrier)
+        // is cleared for step s + 1
+        p.best[((s + 1) % 3) * kRows + r] = 0ull;
+      }
+      uint32_t best_key = 0;
+      int best_idx = 0x7fffffff;
+      if (ok)
+        ok = epilogue_step(p, k, kBlock && s + 1 < steps ? s + 1 : -1, s * n_mine, n_mine, r, live, tmem, bars,
+                           abort_flag, bnext, best_key, best_idx);
+      if (!ok) *abort_flag = 1;
+      publish(p, best_now, r, live, best_key, best_idx);
+      // the confidence is off the MMA pipeline's path: after the tiles
+      if (ok) confidence_rows(p, k, warp, lane, prev_of);
+      if (kBlock) {
+        __threadfence();
+        epilogue_sync();
+        if (threadIdx.x == 0) grid_barrier(p, abort_flag);
+        epilogue_sync();
       }
     }
-    const uint4* src = reinterpret_cast<const uint4*>(p.emb_table + tok * p.rank);
-    for (int c = 0; c < chunks; ++c)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint4 v = live ? __ldg(src + c * 8 + j) : make_uint4(0, 0, 0, 0);
-        *reinterpret_cast<uint4*>(smem + kSmemA + c * 16384 + r * 128 + ((j ^ (r & 7)) << 4)) = v;
-      }
-    fence_proxy_async_smem();
-    mbar_arrive(bar(kBarAReady));
-    // ---- epilogue: running first-maximum over this CTA's tiles --------------------
-    // best_key: 16-bit order key of the best bf16 logit so far (0: none yet),
-    // best_idx its vocabulary index (tiles come in increasing vocabulary order,
-    // so a later tile replaces it only with a strictly larger key).
-    uint32_t best_key = 0;
-    int best_idx = 0x7fffffff;
-    const __nv_bfloat16* brow = p.base + (static_cast<long long>(r) * p.base_stride_r + p.k) * p.vocab;
-    const uint32_t lane_addr = static_cast<uint32_t>(warp * 32) << 16;
-    bool ok = true;
-    // this request's 128 base logits of a tile, one tile ahead of the MMA result
-    // they are added to, so their DRAM latency overlaps the previous tile's work
-    auto load_base = [&](int t, uint4 (&raw)[16]) {
-      const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
-#pragma unroll
-      for (int q = 0; q < 16; ++q)
-        raw[q] = (live && t < n_mine && v0 + q * 8 < p.vocab)
-                     ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8)) : make_uint4(0, 0, 0, 0);
-    };
-    uint4 bnext[16];
-    load_base(0, bnext);
-    for (int t = 0; t < n_mine; ++t) {
-      const int b = t & 1;
-      const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
-      const int nvalid = min(kVocabTile, p.vocab - v0);   // the last tile may be partial
-      uint4 braw[16];
-#pragma unroll
-      for (int q = 0; q < 16; ++q) braw[q] = bnext[q];
-      load_base(t + 1, bnext);
-      ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      tc_fence_after();
-      // one running max per 32-column chunk of packed (key << 16 | 127 - column)
-      uint32_t chain[4] = {0u, 0u, 0u, 0u};
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        float d[64];
-        tmem_ld64(tmem + lane_addr + b * 128 + h * 64, d);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int col = h * 64 + 2 * i;
-          // projection output to bf16, plus the bf16 base logit, sum to bf16
-          const uint32_t r1 = pack_bf16x2(d[2 * i], d[2 * i + 1]);
-          const uint4& bq = braw[col >> 3];
-          const uint32_t bb = ((col & 7) >> 1) == 0 ? bq.x : ((col & 7) >> 1) == 1 ? bq.y
-                            : ((col & 7) >> 1) == 2 ? bq.z : bq.w;
-          const float s0 = __uint_as_float(r1 << 16) + __uint_as_float(bb << 16);
-          const float s1 = __uint_as_float(r1 & 0xffff0000u) + __uint_as_float(bb & 0xffff0000u);
-          const uint32_t k = bf16x2_order_keys(pack_bf16x2(s0, s1));
-          uint32_t p0 = (k << 16) | static_cast<uint32_t>(127 - col);
-          uint32_t p1 = (k & 0xffff0000u) | static_cast<uint32_t>(126 - col);
-          if (nvalid < kVocabTile) {
-            p0 = col < nvalid ? p0 : 0u;
-            p1 = col + 1 < nvalid ? p1 : 0u;
-          }
-          chain[col >> 5] = max(chain[col >> 5], max(p0, p1));
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(bar(kBarDFree0 + b));
-      const uint32_t tb = max(max(chain[0], chain[1]), max(chain[2], chain[3]));
-      if (live && (tb >> 16) > best_key) {
-        best_key = tb >> 16;
-        best_idx = v0 + 127 - static_cast<int>(tb & 0xffffu);
-      }
+    if (kBlock && blockIdx.x == 0) {
+      // after the last barrier: the last step's tokens, and the two buffers in use cleared
+      const int last = steps - 1;
+      const unsigned long long v = __ldcg(p.best + (last % 3) * kRows + r);
+      if (live) p.tokens[r * p.tok_stride + last] = v ? packed_token(v) : 0;
+      p.best[(last % 3) * kRows + r] = 0ull;
+      p.best[((last + 2) % 3) * kRows + r] = 0ull;
     }
-    if (!ok) *abort_flag = 1;
-    // ---- confidence (before the token): request r on CTA r % grid, one warp ------
-    for (int rr = static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) * warp; rr < p.num_requests;
-         rr += 4 * static_cast<int>(gridDim.x)) {
-      long long t = p.prev[rr * p.prev_stride];
-      t = (t < 0 || t >= p.vocab) ? 0 : t;
-      const __nv_bfloat16* h = p.hidden + (static_cast<long long>(rr) * p.base_stride_r + p.k) * p.hidden_dim;
-      const __nv_bfloat16* em = p.emb_table + t * p.rank;
-      float acc = 0.f;
-      if (p.conf_vec) {
-        // 8 bf16 per 16-byte load, all of a lane's loads in flight together
-        auto dot8 = [](uint4 a, uint4 b, float acc) {
-          const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&a);
-          const __nv_bfloat16* y = reinterpret_cast<const __nv_bfloat16*>(&b);
-#pragma unroll
-          for (int e = 0; e < 8; ++e) acc = fmaf(__bfloat162float(x[e]), __bfloat162float(y[e]), acc);
-          return acc;
-        };
-#pragma unroll 4
-        for (int i = lane * 8; i < p.hidden_dim; i += 256)
-          acc = dot8(__ldg(reinterpret_cast<const uint4*>(h + i)), __ldg(reinterpret_cast<const uint4*>(p.conf_w + i)),
-                     acc);
-#pragma unroll 2
-        for (int i = lane * 8; i < p.rank; i += 256)
-          acc = dot8(__ldg(reinterpret_cast<const uint4*>(em + i)),
-                     __ldg(reinterpret_cast<const uint4*>(p.conf_w + p.hidden_dim + i)), acc);
-      } else {
-        for (int i = lane; i < p.hidden_dim; i += 32)
-          acc = fmaf(__bfloat162float(h[i]), __bfloat162float(p.conf_w[i]), acc);
-        for (int i = lane; i < p.rank; i += 32)
-          acc = fmaf(__bfloat162float(em[i]), __bfloat162float(p.conf_w[p.hidden_dim + i]), acc);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-      if (lane == 0) {
-        // bf16 Linear output (fp32 dot + bias, rounded once), then a bf16 sigmoid
-        const float logit = bf16_round(acc + p.conf_b);
-        p.conf[rr * p.tok_stride + p.k] = bf16_round(1.f / (1.f + expf(-logit)));
-      }
-    }
-    if (live && best_idx != 0x7fffffff)
-      atomicMax(p.best + r, (static_cast<unsigned long long>(best_key) << 32) |
-                                static_cast<unsigned long long>(0xffffffffu - static_cast<unsigned int>(best_idx)));
   } else if (warp == 4) {
     if (lane == 0) {
       constexpr uint32_t kIdesc = instr_desc(0);
-      bool ok = wait_or_abort(bar(kBarAReady), 0, abort_flag);
-      tc_fence_after();
-      for (int t = 0; t < n_mine && ok; ++t) {
-        const int st = t & 1, b = t & 1;
-        if (!(ok = wait_or_abort(bar(kBarWFull0 + st), (t >> 1) & 1, abort_flag))) break;
-        if (!(ok = wait_or_abort(bar(kBarDFree0 + b), ((t >> 1) & 1) ^ 1, abort_flag))) break;
+      bool ok = true;
+      for (int s = 0; s < steps && ok; ++s) {
+        if (!(ok = wait_or_abort(bar(kBarAReady), s & 1, abort_flag))) break;
         tc_fence_after();
-        const uint32_t wbase = sbase + kSmemW + st * 65536;
-        for (int kk = 0; kk < p.rank / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-          umma_bf16(tmem + b * 128, smem_desc(sbase + kSmemA + off, 16, 1024), smem_desc(wbase + off, 16, 1024),
-                    kIdesc, kk > 0);
+        for (int t = 0; t < n_mine && ok; ++t) {
+          const int g = s * n_mine + t, st = g & 1, b = g & 1;
+          if (!(ok = wait_or_abort(bar(kBarWFull0 + st), (g >> 1) & 1, abort_flag))) break;
+          if (!(ok = wait_or_abort(bar(kBarDFree0 + b), ((g >> 1) & 1) ^ 1, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t wbase = sbase + kSmemW + st * 65536;
+          for (int kk = 0; kk < p.rank / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
+            umma_bf16(tmem + b * 128, smem_desc(sbase + kSmemA + off, 16, 1024), smem_desc(wbase + off, 16, 1024),
+                      kIdesc, kk > 0);
+          }
+          umma_commit(bar(kBarDFull0 + b));
+          umma_commit(bar(kBarWEmpty0 + st));
         }
-        umma_commit(bar(kBarDFull0 + b));
-        umma_commit(bar(kBarWEmpty0 + st));
+        umma_commit(bar(kBarAFree));               // the A tile may be refilled for the next step
       }
       if (!ok) *abort_flag = 1;
       umma_commit(bar(kBarDrain));
@@ -304,15 +440,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     if (lane == 0) {
+      // the projection-weight tiles of every step, streamed without waiting for the tokens
       int armed[2] = {0, 0};
       bool ok = true;
-      for (int t = 0; t < n_mine && ok; ++t) {
-        const int st = t & 1;
+      for (int g = 0; g < steps * n_mine && ok; ++g) {
+        const int st = g & 1, t = g % n_mine;
         const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
-        if (!(ok = wait_or_abort(bar(kBarWEmpty0 + st), ((t >> 1) & 1) ^ 1, abort_flag))) break;
+        if (!(ok = wait_or_abort(bar(kBarWEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
         mbar_arrive_expect_tx(bar(kBarWFull0 + st), tile_bytes);
         for (int c = 0; c < chunks; ++c)
-          tma_load_2d(sbase + kSmemW + st * 65536 + c * 16384, &wmap, c * 64, v0, bar(kBarWFull0 + st));
+          tma_load_2d(sbase + kSmemW + st * 65536 + c * 16384, wmap, c * 64, v0, bar(kBarWFull0 + st));
         ++armed[st];
       }
       if (!ok) *abort_flag = 1;
@@ -323,25 +460,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // ---- the last CTA to arrive publishes the tokens and clears the scratch -------
-  __threadfence();
-  tc_fence_before();
-  __syncthreads();
-  volatile int* last = reinterpret_cast<volatile int*>(smem + kSmemLast);
-  if (threadIdx.x == 0) *last = atomicAdd(p.arrivals, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (*last) {
+  if (!kBlock) {
+    // ---- the last CTA to arrive publishes the tokens and clears the scratch -----
     __threadfence();
-    const int r = threadIdx.x;
-    if (r < kRows) {
-      const unsigned long long v = atomicExch(p.best + r, 0ull);
-      if (r < p.num_requests)
-        p.tokens[r * p.tok_stride + p.k] = static_cast<long long>(0xffffffffu - static_cast<unsigned int>(v));
+    tc_fence_before();
+    __syncthreads();
+    volatile int* last = reinterpret_cast<volatile int*>(smem + kSmemLast);
+    if (threadIdx.x == 0) *last = atomicAdd(p.arrivals, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (*last) {
+      __threadfence();
+      const int r = threadIdx.x;
+      if (r < kRows) {
+        const unsigned long long v = atomicExch(p.best + r, 0ull);
+        if (r < p.num_requests) p.tokens[r * p.tok_stride + p.k] = packed_token(v);
+      }
+      if (threadIdx.x == 0) atomicExch(p.arrivals, 0u);
     }
-    if (threadIdx.x == 0) atomicExch(p.arrivals, 0u);
+    tc_fence_after();
+  } else {
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
   }
-  tc_fence_after();
   if (warp == 4) tmem_dealloc(tmem, kTmemCols);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    markov_step_kernel(const __grid_constant__ CUtensorMap wmap, Params p) {
+  markov_body<false>(&wmap, p);
+}
+
+// Cooperative launch only (all CTAs resident: the grid barrier waits on them).
+__global__ void __launch_bounds__(kThreads, 1)
+    markov_block_kernel(const __grid_constant__ CUtensorMap wmap, Params p) {
+  markov_body<true>(&wmap, p);
 }
 
 }  // namespace markov

@@ -301,7 +301,8 @@ _markov_scratch = {}
 def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, anchors, block_size):
     """Serial greedy Markov proposal of one draft block for every request on the
     GPU (DSparkDraft._sample_greedy, dspark_qwen/model.py:210-221), one fused
-    tcgen05 launch per block position (``dspark_markov_step``).
+    tcgen05 kernel: all positions in one cooperative launch (``dspark_markov_block``),
+    or one launch per position (``dspark_markov_step``) for blocks over 64.
 
     ``proj_weight``/``emb_table`` [V, rank] bf16 (markov_projection.weight /
     markov_embedding.weight), ``conf_weight`` [H + rank] bf16, ``conf_bias`` a float,
@@ -332,6 +333,14 @@ def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, 
     lib, stream = _lib.load_library(), _stream(device)
     for r0 in range(0, r, 128):
         n = min(128, r - r0)
+        if block_size <= 64:
+            # every position of the block in one cooperative launch
+            _lib.check(lib.dspark_markov_block(
+                proj_weight.data_ptr(), emb_table.data_ptr(), v, rank, base[r0 * block_size:].data_ptr(), block_size,
+                anchors[r0:].data_ptr(), hidden[r0 * block_size:].data_ptr(), h, conf_weight.data_ptr(),
+                float(conf_bias), tokens[r0:].data_ptr(), conf[r0:].data_ptr(), n, scratch.data_ptr(), stream),
+                'dspark_markov_block')
+            continue
         for k in range(block_size):
             prev, prev_stride = ((anchors[r0:].data_ptr(), 1) if k == 0
                                  else (tokens[r0:, k - 1:].data_ptr(), block_size))

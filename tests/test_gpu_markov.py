@@ -104,3 +104,62 @@ def test_packed_draft_uses_fused_markov(pkg):
                 assert logits[ref] - logits[toks[k]] <= 2.0 ** (np.floor(np.log2(abs(float(logits[ref])))) - 7)
             prev = torch.tensor([toks[k]], device=dev())
     status_clean(pkg)
+
+
+def test_markov_block_launch_equals_step_launches(pkg):
+    """All positions of a block in one cooperative launch (dspark_markov_block) give
+    the tokens and confidences of one launch per position (dspark_markov_step),
+    bit for bit: 128 requests, a vocabulary whose last tile is partial, twice in a
+    row (the scratch is left usable)."""
+    from importlib import import_module
+    _lib = import_module('qwen3-dspark_b200._lib')
+    kern = import_module('qwen3-dspark_b200.kernels')
+    r, vocab, rank, hdim, block = 128, 65544, 256, 1024, 7
+    w, e, cw, hidden, base, anchors, cb = make(77, r, vocab, rank, hdim, block)
+    lib = _lib.load_library()
+    stream = torch.cuda.current_stream().cuda_stream
+    for rep in range(2):
+        fused_t, fused_c = pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+        scratch = torch.zeros(int(lib.dspark_markov_scratch_bytes()), dtype=torch.uint8, device=dev())
+        toks = torch.empty((r, block), dtype=torch.long, device=dev())
+        conf = torch.empty((r, block), dtype=torch.float32, device=dev())
+        for k in range(block):
+            prev, stride = (anchors.data_ptr(), 1) if k == 0 else (toks[:, k - 1:].data_ptr(), block)
+            _lib.check(lib.dspark_markov_step(w.data_ptr(), e.data_ptr(), vocab, rank, base.data_ptr(), block, k, prev,
+                                              stride, hidden.data_ptr(), hdim, cw.data_ptr(), float(cb),
+                                              toks.data_ptr(), conf.data_ptr(), block, r, scratch.data_ptr(), stream),
+                       'dspark_markov_step')
+        torch.cuda.synchronize()
+        assert torch.equal(fused_t, toks), rep
+        assert torch.equal(fused_c, conf), rep
+        assert int(scratch[:3 * 128 * 8].count_nonzero()) == 0
+        key = (dev().index, torch.cuda.current_stream().cuda_stream)
+        assert int(kern._markov_scratch[key][:3 * 128 * 8 + 4].count_nonzero()) == 0   # best buffers, counter
+    status_clean(pkg)
+
+
+def test_markov_ties_zero_and_nan_follow_torch_argmax(pkg):
+    """With a zero projection the logits are exactly the bf16 base rows, so the
+    kernel must pick torch.argmax's index: planted equal maxima in different tiles
+    (and CTAs) resolve to the lowest index, -0 and +0 compare equal, a NaN wins
+    (the first NaN)."""
+    r, vocab, rank, hdim, block = 6, 40960, 64, 256, 2
+    w, e, cw, hidden, base, anchors, cb = make(5, r, vocab, rank, hdim, block)
+    w.zero_()
+    b = (-torch.rand(r * block, vocab, device=dev()) - 1.0).to(torch.bfloat16)   # all in [-2, -1)
+    b[0, 300] = b[0, 39000] = 5.0                    # equal maxima in different tiles
+    b[1, 17] = b[1, 18] = 3.0                        # adjacent equal maxima
+    b[2, 5000] = -0.0
+    b[2, 100] = 0.0                                  # +0 before -0: the lower index wins
+    b[3, 7000] = float('nan')
+    b[3, 20000] = float('nan')
+    b[3, 10] = 9.0                                   # NaN beats 9
+    b[4, vocab - 1] = 7.0                            # the last column of the vocabulary
+    b[5:7, 123] = 1.0
+    toks, _ = pkg.markov_greedy(w, e, cw, cb, hidden, b, anchors, block)
+    torch.cuda.synchronize()
+    for k in range(block):
+        rows = torch.arange(r, device=dev()) * block + k
+        ref = (b[rows].float() + 0.0).argmax(-1)
+        assert torch.equal(toks[:, k], ref), (k, toks[:, k].tolist(), ref.tolist())
+    status_clean(pkg)
