@@ -571,11 +571,14 @@ def markov_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, hdim
             toks.append(prev)
         return torch.stack(toks, 1), torch.stack(confs, 1)
 
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
     def timed(fn):
         for _ in range(warmup):
             fn()
         pairs = []
         for _ in range(iters):
+            flush.zero_()                   # L2 written over: nothing carries over between blocks
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()

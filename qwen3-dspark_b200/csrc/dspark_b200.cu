@@ -543,6 +543,7 @@ int markov_setup(const void* proj_weight, const void* emb_table, int vocab, int 
   p.arrivals = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(scratch) + 3 * markov::kRows * 8);
   p.generation = p.arrivals + 1;
   p.num_requests = num_requests;
+  p.dup = num_requests <= 64;
   p.vocab = vocab;
   p.rank = rank;
   p.tiles = (vocab + markov::kVocabTile - 1) / markov::kVocabTile;

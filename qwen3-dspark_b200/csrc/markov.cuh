@@ -35,8 +35,11 @@
 // Roles (192 threads, persistent CTAs over the vocabulary tiles):
 //   warps 0-3  per step: gather emb rows into shared memory (A operand),
 //              confidence (one warp per request, spread over the CTAs),
-//              epilogue (thread r = request r = TMEM lane r; the base row of
-//              the next tile is loaded while the current tile is reduced);
+//              epilogue (thread m = TMEM lane m; the base row of the next tile
+//              is loaded while the current tile is reduced). With at most 64
+//              requests request r fills rows r and r + 64, and the threads of
+//              the two rows reduce one half of the columns each, so all four
+//              warps (TMEM lane quarters) do useful work;
 //   warp 4     TMEM owner and MMA issuer (one thread);
 //   warp 5     TMA producer of the projection-weight tiles (two stages).
 #pragma once
@@ -96,6 +99,7 @@ struct Params {
   unsigned int* arrivals;           // CTA arrival counter (zero between calls)
   unsigned int* generation;         // grid-barrier generation
   int num_requests;                 // R <= 128
+  int dup;                          // R <= 64: request r also in row r + 64 (column halves split)
   int vocab;                        // V, multiple of 8
   int rank;                         // multiple of 64, <= 256
   int tiles;                        // ceil(V / 128)
@@ -214,15 +218,16 @@ __device__ __forceinline__ void confidence_rows(const Params& p, int k, int warp
   }
 }
 
-// Request r's 128 base logits of tile t at block position k (zeros past the
-// vocabulary or for padding rows).
-__device__ __forceinline__ void load_base(const Params& p, int k, int t, int n_mine, int r, bool live,
-                                          uint4 (&raw)[16]) {
+// Request r's base logits of tile t at block position k, columns c0 .. c0 +
+// 64 nh - 1 of the tile (raw[q] = columns c0 + 8q ..; zeros past the vocabulary
+// or for padding rows).
+__device__ __forceinline__ void load_base(const Params& p, int k, int t, int n_mine, int r, bool live, int c0,
+                                          int nh, uint4 (&raw)[16]) {
   const __nv_bfloat16* brow = p.base + (static_cast<long long>(r) * p.base_stride_r + k) * p.vocab;
-  const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
+  const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile + c0;
 #pragma unroll
   for (int q = 0; q < 16; ++q)
-    raw[q] = (live && t < n_mine && v0 + q * 8 < p.vocab)
+    raw[q] = (live && t < n_mine && q < nh * 8 && v0 + q * 8 < p.vocab)
                  ? __ldg(reinterpret_cast<const uint4*>(brow + v0 + q * 8)) : make_uint4(0, 0, 0, 0);
 }
 
@@ -233,8 +238,9 @@ __device__ __forceinline__ void load_base(const Params& p, int k, int t, int n_m
 // loads the first tile of block position k_next (if >= 0), so their DRAM latency
 // overlaps other work.
 __device__ __forceinline__ bool epilogue_step(const Params& p, int k, int k_next, int g0, int n_mine, int r,
-                                              bool live, uint32_t tmem, uint32_t bars, volatile int* abort_flag,
-                                              uint4 (&bnext)[16], uint32_t& best_key, int& best_idx) {
+                                              bool live, int c0, int nh, uint32_t tmem, uint32_t bars,
+                                              volatile int* abort_flag, uint4 (&bnext)[16], uint32_t& best_key,
+                                              int& best_idx) {
   auto bar = [&](int i) { return bars + 8u * i; };
   const int warp = threadIdx.x >> 5;
   best_key = 0;
@@ -248,26 +254,29 @@ __device__ __forceinline__ bool epilogue_step(const Params& p, int k, int k_next
 #pragma unroll
     for (int q = 0; q < 16; ++q) braw[q] = bnext[q];
     if (t + 1 < n_mine)
-      load_base(p, k, t + 1, n_mine, r, live, bnext);
+      load_base(p, k, t + 1, n_mine, r, live, c0, nh, bnext);
     else if (k_next >= 0)
-      load_base(p, k_next, 0, n_mine, r, live, bnext);
+      load_base(p, k_next, 0, n_mine, r, live, c0, nh, bnext);
     const bool ok = wait_or_abort(bar(kBarDFull0 + b), (g >> 1) & 1, abort_flag);
     if (!__all_sync(0xffffffffu, ok)) return false;
     tc_fence_after();
-    // one running max per 32-column chunk of packed (key << 16 | 127 - column)
+    // running maxima of packed (key << 16 | 127 - column) over this thread's
+    // columns c0 .. (two independent chains per 64 columns)
     uint32_t chain[4] = {0u, 0u, 0u, 0u};
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
+      if (h >= nh) break;
       float d[64];
-      tmem_ld64(tmem + lane_addr + b * 128 + h * 64, d);
+      tmem_ld64(tmem + lane_addr + b * 128 + c0 + h * 64, d);
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const int col = h * 64 + 2 * i;
+        const int lc = h * 64 + 2 * i;             // column relative to c0 (static)
+        const int col = c0 + lc;
         // projection output to bf16, plus the bf16 base logit, sum to bf16
         const uint32_t r1 = pack_bf16x2(d[2 * i], d[2 * i + 1]);
-        const uint4& bq = braw[col >> 3];
-        const uint32_t bb = ((col & 7) >> 1) == 0 ? bq.x : ((col & 7) >> 1) == 1 ? bq.y
-                          : ((col & 7) >> 1) == 2 ? bq.z : bq.w;
+        const uint4& bq = braw[lc >> 3];
+        const uint32_t bb = ((lc & 7) >> 1) == 0 ? bq.x : ((lc & 7) >> 1) == 1 ? bq.y
+                          : ((lc & 7) >> 1) == 2 ? bq.z : bq.w;
         const float s0 = __uint_as_float(r1 << 16) + __uint_as_float(bb << 16);
         const float s1 = __uint_as_float(r1 & 0xffff0000u) + __uint_as_float(bb & 0xffff0000u);
         const uint32_t key = bf16x2_order_keys(pack_bf16x2(s0, s1));
@@ -277,7 +286,7 @@ __device__ __forceinline__ bool epilogue_step(const Params& p, int k, int k_next
           p0 = col < nvalid ? p0 : 0u;
           p1 = col + 1 < nvalid ? p1 : 0u;
         }
-        chain[col >> 5] = max(chain[col >> 5], max(p0, p1));
+        chain[lc >> 5] = max(chain[lc >> 5], max(p0, p1));
       }
     }
     tc_fence_before();
@@ -355,10 +364,12 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
                          ? (p.tiles - 1 - static_cast<int>(blockIdx.x)) / static_cast<int>(gridDim.x) + 1 : 0;
 
   if (warp < 4) {
-    const int r = threadIdx.x;
+    const int m = threadIdx.x;                     // A row / TMEM lane
+    const int r = p.dup ? (m & 63) : m;            // its request
     const bool live = r < p.num_requests;
+    const int c0 = p.dup ? (m >> 6) * 64 : 0, nh = p.dup ? 1 : 2;   // its columns
     uint4 bnext[16];                               // base logits of the next tile to reduce
-    load_base(p, kBlock ? 0 : p.k, 0, n_mine, r, live, bnext);
+    load_base(p, kBlock ? 0 : p.k, 0, n_mine, r, live, c0, nh, bnext);
     for (int s = 0; s < steps; ++s) {
       const int k = kBlock ? s : p.k;
       unsigned long long* const best_now = p.best + (kBlock ? (s % 3) * kRows : 0);
@@ -375,21 +386,21 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
       bool ok = __all_sync(0xffffffffu, !*abort_flag);
       if (ok && s > 0) ok = __all_sync(0xffffffffu, wait_or_abort(bar(kBarAFree), (s - 1) & 1, abort_flag));
       if (ok) {
-        gather_row(p, smem, r, tok, live);
+        gather_row(p, smem, m, tok, live);
         fence_proxy_async_smem();
       }
       mbar_arrive(bar(kBarAReady));
       if (kBlock && blockIdx.x == 0) {
-        if (s > 0 && live) p.tokens[r * p.tok_stride + s - 1] = tok;
+        if (s > 0 && live && m == r) p.tokens[r * p.tok_stride + s - 1] = tok;
         // the buffer of step s - 2 (read by every CTA before the last barrier)
         // is cleared for step s + 1
-        p.best[((s + 1) % 3) * kRows + r] = 0ull;
+        p.best[((s + 1) % 3) * kRows + m] = 0ull;
       }
       uint32_t best_key = 0;
       int best_idx = 0x7fffffff;
       if (ok)
-        ok = epilogue_step(p, k, kBlock && s + 1 < steps ? s + 1 : -1, s * n_mine, n_mine, r, live, tmem, bars,
-                           abort_flag, bnext, best_key, best_idx);
+        ok = epilogue_step(p, k, kBlock && s + 1 < steps ? s + 1 : -1, s * n_mine, n_mine, r, live, c0, nh, tmem,
+                           bars, abort_flag, bnext, best_key, best_idx);
       if (!ok) *abort_flag = 1;
       publish(p, best_now, r, live, best_key, best_idx);
       // the confidence is off the MMA pipeline's path: after the tiles
@@ -404,10 +415,10 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
     if (kBlock && blockIdx.x == 0) {
       // after the last barrier: the last step's tokens, and the two buffers in use cleared
       const int last = steps - 1;
-      const unsigned long long v = __ldcg(p.best + (last % 3) * kRows + r);
-      if (live) p.tokens[r * p.tok_stride + last] = v ? packed_token(v) : 0;
-      p.best[(last % 3) * kRows + r] = 0ull;
-      p.best[((last + 2) % 3) * kRows + r] = 0ull;
+      const unsigned long long v = __ldcg(p.best + (last % 3) * kRows + m);
+      if (m < p.num_requests) p.tokens[m * p.tok_stride + last] = v ? packed_token(v) : 0;
+      p.best[(last % 3) * kRows + m] = 0ull;
+      p.best[((last + 2) % 3) * kRows + m] = 0ull;
     }
   } else if (warp == 4) {
     if (lane == 0) {
