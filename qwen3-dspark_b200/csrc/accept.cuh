@@ -97,7 +97,7 @@ __global__ void __launch_bounds__(kArgmaxThreads) row_argmax_kernel(const T* __r
     ArgBest b = warp_best[0];
     for (int w = 1; w < kArgmaxThreads / 32; ++w)
       if (arg_better(warp_best[w], b)) b = warp_best[w];
-    pred[blockIdx.x] = b.i;
+    pred[blockIdx.x] = b.i == 0x7fffffff ? 0 : b.i;   // a row of -inf only: its first index, as torch.argmax
   }
 }
 

@@ -55,7 +55,8 @@ using train::tc_fence_before;
 using train::tmem_alloc;
 using train::tmem_dealloc;
 using train::tmem_ld32;
-using train::umma_bf16;
+using train::tmem_st32;
+using train::umma_bf16_ts;
 using train::umma_commit;
 using train::wait_or_abort;
 
@@ -64,16 +65,19 @@ constexpr int kRows = 128;        // padded request rows (MMA M)
 constexpr int kVocabTile = 128;   // vocabulary rows per tile (MMA N)
 constexpr int kMaxRank = 256;
 constexpr int kMaxSteps = 64;     // block positions per fused launch
-constexpr uint32_t kSmemA = 0;                           // 128 x rank bf16 (<= 64 KB)
-constexpr uint32_t kSmemW = 65536;                       // 2 stages x 64 KB
-constexpr uint32_t kSmemBar = kSmemW + 2 * 65536;
-enum Barrier { kBarAReady = 0, kBarAFree, kBarWFull0, kBarWFull1, kBarWEmpty0, kBarWEmpty1, kBarDFull0, kBarDFull1,
-               kBarDFree0, kBarDFree1, kBarDrain, kNumBarriers };
+constexpr int kWStages = 3;
+constexpr uint32_t kSmemW = 0;                           // 3 stages x 64 KB (128 vocabulary rows x rank)
+constexpr uint32_t kSmemBar = kSmemW + kWStages * 65536;
+enum Barrier { kBarAReady = 0, kBarAFree, kBarWFull0, kBarWEmpty0 = kBarWFull0 + kWStages,
+               kBarDFull0 = kBarWEmpty0 + kWStages, kBarDFull1, kBarDFree0, kBarDFree1, kBarDrain, kNumBarriers };
 constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
 constexpr uint32_t kSmemAbort = kSmemSlot + 4;
 constexpr uint32_t kSmemLast = kSmemAbort + 4;
 constexpr uint32_t kSmemBytes = 1024 + kSmemLast + 4;
-constexpr uint32_t kTmemCols = 256;                      // two 128-column D buffers
+// TMEM: two 128-column D buffers, then the A operand (the gathered embedding
+// rows, bf16 pairs: column j of lane m = elements 2j, 2j+1 of row m).
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemA = 256;
 // Scratch (zero between calls): three best buffers of kRows packed maxima, the
 // CTA arrival counter, the grid-barrier generation (the only word that is not
 // returned to zero: it only ever advances).
@@ -159,18 +163,17 @@ __device__ __forceinline__ long long checked_token(const Params& p, long long t)
   return t;
 }
 
-// Row r of the A operand (K-major, 128-byte swizzle): the embedding of `tok`,
-// or zeros for a padding row.
-__device__ __forceinline__ void gather_row(const Params& p, uint8_t* smem, int r, long long tok, bool live) {
+// TMEM lane m of the A operand (warp-collective: the warp writes its 32 lanes):
+// the embedding of `tok`, or zeros for a padding row.
+__device__ __forceinline__ void gather_row(const Params& p, uint32_t a_tmem, long long tok, bool live) {
   const uint4* src = reinterpret_cast<const uint4*>(p.emb_table + tok * p.rank);
-  const int chunks = p.rank / 64;
+  const int chunks = p.rank / 64;                  // 32 TMEM columns (64 elements) each
   uint4 v[kMaxRank / 8];                           // every load in flight before the first store
 #pragma unroll
   for (int i = 0; i < kMaxRank / 8; ++i) v[i] = live && i < chunks * 8 ? __ldg(src + i) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-  for (int i = 0; i < kMaxRank / 8; ++i)
-    if (i < chunks * 8)
-      *reinterpret_cast<uint4*>(smem + kSmemA + (i >> 3) * 16384 + r * 128 + (((i & 7) ^ (r & 7)) << 4)) = v[i];
+  for (int c = 0; c < kMaxRank / 64; ++c)
+    if (c < chunks) tmem_st32(a_tmem + 32 * c, *reinterpret_cast<const float(*)[32]>(&v[8 * c]));
 }
 
 // Confidence of block position k (before its token) for the requests of this
@@ -381,14 +384,13 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
         return checked_token(p, packed_token(__ldcg(best_prev + rr)));
       };
       const long long tok = live ? prev_of(r) : 0;
-      // the A tile is free once the previous step's MMAs are done (decisions are
+      // the A operand is free once the previous step's MMAs are done (decisions are
       // warp-uniform: the confidence and the TMEM loads are warp-collective)
       bool ok = __all_sync(0xffffffffu, !*abort_flag);
       if (ok && s > 0) ok = __all_sync(0xffffffffu, wait_or_abort(bar(kBarAFree), (s - 1) & 1, abort_flag));
-      if (ok) {
-        gather_row(p, smem, m, tok, live);
-        fence_proxy_async_smem();
-      }
+      tc_fence_after();
+      if (ok) gather_row(p, tmem + (static_cast<uint32_t>(warp * 32) << 16) + kTmemA, tok, live);
+      tc_fence_before();
       mbar_arrive(bar(kBarAReady));
       if (kBlock && blockIdx.x == 0) {
         if (s > 0 && live && m == r) p.tokens[r * p.tok_stride + s - 1] = tok;
@@ -428,16 +430,15 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
         if (!(ok = wait_or_abort(bar(kBarAReady), s & 1, abort_flag))) break;
         tc_fence_after();
         for (int t = 0; t < n_mine && ok; ++t) {
-          const int g = s * n_mine + t, st = g & 1, b = g & 1;
-          if (!(ok = wait_or_abort(bar(kBarWFull0 + st), (g >> 1) & 1, abort_flag))) break;
+          const int g = s * n_mine + t, st = g % kWStages, b = g & 1;
+          if (!(ok = wait_or_abort(bar(kBarWFull0 + st), (g / kWStages) & 1, abort_flag))) break;
           if (!(ok = wait_or_abort(bar(kBarDFree0 + b), ((g >> 1) & 1) ^ 1, abort_flag))) break;
           tc_fence_after();
           const uint32_t wbase = sbase + kSmemW + st * 65536;
-          for (int kk = 0; kk < p.rank / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * 16384 + (kk & 3) * 32;
-            umma_bf16(tmem + b * 128, smem_desc(sbase + kSmemA + off, 16, 1024), smem_desc(wbase + off, 16, 1024),
-                      kIdesc, kk > 0);
-          }
+          // D = A (TMEM, 8 columns per K=16 step) x W tile (shared memory)
+          for (int kk = 0; kk < p.rank / 16; ++kk)
+            umma_bf16_ts(tmem + b * 128, tmem + kTmemA + kk * 8,
+                         smem_desc(wbase + (kk >> 2) * 16384 + (kk & 3) * 32, 16, 1024), kIdesc, kk > 0);
           umma_commit(bar(kBarDFull0 + b));
           umma_commit(bar(kBarWEmpty0 + st));
         }
@@ -452,12 +453,12 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
   } else {
     if (lane == 0) {
       // the projection-weight tiles of every step, streamed without waiting for the tokens
-      int armed[2] = {0, 0};
+      int armed[kWStages] = {};
       bool ok = true;
       for (int g = 0; g < steps * n_mine && ok; ++g) {
-        const int st = g & 1, t = g % n_mine;
+        const int st = g % kWStages, t = g % n_mine;
         const int v0 = (static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x)) * kVocabTile;
-        if (!(ok = wait_or_abort(bar(kBarWEmpty0 + st), ((g >> 1) & 1) ^ 1, abort_flag))) break;
+        if (!(ok = wait_or_abort(bar(kBarWEmpty0 + st), ((g / kWStages) & 1) ^ 1, abort_flag))) break;
         mbar_arrive_expect_tx(bar(kBarWFull0 + st), tile_bytes);
         for (int c = 0; c < chunks; ++c)
           tma_load_2d(sbase + kSmemW + st * 65536 + c * 16384, wmap, c * 64, v0, bar(kBarWFull0 + st));
@@ -465,7 +466,7 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
       }
       if (!ok) *abort_flag = 1;
       volatile int never = 0;
-      for (int st = 0; st < 2; ++st)
+      for (int st = 0; st < kWStages; ++st)
         if (armed[st]) wait_or_abort(bar(kBarWFull0 + st), (armed[st] - 1) & 1, &never);
     }
     __syncwarp();

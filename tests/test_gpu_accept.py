@@ -88,3 +88,38 @@ def test_refusals(pkg):
         pkg.greedy_accept(logits, tokens, cu.long())
     with pytest.raises(ValueError):
         pkg.greedy_accept(logits, tokens, cu, budget=torch.zeros(2, dtype=torch.int32, device=dev()))
+
+
+@pytest.mark.parametrize('dtype', [torch.bfloat16, torch.float32])
+def test_argmax_edges_match_torch(pkg, dtype):
+    """dspark_row_argmax vs torch.argmax: equal maxima at the two ends of a row (the
+    lowest index wins), rows of -inf only (index 0), signed zeros (equal), NaN
+    (the first one), rows all equal, tiny vocabularies, and rows that are not
+    16-byte aligned (a padded leading dimension)."""
+    from importlib import import_module
+    _lib = import_module('qwen3-dspark_b200._lib')
+    lib = _lib.load_library()
+    code = _lib.DTYPE_BF16 if dtype == torch.bfloat16 else _lib.DTYPE_F32
+    stream = torch.cuda.current_stream().cuda_stream
+    for vocab, ld in ((151936, 151936), (1001, 1003), (7, 7), (3, 5), (1, 1), (4099, 4099)):
+        g = torch.Generator(device='cpu').manual_seed(vocab)
+        buf = torch.randn(12, ld, generator=g).to(dtype)
+        x = buf[:, :vocab]
+        x[0, vocab - 1] = 50.0
+        x[0, 0] = 50.0                                   # first and last element tie
+        x[1] = float('-inf')                             # nothing but -inf
+        x[2] = -1.0
+        x[2, vocab // 2] = -0.0
+        x[2, vocab - 1] = 0.0                            # -0 == +0: the earlier one
+        x[3, vocab // 3] = float('nan')                  # NaN beats numbers
+        x[4, vocab - 1] = float('nan')
+        x[4, vocab // 4] = float('nan')                  # the first NaN
+        x[5] = 1.0                                       # all equal: index 0
+        buf_d = buf.to(dev())
+        pred = torch.empty(12, dtype=torch.int32, device=dev())
+        _lib.check(lib.dspark_row_argmax(buf_d.data_ptr(), ld, 12, vocab, code, pred.data_ptr(), stream),
+                   'dspark_row_argmax')
+        torch.cuda.synchronize()
+        ref = buf[:, :vocab].float().argmax(-1).to(torch.int32)
+        assert torch.equal(pred.cpu(), ref), (vocab, ld, pred.cpu().tolist(), ref.tolist())
+    status_clean(pkg)
