@@ -57,7 +57,14 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     for vocab, rank, r in ((1001, 256, 4), (1024, 96, 4), (1024, 320, 4), (1024, 256, 129)):   # refused shapes
         assert lib.dspark_markov_step(fake, fake, vocab, rank, fake, 7, 0, fake, 1, fake, 1024, fake, 0.0, fake,
                                       fake, 7, r, fake, None) == 1
-    assert lib.dspark_markov_scratch_bytes() >= 128 * 8
+    # the block entry: block sizes 1..64, the same operand rules, anchors required
+    for vocab, rank, r, bs in ((1001, 256, 4, 7), (1024, 96, 4, 7), (1024, 256, 129, 7), (1024, 256, 4, 0),
+                               (1024, 256, 4, 65)):
+        assert lib.dspark_markov_block(fake, fake, vocab, rank, fake, bs, fake, fake, 1024, fake, 0.0, fake, fake, r,
+                                       fake, None) == 1
+    assert lib.dspark_markov_block(fake, fake, 1024, 256, fake, 7, None, fake, 1024, fake, 0.0, fake, fake, 4, fake,
+                                   None) == 1
+    assert lib.dspark_markov_scratch_bytes() >= 3 * 128 * 8 + 8
     # stochastic acceptance: target rows must be draft rows + requests, temperature > 0
     for rows, temp in ((4, 1.0), (3, 0.0), (3, float('nan'))):
         assert lib.dspark_stochastic_accept(fake, 1000, 1, 1000, temp, rows, fake, 1, fake, fake, 2, fake, 2, None, 0,
