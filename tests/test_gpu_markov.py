@@ -163,3 +163,35 @@ def test_markov_ties_zero_and_nan_follow_torch_argmax(pkg):
         ref = (b[rows].float() + 0.0).argmax(-1)
         assert torch.equal(toks[:, k], ref), (k, toks[:, k].tolist(), ref.tolist())
     status_clean(pkg)
+
+
+@pytest.mark.parametrize('block', [1, 2, 65])
+def test_markov_block_sizes_equal_step_launches(pkg, block):
+    """Blocks of one and two positions (the fused launch's buffer rotation at its
+    shortest) and of 65 positions (over the fused limit: one launch per position)
+    give the per-position launches' tokens and confidences bit for bit, and leave
+    the scratch ready for the next call."""
+    from importlib import import_module
+    _lib = import_module('qwen3-dspark_b200._lib')
+    kern = import_module('qwen3-dspark_b200.kernels')
+    r, vocab, rank, hdim = 64, 8192, 128, 256
+    w, e, cw, hidden, base, anchors, cb = make(block + 3, r, vocab, rank, hdim, block)
+    lib = _lib.load_library()
+    stream = torch.cuda.current_stream().cuda_stream
+    for rep in range(2):
+        fused_t, fused_c = pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+        scratch = torch.zeros(int(lib.dspark_markov_scratch_bytes()), dtype=torch.uint8, device=dev())
+        toks = torch.empty((r, block), dtype=torch.long, device=dev())
+        conf = torch.empty((r, block), dtype=torch.float32, device=dev())
+        for k in range(block):
+            prev, stride = (anchors.data_ptr(), 1) if k == 0 else (toks[:, k - 1:].data_ptr(), block)
+            _lib.check(lib.dspark_markov_step(w.data_ptr(), e.data_ptr(), vocab, rank, base.data_ptr(), block, k, prev,
+                                              stride, hidden.data_ptr(), hdim, cw.data_ptr(), float(cb),
+                                              toks.data_ptr(), conf.data_ptr(), block, r, scratch.data_ptr(), stream),
+                       'dspark_markov_step')
+        torch.cuda.synchronize()
+        assert torch.equal(fused_t, toks), (block, rep)
+        assert torch.equal(fused_c, conf), (block, rep)
+        key = (dev().index, torch.cuda.current_stream().cuda_stream)
+        assert int(kern._markov_scratch[key][:3 * 128 * 8 + 4].count_nonzero()) == 0
+    status_clean(pkg)
