@@ -268,7 +268,10 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
  * refusal of the reference's checks (1 non-finite logits, 2 draft row not a law, 3 token
  * out of range, 4 proposal with zero draft mass, 5 zero residual mass, 6 uniform outside
  * [0, 1), 7 inconsistent offsets), in which case count is 0. scratch: device memory of
- * dspark_stochastic_scratch_bytes(target_rows + draft_rows) bytes. Two launches.
+ * dspark_stochastic_scratch_bytes(target_rows + draft_rows) bytes (the row
+ * statistics and a 512 KB table of x / T for every bf16 bit pattern, so the
+ * float64 passes read x / T instead of dividing). Three launches for bf16
+ * logits (the table first), two for f32.
  */
 size_t dspark_stochastic_scratch_bytes(int rows);
 int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vocab, double temperature,

@@ -669,8 +669,16 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
   return launch_status();
 }
 
+namespace {
+// Stochastic scratch: the row statistics, then (256-byte aligned) the table of
+// x / T for every bf16 bit pattern.
+size_t stochastic_table_offset(int rows) {
+  return (static_cast<size_t>(rows) * sizeof(sampling::RowStats) + 255) & ~static_cast<size_t>(255);
+}
+}  // namespace
+
 size_t dspark_stochastic_scratch_bytes(int rows) {
-  return rows > 0 ? static_cast<size_t>(rows) * sizeof(sampling::RowStats) : 0;
+  return rows > 0 ? stochastic_table_offset(rows) + sampling::kScaledTableSize * sizeof(double) : 0;
 }
 
 int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vocab, double temperature,
@@ -694,6 +702,15 @@ int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vo
   p.q = q;
   p.draft_rows = draft_rows;
   p.stats = static_cast<sampling::RowStats*>(scratch);
+  p.scaled = nullptr;
+  if (dtype == DSPARK_DTYPE_BF16) {
+    double* table = reinterpret_cast<double*>(static_cast<uint8_t*>(scratch) +
+                                              stochastic_table_offset(target_rows + draft_rows));
+    sampling::scaled_table_kernel<<<sampling::kScaledTableSize / 256, 256, 0, stream>>>(table, temperature);
+    const int st0 = launch_status();
+    if (st0 != DSPARK_OK) return st0;
+    p.scaled = table;
+  }
   p.tokens = tokens;
   p.cu_n = cu_n;
   p.num_requests = num_requests;

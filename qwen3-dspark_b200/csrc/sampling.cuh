@@ -7,7 +7,10 @@
 // past the end (sample_categorical, :77-84), and the stop rules of
 // verify_proposal (:114-162).
 //
-// Two launches. law_stats_kernel: one CTA per target row (max of x / T, the sum of
+// Three launches. scaled_table_kernel (bf16 logits only): x / T for all 65536
+// bf16 bit patterns, the same IEEE division the reference does per element, so
+// the later passes read it instead of dividing (the divisions were most of
+// their float64 work). law_stats_kernel: one CTA per target row (max of x / T, the sum of
 // exp(x / T - max) and the sum of the normalised weights) and one per draft row
 // (a law: finite, in [0, 1], sum within 1e-12 of one). stochastic_accept_kernel:
 // one CTA per request; thread 0 walks the proposals with the request's uniforms
@@ -42,8 +45,11 @@ struct RowStats {
   int pad;
 };
 
+constexpr int kScaledTableSize = 65536;   // one float64 per bf16 bit pattern
+
 struct Params {
   const void* logits;        // target rows, [rows, ld] bf16 or f32
+  const double* scaled;      // bf16: x / T per bit pattern (kScaledTableSize); f32: null
   long long ld;
   int dtype;                 // 0 bf16, 1 f32
   int vocab;
@@ -64,11 +70,61 @@ struct Params {
   int* result;               // [R, 8]: count, accepted, rejected, extra, reason, draws, status, 0
 };
 
-__device__ __forceinline__ double load_logit(const Params& p, long long row, int i) {
+// x / T of the logit at (row, i): a table read for bf16 (x takes one of 65536
+// values), the division for f32. Non-finite x gives non-finite x / T (T is
+// finite and positive), so a finiteness check of x / T covers both.
+__device__ __forceinline__ double load_scaled(const Params& p, long long row, int i) {
   if (p.dtype == 0)
-    return static_cast<double>(
-        __bfloat162float(static_cast<const __nv_bfloat16*>(p.logits)[row * p.ld + i]));
-  return static_cast<double>(static_cast<const float*>(p.logits)[row * p.ld + i]);
+    return p.scaled[static_cast<const unsigned short*>(p.logits)[row * p.ld + i]];
+  return static_cast<double>(static_cast<const float*>(p.logits)[row * p.ld + i]) / p.temperature;
+}
+
+// Calls f(i, x_i / T) for this thread's share of row `row`: 8 consecutive bf16
+// (one 16-byte load, their 8 table reads independent of each other, so they
+// are in flight together) or 4 f32 per step when the row is 16-byte aligned,
+// element by element otherwise and for the tail.
+template <class F>
+__device__ __forceinline__ void for_scaled(const Params& p, long long row, F f) {
+  if (p.dtype == 0) {
+    const unsigned short* r = static_cast<const unsigned short*>(p.logits) + row * p.ld;
+    int i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+      const int nv = p.vocab / 8;
+      for (int v = threadIdx.x; v < nv; v += kThreads) {
+        const uint4 raw = __ldg(reinterpret_cast<const uint4*>(r) + v);
+        const unsigned short* h = reinterpret_cast<const unsigned short*>(&raw);
+        double x[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[e] = __ldg(p.scaled + h[e]);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f(v * 8 + e, x[e]);
+      }
+      i0 = nv * 8;
+    }
+    for (int i = i0 + threadIdx.x; i < p.vocab; i += kThreads) f(i, p.scaled[r[i]]);
+  } else {
+    const float* r = static_cast<const float*>(p.logits) + row * p.ld;
+    int i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(r) & 15) == 0) {
+      const int nv = p.vocab / 4;
+      for (int v = threadIdx.x; v < nv; v += kThreads) {
+        const float4 raw = __ldg(reinterpret_cast<const float4*>(r) + v);
+        f(v * 4, static_cast<double>(raw.x) / p.temperature);
+        f(v * 4 + 1, static_cast<double>(raw.y) / p.temperature);
+        f(v * 4 + 2, static_cast<double>(raw.z) / p.temperature);
+        f(v * 4 + 3, static_cast<double>(raw.w) / p.temperature);
+      }
+      i0 = nv * 4;
+    }
+    for (int i = i0 + threadIdx.x; i < p.vocab; i += kThreads) f(i, static_cast<double>(r[i]) / p.temperature);
+  }
+}
+
+__global__ void scaled_table_kernel(double* table, double temperature) {
+  const int b = blockIdx.x * blockDim.x + threadIdx.x;
+  if (b < kScaledTableSize)
+    table[b] = static_cast<double>(__bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b)))) /
+               temperature;
 }
 
 template <typename T, typename Op>
@@ -108,20 +164,17 @@ __global__ void __launch_bounds__(kThreads) law_stats_kernel(const Params p) {
   if (row < p.target_rows) {
     int bad = 0;
     double m = -INFINITY;
-    for (int i = threadIdx.x; i < p.vocab; i += kThreads) {
-      const double x = load_logit(p, row, i);
-      const double s = x / p.temperature;
-      if (!isfinite(x) || !isfinite(s)) bad = 1;
+    for_scaled(p, row, [&](int, double s) {
+      if (!isfinite(s)) bad = 1;
       m = s > m ? s : m;
-    }
+    });
     bad = block_reduce(bad, iscr, OrOp());
     m = block_reduce(m, dscr, MaxOp());
     double sum = 0.0;
-    for (int i = threadIdx.x; i < p.vocab; i += kThreads) sum += exp(load_logit(p, row, i) / p.temperature - m);
+    for_scaled(p, row, [&](int, double s) { sum += exp(s - m); });
     sum = block_reduce(sum, dscr, SumOp());
     double sum2 = 0.0;
-    for (int i = threadIdx.x; i < p.vocab; i += kThreads)
-      sum2 += exp(load_logit(p, row, i) / p.temperature - m) / sum;
+    for_scaled(p, row, [&](int, double s) { sum2 += exp(s - m) / sum; });
     sum2 = block_reduce(sum2, dscr, SumOp());
     if (threadIdx.x == 0) p.stats[row] = RowStats{m, sum, sum2, bad ? kBadLogits : kOk, 0};
   } else if (row < p.target_rows + p.draft_rows) {
@@ -145,7 +198,7 @@ __global__ void __launch_bounds__(kThreads) law_stats_kernel(const Params p) {
 
 // Target law value at (row, i).
 __device__ __forceinline__ double law_at(const Params& p, const RowStats& st, long long row, int i) {
-  return exp(load_logit(p, row, i) / p.temperature - st.m) / st.s / st.s2;
+  return exp(load_scaled(p, row, i) - st.m) / st.s / st.s2;
 }
 
 __global__ void __launch_bounds__(kThreads) stochastic_accept_kernel(const Params p) {
@@ -246,7 +299,7 @@ __global__ void __launch_bounds__(kThreads) stochastic_accept_kernel(const Param
     double mass = 1.0;
     if (q) {
       double sum = 0.0;
-      for (int i = threadIdx.x; i < p.vocab; i += kThreads) sum += value(i);
+      for_scaled(p, trow, [&](int i, double s) { sum += fmax(exp(s - st.m) / st.s / st.s2 - q[i], 0.0); });
       mass = block_reduce(sum, dscr, SumOp());
     }
     const int chunk = (p.vocab + kThreads - 1) / kThreads;
@@ -267,13 +320,18 @@ __global__ void __launch_bounds__(kThreads) stochastic_accept_kernel(const Param
     int found = p.vocab;
     const double uu = sh_u;
     double cdf = prefix;
-    for (int i = lo; i < hi; ++i) {
-      cdf += q ? value(i) / mass : value(i);
-      if (cdf > uu) {
-        found = i;
-        break;
+    // A chunk whose end (prefix + local) lies more than 1e-12 below u cannot hold
+    // the crossing: the sequential sum below differs from prefix + local by at
+    // most a few hundred ulps of 1 (< 1e-13). Only the one or two chunks at the
+    // crossing scan element by element (the strict CDF rule of the reference).
+    if (prefix + local > uu - 1e-12)
+      for (int i = lo; i < hi; ++i) {
+        cdf += q ? value(i) / mass : value(i);
+        if (cdf > uu) {
+          found = i;
+          break;
+        }
       }
-    }
     found = block_reduce(found, iscr, MinIntOp());
     last_pos = block_reduce(last_pos, iscr, MaxIntOp());
     if (threadIdx.x == 0) {
