@@ -504,7 +504,9 @@ def graph_leg(pkg, device, rank, warmup, steps, cfg=GRAPH):
 def accept_leg(pkg, device, warmup, iters=20, vocab=151936):
     """On-device greedy acceptance for one config-3 verify round: argmax over the
     logits of 128 x 7 verified rows (Qwen3 vocab 151936, bf16: 272 MB, larger than
-    L2) + the accept rule. HBM roofline: the logits are read once."""
+    L2, and L2 written over before each round) + the accept rule, with the EOS ids
+    kept on the device as the round loops keep them. HBM roofline: the logits are
+    read once."""
     import torch
     r, q = VERIFY['requests'], VERIFY['q']
     n = r * q
@@ -514,13 +516,16 @@ def accept_leg(pkg, device, warmup, iters=20, vocab=151936):
     tokens = torch.randint(0, vocab, (n,), device=device, generator=gen)
     cu = torch.arange(0, n + 1, q, dtype=torch.int32, device=device)
     budget = torch.full((r,), 64, dtype=torch.int32, device=device)
+    eos = torch.tensor([151645], dtype=torch.long, device=device)   # on the device once, as the round loops keep it
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     for _ in range(warmup):
-        pkg.greedy_accept(logits, tokens, cu, (151645,), budget)
+        pkg.greedy_accept(logits, tokens, cu, eos, budget)
     pairs = []
     for _ in range(iters):
+        flush.zero_()                       # L2 written over: no logits carried over from the last round
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
-        pkg.greedy_accept(logits, tokens, cu, (151645,), budget)
+        pkg.greedy_accept(logits, tokens, cu, eos, budget)
         b.record()
         pairs.append((a, b))
     torch.cuda.synchronize(device)
