@@ -18,7 +18,7 @@
 
 namespace dspark {
 
-constexpr int kArgmaxThreads = 512;
+constexpr int kArgmaxThreads = 256;
 
 struct ArgBest {
   float v;
@@ -46,7 +46,9 @@ __device__ __forceinline__ void scan_one(ArgBest& best, float x, int idx) {
   if (x > best.v || (x != x && best.v == best.v)) best = ArgBest{x, idx};
 }
 
-// One CTA per row; 4 independent 16-byte loads in flight per thread when the
+// One CTA of 256 threads per row (eight per SM: a config-3 round's 896 rows are
+// all resident at once; 512-thread CTAs left a half-occupied second wave and
+// measured 7% slower); 4 independent 16-byte loads in flight per thread when the
 // row start is 16-byte aligned (the element tail and unaligned rows go scalar).
 template <typename T>
 __global__ void __launch_bounds__(kArgmaxThreads) row_argmax_kernel(const T* __restrict__ logits, long long ld,
