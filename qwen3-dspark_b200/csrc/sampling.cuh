@@ -22,7 +22,7 @@
 namespace dspark {
 namespace sampling {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 1024;   // one CTA per SM at 64 registers: twice the warps of 512 for the per-request kernel
 
 enum Status {
   kOk = 0,
