@@ -251,14 +251,16 @@ struct Walker {
 
 // CTA ranges are equal shares of *work*, not of tiles: an item costs its tiles
 // plus kItemCost tiles' worth of switching (the q prologue, the partial write of
-// a cut item and the pipeline refill; per-CTA traces put an item switch at about
-// four tiles of streaming time). The tiles of all items are numbered in request
+// a cut item and the pipeline refill). Per-CTA traces put an item switch at about
+// four tiles of streaming time, but whole layers of configs 2 and 3 measure
+// shortest with 8-16 (charging the switch more also steers the cuts of long
+// items away from CTAs that already hold several starts); 12 is used. The tiles of all items are numbered in request
 // order and each item is preceded by a kItemCost-unit overhead zone in work
 // units; CTA c owns the tiles of work units [c W / G, (c + 1) W / G), a work
 // position inside an overhead zone meaning the item's first tile. Ranges stay
 // contiguous and ordered in tile space, so a CTA that would otherwise take on
 // two or three item switches gets correspondingly fewer tiles.
-constexpr long long kItemCost = 4;
+constexpr long long kItemCost = 12;
 
 // Ranges a launch of `total` tiles is split into: every CTA of the grid for large
 // launches, and about one range per kMinTilesPerRange tiles for small ones, where
