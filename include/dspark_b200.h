@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 11
+#define DSPARK_ABI_VERSION 12
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -191,6 +191,22 @@ int dspark_row_argmax(const void* logits, long long ld, int rows, int vocab, int
 int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
                          int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
                          int32_t* n_commit, long long* emitted, cudaStream_t stream);
+
+/*
+ * Qwen3RMSNorm.forward of bf16 rows in one launch (the target's input_layernorm,
+ * post_attention_layernorm and final norm; transformers 5.5
+ * models/qwen3/modeling_qwen3.py:62-66, run by the reference's target forward in
+ * dspark_qwen/persistent_qwen_target.py and its draft blocks in
+ * dspark_qwen/model.py:67-86). For each of rows rows of hidden elements
+ * (row strides ld_x / ld_out elements):
+ *   r = rsqrtf(sum(x*x) * fl(1/hidden) + eps),  out = bf16(w * bf16(x * r))
+ * rounded step by step as the torch sequence is; only the order of the float sum
+ * differs. Requires hidden % 8 == 0, strides that are multiples of 8 and 16-byte
+ * aligned x, weight and out; rows == 0 launches nothing (pointers may then be
+ * NULL). All device memory.
+ */
+int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps, int rows, int hidden, void* out,
+                    long long ld_out, cudaStream_t stream);
 
 /*
  * One step of the draft's greedy Markov proposal (DSparkDraft._sample_greedy,

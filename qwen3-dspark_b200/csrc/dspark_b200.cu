@@ -18,6 +18,7 @@
 #include "append.cuh"
 #include "attention.cuh"
 #include "markov.cuh"
+#include "norm.cuh"
 #include "sampling.cuh"
 #include "train.cuh"
 #include "verify.cuh"
@@ -487,6 +488,21 @@ int dspark_row_argmax(const void* logits, long long ld, int rows, int vocab, int
                                                                             ld, vocab, pred);
   else
     row_argmax_kernel<float><<<rows, kArgmaxThreads, 0, stream>>>(static_cast<const float*>(logits), ld, vocab, pred);
+  return launch_status();
+}
+
+int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps, int rows, int hidden, void* out,
+                    long long ld_out, cudaStream_t stream) {
+  if (rows < 0 || rows > (1 << 30) || hidden < 8 || hidden % 8 != 0 || ld_x < hidden || ld_out < hidden ||
+      ld_x % 8 != 0 || ld_out % 8 != 0 || !(eps >= 0.f))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DSPARK_OK;  // empty tensors may carry null pointers
+  if (!x || !weight || !out || !aligned(x, 16) || !aligned(weight, 16) || !aligned(out, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  const float inv_hidden = 1.0f / static_cast<float>(hidden);
+  rms_norm_kernel<<<(rows + kNormRowsPerCta - 1) / kNormRowsPerCta, kNormThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(weight), eps, inv_hidden, rows,
+      hidden, static_cast<__nv_bfloat16*>(out), ld_out);
   return launch_status();
 }
 

@@ -253,6 +253,27 @@ def segment_attention(query, cu_query, query_lengths, key_a, value_a, a_start, a
     return out
 
 
+def rms_norm(x, weight, eps):
+    """``Qwen3RMSNorm.forward`` of bf16 ``x`` [..., hidden] with bf16 ``weight`` [hidden]
+    in one launch (transformers models/qwen3/modeling_qwen3.py:62-66; the reference
+    runs it as eight torch kernels). Same shape and dtype as ``x``; each step rounds as
+    the torch sequence does, only the float sum of squares is associated differently.
+    """
+    hidden = x.shape[-1]
+    if (x.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16 or not x.is_cuda
+            or weight.device != x.device or weight.shape != (hidden,) or hidden % 8 != 0):
+        raise ValueError('bf16 x [..., hidden] and weight [hidden] on one CUDA device, hidden % 8 == 0 required')
+    rows = x.reshape(-1, hidden)
+    if rows.stride(-1) != 1 or rows.stride(0) % 8 != 0 or rows.data_ptr() % 16 != 0:
+        rows = rows.contiguous()
+    w = weight if weight.stride(0) == 1 and weight.data_ptr() % 16 == 0 else weight.contiguous()
+    out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.check(_lib.load_library().dspark_rms_norm(rows.data_ptr(), max(rows.stride(0), hidden), w.data_ptr(),
+                                                   float(eps), rows.shape[0], hidden, out.data_ptr(), hidden,
+                                                   _stream(x.device)), 'dspark_rms_norm')
+    return out
+
+
 def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
     """Greedy acceptance of one verify round on the GPU (cached_decode.py:84-98).
 

@@ -16,6 +16,10 @@ is replaced by one that hands the raw q/k/v projections to the store:
   KV append and bottom-right attention over the resident prefix;
 * float32 model (exact path): transformers' own q_norm/k_norm/RoPE, then
   ``stage_layer`` + ``attend`` on the float32 attention kernel.
+
+In a bf16 model the decoder layers' ``input_layernorm`` / ``post_attention_layernorm``
+and the final ``norm`` also run as one ``rms_norm`` launch each instead of
+transformers' eight-kernel sequence; the float32 model keeps transformers' norms.
 """
 import types
 from dataclasses import dataclass
@@ -23,7 +27,7 @@ from dataclasses import dataclass
 import torch
 from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
 
-from .kernels import HEAD_DIM, HKV, HQ
+from .kernels import HEAD_DIM, HKV, HQ, rms_norm
 from .kv_store import B200PersistentTargetKV
 
 
@@ -37,6 +41,10 @@ class TargetFeatures:
     def context_for(self, request):
         off, q, _ = self.spans[request]
         return self.context[:, off:off + q]
+
+
+def _fused_norm_forward(norm, hidden_states):
+    return rms_norm(hidden_states, norm.weight, norm.variance_epsilon)
 
 
 class B200Qwen3Target:
@@ -71,8 +79,13 @@ class B200Qwen3Target:
         self._orig_forward = {}
         for layer in model.model.layers:
             att = layer.self_attn
-            self._orig_forward[att] = att.forward
+            self._orig_forward[att] = vars(att).get('forward')
             att.forward = types.MethodType(self._attention_forward(), att)
+        if self.dtype == torch.bfloat16:
+            norms = [m for layer in model.model.layers for m in (layer.input_layernorm, layer.post_attention_layernorm)]
+            for norm in norms + [model.model.norm]:
+                self._orig_forward[norm] = vars(norm).get('forward')
+                norm.forward = types.MethodType(_fused_norm_forward, norm)
 
     @property
     def device(self):
@@ -283,10 +296,13 @@ class B200Qwen3Target:
                 for r, (off, q, _) in features.spans.items()}
 
     def close(self):
-        """Restore the model's attention forwards and release captured programs."""
+        """Restore the model's attention and norm forwards and release captured programs."""
         self._graphs.clear()
         for hook in self._hooks:
             hook.remove()
-        for att, fwd in self._orig_forward.items():
-            att.forward = fwd
+        for module, fwd in self._orig_forward.items():   # None: the class's forward was in use
+            if fwd is None:
+                del module.forward
+            else:
+                module.forward = fwd
         self._hooks, self._orig_forward = [], {}

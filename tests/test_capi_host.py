@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 11
+    assert lib.dspark_abi_version() == 12
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -51,6 +51,15 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert lib.dspark_row_argmax(None, 16, 1, 16, 0, None, None) == 1
     assert lib.dspark_row_argmax(ctypes.c_void_p(16), 8, 1, 16, 0, ctypes.c_void_p(16), None) == 1   # ld < vocab
     assert lib.dspark_greedy_accept(None, None, None, 1, 1, None, 0, None, None, None, None, None) == 1
+    # bf16 RMSNorm: null pointers, hidden not a multiple of 8, short or unaligned strides, misaligned rows
+    fake16 = ctypes.c_void_p(256)
+    assert lib.dspark_rms_norm(None, 1024, fake16, 1e-6, 4, 1024, fake16, 1024, None) == 1
+    for ld_x, hidden, ld_out, ptr in ((1020, 1020, 1020, 256), (512, 1024, 1024, 256), (1028, 1024, 1024, 256),
+                                      (1024, 1024, 1024, 258)):
+        p = ctypes.c_void_p(ptr)
+        assert lib.dspark_rms_norm(p, ld_x, fake16, 1e-6, 4, hidden, fake16, ld_out, None) == 1
+    assert lib.dspark_rms_norm(fake16, 1024, fake16, -1.0, 4, 1024, fake16, 1024, None) == 1   # negative eps
+    assert lib.dspark_rms_norm(fake16, 1024, fake16, 1e-6, 0, 1024, fake16, 1024, None) == 0    # no rows: no launch
     assert lib.dspark_markov_step(None, None, 1024, 256, None, 7, 0, None, 1, None, 1024, None, 0.0, None, None, 7, 1,
                                   None, None) == 1
     fake = ctypes.c_void_p(256)
