@@ -25,7 +25,8 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, sample_rows, segment_attention
+from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, rms_norm, sample_rows,
+                      segment_attention)
 from .kv_store import _upload
 
 
@@ -193,6 +194,27 @@ class B200PackedDraft:
         r0, n = self.slot_rows[self._slots[request]], self._lengths[request]
         return tuple((k[r0:r0 + n].clone(), v[r0:r0 + n].clone()) for k, v in zip(self.pool_k, self.pool_v))
 
+    # -- bf16 norms in one launch each ---------------------------------------------
+    @staticmethod
+    def _norm(module, x):
+        """``module(x)`` for a Qwen3RMSNorm; bf16 activations and weights take the fused
+        ``rms_norm`` launch (the same rounding steps) instead of transformers' eight
+        kernels. The draft module itself is left as it is (its training forward keeps
+        autograd through transformers' norm)."""
+        if x.dtype == torch.bfloat16 and module.weight.dtype == torch.bfloat16:
+            return rms_norm(x, module.weight, module.variance_epsilon)
+        return module(x)
+
+    def _project(self, att, x, cos, sin):
+        """``att.project_q`` and ``att.project_kv`` (model.py:41-45) with the q/k norms
+        through ``_norm``: q [n, Hq, D], k and v [n, Hkv, D]."""
+        n = x.shape[1]
+        q = self._norm(att.q_norm, att.q_proj(x).view(1, n, att.heads, att.dim)).transpose(1, 2)
+        k = self._norm(att.k_norm, att.k_proj(x).view(1, n, att.kv_heads, att.dim)).transpose(1, 2)
+        v = att.v_proj(x).view(1, n, att.kv_heads, att.dim).transpose(1, 2)
+        return (rotate_half_rope(q, cos, sin)[0].transpose(0, 1), rotate_half_rope(k, cos, sin)[0].transpose(0, 1),
+                v[0].transpose(0, 1))
+
     # -- context append (packed_draft.py:129-168) ---------------------------------
     def _fused_append_ready(self):
         d = self.draft
@@ -224,7 +246,7 @@ class B200PackedDraft:
         row j of request i sits at position ctx_len[i] + j and is written to its slot
         when j < count[i], else to the trash row. No host reads: capturable."""
         d = self.draft
-        context = d.context_norm(d.fc(feat.to(d.fc.weight.dtype)))
+        context = self._norm(d.context_norm, d.fc(feat.to(d.fc.weight.dtype)))
         if self._fused_append_ready():
             kv_weight, k_norm_w, inv_freq = self._append_operands()
             draft_append(context[0], kv_weight, k_norm_w, inv_freq, meta, r, self.pool_k, self.pool_v,
@@ -373,14 +395,14 @@ class B200PackedDraft:
         qlens = [size] * r
         for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
             att = layer.attention
-            x = layer.input_norm(z)
-            q = att.project_q(x, cos, sin).to(self.kv_dtype).contiguous()
-            kb, vb = att.project_kv(x, cos, sin)
+            x = self._norm(layer.input_norm, z)
+            q, kb, vb = self._project(att, x, cos, sin)
+            q = q.to(self.kv_dtype).contiguous()
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
             z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + layer.mlp(layer.post_norm(z))
-        hidden = d.norm(z)[0]
+            z = z + layer.mlp(self._norm(layer.post_norm, z))
+        hidden = self._norm(d.norm, z)[0]
         work = dict(requests=r, query_rows=r * size, attention_calls=len(d.layers),
                     context_block_concatenation_kv_bytes=0, gathered_kv_bytes=0)
         return DraftFeatures(hidden, requests, size, tuple(self._lengths[q] for q in requests), work)
@@ -399,14 +421,14 @@ class B200PackedDraft:
         qlens = [size] * r
         for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
             att = layer.attention
-            x = layer.input_norm(z)
-            q = att.project_q(x, cos, sin).to(self.kv_dtype).contiguous()
-            kb, vb = att.project_kv(x, cos, sin)
+            x = self._norm(layer.input_norm, z)
+            q, kb, vb = self._project(att, x, cos, sin)
+            q = q.to(self.kv_dtype).contiguous()
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
             z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + layer.mlp(layer.post_norm(z))
-        hidden = d.norm(z)[0].contiguous()
+            z = z + layer.mlp(self._norm(layer.post_norm, z))
+        hidden = self._norm(d.norm, z)[0].contiguous()
         base = d.lm_head(hidden).contiguous()
         return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),
                              self._confidence_bias(), hidden, base, anchor_buf, size)
