@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 12
+#define DSPARK_ABI_VERSION 13
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -207,6 +207,21 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
  */
 int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps, int rows, int hidden, void* out,
                     long long ld_out, cudaStream_t stream);
+
+/*
+ * The draft block's q/k head norms and rotate-half RoPE in one launch (bf16,
+ * head_dim 128; project_q / project_kv of dspark_qwen/model.py:41-45 with rotate,
+ * model.py:22-24). Row i of q (row stride ld_q elements) holds q_heads heads, of k
+ * (ld_k) kv_heads heads; cos_table / sin_table are the rotary module's bf16 rows
+ * (stride ld_cs). Per head: y = Qwen3RMSNorm(x) as in dspark_rms_norm, then
+ * out[d] = bf16(bf16(y[d] cos[d]) + bf16(rot[d] sin[d])) with rot = (-y[64:], y[:64]),
+ * rounded where torch's bf16 ops round. Outputs packed [rows, heads, 128]. Strides
+ * multiples of 4, 8-byte aligned pointers; rows == 0 launches nothing. Device memory.
+ */
+int dspark_qk_norm_rope(const void* q, long long ld_q, const void* k, long long ld_k, const void* q_norm_weight,
+                        const void* k_norm_weight, float q_eps, float k_eps, const void* cos_table,
+                        const void* sin_table, long long ld_cs, int rows, int q_heads, int kv_heads, void* q_out,
+                        void* k_out, cudaStream_t stream);
 
 /*
  * One step of the draft's greedy Markov proposal (DSparkDraft._sample_greedy,

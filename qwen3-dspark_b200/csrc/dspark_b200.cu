@@ -506,6 +506,29 @@ int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps
   return launch_status();
 }
 
+int dspark_qk_norm_rope(const void* q, long long ld_q, const void* k, long long ld_k, const void* q_norm_weight,
+                        const void* k_norm_weight, float q_eps, float k_eps, const void* cos_table,
+                        const void* sin_table, long long ld_cs, int rows, int q_heads, int kv_heads, void* q_out,
+                        void* k_out, cudaStream_t stream) {
+  if (rows < 0 || rows > (1 << 24) || q_heads < 1 || kv_heads < 1 || q_heads > 256 || kv_heads > 256 ||
+      ld_q < static_cast<long long>(q_heads) * kRopeDim || ld_k < static_cast<long long>(kv_heads) * kRopeDim ||
+      ld_cs < kRopeDim || ld_q % 4 != 0 || ld_k % 4 != 0 || ld_cs % 4 != 0 || !(q_eps >= 0.f) || !(k_eps >= 0.f))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DSPARK_OK;  // empty tensors may carry null pointers
+  if (!q || !k || !q_norm_weight || !k_norm_weight || !cos_table || !sin_table || !q_out || !k_out ||
+      !aligned(q, 8) || !aligned(k, 8) || !aligned(q_norm_weight, 8) || !aligned(k_norm_weight, 8) ||
+      !aligned(cos_table, 8) || !aligned(sin_table, 8) || !aligned(q_out, 8) || !aligned(k_out, 8))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  const long long items = static_cast<long long>(rows) * (q_heads + kv_heads);
+  qk_norm_rope_kernel<<<static_cast<unsigned>((items + kNormRowsPerCta - 1) / kNormRowsPerCta), kNormThreads, 0,
+                        stream>>>(
+      static_cast<const __nv_bfloat16*>(q), ld_q, static_cast<const __nv_bfloat16*>(k), ld_k,
+      static_cast<const __nv_bfloat16*>(q_norm_weight), static_cast<const __nv_bfloat16*>(k_norm_weight), q_eps,
+      k_eps, static_cast<const __nv_bfloat16*>(cos_table), static_cast<const __nv_bfloat16*>(sin_table), ld_cs, rows,
+      q_heads, kv_heads, static_cast<__nv_bfloat16*>(q_out), static_cast<__nv_bfloat16*>(k_out));
+  return launch_status();
+}
+
 int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
                          int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
                          int32_t* n_commit, long long* emitted, cudaStream_t stream) {

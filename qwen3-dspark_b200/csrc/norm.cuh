@@ -67,4 +67,82 @@ __global__ void __launch_bounds__(kNormThreads)
   }
 }
 
+// Per-head RMSNorm and rotate-half RoPE of the draft block's projected q and k
+// rows (head_dim 128): the draft's project_q / project_kv (dspark_qwen/model.py:
+// 41-45, rotate at model.py:22-24) as one launch instead of eight norm kernels,
+// neg, cat, two products, a sum and a copy per tensor. For head vector x with
+// norm weight w and the rotary module's bf16 cos/sin of its row:
+//   y = bf16(w * bf16(x * rsqrtf(sum(x*x) * (1/128) + eps)))     (Qwen3RMSNorm)
+//   rot[d] = -y[d + 64] (d < 64), y[d - 64] (d >= 64)
+//   out[d] = bf16(bf16(y[d] * cos[d]) + bf16(rot[d] * sin[d]))
+// rounded where torch's bf16 ops round. One warp per (row, head); lane l holds
+// dims 4l..4l+3 and its rotation partner is lane l ^ 16. Outputs are packed
+// [rows, heads, 128].
+constexpr int kRopeDim = 128;
+
+__global__ void __launch_bounds__(kNormThreads)
+    qk_norm_rope_kernel(const __nv_bfloat16* __restrict__ q, long long ld_q, const __nv_bfloat16* __restrict__ k,
+                        long long ld_k, const __nv_bfloat16* __restrict__ q_w, const __nv_bfloat16* __restrict__ k_w,
+                        float q_eps, float k_eps, const __nv_bfloat16* __restrict__ cos_t,
+                        const __nv_bfloat16* __restrict__ sin_t, long long ld_cs, int rows, int q_heads, int kv_heads,
+                        __nv_bfloat16* __restrict__ q_out, __nv_bfloat16* __restrict__ k_out) {
+  const int lane = threadIdx.x & 31;
+  const int heads = q_heads + kv_heads;
+  const long long item = static_cast<long long>(blockIdx.x) * kNormRowsPerCta + (threadIdx.x >> 5);
+  if (item >= static_cast<long long>(rows) * heads) return;
+  const long long row = item / heads;
+  const int h = static_cast<int>(item - row * heads);
+  const bool is_q = h < q_heads;
+  const int hh = is_q ? h : h - q_heads;
+  const __nv_bfloat16* src = is_q ? q + row * ld_q + hh * kRopeDim : k + row * ld_k + hh * kRopeDim;
+  const __nv_bfloat16* w = is_q ? q_w : k_w;
+  __nv_bfloat16* dst = is_q ? q_out + (row * q_heads + hh) * kRopeDim : k_out + (row * kv_heads + hh) * kRopeDim;
+  const float eps = is_q ? q_eps : k_eps;
+
+  const uint2 u = *reinterpret_cast<const uint2*>(src + 4 * lane);
+  const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 x0 = __bfloat1622float2(p[0]), x1 = __bfloat1622float2(p[1]);
+  float acc = 0.f;
+  acc = fmaf(x0.x, x0.x, acc);
+  acc = fmaf(x0.y, x0.y, acc);
+  acc = fmaf(x1.x, x1.x, acc);
+  acc = fmaf(x1.y, x1.y, acc);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  const float r = rsqrtf(__fadd_rn(__fmul_rn(acc, 1.0f / kRopeDim), eps));
+  const uint2 wu = *reinterpret_cast<const uint2*>(w + 4 * lane);
+  const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wu);
+  const float xs[4] = {x0.x, x0.y, x1.x, x1.y};
+  const float2 w0 = __bfloat1622float2(wp[0]), w1 = __bfloat1622float2(wp[1]);
+  const float ws[4] = {w0.x, w0.y, w1.x, w1.y};
+  float y[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float n = __bfloat162float(__float2bfloat16_rn(__fmul_rn(xs[j], r)));
+    y[j] = __bfloat162float(__float2bfloat16_rn(__fmul_rn(ws[j], n)));
+  }
+  const bool low = lane < 16;
+  const uint2 cu = *reinterpret_cast<const uint2*>(cos_t + row * ld_cs + 4 * lane);
+  const uint2 su = *reinterpret_cast<const uint2*>(sin_t + row * ld_cs + 4 * lane);
+  const __nv_bfloat162* cp = reinterpret_cast<const __nv_bfloat162*>(&cu);
+  const __nv_bfloat162* sp = reinterpret_cast<const __nv_bfloat162*>(&su);
+  const float2 c0 = __bfloat1622float2(cp[0]), c1 = __bfloat1622float2(cp[1]);
+  const float2 s0 = __bfloat1622float2(sp[0]), s1 = __bfloat1622float2(sp[1]);
+  const float cs[4] = {c0.x, c0.y, c1.x, c1.y}, sn[4] = {s0.x, s0.y, s1.x, s1.y};
+  float o[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float partner = __shfl_xor_sync(0xffffffffu, y[j], 16);
+    const float rot = low ? -partner : partner;
+    const float a = __bfloat162float(__float2bfloat16_rn(__fmul_rn(y[j], cs[j])));
+    const float b = __bfloat162float(__float2bfloat16_rn(__fmul_rn(rot, sn[j])));
+    o[j] = __fadd_rn(a, b);
+  }
+  uint2 out;
+  __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(&out);
+  op[0] = __floats2bfloat162_rn(o[0], o[1]);
+  op[1] = __floats2bfloat162_rn(o[2], o[3]);
+  *reinterpret_cast<uint2*>(dst + 4 * lane) = out;
+}
+
 }  // namespace dspark

@@ -25,8 +25,8 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, rms_norm, sample_rows,
-                      segment_attention)
+from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, qk_norm_rope, rms_norm,
+                      sample_rows, segment_attention)
 from .kv_store import _upload
 
 
@@ -206,9 +206,16 @@ class B200PackedDraft:
         return module(x)
 
     def _project(self, att, x, cos, sin):
-        """``att.project_q`` and ``att.project_kv`` (model.py:41-45) with the q/k norms
-        through ``_norm``: q [n, Hq, D], k and v [n, Hkv, D]."""
+        """``att.project_q`` and ``att.project_kv`` (model.py:41-45): q [n, Hq, D], k and v
+        [n, Hkv, D]. bf16 drafts run the q/k norms and RoPE as one ``qk_norm_rope``
+        launch; other dtypes take transformers' norms and the torch rotation."""
         n = x.shape[1]
+        if (x.dtype == cos.dtype == torch.bfloat16 and att.dim == HEAD_DIM
+                and att.q_norm.weight.dtype == att.k_norm.weight.dtype == torch.bfloat16):
+            q, k = qk_norm_rope(att.q_proj(x)[0], att.k_proj(x)[0], att.q_norm.weight, att.k_norm.weight,
+                                att.q_norm.variance_epsilon, att.k_norm.variance_epsilon, cos[0], sin[0],
+                                att.heads, att.kv_heads)
+            return q, k, att.v_proj(x)[0].view(n, att.kv_heads, att.dim)
         q = self._norm(att.q_norm, att.q_proj(x).view(1, n, att.heads, att.dim)).transpose(1, 2)
         k = self._norm(att.k_norm, att.k_proj(x).view(1, n, att.kv_heads, att.dim)).transpose(1, 2)
         v = att.v_proj(x).view(1, n, att.kv_heads, att.dim).transpose(1, 2)

@@ -274,6 +274,33 @@ def rms_norm(x, weight, eps):
     return out
 
 
+def qk_norm_rope(q, k, q_norm_weight, k_norm_weight, q_eps, k_eps, cos, sin, q_heads, kv_heads):
+    """The draft block's q/k head RMSNorm + rotate-half RoPE (model.py:41-45, 22-24) in
+    one launch: ``q`` [n, q_heads * 128] and ``k`` [n, kv_heads * 128] bf16 rows (unit
+    column stride), ``cos`` / ``sin`` [n, 128] the rotary module's bf16 tables. Returns
+    packed (q [n, q_heads, 128], k [n, kv_heads, 128]), rounded as torch's bf16 ops."""
+    n = q.shape[0]
+    ok = (q.ndim == k.ndim == cos.ndim == sin.ndim == 2 and k.shape[0] == cos.shape[0] == sin.shape[0] == n
+          and q.shape[1] == q_heads * HEAD_DIM and k.shape[1] == kv_heads * HEAD_DIM
+          and cos.shape[1] == sin.shape[1] == HEAD_DIM and cos.stride() == sin.stride()
+          and all(t.dtype == torch.bfloat16 and t.is_cuda and t.device == q.device
+                  for t in (q, k, cos, sin, q_norm_weight, k_norm_weight))
+          and q_norm_weight.shape == k_norm_weight.shape == (HEAD_DIM,))
+    if not ok:
+        raise ValueError('bf16 q [n, Hq*128], k [n, Hkv*128], cos/sin [n, 128] and 128-wide norm weights on one '
+                         'CUDA device required')
+    q, k, cos, sin = (t if t.stride(-1) == 1 else t.contiguous() for t in (q, k, cos, sin))
+    qw, kw = q_norm_weight.contiguous(), k_norm_weight.contiguous()
+    q_out = torch.empty((n, q_heads, HEAD_DIM), dtype=torch.bfloat16, device=q.device)
+    k_out = torch.empty((n, kv_heads, HEAD_DIM), dtype=torch.bfloat16, device=q.device)
+    ld = lambda t: max(t.stride(0), t.shape[1])  # noqa: E731  (a single row may carry any stride)
+    _lib.check(_lib.load_library().dspark_qk_norm_rope(
+        q.data_ptr(), ld(q), k.data_ptr(), ld(k), qw.data_ptr(), kw.data_ptr(), float(q_eps), float(k_eps),
+        cos.data_ptr(), sin.data_ptr(), ld(cos), n, q_heads, kv_heads, q_out.data_ptr(), k_out.data_ptr(),
+        _stream(q.device)), 'dspark_qk_norm_rope')
+    return q_out, k_out
+
+
 def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
     """Greedy acceptance of one verify round on the GPU (cached_decode.py:84-98).
 

@@ -100,3 +100,84 @@ def test_bf16_target_runs_its_norms_fused_and_restores_them(pkg):
     target.close()
     assert not any('forward' in vars(m) for m in norms)
     status_clean(pkg)
+
+
+def integer_rows(seed, rows, width, bound):
+    """bf16 rows of small integers: every partial sum of squares is an exact float, so
+    the sum no longer depends on its association and results must be bit-identical."""
+    g = np.random.Generator(np.random.PCG64(seed))
+    return torch.from_numpy(g.integers(-bound, bound + 1, (rows, width)).astype(np.float32)).to(dev(),
+                                                                                              torch.bfloat16)
+
+
+def test_rms_norm_bit_exact_when_the_sum_is_exact(pkg):
+    x = integer_rows(3, 300, 1024, 8)
+    _, w = inputs(4, 1, 1024)
+    with torch.no_grad():
+        ref = hf_norm(w, 1e-6)(x)
+    assert torch.equal(pkg.rms_norm(x, w, 1e-6), ref)
+    status_clean(pkg)
+
+
+def rope_reference(x, heads, weight, eps, cos, sin):
+    """The draft's torch path: Qwen3RMSNorm over each head, then rotate-half RoPE."""
+    from importlib import import_module
+    rotate = import_module('qwen3-dspark_b200.draft').rotate_half_rope
+    n = x.shape[0]
+    with torch.no_grad():
+        y = hf_norm(weight, eps)(x.view(1, n, heads, 128)).transpose(1, 2)
+        return rotate(y, cos, sin)[0].transpose(0, 1).contiguous()
+
+
+def rope_tables(n, seed):
+    import inputs as I
+    from transformers import Qwen3Config
+    from transformers.models.qwen3.modeling_qwen3 import Qwen3RotaryEmbedding
+    rot = Qwen3RotaryEmbedding(Qwen3Config(**I.TINY_TARGET)).to(dev())
+    g = np.random.Generator(np.random.PCG64(seed))
+    pos = torch.from_numpy(g.integers(0, 40000, n)).to(dev())
+    return rot(torch.zeros(1, dtype=torch.bfloat16, device=dev()), pos[None])
+
+
+@pytest.mark.parametrize('exact', [False, True])
+def test_qk_norm_rope_matches_the_draft_torch_path(pkg, exact):
+    n, hq, hkv = 224, 16, 8
+    if exact:
+        q, k = integer_rows(5, n, hq * 128, 6), integer_rows(6, n, hkv * 128, 6)
+    else:
+        q, _ = inputs(5, n, hq * 128, 2.0)
+        k, _ = inputs(6, n, hkv * 128, 0.3)
+    _, qw = inputs(7, 1, 128)
+    _, kw = inputs(8, 1, 128)
+    cos, sin = rope_tables(n, 9)
+    assert cos.dtype == torch.bfloat16 and cos.shape == (1, n, 128)
+    got_q, got_k = pkg.qk_norm_rope(q, k, qw, kw, 1e-6, 1e-6, cos[0], sin[0], hq, hkv)
+    ref_q = rope_reference(q, hq, qw, 1e-6, cos, sin)
+    ref_k = rope_reference(k, hkv, kw, 1e-6, cos, sin)
+    for got, ref in ((got_q, ref_q), (got_k, ref_k)):
+        assert got.shape == ref.shape
+        if exact:
+            assert torch.equal(got, ref)
+        else:
+            diff = (got.float() - ref.float()).abs()
+            assert float(diff.max()) <= 2e-2
+            assert float((diff == 0).float().mean()) >= 0.999
+    status_clean(pkg)
+
+
+def test_qk_norm_rope_row_strides_and_refusals(pkg):
+    n = 9
+    q, _ = inputs(10, n, 2 * 128 + 64)                   # rows of a wider buffer: stride 320
+    k, _ = inputs(11, n, 128)
+    _, w = inputs(12, 1, 128)
+    cos, sin = rope_tables(n, 13)
+    got_q, got_k = pkg.qk_norm_rope(q[:, :256], k, w, w, 1e-6, 1e-6, cos[0], sin[0], 2, 1)
+    want_q, want_k = pkg.qk_norm_rope(q[:, :256].contiguous(), k, w, w, 1e-6, 1e-6, cos[0], sin[0], 2, 1)
+    assert torch.equal(got_q, want_q) and torch.equal(got_k, want_k)
+    empty_q, empty_k = pkg.qk_norm_rope(q[:0, :256], k[:0], w, w, 1e-6, 1e-6, cos[0, :0], sin[0, :0], 2, 1)
+    assert empty_q.shape == (0, 2, 128) and empty_k.shape == (0, 1, 128)
+    with pytest.raises(ValueError):
+        pkg.qk_norm_rope(q[:, :256].float(), k, w, w, 1e-6, 1e-6, cos[0], sin[0], 2, 1)
+    with pytest.raises(ValueError):
+        pkg.qk_norm_rope(q[:, :256], k, w, w, 1e-6, 1e-6, cos[0], sin[0], 3, 1)
+    status_clean(pkg)
