@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 13
+#define DSPARK_ABI_VERSION 14
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -222,6 +222,18 @@ int dspark_qk_norm_rope(const void* q, long long ld_q, const void* k, long long 
                         const void* k_norm_weight, float q_eps, float k_eps, const void* cos_table,
                         const void* sin_table, long long ld_cs, int rows, int q_heads, int kv_heads, void* q_out,
                         void* k_out, cudaStream_t stream);
+
+/*
+ * Gated activation of a Qwen3MLP from one merged [gate; up] projection (bf16):
+ * row i of gate_up (stride ld elements) holds inter gate then inter up values;
+ * out[i, c] = bf16(bf16(silu(g)) * u) with silu(g) = g / (1 + expf(-g)) in float,
+ * as torch's silu and bf16 product round. Replaces act_fn(gate_proj(x)) *
+ * up_proj(x) of transformers' Qwen3MLP.forward (two GEMMs and two elementwise
+ * kernels) after a single GEMM. inter % 8 == 0, strides multiples of 8, 16-byte
+ * aligned pointers; rows == 0 launches nothing. Device memory.
+ */
+int dspark_silu_mul(const void* gate_up, long long ld, int rows, int inter, void* out, long long ld_out,
+                    cudaStream_t stream);
 
 /*
  * One step of the draft's greedy Markov proposal (DSparkDraft._sample_greedy,

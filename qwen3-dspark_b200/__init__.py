@@ -15,7 +15,7 @@ is missing or the device is not an sm_100 GPU.
 from . import _lib
 from .build import LIB_PATH, build
 from .kernels import (BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, TRAIN_BACKEND, B200CapacityKernel,
-                      B200DraftKernel, B200TrainingLayoutKernel, B200VarlenKernel, draft_append, float64_law, greedy_accept, markov_greedy, qk_norm_rope, rms_norm,
+                      B200DraftKernel, B200TrainingLayoutKernel, B200VarlenKernel, draft_append, float64_law, greedy_accept, markov_greedy, qk_norm_rope, rms_norm, silu_mul,
                       sample_rows, stochastic_accept,
                       runtime_identity, segment_attention)
 from .kv_store import B200PersistentTargetKV, Slot, Transaction, rope_inv_freq
@@ -44,5 +44,5 @@ __all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'TRAIN_BACKE
            'B200DraftKernel', 'B200TrainingLayoutKernel', 'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH',
            'PackedLayout', 'PersistentAttentionLayout', 'TrainingLayout', 'Slot', 'Transaction', 'B200PackedDraft',
            'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target', 'speculative_greedy', 'speculative_greedy_pipelined', 'speculative_sample', 'accept_greedy', 'build',
-           'draft_append', 'float64_law', 'greedy_accept', 'markov_greedy', 'qk_norm_rope', 'rms_norm', 'sample_rows', 'stochastic_accept', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
+           'draft_append', 'float64_law', 'greedy_accept', 'markov_greedy', 'qk_norm_rope', 'rms_norm', 'silu_mul', 'sample_rows', 'stochastic_accept', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
            'segment_attention']

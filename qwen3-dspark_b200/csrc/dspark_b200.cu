@@ -529,6 +529,19 @@ int dspark_qk_norm_rope(const void* q, long long ld_q, const void* k, long long 
   return launch_status();
 }
 
+int dspark_silu_mul(const void* gate_up, long long ld, int rows, int inter, void* out, long long ld_out,
+                    cudaStream_t stream) {
+  if (rows < 0 || rows > (1 << 24) || inter < 8 || inter % 8 != 0 || inter > (1 << 24) ||
+      ld < 2ll * inter || ld % 8 != 0 || ld_out < inter || ld_out % 8 != 0)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DSPARK_OK;  // empty tensors may carry null pointers
+  if (!gate_up || !out || !aligned(gate_up, 16) || !aligned(out, 16)) return DSPARK_ERR_INVALID_ARGUMENT;
+  const long long threads = static_cast<long long>(rows) * (inter / 8);
+  silu_mul_kernel<<<static_cast<unsigned>((threads + kSiluThreads - 1) / kSiluThreads), kSiluThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(gate_up), ld, rows, inter, static_cast<__nv_bfloat16*>(out), ld_out);
+  return launch_status();
+}
+
 int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int32_t* cu_q, int num_requests,
                          int total_rows, const long long* eos, int n_eos, const int32_t* budget, int32_t* accepted,
                          int32_t* n_commit, long long* emitted, cudaStream_t stream) {

@@ -145,4 +145,38 @@ __global__ void __launch_bounds__(kNormThreads)
   *reinterpret_cast<uint2*>(dst + 4 * lane) = out;
 }
 
+// Gated activation of a Qwen3MLP (transformers models/qwen3/modeling_qwen3.py,
+// Qwen3MLP.forward: down_proj(act_fn(gate_proj(x)) * up_proj(x))) from ONE
+// merged [gate; up] projection: row i of gate_up (stride ld elements) holds the
+// inter gate values, then the inter up values. For g, u of one column:
+//   out = bf16(float(bf16(g / (1 + expf(-g)))) * float(u))
+// which is torch's silu kernel on a bf16 tensor (float math, rounded to bf16)
+// followed by the bf16 product. 8 columns per thread, 16-byte loads and stores.
+constexpr int kSiluThreads = 256;
+
+__global__ void __launch_bounds__(kSiluThreads)
+    silu_mul_kernel(const __nv_bfloat16* __restrict__ gate_up, long long ld, int rows, int inter,
+                    __nv_bfloat16* __restrict__ out, long long ld_out) {
+  const int vecs = inter >> 3;
+  const long long idx = static_cast<long long>(blockIdx.x) * kSiluThreads + threadIdx.x;
+  if (idx >= static_cast<long long>(rows) * vecs) return;
+  const long long row = idx / vecs;
+  const int c = static_cast<int>(idx - row * vecs) * 8;
+  const uint4 gv = *reinterpret_cast<const uint4*>(gate_up + row * ld + c);
+  const uint4 uv = *reinterpret_cast<const uint4*>(gate_up + row * ld + inter + c);
+  const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&gv);
+  const __nv_bfloat162* u2 = reinterpret_cast<const __nv_bfloat162*>(&uv);
+  uint4 ov;
+  __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const float2 g = __bfloat1622float2(g2[j]);
+    const float2 u = __bfloat1622float2(u2[j]);
+    const float ax = __bfloat162float(__float2bfloat16_rn(g.x / (1.0f + expf(-g.x))));
+    const float ay = __bfloat162float(__float2bfloat16_rn(g.y / (1.0f + expf(-g.y))));
+    o2[j] = __floats2bfloat162_rn(__fmul_rn(ax, u.x), __fmul_rn(ay, u.y));
+  }
+  *reinterpret_cast<uint4*>(out + row * ld_out + c) = ov;
+}
+
 }  // namespace dspark

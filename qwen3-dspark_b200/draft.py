@@ -25,8 +25,8 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, qk_norm_rope, rms_norm,
-                      sample_rows, segment_attention)
+from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
+                      rms_norm, sample_rows, segment_attention, silu_mul)
 from .kv_store import _upload
 
 
@@ -204,6 +204,23 @@ class B200PackedDraft:
         if x.dtype == torch.bfloat16 and module.weight.dtype == torch.bfloat16:
             return rms_norm(x, module.weight, module.variance_epsilon)
         return module(x)
+
+    def _mlp(self, mlp, x):
+        """``mlp(x)``; a bf16 Qwen3MLP runs gate and up as one GEMM over a merged copy of
+        the two weights and ``silu_mul``. The copy is rebuilt when either weight
+        changes; replaced copies stay allocated, since a captured proposal keeps
+        reading the copy it was captured with."""
+        if x.dtype != torch.bfloat16 or not merged_mlp_ready(mlp):
+            return mlp(x)
+        cache = self.__dict__.setdefault('_merged_mlp', {})
+        key = tuple((t.data_ptr(), t._version) for t in (mlp.gate_proj.weight, mlp.up_proj.weight))
+        hit = cache.get(id(mlp))
+        if hit is None or hit[0] != key:
+            if hit is not None:
+                self.__dict__.setdefault('_retired_mlp', []).append(hit[1])
+            hit = (key, torch.cat((mlp.gate_proj.weight, mlp.up_proj.weight)).detach().contiguous())
+            cache[id(mlp)] = hit
+        return mlp.down_proj(silu_mul(torch.nn.functional.linear(x, hit[1]), mlp.gate_proj.out_features))
 
     def _project(self, att, x, cos, sin):
         """``att.project_q`` and ``att.project_kv`` (model.py:41-45): q [n, Hq, D], k and v
@@ -408,7 +425,7 @@ class B200PackedDraft:
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
             z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + layer.mlp(self._norm(layer.post_norm, z))
+            z = z + self._mlp(layer.mlp, self._norm(layer.post_norm, z))
         hidden = self._norm(d.norm, z)[0]
         work = dict(requests=r, query_rows=r * size, attention_calls=len(d.layers),
                     context_block_concatenation_kv_bytes=0, gathered_kv_bytes=0)
@@ -434,7 +451,7 @@ class B200PackedDraft:
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
             z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + layer.mlp(self._norm(layer.post_norm, z))
+            z = z + self._mlp(layer.mlp, self._norm(layer.post_norm, z))
         hidden = self._norm(d.norm, z)[0].contiguous()
         base = d.lm_head(hidden).contiguous()
         return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),

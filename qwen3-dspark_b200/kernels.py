@@ -301,6 +301,31 @@ def qk_norm_rope(q, k, q_norm_weight, k_norm_weight, q_eps, k_eps, cos, sin, q_h
     return q_out, k_out
 
 
+def silu_mul(gate_up, inter):
+    """``act_fn(gate) * up`` of a Qwen3MLP from one merged projection ``gate_up``
+    [..., 2 * inter] bf16 (gate columns first); returns [..., inter] bf16, rounded as
+    torch's silu kernel and bf16 product round."""
+    if (gate_up.dtype != torch.bfloat16 or not gate_up.is_cuda or gate_up.shape[-1] != 2 * inter
+            or inter % 8 != 0 or inter < 8):
+        raise ValueError('bf16 gate_up [..., 2 * inter] on a CUDA device with inter % 8 == 0 required')
+    rows = gate_up.reshape(-1, 2 * inter)
+    if rows.stride(-1) != 1 or rows.stride(0) % 8 != 0 or rows.data_ptr() % 16 != 0:
+        rows = rows.contiguous()
+    out = torch.empty(gate_up.shape[:-1] + (inter,), dtype=torch.bfloat16, device=gate_up.device)
+    _lib.check(_lib.load_library().dspark_silu_mul(rows.data_ptr(), max(rows.stride(0), 2 * inter), rows.shape[0],
+                                                   inter, out.data_ptr(), inter, _stream(gate_up.device)),
+               'dspark_silu_mul')
+    return out
+
+
+def merged_mlp_ready(mlp):
+    """A bf16 Qwen3MLP whose gate/up projections can run as one GEMM + ``silu_mul``."""
+    g, u = mlp.gate_proj, mlp.up_proj
+    return (g.bias is None and u.bias is None and g.weight.dtype == u.weight.dtype == torch.bfloat16
+            and g.weight.shape == u.weight.shape and g.out_features % 8 == 0
+            and (type(mlp.act_fn).__name__ == 'SiLUActivation' or type(mlp.act_fn) is torch.nn.SiLU))
+
+
 def greedy_accept(logits, tokens, cu_query, eos_ids=(), budget=None):
     """Greedy acceptance of one verify round on the GPU (cached_decode.py:84-98).
 

@@ -19,7 +19,10 @@ is replaced by one that hands the raw q/k/v projections to the store:
 
 In a bf16 model the decoder layers' ``input_layernorm`` / ``post_attention_layernorm``
 and the final ``norm`` also run as one ``rms_norm`` launch each instead of
-transformers' eight-kernel sequence; the float32 model keeps transformers' norms.
+transformers' eight-kernel sequence, and each MLP projects gate and up with ONE GEMM
+(``gate_proj.weight`` and ``up_proj.weight`` become views of one [gate; up] buffer,
+values unchanged) followed by ``silu_mul``. The float32 model keeps transformers'
+modules.
 """
 import types
 from dataclasses import dataclass
@@ -27,7 +30,7 @@ from dataclasses import dataclass
 import torch
 from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
 
-from .kernels import HEAD_DIM, HKV, HQ, rms_norm
+from .kernels import HEAD_DIM, HKV, HQ, merged_mlp_ready, rms_norm, silu_mul
 from .kv_store import B200PersistentTargetKV
 
 
@@ -45,6 +48,19 @@ class TargetFeatures:
 
 def _fused_norm_forward(norm, hidden_states):
     return rms_norm(hidden_states, norm.weight, norm.variance_epsilon)
+
+
+def _merged_mlp_forward(mlp):
+    """Rebind gate_proj / up_proj weights as views of one merged buffer and return a
+    forward that runs one GEMM, ``silu_mul`` and down_proj."""
+    merged = torch.cat((mlp.gate_proj.weight.detach(), mlp.up_proj.weight.detach()))
+    inter = mlp.gate_proj.out_features
+    mlp.gate_proj.weight.data = merged[:inter]
+    mlp.up_proj.weight.data = merged[inter:]
+
+    def forward(m, x):
+        return m.down_proj(silu_mul(torch.nn.functional.linear(x, merged), inter))
+    return forward
 
 
 class B200Qwen3Target:
@@ -86,6 +102,10 @@ class B200Qwen3Target:
             for norm in norms + [model.model.norm]:
                 self._orig_forward[norm] = vars(norm).get('forward')
                 norm.forward = types.MethodType(_fused_norm_forward, norm)
+            for layer in model.model.layers:
+                if merged_mlp_ready(layer.mlp):
+                    self._orig_forward[layer.mlp] = vars(layer.mlp).get('forward')
+                    layer.mlp.forward = types.MethodType(_merged_mlp_forward(layer.mlp), layer.mlp)
 
     @property
     def device(self):
@@ -296,7 +316,8 @@ class B200Qwen3Target:
                 for r, (off, q, _) in features.spans.items()}
 
     def close(self):
-        """Restore the model's attention and norm forwards and release captured programs."""
+        """Restore the model's attention, norm and MLP forwards and release captured
+        programs (merged gate/up weights stay views of their shared buffer)."""
         self._graphs.clear()
         for hook in self._hooks:
             hook.remove()

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 13
+    assert lib.dspark_abi_version() == 14
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -67,6 +67,12 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert lib.dspark_qk_norm_rope(ctypes.c_void_p(258), 2048, f, 1024, f, f, 1e-6, 1e-6, f, f, 128, 4, 16, 8, f,
                                    f, None) == 1
     assert lib.dspark_qk_norm_rope(None, 2048, f, 1024, f, f, 1e-6, 1e-6, f, f, 128, 4, 16, 8, f, f, None) == 1
+    # merged gate/up activation: stride shorter than both halves, inter not a multiple of 8, null, misaligned
+    assert lib.dspark_silu_mul(f, 3000, 4, 1536, f, 1536, None) == 1
+    assert lib.dspark_silu_mul(f, 3072, 4, 1532, f, 1532, None) == 1
+    assert lib.dspark_silu_mul(None, 3072, 4, 1536, f, 1536, None) == 1
+    assert lib.dspark_silu_mul(f, 3072, 4, 1536, ctypes.c_void_p(264), 1536, None) == 1
+    assert lib.dspark_silu_mul(None, 3072, 0, 1536, None, 1536, None) == 0
     assert lib.dspark_qk_norm_rope(None, 2048, None, 1024, None, None, 1e-6, 1e-6, None, None, 128, 0, 16, 8, None,
                                    None, None) == 0
     assert lib.dspark_markov_step(None, None, 1024, 256, None, 7, 0, None, 1, None, 1024, None, 0.0, None, None, 7, 1,

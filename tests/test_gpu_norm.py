@@ -181,3 +181,49 @@ def test_qk_norm_rope_row_strides_and_refusals(pkg):
     with pytest.raises(ValueError):
         pkg.qk_norm_rope(q[:, :256], k, w, w, 1e-6, 1e-6, cos[0], sin[0], 3, 1)
     status_clean(pkg)
+
+
+def test_silu_mul_matches_torch_silu_times_up(pkg):
+    g = np.random.Generator(np.random.PCG64(21))
+    gu = torch.from_numpy(g.standard_normal((257, 2 * 3072)).astype(np.float32) * 3).to(dev(), torch.bfloat16)
+    gu[0, :16] = torch.tensor([0, -0.0, 1e-30, -1e-30, 88, -88, 100, -100, 1e4, -1e4, 3e38, -3e38,
+                               float('inf'), float('-inf'), 0.5, -0.5])
+    got = pkg.silu_mul(gu, 3072)
+    with torch.no_grad():
+        ref = torch.nn.functional.silu(gu[:, :3072]) * gu[:, 3072:]
+    same = (got.view(torch.int16) == ref.view(torch.int16)) | (torch.isnan(got) & torch.isnan(ref))
+    finite = torch.isfinite(ref) & torch.isfinite(got)
+    assert float(same.float().mean()) >= 0.999
+    assert int(ulp_distance(torch.where(finite, got, 0), torch.where(finite, ref, 0)).max()) <= 1
+    assert torch.equal(torch.isnan(got), torch.isnan(ref))
+    # rows of a wider buffer and the empty case
+    wide = torch.zeros((257, 2 * 3072 + 64), dtype=torch.bfloat16, device=dev())
+    wide[:, :2 * 3072] = gu
+    assert torch.equal(pkg.silu_mul(wide[:, :2 * 3072], 3072).view(torch.int16), got.view(torch.int16))
+    assert pkg.silu_mul(gu[:0], 3072).shape == (0, 3072)
+    with pytest.raises(ValueError):
+        pkg.silu_mul(gu, 3000)
+    status_clean(pkg)
+
+
+def test_bf16_target_mlp_runs_merged_and_matches_transformers(pkg):
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    import inputs as I
+    cfg = Qwen3Config(**I.TINY_TARGET)
+    model = Qwen3ForCausalLM(cfg).eval().to(dev(), torch.bfloat16)
+    mlp = model.model.layers[1].mlp
+    x, _ = inputs(31, 40, cfg.hidden_size)
+    with torch.no_grad():
+        ref = mlp(x[None])
+        gate_before = mlp.gate_proj.weight.clone()
+    target = pkg.B200Qwen3Target(model, (), slots=1, context_capacity=64, max_query_tokens=64)
+    assert 'forward' in vars(mlp)
+    assert torch.equal(mlp.gate_proj.weight, gate_before)              # views of the merged buffer, same values
+    assert mlp.up_proj.weight.data_ptr() == mlp.gate_proj.weight.data_ptr() + mlp.gate_proj.weight.numel() * 2
+    with torch.no_grad():
+        got = mlp(x[None])
+    err = (got.float() - ref.float()).abs().max().item()
+    assert err <= 0.02 * ref.float().abs().max().item() + 1e-3, err
+    target.close()
+    assert 'forward' not in vars(mlp)
+    status_clean(pkg)
