@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 14
+#define DSPARK_ABI_VERSION 15
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -152,6 +152,23 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
                         void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
                         void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, int path,
                         void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/*
+ * dspark_verify_fused with row strides (elements) for the q/k/v projections, e.g.
+ * column blocks of one merged [n, (16 + 8 + 8) * 128] q|k|v GEMM output, so a host
+ * runs one projection GEMM per layer instead of three. Strides must be multiples
+ * of 8 and at least the packed row (16 * 128, 8 * 128, 8 * 128). Packed strides
+ * behave exactly as dspark_verify_fused; other strides take the prep path (its
+ * kernel reads the strided rows and writes packed q and scratch K/V), and
+ * path == DSPARK_VERIFY_FUSED with them is refused.
+ */
+int dspark_verify_strided(const void* q_raw, long long ld_q, const void* k_raw, long long ld_k, const void* v_raw,
+                          long long ld_v, const void* q_norm_weight, const void* k_norm_weight,
+                          const void* rope_table, float eps, const int32_t* cu_q, const int32_t* slot_row,
+                          const int32_t* ctx_len, int num_requests, int total_q, int max_q, void* resident_k,
+                          void* resident_v, long long rows_per_layer, void* scratch_k, void* scratch_v,
+                          int scratch_rows, int num_layers, int layer, float scale, int path, void* out,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
  * Commit / rollback for all layers in one launch: for every request copy

@@ -381,14 +381,24 @@ int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t*
   return launch_status();
 }
 
-int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
-                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
-                        const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
-                        void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
-                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, int path,
-                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+namespace {
+
+// Body of dspark_verify_fused / dspark_verify_strided. Row strides other than the
+// packed ones are read by the prep kernel only: the fused kernel's new-row
+// sources are packed, so strided projections always take the prep path.
+int verify_impl(const void* q_raw, long long ld_q, const void* k_raw, long long ld_k, const void* v_raw,
+                long long ld_v, const void* q_norm_weight, const void* k_norm_weight, const void* rope_table,
+                float eps, const int32_t* cu_q, const int32_t* slot_row, const int32_t* ctx_len, int num_requests,
+                int total_q, int max_q, void* resident_k, void* resident_v, long long rows_per_layer,
+                void* scratch_k, void* scratch_v, int scratch_rows, int num_layers, int layer, float scale,
+                int path, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
   if (path != DSPARK_VERIFY_AUTO && path != DSPARK_VERIFY_FUSED && path != DSPARK_VERIFY_PREP)
     return DSPARK_ERR_INVALID_ARGUMENT;
+  const long long q_row = static_cast<long long>(kQHeads) * kHeadDim, kv_row = static_cast<long long>(kKVHeads) * kHeadDim;
+  if (ld_q < q_row || ld_k < kv_row || ld_v < kv_row || ld_q % 8 != 0 || ld_k % 8 != 0 || ld_v % 8 != 0)
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  const bool packed = ld_q == q_row && ld_k == kv_row && ld_v == kv_row;
+  if (!packed && path == DSPARK_VERIFY_FUSED) return DSPARK_ERR_INVALID_ARGUMENT;
   if (!common_ok(q_raw, out, cu_q, num_requests, total_q, scale, DSPARK_DTYPE_BF16) || !k_raw || !v_raw ||
       !q_norm_weight || !k_norm_weight || !rope_table || !aligned(rope_table, 16) || !slot_row || !ctx_len ||
       !resident_k || !resident_v ||
@@ -424,7 +434,7 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
   p.scratch_rows = scratch_rows;
   const uint8_t* rk = static_cast<const uint8_t*>(resident_k) + res_row0 * row_bytes;
   const uint8_t* rv = static_cast<const uint8_t*>(resident_v) + res_row0 * row_bytes;
-  const bool prep = path == DSPARK_VERIFY_PREP ||
+  const bool prep = path == DSPARK_VERIFY_PREP || !packed ||
                     (path == DSPARK_VERIFY_AUTO && (total_q < kVerifyPrepMaxRows || max_q > kVerifyFusedMaxQ));
   if (prep) {
     // q_norm/k_norm + RoPE + KV append once per new row, then the plain causal
@@ -436,7 +446,7 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
                         static_cast<const __nv_bfloat16*>(v_raw), static_cast<const __nv_bfloat16*>(q_norm_weight),
                         static_cast<const __nv_bfloat16*>(k_norm_weight), static_cast<const uint32_t*>(rope_table),
                         static_cast<__nv_bfloat16*>(out), reinterpret_cast<__nv_bfloat16*>(sk),
-                        reinterpret_cast<__nv_bfloat16*>(sv), total_q, eps};
+                        reinterpret_cast<__nv_bfloat16*>(sv), total_q, eps, ld_q, ld_k, ld_v};
     const long long warps = static_cast<long long>(total_q) * 32;
     verify_prep_kernel<<<static_cast<unsigned>((warps + 7) / 8), 256, 0, stream>>>(vp);
     int st = launch_status();
@@ -449,6 +459,33 @@ int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw,
   // in shared memory and writes the scratch rows itself.
   KeySources src{rk, rv, rows_per_layer, k_raw, v_raw, total_q};
   return run_attention(p, src, DSPARK_DTYPE_BF16, max_q, workspace, workspace_bytes, stream, true);
+}
+
+}  // namespace
+
+int dspark_verify_fused(const void* q_raw, const void* k_raw, const void* v_raw, const void* q_norm_weight,
+                        const void* k_norm_weight, const void* rope_table, float eps, const int32_t* cu_q,
+                        const int32_t* slot_row, const int32_t* ctx_len, int num_requests, int total_q, int max_q,
+                        void* resident_k, void* resident_v, long long rows_per_layer, void* scratch_k,
+                        void* scratch_v, int scratch_rows, int num_layers, int layer, float scale, int path,
+                        void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return verify_impl(q_raw, kQHeads * kHeadDim, k_raw, kKVHeads * kHeadDim, v_raw, kKVHeads * kHeadDim,
+                     q_norm_weight, k_norm_weight, rope_table, eps, cu_q, slot_row, ctx_len, num_requests, total_q,
+                     max_q, resident_k, resident_v, rows_per_layer, scratch_k, scratch_v, scratch_rows, num_layers,
+                     layer, scale, path, out, workspace, workspace_bytes, stream);
+}
+
+int dspark_verify_strided(const void* q_raw, long long ld_q, const void* k_raw, long long ld_k, const void* v_raw,
+                          long long ld_v, const void* q_norm_weight, const void* k_norm_weight,
+                          const void* rope_table, float eps, const int32_t* cu_q, const int32_t* slot_row,
+                          const int32_t* ctx_len, int num_requests, int total_q, int max_q, void* resident_k,
+                          void* resident_v, long long rows_per_layer, void* scratch_k, void* scratch_v,
+                          int scratch_rows, int num_layers, int layer, float scale, int path, void* out,
+                          void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return verify_impl(q_raw, ld_q, k_raw, ld_k, v_raw, ld_v, q_norm_weight, k_norm_weight, rope_table, eps, cu_q,
+                     slot_row, ctx_len, num_requests, total_q, max_q, resident_k, resident_v, rows_per_layer,
+                     scratch_k, scratch_v, scratch_rows, num_layers, layer, scale, path, out, workspace,
+                     workspace_bytes, stream);
 }
 
 int dspark_commit_kv(void* resident_k, void* resident_v, const void* scratch_k, const void* scratch_v,

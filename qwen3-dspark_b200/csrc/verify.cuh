@@ -54,6 +54,7 @@ struct VerifyPrepParams {
   __nv_bfloat16* scratch_v;
   int total_q;
   float eps;
+  long long ld_q, ld_k, ld_v;   // row strides of q_raw / k_raw / v_raw in elements
 };
 
 __global__ void __launch_bounds__(256) verify_prep_kernel(const VerifyPrepParams p) {
@@ -66,15 +67,16 @@ __global__ void __launch_bounds__(256) verify_prep_kernel(const VerifyPrepParams
   __nv_bfloat16* dst;
   const __nv_bfloat16* w = nullptr;
   if (vec < kQHeads) {
-    src = p.q_raw + (static_cast<size_t>(row) * kQHeads + vec) * kHeadDim;
+    src = p.q_raw + static_cast<size_t>(row) * p.ld_q + static_cast<size_t>(vec) * kHeadDim;
     dst = p.q_out + (static_cast<size_t>(row) * kQHeads + vec) * kHeadDim;
     w = p.q_w;
   } else if (vec < kQHeads + kKVHeads) {
-    src = p.k_raw + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads) * kHeadDim;
+    src = p.k_raw + static_cast<size_t>(row) * p.ld_k + static_cast<size_t>(vec - kQHeads) * kHeadDim;
     dst = p.scratch_k + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads) * kHeadDim;
     w = p.k_w;
   } else {
-    src = p.v_raw + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads - kKVHeads) * kHeadDim;
+    src = p.v_raw + static_cast<size_t>(row) * p.ld_v +
+          static_cast<size_t>(vec - kQHeads - kKVHeads) * kHeadDim;
     dst = p.scratch_v + (static_cast<size_t>(row) * kKVHeads + vec - kQHeads - kKVHeads) * kHeadDim;
   }
   const uint2 raw = *reinterpret_cast<const uint2*>(src + d0);

@@ -306,6 +306,9 @@ class B200PersistentTargetKV:
         ``path``: 'fused' (norm/RoPE/append inside the attention kernel), 'prep' (a
         prep kernel per layer, then the attention kernel) or 'auto' (prep below 512
         new rows or for chunks longer than 16 rows); all give the same values.
+        q/k/v may be row-strided views (heads and head dims packed, row stride a
+        multiple of 8), e.g. column blocks of one merged q|k|v projection; strided
+        rows take the prep path.
         """
         self._transaction(tx)
         if type(layer) is not int or not 0 <= layer < self.layers or layer in self._staged:
@@ -318,13 +321,21 @@ class B200PersistentTargetKV:
         for x, shape in ((q_raw, (n, HQ, HEAD_DIM)), (k_raw, (n, HKV, HEAD_DIM)), (v_raw, (n, HKV, HEAD_DIM)),
                          (q_norm_weight, (HEAD_DIM,)), (k_norm_weight, (HEAD_DIM,))):
             if (not isinstance(x, torch.Tensor) or tuple(x.shape) != shape or x.dtype != self.dtype
-                    or x.device != self.device or not x.is_contiguous()):
-                raise ValueError('Verify inputs must be contiguous bf16 q/k/v projections and norm weights')
+                    or x.device != self.device):
+                raise ValueError('Verify inputs must be bf16 q/k/v projections and norm weights')
+            if len(shape) == 1:
+                ok = x.is_contiguous()
+            else:                                   # rows may be strided, each row's heads packed
+                ok = (x.stride(2) == 1 and x.stride(1) == HEAD_DIM
+                      and (n == 1 or (x.stride(0) >= shape[1] * HEAD_DIM and x.stride(0) % 8 == 0)))
+            if not ok:
+                raise ValueError('Verify q/k/v rows must hold packed heads (row stride a multiple of 8)')
+        lds = [x.stride(0) if n > 1 else x.shape[1] * HEAD_DIM for x in (q_raw, k_raw, v_raw)]
         if (not isinstance(inv_freq, torch.Tensor) or inv_freq.shape != (HEAD_DIM // 2,)
                 or inv_freq.dtype != torch.float32 or inv_freq.device != self.device):
             raise ValueError('inv_freq must be float32 [64] on the store device')
         if out is None:
-            out = torch.empty_like(q_raw)
+            out = torch.empty((n, HQ, HEAD_DIM), dtype=self.dtype, device=self.device)
         cu_q, slot_row, ctx, _cap = self._meta(tx)
         stream = torch.cuda.current_stream(self.device).cuda_stream
         lib = _lib.load_library()
@@ -340,14 +351,14 @@ class B200PersistentTargetKV:
             tx.rope.clear()
             tx.rope[key] = table
         ws = _lib.workspace(self.device, stream)
-        _lib.check(lib.dspark_verify_fused(
-            q_raw.data_ptr(), k_raw.data_ptr(), v_raw.data_ptr(), q_norm_weight.data_ptr(),
+        _lib.check(lib.dspark_verify_strided(
+            q_raw.data_ptr(), lds[0], k_raw.data_ptr(), lds[1], v_raw.data_ptr(), lds[2], q_norm_weight.data_ptr(),
             k_norm_weight.data_ptr(), table.data_ptr(), float(eps), cu_q.data_ptr(), slot_row.data_ptr(),
             ctx.data_ptr(), len(tx.query_lengths), n, max(tx.query_lengths), self._keys.data_ptr(),
             self._values.data_ptr(),
             self.rows_per_layer, self.scratch_keys.data_ptr(), self.scratch_values.data_ptr(),
             self.max_query_tokens, self.layers, layer, float(scale), _lib.VERIFY_PATHS[path], out.data_ptr(),
-            ws.data_ptr(), ws.numel(), stream), 'dspark_verify_fused')
+            ws.data_ptr(), ws.numel(), stream), 'dspark_verify_strided')
         self._staged.add(layer)
         return out
 

@@ -19,9 +19,10 @@ is replaced by one that hands the raw q/k/v projections to the store:
 
 In a bf16 model the decoder layers' ``input_layernorm`` / ``post_attention_layernorm``
 and the final ``norm`` also run as one ``rms_norm`` launch each instead of
-transformers' eight-kernel sequence, and each MLP projects gate and up with ONE GEMM
-(``gate_proj.weight`` and ``up_proj.weight`` become views of one [gate; up] buffer,
-values unchanged) followed by ``silu_mul``. The float32 model keeps transformers'
+transformers' eight-kernel sequence, each attention projects q, k and v with ONE GEMM
+whose column blocks go to ``verify_layer`` as row-strided views, and each MLP projects
+gate and up with ONE GEMM followed by ``silu_mul`` (the projection weights become views
+of one merged buffer per layer and kind, values and memory unchanged). The float32 model keeps transformers'
 modules.
 """
 import types
@@ -50,13 +51,22 @@ def _fused_norm_forward(norm, hidden_states):
     return rms_norm(hidden_states, norm.weight, norm.variance_epsilon)
 
 
+def _merge_linears(linears):
+    """One [out_1 + out_2 + ...; in] buffer holding the linears' weights; each weight
+    becomes a view of its block (values unchanged)."""
+    merged = torch.cat([lin.weight.detach() for lin in linears])
+    off = 0
+    for lin in linears:
+        lin.weight.data = merged[off:off + lin.out_features]
+        off += lin.out_features
+    return merged
+
+
 def _merged_mlp_forward(mlp):
     """Rebind gate_proj / up_proj weights as views of one merged buffer and return a
     forward that runs one GEMM, ``silu_mul`` and down_proj."""
-    merged = torch.cat((mlp.gate_proj.weight.detach(), mlp.up_proj.weight.detach()))
+    merged = _merge_linears((mlp.gate_proj, mlp.up_proj))
     inter = mlp.gate_proj.out_features
-    mlp.gate_proj.weight.data = merged[:inter]
-    mlp.up_proj.weight.data = merged[inter:]
 
     def forward(m, x):
         return m.down_proj(silu_mul(torch.nn.functional.linear(x, merged), inter))
@@ -93,6 +103,7 @@ class B200Qwen3Target:
         self._hooks = [model.model.layers[i].register_forward_hook(self._hook(i)) for i in self.layer_ids]
         self._graphs = {}
         self._orig_forward = {}
+        self._qkv = {}
         for layer in model.model.layers:
             att = layer.self_attn
             self._orig_forward[att] = vars(att).get('forward')
@@ -103,6 +114,9 @@ class B200Qwen3Target:
                 self._orig_forward[norm] = vars(norm).get('forward')
                 norm.forward = types.MethodType(_fused_norm_forward, norm)
             for layer in model.model.layers:
+                att = layer.self_attn
+                if all(lin.bias is None for lin in (att.q_proj, att.k_proj, att.v_proj)):
+                    self._qkv[att] = _merge_linears((att.q_proj, att.k_proj, att.v_proj))
                 if merged_mlp_ready(layer.mlp):
                     self._orig_forward[layer.mlp] = vars(layer.mlp).get('forward')
                     layer.mlp.forward = types.MethodType(_merged_mlp_forward(layer.mlp), layer.mlp)
@@ -131,11 +145,18 @@ class B200Qwen3Target:
             if tx is None or hidden_states.shape[0] != 1:
                 raise RuntimeError('B200 attention runs inside a verify transaction on one packed row')
             n = hidden_states.shape[1]
-            q = att.q_proj(hidden_states).view(n, HQ, HEAD_DIM)
-            k = att.k_proj(hidden_states).view(n, HKV, HEAD_DIM)
-            v = att.v_proj(hidden_states).view(n, HKV, HEAD_DIM)
+            merged = target._qkv.get(att)
+            if merged is not None:                  # one GEMM; q/k/v are row-strided column blocks
+                qkv = torch.nn.functional.linear(hidden_states, merged)[0]
+                q = qkv[:, :HQ * HEAD_DIM].view(n, HQ, HEAD_DIM)
+                k = qkv[:, HQ * HEAD_DIM:(HQ + HKV) * HEAD_DIM].view(n, HKV, HEAD_DIM)
+                v = qkv[:, (HQ + HKV) * HEAD_DIM:].view(n, HKV, HEAD_DIM)
+            else:
+                q = att.q_proj(hidden_states).view(n, HQ, HEAD_DIM)
+                k = att.k_proj(hidden_states).view(n, HKV, HEAD_DIM)
+                v = att.v_proj(hidden_states).view(n, HKV, HEAD_DIM)
             if target.dtype == torch.bfloat16:
-                out = target.pool.verify_layer(tx, att.layer_idx, q.contiguous(), k.contiguous(), v.contiguous(),
+                out = target.pool.verify_layer(tx, att.layer_idx, q, k, v,
                                                att.q_norm.weight, att.k_norm.weight, inv_freq=target.inv_freq,
                                                eps=target.eps)
             else:

@@ -161,3 +161,41 @@ def test_store_refusals(pkg):
     assert store.length(a) == 0
     with pytest.raises(ValueError):
         store.abort(tx)
+
+
+def test_strided_projection_rows_equal_packed_rows(pkg):
+    """q/k/v as column blocks of one merged [n, 4096] projection (row stride 4096, the
+    target's single q|k|v GEMM) give the packed inputs' output and scratch K/V bit for
+    bit on the prep path; 'auto' takes the prep path for them and 'fused' refuses them."""
+    g = I.rng(21)
+    contexts, qlens = [5, 600, 0], [8, 8, 8]
+    caps = [c + 16 for c in contexts]
+    nq = sum(qlens)
+    inv = pkg.rope_inv_freq(I.ROPE_THETA, device=dev())
+    qkv = bits_to_dev(f32_to_bf16_bits(I.normal(g, (nq, 32 * 128)) * 2))
+    qw = bits_to_dev(f32_to_bf16_bits(1 + 0.1 * I.normal(g, (128,))))
+    kw = bits_to_dev(f32_to_bf16_bits(1 + 0.1 * I.normal(g, (128,))))
+    q = qkv[:, :2048].view(nq, 16, 128)
+    k = qkv[:, 2048:3072].view(nq, 8, 128)
+    v = qkv[:, 3072:].view(nq, 8, 128)
+    results = []
+    for strided in (False, True):
+        store, _ = make_store(pkg, 1, caps, nq, g)
+        handles = [store.add_request(f'r{i}') for i in range(3)]
+        for h, c in zip(handles, contexts):
+            if c:
+                kv = bits_to_dev(f32_to_bf16_bits(I.normal(I.rng(30 + c), (2, 1, c, 8, 128))))
+                store.load_prefix(h, kv[0], kv[1])
+        tx = store.begin(handles, query_lengths=qlens)
+        args = (q, k, v) if strided else (q.contiguous(), k.contiguous(), v.contiguous())
+        if strided:
+            with pytest.raises(ValueError):
+                store.verify_layer(tx, 0, *args, qw, kw, inv_freq=inv, eps=I.RMS_EPS, path='fused')
+        out = store.verify_layer(tx, 0, *args, qw, kw, inv_freq=inv, eps=I.RMS_EPS,
+                                 path='auto' if strided else 'prep')
+        torch.cuda.synchronize()
+        results.append((out.clone(), store.scratch_keys[:nq].clone(), store.scratch_values[:nq].clone()))
+        store.abort(tx)
+    for a, b in zip(*results):
+        assert torch.equal(a.view(torch.int16), b.view(torch.int16))
+    status_clean(pkg)
