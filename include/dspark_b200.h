@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 15
+#define DSPARK_ABI_VERSION 16
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -224,6 +224,16 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
  */
 int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps, int rows, int hidden, void* out,
                     long long ld_out, cudaStream_t stream);
+
+/*
+ * Residual add + Qwen3RMSNorm in one launch (bf16): sum_out = bf16(x + delta),
+ * torch's bf16 add of a decoder layer's residual and sublayer output, and out =
+ * dspark_rms_norm(sum_out). Same rules as dspark_rms_norm for every pointer and
+ * stride; x and delta must not overlap out or sum_out.
+ */
+int dspark_add_rms_norm(const void* x, long long ld_x, const void* delta, long long ld_d, const void* weight,
+                        float eps, int rows, int hidden, void* out, long long ld_out, void* sum_out,
+                        long long ld_sum, cudaStream_t stream);
 
 /*
  * The draft block's q/k head norms and rotate-half RoPE in one launch (bf16,

@@ -14,7 +14,7 @@ is missing or the device is not an sm_100 GPU.
 """
 from . import _lib
 from .build import LIB_PATH, build
-from .kernels import (BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, TRAIN_BACKEND, B200CapacityKernel,
+from .kernels import (add_rms_norm, BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, TRAIN_BACKEND, B200CapacityKernel,
                       B200DraftKernel, B200TrainingLayoutKernel, B200VarlenKernel, draft_append, float64_law, greedy_accept, markov_greedy, qk_norm_rope, rms_norm, silu_mul,
                       sample_rows, stochastic_accept,
                       runtime_identity, segment_attention)
@@ -40,7 +40,7 @@ load_library = _lib.load_library
 read_device_status = _lib.read_device_status
 launch_count = _lib.launch_count
 
-__all__ = ['BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'TRAIN_BACKEND', 'B200CapacityKernel',
+__all__ = ['add_rms_norm', 'BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCALE', 'TRAIN_BACKEND', 'B200CapacityKernel',
            'B200DraftKernel', 'B200TrainingLayoutKernel', 'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH',
            'PackedLayout', 'PersistentAttentionLayout', 'TrainingLayout', 'Slot', 'Transaction', 'B200PackedDraft',
            'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target', 'speculative_greedy', 'speculative_greedy_pipelined', 'speculative_sample', 'accept_greedy', 'build',

@@ -43,6 +43,7 @@ SIGNATURES = {
     'dspark_rms_norm': (_i, [_vp, _ll, _vp, _f, _i, _i, _vp, _ll, _vp]),
     'dspark_qk_norm_rope': (_i, [_vp, _ll, _vp, _ll, _vp, _vp, _f, _f, _vp, _vp, _ll, _i, _i, _i, _vp, _vp, _vp]),
     'dspark_silu_mul': (_i, [_vp, _ll, _i, _i, _vp, _ll, _vp]),
+    'dspark_add_rms_norm': (_i, [_vp, _ll, _vp, _ll, _vp, _f, _i, _i, _vp, _ll, _vp, _ll, _vp]),
     'dspark_greedy_accept': (_i, [_vp, _vp, _vp, _i, _i, _vp, _i, _vp, _vp, _vp, _vp, _vp]),
     'dspark_train_attn': (_i, [_vp, _vp, _vp, _i, _ll, _vp, _i, _f, _vp, _vp]),
     'dspark_stochastic_scratch_bytes': (_sz, [_i]),
@@ -70,7 +71,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 15:
+        if lib.dspark_abi_version() != 16:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

@@ -537,9 +537,28 @@ int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps
   if (!x || !weight || !out || !aligned(x, 16) || !aligned(weight, 16) || !aligned(out, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
   const float inv_hidden = 1.0f / static_cast<float>(hidden);
-  rms_norm_kernel<<<(rows + kNormRowsPerCta - 1) / kNormRowsPerCta, kNormThreads, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(weight), eps, inv_hidden, rows,
-      hidden, static_cast<__nv_bfloat16*>(out), ld_out);
+  rms_norm_kernel<false><<<(rows + kNormRowsPerCta - 1) / kNormRowsPerCta, kNormThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ld_x, nullptr, 0, static_cast<const __nv_bfloat16*>(weight), eps,
+      inv_hidden, rows, hidden, static_cast<__nv_bfloat16*>(out), ld_out, nullptr, 0);
+  return launch_status();
+}
+
+int dspark_add_rms_norm(const void* x, long long ld_x, const void* delta, long long ld_d, const void* weight,
+                        float eps, int rows, int hidden, void* out, long long ld_out, void* sum_out,
+                        long long ld_sum, cudaStream_t stream) {
+  if (rows < 0 || rows > (1 << 30) || hidden < 8 || hidden % 8 != 0 || ld_x < hidden || ld_d < hidden ||
+      ld_out < hidden || ld_sum < hidden || ld_x % 8 != 0 || ld_d % 8 != 0 || ld_out % 8 != 0 || ld_sum % 8 != 0 ||
+      !(eps >= 0.f))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DSPARK_OK;  // empty tensors may carry null pointers
+  if (!x || !delta || !weight || !out || !sum_out || !aligned(x, 16) || !aligned(delta, 16) ||
+      !aligned(weight, 16) || !aligned(out, 16) || !aligned(sum_out, 16))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  const float inv_hidden = 1.0f / static_cast<float>(hidden);
+  rms_norm_kernel<true><<<(rows + kNormRowsPerCta - 1) / kNormRowsPerCta, kNormThreads, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(delta), ld_d,
+      static_cast<const __nv_bfloat16*>(weight), eps, inv_hidden, rows, hidden, static_cast<__nv_bfloat16*>(out),
+      ld_out, static_cast<__nv_bfloat16*>(sum_out), ld_sum);
   return launch_status();
 }
 

@@ -25,18 +25,41 @@ namespace dspark {
 constexpr int kNormThreads = 256;
 constexpr int kNormRowsPerCta = kNormThreads / 32;
 
+// Residual form (kAdd): the rows normalised are s = bf16(x + delta), torch's bf16
+// add of a decoder layer's residual and sublayer output; s is also written to
+// sum_out (the new residual). Inputs must not overlap the outputs: the second
+// pass recomputes s from x and delta.
+template <bool kAdd>
 __global__ void __launch_bounds__(kNormThreads)
-    rms_norm_kernel(const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ weight,
-                    float eps, float inv_hidden, int rows, int hidden, __nv_bfloat16* __restrict__ out,
-                    long long ld_out) {
+    rms_norm_kernel(const __nv_bfloat16* __restrict__ x, long long ld_x, const __nv_bfloat16* __restrict__ delta,
+                    long long ld_d, const __nv_bfloat16* __restrict__ weight, float eps, float inv_hidden, int rows,
+                    int hidden, __nv_bfloat16* __restrict__ out, long long ld_out, __nv_bfloat16* __restrict__ sum_out,
+                    long long ld_sum) {
   const int lane = threadIdx.x & 31;
   const long long row = static_cast<long long>(blockIdx.x) * kNormRowsPerCta + (threadIdx.x >> 5);
   if (row >= rows) return;
   const uint4* xr = reinterpret_cast<const uint4*>(x + row * ld_x);
+  const uint4* dr = reinterpret_cast<const uint4*>(delta + (kAdd ? row * ld_d : 0));
+  // the row's value vector v: x, or bf16(x + delta) in the residual form
+  auto load = [&](int v) {
+    uint4 u = __ldg(xr + v);
+    if constexpr (kAdd) {
+      const uint4 d = __ldg(dr + v);
+      __nv_bfloat162* up = reinterpret_cast<__nv_bfloat162*>(&u);
+      const __nv_bfloat162* dp = reinterpret_cast<const __nv_bfloat162*>(&d);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 a = __bfloat1622float2(up[j]), b = __bfloat1622float2(dp[j]);
+        up[j] = __floats2bfloat162_rn(__fadd_rn(a.x, b.x), __fadd_rn(a.y, b.y));
+      }
+    }
+    return u;
+  };
   const int nvec = hidden >> 3;
   float acc = 0.f;
   for (int v = lane; v < nvec; v += 32) {
-    const uint4 u = __ldg(xr + v);
+    const uint4 u = load(v);
+    if constexpr (kAdd) reinterpret_cast<uint4*>(sum_out + row * ld_sum)[v] = u;
     const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -51,7 +74,7 @@ __global__ void __launch_bounds__(kNormThreads)
   const uint4* wr = reinterpret_cast<const uint4*>(weight);
   uint4* orow = reinterpret_cast<uint4*>(out + row * ld_out);
   for (int v = lane; v < nvec; v += 32) {
-    const uint4 u = __ldg(xr + v), wu = __ldg(wr + v);
+    const uint4 u = load(v), wu = __ldg(wr + v);
     const __nv_bfloat162* p = reinterpret_cast<const __nv_bfloat162*>(&u);
     const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wu);
     uint4 o;

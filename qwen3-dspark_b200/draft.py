@@ -25,7 +25,7 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import (HEAD_DIM, HKV, HQ, draft_append, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
+from .kernels import (HEAD_DIM, HKV, HQ, add_rms_norm, draft_append, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
                       rms_norm, sample_rows, segment_attention, silu_mul)
 from .kv_store import _upload
 
@@ -222,6 +222,14 @@ class B200PackedDraft:
             cache[id(mlp)] = hit
         return mlp.down_proj(silu_mul(torch.nn.functional.linear(x, hit[1]), mlp.gate_proj.out_features))
 
+    @staticmethod
+    def _add_norm(module, z, delta):
+        """``(z + delta, module(z + delta))``; bf16 as one ``add_rms_norm`` launch."""
+        if z.dtype == delta.dtype == module.weight.dtype == torch.bfloat16:
+            return add_rms_norm(z, delta, module.weight, module.variance_epsilon)
+        z = z + delta
+        return z, module(z)
+
     def _project(self, att, x, cos, sin):
         """``att.project_q`` and ``att.project_kv`` (model.py:41-45): q [n, Hq, D], k and v
         [n, Hkv, D]. bf16 drafts run the q/k norms and RoPE as one ``qk_norm_rope``
@@ -417,16 +425,20 @@ class B200PackedDraft:
         pos = torch.tensor(positions, dtype=torch.long, device=self.device)
         cos, sin = d.rotary(z, pos[None])
         qlens = [size] * r
+        pending = None                      # the last MLP output, added in the next norm's launch
         for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
             att = layer.attention
-            x = self._norm(layer.input_norm, z)
+            if pending is None:
+                x = self._norm(layer.input_norm, z)
+            else:
+                z, x = self._add_norm(layer.input_norm, z, pending)
             q, kb, vb = self._project(att, x, cos, sin)
             q = q.to(self.kv_dtype).contiguous()
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
-            z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + self._mlp(layer.mlp, self._norm(layer.post_norm, z))
-        hidden = self._norm(d.norm, z)[0]
+            z, x = self._add_norm(layer.post_norm, z, att.o_proj(out.to(z.dtype).reshape(1, r * size, -1)))
+            pending = self._mlp(layer.mlp, x)
+        hidden = (self._norm(d.norm, z) if pending is None else self._add_norm(d.norm, z, pending)[1])[0]
         work = dict(requests=r, query_rows=r * size, attention_calls=len(d.layers),
                     context_block_concatenation_kv_bytes=0, gathered_kv_bytes=0)
         return DraftFeatures(hidden, requests, size, tuple(self._lengths[q] for q in requests), work)
@@ -443,16 +455,21 @@ class B200PackedDraft:
         z = d.embedding(block.reshape(1, r * size)).to(d.fc.weight.dtype)
         cos, sin = d.rotary(z, pos_buf[None])
         qlens = [size] * r
+        pending = None                      # the last MLP output, added in the next norm's launch
         for layer, pk, pv in zip(d.layers, self.pool_k, self.pool_v):
             att = layer.attention
-            x = self._norm(layer.input_norm, z)
+            if pending is None:
+                x = self._norm(layer.input_norm, z)
+            else:
+                z, x = self._add_norm(layer.input_norm, z, pending)
             q, kb, vb = self._project(att, x, cos, sin)
             q = q.to(self.kv_dtype).contiguous()
             out = segment_attention(q, cu_q, qlens, pk, pv, a_start, a_len, kb.to(self.kv_dtype).contiguous(),
                                     vb.to(self.kv_dtype).contiguous(), b_start, b_len, causal=False)
-            z = z + att.o_proj(out.to(z.dtype).reshape(1, r * size, -1))
-            z = z + self._mlp(layer.mlp, self._norm(layer.post_norm, z))
-        hidden = self._norm(d.norm, z)[0].contiguous()
+            z, x = self._add_norm(layer.post_norm, z, att.o_proj(out.to(z.dtype).reshape(1, r * size, -1)))
+            pending = self._mlp(layer.mlp, x)
+        hidden = (self._norm(d.norm, z) if pending is None
+                  else self._add_norm(d.norm, z, pending)[1])[0].contiguous()
         base = d.lm_head(hidden).contiguous()
         return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),
                              self._confidence_bias(), hidden, base, anchor_buf, size)

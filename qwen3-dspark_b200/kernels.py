@@ -274,6 +274,29 @@ def rms_norm(x, weight, eps):
     return out
 
 
+def add_rms_norm(x, delta, weight, eps):
+    """Residual add + ``Qwen3RMSNorm`` in one launch: returns ``(s, rms_norm(s))`` with
+    ``s = x + delta`` rounded to bf16 as torch's add rounds (same shapes as ``x``)."""
+    hidden = x.shape[-1]
+    if (x.dtype != torch.bfloat16 or delta.dtype != torch.bfloat16 or weight.dtype != torch.bfloat16
+            or delta.shape != x.shape or not x.is_cuda or delta.device != x.device or weight.device != x.device
+            or weight.shape != (hidden,) or hidden % 8 != 0):
+        raise ValueError('bf16 x and delta [..., hidden] and weight [hidden] on one CUDA device, hidden % 8 == 0 '
+                         'required')
+    rows = [t.reshape(-1, hidden) for t in (x, delta)]
+    rows = [r if r.stride(-1) == 1 and r.stride(0) % 8 == 0 and r.data_ptr() % 16 == 0 else r.contiguous()
+            for r in rows]
+    w = weight if weight.stride(0) == 1 and weight.data_ptr() % 16 == 0 else weight.contiguous()
+    out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    total = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    n = rows[0].shape[0]
+    _lib.check(_lib.load_library().dspark_add_rms_norm(
+        rows[0].data_ptr(), max(rows[0].stride(0), hidden), rows[1].data_ptr(), max(rows[1].stride(0), hidden),
+        w.data_ptr(), float(eps), n, hidden, out.data_ptr(), hidden, total.data_ptr(), hidden,
+        _stream(x.device)), 'dspark_add_rms_norm')
+    return total, out
+
+
 def qk_norm_rope(q, k, q_norm_weight, k_norm_weight, q_eps, k_eps, cos, sin, q_heads, kv_heads):
     """The draft block's q/k head RMSNorm + rotate-half RoPE (model.py:41-45, 22-24) in
     one launch: ``q`` [n, q_heads * 128] and ``k`` [n, kv_heads * 128] bf16 rows (unit

@@ -19,7 +19,8 @@ is replaced by one that hands the raw q/k/v projections to the store:
 
 In a bf16 model the decoder layers' ``input_layernorm`` / ``post_attention_layernorm``
 and the final ``norm`` also run as one ``rms_norm`` launch each instead of
-transformers' eight-kernel sequence, each attention projects q, k and v with ONE GEMM
+transformers' eight-kernel sequence (the post-attention residual add and its norm as
+one ``add_rms_norm``), each attention projects q, k and v with ONE GEMM
 whose column blocks go to ``verify_layer`` as row-strided views, and each MLP projects
 gate and up with ONE GEMM followed by ``silu_mul`` (the projection weights become views
 of one merged buffer per layer and kind, values and memory unchanged). The float32 model keeps transformers'
@@ -31,7 +32,7 @@ from dataclasses import dataclass
 import torch
 from transformers.models.qwen3.modeling_qwen3 import apply_rotary_pos_emb
 
-from .kernels import HEAD_DIM, HKV, HQ, merged_mlp_ready, rms_norm, silu_mul
+from .kernels import HEAD_DIM, HKV, HQ, add_rms_norm, merged_mlp_ready, rms_norm, silu_mul
 from .kv_store import B200PersistentTargetKV
 
 
@@ -49,6 +50,19 @@ class TargetFeatures:
 
 def _fused_norm_forward(norm, hidden_states):
     return rms_norm(hidden_states, norm.weight, norm.variance_epsilon)
+
+
+def _decoder_layer_forward(layer, hidden_states, attention_mask=None, position_ids=None, past_key_values=None,
+                           use_cache=False, position_embeddings=None, **kwargs):
+    """transformers' Qwen3DecoderLayer.forward with the post-attention residual add and
+    ``post_attention_layernorm`` as one ``add_rms_norm`` launch (bf16)."""
+    h = layer.input_layernorm(hidden_states)
+    h, _ = layer.self_attn(hidden_states=h, attention_mask=attention_mask, position_ids=position_ids,
+                           past_key_values=past_key_values, use_cache=use_cache,
+                           position_embeddings=position_embeddings, **kwargs)
+    norm = layer.post_attention_layernorm
+    residual, h = add_rms_norm(hidden_states, h, norm.weight, norm.variance_epsilon)
+    return residual + layer.mlp(h)
 
 
 def _merge_linears(linears):
@@ -114,6 +128,8 @@ class B200Qwen3Target:
                 self._orig_forward[norm] = vars(norm).get('forward')
                 norm.forward = types.MethodType(_fused_norm_forward, norm)
             for layer in model.model.layers:
+                self._orig_forward[layer] = vars(layer).get('forward')
+                layer.forward = types.MethodType(_decoder_layer_forward, layer)
                 att = layer.self_attn
                 if all(lin.bias is None for lin in (att.q_proj, att.k_proj, att.v_proj)):
                     self._qkv[att] = _merge_linears((att.q_proj, att.k_proj, att.v_proj))

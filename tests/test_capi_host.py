@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 15
+    assert lib.dspark_abi_version() == 16
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -60,6 +60,11 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
         assert lib.dspark_rms_norm(p, ld_x, fake16, 1e-6, 4, hidden, fake16, ld_out, None) == 1
     assert lib.dspark_rms_norm(fake16, 1024, fake16, -1.0, 4, 1024, fake16, 1024, None) == 1   # negative eps
     assert lib.dspark_rms_norm(fake16, 1024, fake16, 1e-6, 0, 1024, fake16, 1024, None) == 0    # no rows: no launch
+    assert lib.dspark_add_rms_norm(fake16, 1024, None, 1024, fake16, 1e-6, 4, 1024, fake16, 1024, fake16, 1024,
+                                   None) == 1                                                  # null delta
+    assert lib.dspark_add_rms_norm(fake16, 1024, fake16, 1020, fake16, 1e-6, 4, 1024, fake16, 1024, fake16, 1024,
+                                   None) == 1                                                  # short stride
+    assert lib.dspark_add_rms_norm(None, 1024, None, 1024, None, 1e-6, 0, 1024, None, 1024, None, 1024, None) == 0
     # draft q/k norm + RoPE: strides shorter than the heads, unaligned pointers, null pointers
     f = ctypes.c_void_p(256)
     assert lib.dspark_qk_norm_rope(f, 2000, f, 1024, f, f, 1e-6, 1e-6, f, f, 128, 4, 16, 8, f, f, None) == 1

@@ -227,3 +227,26 @@ def test_bf16_target_mlp_runs_merged_and_matches_transformers(pkg):
     target.close()
     assert 'forward' not in vars(mlp)
     status_clean(pkg)
+
+
+@pytest.mark.parametrize('exact', [False, True])
+def test_add_rms_norm_matches_torch_add_then_transformers_norm(pkg, exact):
+    if exact:
+        x, d = integer_rows(40, 300, 1024, 4), integer_rows(41, 300, 1024, 4)
+    else:
+        x, _ = inputs(40, 300, 1024, 4.0)
+        d, _ = inputs(41, 300, 1024, 0.5)
+    _, w = inputs(42, 1, 1024)
+    with torch.no_grad():
+        s = x + d
+        ref = hf_norm(w, 1e-6)(s)
+    got_s, got = pkg.add_rms_norm(x, d, w, 1e-6)
+    assert torch.equal(got_s, s)                      # the residual sum is torch's bf16 add
+    if exact:
+        assert torch.equal(got, ref)
+    else:
+        dist = ulp_distance(got, ref)
+        assert int(dist.max()) <= 1 and float((dist == 0).float().mean()) >= 0.999
+    empty_s, empty = pkg.add_rms_norm(x[:0], d[:0], w, 1e-6)
+    assert empty_s.shape == empty.shape == (0, 1024)
+    status_clean(pkg)
