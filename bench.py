@@ -89,9 +89,13 @@ def dist_env():
     return int(os.environ.get('RANK', 0)), int(os.environ.get('WORLD_SIZE', 1)), int(os.environ.get('LOCAL_RANK', 0))
 
 
-def contexts(cfg, rank):
+def contexts(cfg):
+    """The config's context lengths: ``requests`` draws of U{ctx_lo..ctx_hi} from numpy's
+    PCG64 seeded with the config's seed. Every rank uses the same lengths (its K/V
+    values differ), so each rank streams the same bytes and the 1 -> N curve measures
+    the hardware, not the draw."""
     import numpy as np
-    g = np.random.Generator(np.random.PCG64(cfg['seed'] * 1000 + rank))
+    g = np.random.Generator(np.random.PCG64(cfg['seed']))
     return [int(x) for x in g.integers(cfg['ctx_lo'], cfg['ctx_hi'] + 1, cfg['requests'])]
 
 
@@ -162,7 +166,7 @@ class Workload:
             return torch.randn(*shape, device=device, dtype=bf, generator=gen)
 
         # draft: packed [sum(c+7), 8, 128] K/V per layer (context cache rows + block rows)
-        self.draft_ctx = contexts(DRAFT, rank)
+        self.draft_ctx = contexts(DRAFT)
         self.draft_qlens = [BLOCK] * DRAFT['requests']
         self.draft_klens = [c + BLOCK for c in self.draft_ctx]
         self.draft_layout = pkg.PackedLayout.from_lengths(self.draft_qlens, self.draft_klens, device)
@@ -173,7 +177,7 @@ class Workload:
         self.draft_q = [randn(nq, HQ, D) for _ in range(draft_layers)]
         self.draft_kernel = pkg.B200DraftKernel(device)
         # verify: ragged persistent store, capacity = context + growth of every step
-        self.verify_ctx = contexts(VERIFY, rank)
+        self.verify_ctx = contexts(VERIFY)
         L, R, Q = max(verify_layers, 1), VERIFY['requests'], VERIFY['q']
         growth = Q * (steps_total + 2)
         caps = [c + growth for c in self.verify_ctx]
@@ -185,8 +189,7 @@ class Workload:
         for buf in (self.store._keys, self.store._values):
             for layer in range(L):
                 buf[layer * rows:(layer + 1) * rows].normal_(generator=gen)
-        for h, c in zip(self.handles, self.verify_ctx):
-            self.store._lengths[h.index] = c
+        self.store.mirror_lengths(self.handles, self.verify_ctx)
         nqv = R * Q
         self.vq = [randn(nqv, HQ, D) for _ in range(L)]
         self.vk = [randn(nqv, HKV, D) for _ in range(L)]
@@ -421,8 +424,7 @@ def graph_leg(pkg, device, rank, warmup, steps, cfg=GRAPH):
     gen.manual_seed(99 + rank)
     store._keys.normal_(generator=gen)
     store._values.normal_(generator=gen)
-    for h, c in zip(handles, ctx):
-        store._lengths[h.index] = c
+    store.mirror_lengths(handles, ctx)
     bf = torch.bfloat16
     vq = [torch.randn(R * Q, HQ, D, device=device, dtype=bf, generator=gen) for _ in range(L)]
     vk = [torch.randn(R * Q, HKV, D, device=device, dtype=bf, generator=gen) for _ in range(L)]
@@ -660,11 +662,11 @@ def append_leg(pkg, device, warmup, iters=10):
         x = feats(n)
         with torch.no_grad():
             ctx = draft.context_norm(draft.fc(x))[0].contiguous()
-        kv_w, kn_w, inv_freq = fused._append_operands()
+        kv_w, kn_w, rope = fused._append_operands()
         eps = draft.layers[0].attention.k_norm.variance_epsilon
 
         def kernel():
-            pkg.kernels.draft_append(ctx, kv_w, kn_w, inv_freq, meta, r, fused.pool_k, fused.pool_v,
+            pkg.kernels.draft_append(ctx, kv_w, kn_w, rope, meta, r, fused.pool_k, fused.pool_v,
                                      fused.trash_row, eps)
 
         with torch.no_grad():
@@ -867,8 +869,8 @@ def cpu_sample(seconds=12.0, rank=0):
     from oracle import bottom_right_varlen, noncausal_varlen, qk_norm_rope_bf16
     import inputs as I
     g = I.rng(99)
-    dctx = contexts(DRAFT, rank)[:8]
-    vctx = contexts(VERIFY, rank)[:8]
+    dctx = contexts(DRAFT)[:8]
+    vctx = contexts(VERIFY)[:8]
     dq = g.standard_normal((8 * BLOCK, HQ, D), dtype=np.float32)
     dk = g.standard_normal((sum(dctx) + 8 * BLOCK, HKV, D), dtype=np.float32)
     dv = g.standard_normal(dk.shape, dtype=np.float32)

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 16
+#define DSPARK_ABI_VERSION 17
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -108,15 +108,21 @@ int dspark_segment_attn(const void* q, const void* ka, const void* va, long long
                         void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /*
- * cos/sin table of a verify transaction, shared by every layer: for new row r of
- * request i (row cu_q[i] + r, position ctx_len[i] + r) and frequency f < 64,
- * table[row * 64 + f] = bf16 cos | bf16 sin << 16 of float32(position) * inv_freq[f].
- * table: [total_q, 64] uint32, 16-byte aligned. Replaces the per-forward
- * Qwen3RotaryEmbedding.forward of transformers (modeling_qwen3.py:137-148) that the
- * reference's verify runs once per model call (persistent_qwen_target.py:408-410).
+ * cos/sin table of a verify transaction, shared by every layer: new row r of
+ * request i (row cu_q[i] + r) is at position p = ctx_len[i] + r, and
+ * table[row * 64 + f] = rope_cache[p * 64 + f] for the 64 frequencies f.
+ * rope_cache: [cache_rows, 64] uint32 (bf16 cos in the low half, bf16 sin in the
+ * high half, of float32(p) * inv_freq[f]) that the caller evaluates once per model,
+ * on the host, with the float32 ops of its rotary module; the Python layer builds
+ * it with torch's CPU cos/sin, which is what transformers' Qwen3RotaryEmbedding
+ * runs on the reference's CPU path, so the kernels' RoPE is bit-identical to it.
+ * table: [total_q, 64] uint32; both 16-byte aligned. A position >= cache_rows
+ * yields a zero row and sets DSPARK_DEVICE_BAD_ARGUMENT. Replaces the per-forward
+ * Qwen3RotaryEmbedding.forward of transformers (modeling_qwen3.py:137-148) that
+ * the reference's verify runs once per model call (persistent_qwen_target.py:408-410).
  */
-int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t* ctx_len, int num_requests,
-                      int total_q, void* table, cudaStream_t stream);
+int dspark_rope_table(const void* rope_cache, int cache_rows, const int32_t* cu_q, const int32_t* ctx_len,
+                      int num_requests, int total_q, void* table, cudaStream_t stream);
 
 /*
  * Verify layer for a persistent KV store (bf16):

@@ -32,7 +32,7 @@ SIGNATURES = {
                                  _vp, _i, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
     'dspark_verify_strided': (_i, [_vp, _ll, _vp, _ll, _vp, _ll, _vp, _vp, _vp, _f, _vp, _vp, _vp, _i, _i, _i, _vp,
                                    _vp, _ll, _vp, _vp, _i, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
-    'dspark_rope_table': (_i, [_vp, _vp, _vp, _i, _i, _vp, _vp]),
+    'dspark_rope_table': (_i, [_vp, _i, _vp, _vp, _i, _i, _vp, _vp]),
     'dspark_commit_kv': (_i, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _vp]),
     'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
     'dspark_row_argmax': (_i, [_vp, _ll, _i, _i, _i, _vp, _vp]),
@@ -71,7 +71,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 16:
+        if lib.dspark_abi_version() != 17:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

@@ -13,8 +13,9 @@ ROOT = os.path.dirname(PKG)
 LIB_DIR = os.path.join(PKG, 'lib')
 LIB_PATH = os.path.join(LIB_DIR, 'libdspark_b200.so')
 SOURCES = [os.path.join(PKG, 'csrc', 'dspark_b200.cu')]
-DEPENDS = [os.path.join(PKG, 'csrc', f) for f in ('ptx.cuh', 'attention.cuh', 'verify.cuh', 'train.cuh', 'accept.cuh', 'markov.cuh', 'append.cuh', 'sampling.cuh')] + \
-          [os.path.join(ROOT, 'include', 'dspark_b200.h')]
+# every header under csrc/ (a new .cuh is picked up without editing this list) and the C-ABI header
+DEPENDS = sorted(os.path.join(PKG, 'csrc', f) for f in os.listdir(os.path.join(PKG, 'csrc')) if f.endswith('.cuh')) + \
+    [os.path.join(ROOT, 'include', 'dspark_b200.h')]
 ARCH = ['-gencode', 'arch=compute_100a,code=sm_100a']
 
 

@@ -485,6 +485,75 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
   return __bfloat1622float2(b);
 }
 
+// Sum of the 128 squares of one head vector, associated exactly as torch's CPU
+// float32 reduction associates a contiguous 128-element row (8-wide vectors, four
+// vector accumulators; transformers' Qwen3RMSNorm runs pow(2).mean(-1) through it).
+// With d = 32 i + 8 k + j (i, k < 4, j < 8):
+//   acc[k][j] = ((s[0,k,j] + s[1,k,j]) + s[2,k,j]) + s[3,k,j]
+//   P[j]      = ((acc[0][j] + acc[1][j]) + acc[2][j]) + acc[3][j]
+//   total     = (((((((P[0] + P[1]) + P[2]) + P[3]) + P[4]) + P[5]) + P[6]) + P[7])
+// Each add rounds, so the association decides the last bit of the mean square and,
+// through the rsqrt, which bf16 value a normalised element rounds to; with this order
+// the normalised (and roped) head equals the reference's CPU result bit for bit.
+// Explicit _rn intrinsics keep the compiler from contracting or reassociating.
+
+// Warp layout: lane l holds s[r] = square of d = 4 l + r. Result broadcast to all lanes.
+__device__ __forceinline__ float torch_order_sumsq_lane4(const float (&s)[4]) {
+  constexpr unsigned kAll = 0xffffffffu;
+  float t[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {   // lanes 0..7 end with acc[lane >> 1][4 (lane & 1) + r]
+    float a = __fadd_rn(s[r], __shfl_down_sync(kAll, s[r], 8));
+    a = __fadd_rn(a, __shfl_down_sync(kAll, s[r], 16));
+    t[r] = __fadd_rn(a, __shfl_down_sync(kAll, s[r], 24));
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r) {   // lanes 0, 1 end with P[4 lane + r]
+    float a = __fadd_rn(t[r], __shfl_down_sync(kAll, t[r], 2));
+    a = __fadd_rn(a, __shfl_down_sync(kAll, t[r], 4));
+    t[r] = __fadd_rn(a, __shfl_down_sync(kAll, t[r], 6));
+  }
+  float upper[4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r) upper[r] = __shfl_down_sync(kAll, t[r], 1);
+  float total = __fadd_rn(__fadd_rn(__fadd_rn(t[0], t[1]), t[2]), t[3]);
+#pragma unroll
+  for (int r = 0; r < 4; ++r) total = __fadd_rn(total, upper[r]);
+  return __shfl_sync(kAll, total, 0);
+}
+
+// MMA A-fragment layout: the quad (t4 = lane & 3) holds one row; sq[ks][e] is the
+// square of d = 16 ks + 2 t4 + (e & 1) + 8 (e >> 1), i.e. i = ks >> 1,
+// k = 2 (ks & 1) + (e >> 1), j = 2 t4 + (e & 1). Result on all four lanes.
+__device__ __forceinline__ float torch_order_sumsq_quad(const float (&sq)[8][4]) {
+  float p[2];
+#pragma unroll
+  for (int jj = 0; jj < 2; ++jj) {
+    float acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = 2 * (k & 1) + jj, ks0 = k >> 1;
+      float a = __fadd_rn(sq[ks0][e], sq[ks0 + 2][e]);
+      a = __fadd_rn(a, sq[ks0 + 4][e]);
+      acc[k] = __fadd_rn(a, sq[ks0 + 6][e]);
+    }
+    p[jj] = __fadd_rn(__fadd_rn(__fadd_rn(acc[0], acc[1]), acc[2]), acc[3]);
+  }
+  float total = 0.f;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {   // P[2q] and P[2q + 1] live on quad lane q
+    const float pe = __shfl_sync(0xffffffffu, p[0], q, 4), po = __shfl_sync(0xffffffffu, p[1], q, 4);
+    total = q == 0 ? __fadd_rn(pe, po) : __fadd_rn(__fadd_rn(total, pe), po);
+  }
+  return total;
+}
+
+// 1 / sqrt(sum / 128 + eps) with one rounding per step, as torch's CPU
+// mean (sum then divide), add and rsqrt (a rounded sqrt, then a rounded divide).
+__device__ __forceinline__ float rms_reciprocal(float sumsq, float eps) {
+  return __fdiv_rn(1.f, __fsqrt_rn(__fadd_rn(__fmul_rn(sumsq, 0.0078125f), eps)));
+}
+
 // Qwen3 RMSNorm + rotate-half RoPE (bf16 arithmetic order of transformers) of
 // one head of one MMA A-fragment row: regs lo[ks] hold d = 16ks+2t, +1 and
 // hi[ks] hold d = 16ks+2t+8, +9 (t = lane & 3). The quad (4 lanes) holds the
@@ -493,8 +562,7 @@ __device__ __forceinline__ float2 unpack_bf16x2(uint32_t v) {
 __device__ __forceinline__ void norm_rope_fragment(uint32_t (&lo)[8], uint32_t (&hi)[8], const AttnParams& p,
                                                    const __nv_bfloat16* w, const float (&cs)[4][4],
                                                    const float (&sn)[4][4], int t4) {
-  float x[8][4];
-  float ss = 0.f;
+  float x[8][4], sq[8][4];
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks) {
     const float2 a = unpack_bf16x2(lo[ks]), b = unpack_bf16x2(hi[ks]);
@@ -502,10 +570,10 @@ __device__ __forceinline__ void norm_rope_fragment(uint32_t (&lo)[8], uint32_t (
     x[ks][1] = a.y;
     x[ks][2] = b.x;
     x[ks][3] = b.y;
-    ss += a.x * a.x + a.y * a.y + b.x * b.x + b.y * b.y;
+#pragma unroll
+    for (int e = 0; e < 4; ++e) sq[ks][e] = __fmul_rn(x[ks][e], x[ks][e]);
   }
-  ss = quad_sum(ss);
-  const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+  const float rs = rms_reciprocal(torch_order_sumsq_quad(sq), p.eps);
 #pragma unroll
   for (int ks = 0; ks < 8; ++ks)
 #pragma unroll
@@ -558,10 +626,8 @@ __device__ __forceinline__ void rope_new_rows_in_smem(const AttnParams& p, const
     const uint32_t csw[4] = {cs4.x, cs4.y, cs4.z, cs4.w};
     const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
     const float x[4] = {a.x, a.y, b.x, b.y};
-    float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+    const float sq[4] = {__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1]), __fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])};
+    const float rs = rms_reciprocal(torch_order_sumsq_lane4(sq), p.eps);
     float y[4], partner[4], out[4];
 #pragma unroll
     for (int e = 0; e < 4; ++e) y[e] = bf16r(w[e] * bf16r(x[e] * rs));

@@ -372,12 +372,14 @@ int dspark_segment_attn(const void* q, const void* ka, const void* va, long long
   return run_attention(p, src, dtype, max_q, workspace, workspace_bytes, stream);
 }
 
-int dspark_rope_table(const float* inv_freq, const int32_t* cu_q, const int32_t* ctx_len, int num_requests,
-                      int total_q, void* table, cudaStream_t stream) {
-  if (!inv_freq || !cu_q || !ctx_len || !table || num_requests < 1 || total_q < 1 || !aligned(table, 16))
+int dspark_rope_table(const void* rope_cache, int cache_rows, const int32_t* cu_q, const int32_t* ctx_len,
+                      int num_requests, int total_q, void* table, cudaStream_t stream) {
+  if (!rope_cache || cache_rows < 1 || !cu_q || !ctx_len || !table || num_requests < 1 || total_q < 1 ||
+      !aligned(table, 16) || !aligned(rope_cache, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
-  rope_table_kernel<<<(total_q + 3) / 4, 256, 0, stream>>>(inv_freq, cu_q, ctx_len, num_requests, total_q,
-                                                          static_cast<uint32_t*>(table));
+  rope_table_kernel<<<(total_q + 15) / 16, 256, 0, stream>>>(static_cast<const uint4*>(rope_cache), cache_rows,
+                                                            cu_q, ctx_len, num_requests, total_q,
+                                                            static_cast<uint4*>(table));
   return launch_status();
 }
 

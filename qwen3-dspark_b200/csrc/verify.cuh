@@ -16,22 +16,28 @@ __device__ __forceinline__ int find_request(const int* cu, int n, int row) {
   return lo;
 }
 
-// cos/sin table of a verify transaction, shared by all layers: for new row r
-// of request i (global row cu_q[i] + r, position ctx_len[i] + r) and frequency
-// f: angle = float(position) * inv_freq[f] in float32, cos and sin rounded to
-// bf16 and packed (cos low, sin high). Same values as the transformers rotary
-// module computes once per forward (modeling_qwen3.py:137-148).
-__global__ void __launch_bounds__(256) rope_table_kernel(const float* __restrict__ inv_freq, const int* cu_q,
-                                                         const int* ctx_len, int num_requests, int total_q,
-                                                         uint32_t* table) {
-  const int row = blockIdx.x * 4 + (threadIdx.x >> 6);
-  const int f = threadIdx.x & 63;
+// cos/sin table of a transaction, shared by all layers: new row r of request i
+// (global row cu_q[i] + r) is at position ctx_len[i] + r, and its table row is that
+// position's row of the caller's rotary cache (bf16 cos | bf16 sin << 16 per
+// frequency, evaluated once on the host by the same float32 ops as the model's
+// rotary module, so the kernels use the reference's cos/sin values bit for bit).
+// One thread per 16-byte quarter-chunk: 16 threads per row. A position outside the
+// cache raises kStatusBadArgument and gives a zero row.
+__global__ void __launch_bounds__(256) rope_table_kernel(const uint4* __restrict__ cache, int cache_rows,
+                                                         const int* cu_q, const int* ctx_len, int num_requests,
+                                                         int total_q, uint4* table) {
+  const int row = blockIdx.x * 16 + (threadIdx.x >> 4);
+  const int c = threadIdx.x & 15;
   if (row >= total_q) return;
   const int req = min(find_request(cu_q, num_requests + 1, row), num_requests - 1);
   const int pos = ctx_len[req] + (row - cu_q[req]);
-  float sn, cs;
-  sincosf(static_cast<float>(pos) * inv_freq[f], &sn, &cs);
-  table[static_cast<size_t>(row) * 64 + f] = pack_bf16x2(cs, sn);
+  uint4 v = make_uint4(0u, 0u, 0u, 0u);
+  if (pos >= 0 && pos < cache_rows) {
+    v = cache[static_cast<size_t>(pos) * 16 + c];
+  } else if (c == 0) {
+    atomicOr(&g_device_status, kStatusBadArgument);
+  }
+  table[static_cast<size_t>(row) * 16 + c] = v;
 }
 
 // Verify-layer preparation of the new rows, shared by every tile that reads
@@ -86,10 +92,8 @@ __global__ void __launch_bounds__(256) verify_prep_kernel(const VerifyPrepParams
   }
   const float2 a = unpack_bf16x2(raw.x), b = unpack_bf16x2(raw.y);
   float x[4] = {a.x, a.y, b.x, b.y};
-  float ss = x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3];
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-  const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+  const float sq[4] = {__fmul_rn(x[0], x[0]), __fmul_rn(x[1], x[1]), __fmul_rn(x[2], x[2]), __fmul_rn(x[3], x[3])};
+  const float rs = rms_reciprocal(torch_order_sumsq_lane4(sq), p.eps);
   const uint2 wr = *reinterpret_cast<const uint2*>(w + d0);
   const float2 wa = unpack_bf16x2(wr.x), wb = unpack_bf16x2(wr.y);
   const float wv[4] = {wa.x, wa.y, wb.x, wb.y};

@@ -25,7 +25,7 @@ import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
-from .kernels import (HEAD_DIM, HKV, HQ, add_rms_norm, draft_append, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
+from .kernels import (HEAD_DIM, HKV, HQ, add_rms_norm, draft_append, rope_cache, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
                       rms_norm, sample_rows, segment_attention, silu_mul)
 from .kv_store import _upload
 
@@ -257,8 +257,10 @@ class B200PackedDraft:
 
     def _append_operands(self):
         """Stacked [k_proj; v_proj] weights of every layer, the stacked k_norm weights and
-        the float32 rotary frequencies for the fused append, rebuilt when one changes. A captured append reads
-        the stacks made when it was captured."""
+        the rotary cos/sin cache (``rope_cache``) for the fused append, rebuilt when one
+        changes. A captured append reads the stacks made when it was captured. The cache
+        covers every slot position plus a margin for the uncommitted rows of a
+        fixed-shape chunk (they sit past the slot's length and land in the trash row)."""
         d = self.draft
         params = [t for layer in d.layers for t in (layer.attention.k_proj.weight, layer.attention.v_proj.weight,
                                                     layer.attention.k_norm.weight)] + [d.rotary.inv_freq]
@@ -267,10 +269,9 @@ class B200PackedDraft:
             self._kv_weight = torch.cat([torch.cat((layer.attention.k_proj.weight, layer.attention.v_proj.weight))
                                          for layer in d.layers]).contiguous()
             self._k_norm_w = torch.stack([layer.attention.k_norm.weight for layer in d.layers]).contiguous()
-            # the rotary module's frequencies in float32, as its forward uses them
-            self._inv_freq = d.rotary.inv_freq.float().contiguous()
+            self._rope = rope_cache(d.rotary.inv_freq.float(), max(self.capacities) + 1024, self.device)
             self._append_key = key
-        return self._kv_weight, self._k_norm_w, self._inv_freq
+        return self._kv_weight, self._k_norm_w, self._rope
 
     def _append_rows(self, feat, meta, r, n):
         """Project n feature rows [1, n, F] and write them into the pool. ``meta`` is an
@@ -280,8 +281,8 @@ class B200PackedDraft:
         d = self.draft
         context = self._norm(d.context_norm, d.fc(feat.to(d.fc.weight.dtype)))
         if self._fused_append_ready():
-            kv_weight, k_norm_w, inv_freq = self._append_operands()
-            draft_append(context[0], kv_weight, k_norm_w, inv_freq, meta, r, self.pool_k, self.pool_v,
+            kv_weight, k_norm_w, rope = self._append_operands()
+            draft_append(context[0], kv_weight, k_norm_w, rope, meta, r, self.pool_k, self.pool_v,
                          self.trash_row, d.layers[0].attention.k_norm.variance_epsilon)
             return
         cu, slot, ctx, cnt = (meta[:r + 1].long(), meta[r + 1:2 * r + 1].long(), meta[2 * r + 1:3 * r + 1].long(),

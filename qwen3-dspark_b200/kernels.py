@@ -21,6 +21,8 @@ configurations) run on the library's float32 CUDA-core kernel.
 """
 import math
 
+import numpy as np
+
 import torch
 
 from . import _lib
@@ -448,7 +450,43 @@ def markov_greedy(proj_weight, emb_table, conf_weight, conf_bias, hidden, base, 
     return tokens, conf
 
 
-def draft_append(context, kv_weight, k_norm_weight, inv_freq, meta, num_requests, pool_k, pool_v, trash_row, eps):
+def rope_cache(inv_freq, rows, device):
+    """Rotary cos/sin cache [rows, 64] int32 for positions 0..rows-1: per frequency f,
+    bf16 cos of float32(p) * inv_freq[f] in the low 16 bits and bf16 sin in the high 16.
+
+    Evaluated on the host with torch's float32 CPU ops, the ones transformers'
+    ``Qwen3RotaryEmbedding.forward`` runs on the reference's CPU path (angle = one
+    rounded float32 product, then ``cos``/``sin``, then the cast to bf16;
+    modeling_qwen3.py:137-148), so a kernel that gathers rows of this cache applies
+    the reference's RoPE values bit for bit. ``inv_freq`` may live on any device; it
+    is copied to the host once, so build the cache outside CUDA-graph capture.
+    """
+    freqs = inv_freq.detach().to('cpu', torch.float32).reshape(-1)
+    if freqs.numel() != HEAD_DIM // 2 or type(rows) is not int or rows < 1:
+        raise ValueError('rope cache needs 64 float32 frequencies and a positive row count')
+    angle = torch.arange(rows, dtype=torch.float32)[:, None] * freqs[None, :]
+    bits = lambda t: t.to(torch.bfloat16).view(torch.int16).numpy().astype(np.uint32) & 0xFFFF  # noqa: E731
+    packed = bits(angle.cos()) | (bits(angle.sin()) << 16)
+    return torch.from_numpy(packed.view(np.int32)).to(device)
+
+
+def rope_table(cache, cu_rows, ctx_len, num_requests, total_rows, out=None):
+    """Per-row cos/sin table [total_rows, 64] int32 gathered from ``cache`` (``rope_cache``):
+    row g of request i (cu_rows[i] <= g < cu_rows[i + 1]) takes the cache row of position
+    ctx_len[i] + g - cu_rows[i] (``dspark_rope_table``)."""
+    device = cache.device
+    if (cache.dtype != torch.int32 or cache.ndim != 2 or cache.shape[1] != HEAD_DIM // 2
+            or not cache.is_contiguous() or cu_rows.dtype != torch.int32 or ctx_len.dtype != torch.int32):
+        raise ValueError('rope cache must be contiguous int32 [rows, 64] with int32 metadata')
+    if out is None:
+        out = torch.empty((total_rows, HEAD_DIM // 2), dtype=torch.int32, device=device)
+    _lib.check(_lib.load_library().dspark_rope_table(cache.data_ptr(), cache.shape[0], cu_rows.data_ptr(),
+                                                     ctx_len.data_ptr(), num_requests, total_rows, out.data_ptr(),
+                                                     _stream(device)), 'dspark_rope_table')
+    return out
+
+
+def draft_append(context, kv_weight, k_norm_weight, rope, meta, num_requests, pool_k, pool_v, trash_row, eps):
     """Fused draft-context append (``dspark_rope_table`` + ``dspark_draft_append``):
     every layer's k = RoPE(k_norm(k_proj(context))) and v = v_proj(context) of the
     context rows, written into the layer's pool (PackedDraft.append_committed's
@@ -456,7 +494,8 @@ def draft_append(context, kv_weight, k_norm_weight, inv_freq, meta, num_requests
 
     ``context`` [n, hidden] bf16 (fc + context_norm output), ``kv_weight``
     [layers * 2048, hidden] bf16 (per layer k_proj then v_proj weight rows),
-    ``k_norm_weight`` [layers, 128] bf16, ``inv_freq`` [64] float32, ``meta`` int32
+    ``k_norm_weight`` [layers, 128] bf16, ``rope`` the rotary cache (``rope_cache``) covering
+    every position written, ``meta`` int32
     [4R + 1] on the device: cu_rows (R + 1), slot_row, ctx_len, count (R each).
     ``pool_k``/``pool_v``: per-layer [pool_rows, 8, 128] bf16 pools; row j of request
     i lands in slot_row[i] + ctx_len[i] + j when j < count[i], else in ``trash_row``.
@@ -472,13 +511,11 @@ def draft_append(context, kv_weight, k_norm_weight, inv_freq, meta, num_requests
     if (kv_weight.shape != (layers * 2 * HKV * HEAD_DIM, hidden) or k_norm_weight.shape != (layers, HEAD_DIM)
             or len(pool_v) != layers or any(t.shape != (rows, HKV, HEAD_DIM) for t in (*pool_k, *pool_v))
             or meta.dtype != torch.int32 or meta.shape != (4 * num_requests + 1,) or meta.device != device
-            or inv_freq.dtype != torch.float32 or inv_freq.shape != (HEAD_DIM // 2,) or inv_freq.device != device):
+            or rope.device != device):
         raise ValueError('Draft append shapes do not match')
-    table = torch.empty((n, HEAD_DIM // 2), dtype=torch.int32, device=device)
     r = num_requests
+    table = rope_table(rope, meta, meta[2 * r + 1:], r, n)
     lib, stream = _lib.load_library(), _stream(device)
-    _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), meta.data_ptr(), meta[2 * r + 1:].data_ptr(), r, n,
-                                     table.data_ptr(), stream), 'dspark_rope_table')
     pk = (ctypes.c_void_p * layers)(*[t.data_ptr() for t in pool_k])
     pv = (ctypes.c_void_p * layers)(*[t.data_ptr() for t in pool_v])
     _lib.check(lib.dspark_draft_append(context.data_ptr(), n, hidden, kv_weight.data_ptr(), layers,

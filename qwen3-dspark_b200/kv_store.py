@@ -20,20 +20,69 @@ capacities this is byte-for-byte the reference's ``[layers, slots, C, H, D]``
 layout (``keys`` returns that view); ragged ``slot_capacities`` let long and
 short requests share HBM without padding every slot to the longest context.
 """
+import heapq
 from dataclasses import dataclass
 from typing import Mapping
 
 import torch
 
 from . import _lib
-from .kernels import HEAD_DIM, HKV, HQ, SCALE, runtime_identity
+from .kernels import HEAD_DIM, HKV, HQ, SCALE, rope_cache, rope_table, runtime_identity
 
 
 @dataclass(frozen=True)
 class Slot:
+    """Handle of one admitted request: its id, its resident slot and the slot's
+    generation when it was issued (the reference's ``Slot`` fields)."""
     request: str
     index: int
     incarnation: int
+
+
+class _SlotTable:
+    """Resident-slot ownership: which request holds which slot, and its committed length.
+
+    A slot's generation advances every time a request is admitted into it, and the
+    table keeps the one handle object it issued for the current generation. A handle
+    is honoured only if it IS that object: a handle kept past ``release`` (the slot
+    reused by a new request), a copy of a live handle, an equal-valued handle built by
+    hand or one issued by another store all fail the same single identity check.
+    Admission takes the lowest free index, so slot assignment is deterministic.
+    """
+
+    def __init__(self, count):
+        self.count = count
+        self.generation = [0] * count
+        self.holder = [None] * count        # issued Slot of the live generation, or None
+        self.length = [0] * count           # committed rows per slot (host mirror)
+        self._free = list(range(count))     # min-heap of unoccupied indices
+        self._requests = set()
+
+    def admit(self, request):
+        if not isinstance(request, str) or not request or request in self._requests:
+            raise ValueError('request id must be a non-empty string that is not already resident')
+        if not self._free:
+            raise ValueError('no free resident slot: every slot holds a request')
+        i = heapq.heappop(self._free)
+        self.generation[i] += 1
+        handle = Slot(request, i, self.generation[i])
+        self.holder[i], self.length[i] = handle, 0
+        self._requests.add(request)
+        return handle
+
+    def index_of(self, handle):
+        i = handle.index if type(handle) is Slot else None
+        if type(i) is not int or not 0 <= i < self.count or self.holder[i] is not handle:
+            raise ValueError('request handle is stale, copied or issued by another store')
+        return i
+
+    def release(self, i):
+        self._requests.discard(self.holder[i].request)
+        self.holder[i], self.length[i] = None, 0
+        heapq.heappush(self._free, i)
+
+    def resident_tokens(self):
+        return sum(self.length)
 
 
 @dataclass(frozen=True)
@@ -102,14 +151,13 @@ class B200PersistentTargetKV:
         self._values = torch.zeros_like(self._keys)
         self.scratch_keys = torch.zeros((layers * max_query_tokens, heads, dim), dtype=dtype, device=self.device)
         self.scratch_values = torch.zeros_like(self.scratch_keys)
-        self._owners = [None] * slots
-        self._handles = [None] * slots
-        self._incarnations = [0] * slots
-        self._lengths = [0] * slots
+        self._table = _SlotTable(slots)
+        self._lengths = self._table.length   # committed rows per slot index (host mirror)
         self._sequence = 0
         self._pending = None
         self._staged = set()
         self._buckets = {}
+        self._rotary = {}
         self.failed = False
 
     # -- views -----------------------------------------------------------------
@@ -130,69 +178,74 @@ class B200PersistentTargetKV:
         r0 = self.slot_rows[i] + start
         return x.view(self.layers, self.rows_per_layer, self.heads, self.dim)[:, r0:r0 + n]
 
-    # -- slot lifecycle (persistent_target_kv.py:204-268) -----------------------
-    def _healthy(self):
+    # -- slot lifecycle ----------------------------------------------------------
+    # Observable contract of the reference store (persistent_target_kv.py:204-265):
+    # a store poisoned by a failed copy refuses everything with RuntimeError;
+    # admission, removal and prefix loads are refused with RuntimeError while a
+    # transaction is open; a bad request id, a full store or a handle that is not
+    # the live one for its slot are refused with ValueError.
+    def _usable(self, *, idle=False):
         if self.failed:
-            raise RuntimeError('Store invalidated by copy failure; construct a new store')
-
-    def _idle(self):
-        self._healthy()
-        if self._pending is not None:
-            raise RuntimeError('Outstanding verification transaction')
+            raise RuntimeError('store is poisoned by a failed device copy; build a new store')
+        if idle and self._pending is not None:
+            raise RuntimeError('a verify transaction is open; commit or abort it first')
 
     def _slot(self, handle):
-        self._healthy()
-        if (not isinstance(handle, Slot) or not 0 <= handle.index < self.slot_capacity
-                or self._handles[handle.index] is not handle or self._owners[handle.index] != handle.request
-                or self._incarnations[handle.index] != handle.incarnation):
-            raise ValueError('Stale or foreign request incarnation')
-        return handle.index
+        self._usable()
+        return self._table.index_of(handle)
 
     def add_request(self, request):
-        self._idle()
-        if not isinstance(request, str) or not request or request in self._owners:
-            raise ValueError('New nonempty request identity required')
-        if None not in self._owners:
-            raise ValueError('Resident slot capacity exhausted')
-        i = self._owners.index(None)
-        self._incarnations[i] += 1
-        self._owners[i], self._lengths[i] = request, 0
-        handle = Slot(request, i, self._incarnations[i])
-        self._handles[i] = handle
-        return handle
+        self._usable(idle=True)
+        return self._table.admit(request)
 
     def remove_request(self, handle):
-        self._idle()
-        i = self._slot(handle)
-        self._owners[i], self._lengths[i], self._handles[i] = None, 0, None
+        """Free the request's slot; its rows stay in memory but no later handle reaches them."""
+        self._usable(idle=True)
+        self._table.release(self._table.index_of(handle))
 
     def length(self, handle):
         return self._lengths[self._slot(handle)]
+
+    def handle_of(self, index):
+        """The live handle of slot ``index`` (None when the slot is free)."""
+        return self._table.holder[index]
+
+    def mirror_lengths(self, handles, lengths):
+        """Set the host's committed-length mirror of ``handles`` after the device changed
+        the lengths itself (the pipelined decode loop commits from device-side counts)
+        or after a caller filled resident rows directly (benchmarks)."""
+        self._usable(idle=True)
+        indices = [self._slot(h) for h in handles]
+        lengths = [int(n) for n in lengths]
+        if len(indices) != len(lengths) or any(not 0 <= n <= self.capacities[i] for i, n in zip(indices, lengths)):
+            raise ValueError('one length within its slot capacity per handle required')
+        for i, n in zip(indices, lengths):
+            self._lengths[i] = n
 
     def _kv(self, keys, values, shape):
         for x in (keys, values):
             if (not isinstance(x, torch.Tensor) or tuple(x.shape) != shape or x.device != self.device
                     or x.dtype != self.dtype or x.requires_grad):
-                raise ValueError('KV shape, device, dtype and no-autograd contract required')
+                raise ValueError(f'K/V must be {shape} {self.dtype} tensors on {self.device} without autograd')
 
     @torch.no_grad()
     def load_prefix(self, handle, keys, values):
         """Bootstrap committed KV [L, n, H, D] into an empty slot."""
-        self._idle()
+        self._usable(idle=True)
         i = self._slot(handle)
-        if self._lengths[i] or not isinstance(keys, torch.Tensor) or keys.ndim != 4:
-            raise ValueError('Prefix bootstrap requires empty slot and [L,C,H,D] KV')
+        if self._lengths[i]:
+            raise ValueError('prefix load needs an empty slot')
+        if not isinstance(keys, torch.Tensor) or keys.ndim != 4 or not 0 <= keys.shape[1] <= self.capacities[i]:
+            raise ValueError('prefix K/V must be [layers, n, heads, dim] with n within the slot capacity')
         n = keys.shape[1]
-        if not 0 <= n <= self.capacities[i]:
-            raise ValueError('Prefix exceeds resident context capacity')
         self._kv(keys, values, (self.layers, n, self.heads, self.dim))
         try:
             self._slot_rows_view(self._keys, i, 0, n).copy_(keys)
             self._slot_rows_view(self._values, i, 0, n).copy_(values)
-            self._lengths[i] = n
         except Exception:
             self.failed = True
             raise
+        self._lengths[i] = n
 
     # -- fixed-buffer buckets (graph capture; persistent_qwen_graph.py:198-275) ---
     def bind_bucket(self, bucket):
@@ -201,7 +254,7 @@ class B200PersistentTargetKV:
         metadata into those buffers, so a verify program captured once under
         ``capture_transaction(bucket)`` can be replayed for every transaction of the
         bucket. Metadata is still built on the host (as the reference's graph does)."""
-        self._healthy()
+        self._usable()
         qlens = tuple(bucket.query_lengths)
         if (not qlens or any(type(q) is not int or q < 1 for q in qlens) or sum(qlens) > self.max_query_tokens
                 or len(qlens) > self.slot_capacity):
@@ -219,7 +272,7 @@ class B200PersistentTargetKV:
         is a valid empty-context layout (every request reads only its new rows), so
         warm-up launches are well defined; a capture records launches without running
         them. End it with ``abort``."""
-        self._idle()
+        self._usable(idle=True)
         buffers = self.bind_bucket(bucket)
         qlens = tuple(bucket.query_lengths)
         cu = [0]
@@ -248,7 +301,7 @@ class B200PersistentTargetKV:
         ``query_lengths`` (or ``bucket.query_lengths``) gives each request's new rows.
         One host->device copy of [cu_q | slot_row | ctx_len | slot_cap] as int32.
         """
-        self._idle()
+        self._usable(idle=True)
         handles = tuple(handles)
         if query_lengths is None:
             if bucket is None:
@@ -282,18 +335,29 @@ class B200PersistentTargetKV:
         return tx
 
     def _transaction(self, tx):
-        self._healthy()
+        self._usable()
         if tx is not self._pending:
-            raise ValueError('Stale, copied or foreign transaction')
+            raise ValueError('transaction is not the open one of this store (stale, copied or foreign)')
         for h, c in zip(tx.slots, tx.context_lengths):
             if self._lengths[self._slot(h)] != c:
-                raise RuntimeError('Committed state changed during verification')
+                raise RuntimeError('a request\'s committed length changed while its transaction was open')
 
     @staticmethod
     def _meta(tx):
         r = len(tx.query_lengths)
         m = tx.meta
         return m[:r + 1], m[r + 1:2 * r + 1], m[2 * r + 1:3 * r + 1], m[3 * r + 1:4 * r + 1]
+
+    def rotary_cache(self, inv_freq):
+        """The [context_capacity, 64] cos/sin cache of ``inv_freq`` (``rope_cache``), built
+        on the host the first time these frequencies are seen and kept for the store's
+        life (every position a verify row can take is below ``context_capacity``)."""
+        key = (inv_freq.data_ptr(), inv_freq._version)
+        cache = self._rotary.get(key)
+        if cache is None:
+            cache = rope_cache(inv_freq, self.context_capacity, self.device)
+            self._rotary[key] = cache
+        return cache
 
     @torch.no_grad()
     def verify_layer(self, tx, layer, q_raw, k_raw, v_raw, q_norm_weight, k_norm_weight, *, inv_freq,
@@ -342,12 +406,9 @@ class B200PersistentTargetKV:
         key = (inv_freq.data_ptr(), inv_freq._version)
         table = tx.rope.get(key)
         if table is None:
-            # cos/sin of every new row's position, once for all layers of this transaction
-            table = tx.table if tx.table is not None else torch.empty((n, HEAD_DIM // 2), dtype=torch.int32,
-                                                                       device=self.device)
-            _lib.check(lib.dspark_rope_table(inv_freq.data_ptr(), cu_q.data_ptr(), ctx.data_ptr(),
-                                             len(tx.query_lengths), n, table.data_ptr(), stream),
-                       'dspark_rope_table')
+            # cos/sin of every new row's position, gathered once for all layers of this
+            # transaction from the rotary cache of these frequencies
+            table = rope_table(self.rotary_cache(inv_freq), cu_q, ctx, len(tx.query_lengths), n, out=tx.table)
             tx.rope.clear()
             tx.rope[key] = table
         ws = _lib.workspace(self.device, stream)

@@ -71,26 +71,35 @@ class PackedLayout:
         return cls(tuple(range(len(q))), q, k, cumulative(q, device), cumulative(k, device),
                    torch.arange(sum(k), device=device), sum(k))
 
+    # Sizes the reference's adapters read off a layout: packed query rows, packed key
+    # rows, and the number of (query, key) pairs a dense per-request product covers.
     @property
     def query_tokens(self):
-        return sum(self.query_lengths)
+        return int(sum(self.query_lengths))
 
     @property
     def gathered_key_tokens(self):
-        return sum(self.key_lengths)
+        return int(sum(self.key_lengths))
 
     @property
     def pair_domain(self):
-        return sum(q * k for q, k in zip(self.query_lengths, self.key_lengths))
+        return int(sum(nq * nk for nq, nk in zip(self.query_lengths, self.key_lengths)))
 
     def gather_kv(self, key, value):
-        """[1,Hkv,physical_K,D] cache -> packed [sum K, Hkv, D] (varlen_target.py:74-82)."""
-        if (key.ndim != 4 or key.shape[0] != 1 or value.shape != key.shape
-                or key.shape[2] != self.physical_key_tokens or key.device != self.gather_indices.device
-                or value.device != key.device or value.dtype != key.dtype):
-            raise ValueError('Expected matching [1,Hkv,physical_K,D] cache tensors')
-        return tuple(x.index_select(2, self.gather_indices).squeeze(0).transpose(0, 1).contiguous()
-                     for x in (key, value))
+        """Pack the layout's key rows out of a head-major cache pair.
+
+        ``key``/``value``: [1, Hkv, physical_key_tokens, D] on the layout's device, one
+        dtype. Returns two [sum K, Hkv, D] tensors holding, request after request, the
+        rows ``gather_indices`` names: the request-contiguous THD operand the kernels read
+        (the reference's ``PackedLayout.gather_kv``, varlen_target.py:74-82)."""
+        want = (1, key.shape[1] if key.ndim == 4 else -1, self.physical_key_tokens,
+                key.shape[-1] if key.ndim == 4 else -1)
+        if (key.ndim != 4 or tuple(key.shape) != want or tuple(value.shape) != want or value.dtype != key.dtype
+                or not key.device == value.device == self.gather_indices.device):
+            raise ValueError(f'gather_kv needs a key/value pair of shape [1, Hkv, {self.physical_key_tokens}, D], '
+                             'one dtype, on the layout device')
+        rows = self.gather_indices
+        return tuple(x[0].permute(1, 0, 2)[rows] for x in (key, value))
 
 
 @dataclass(frozen=True)

@@ -289,7 +289,7 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
     ag = draft._append_graphs[(R, width)]
     i32 = torch.int32
     cu_t = [width * i for i in range(R + 1)]
-    ctx0 = [store._lengths[s] for s in slots]
+    ctx0 = [store.length(h) for h in handles]
     dlen0 = [draft._lengths[r] for r in requests]
     if any(c + max_new_tokens + width > store.capacities[s] for c, s in zip(ctx0, slots)):
         raise ValueError('Request slots cannot hold max_new_tokens plus one verify chunk')
@@ -374,8 +374,7 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
         k += 1
     torch.cuda.synchronize(dev)
     # the host mirrors of the committed lengths follow the device state
-    for s, r, c in zip(slots, requests, ctx.tolist()):
-        store._lengths[s] = c
+    store.mirror_lengths(handles, ctx.tolist())
     for r, d in zip(requests, dlen.tolist()):
         draft._lengths[r] = d
     return output, rounds

@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 16
+    assert lib.dspark_abi_version() == 17
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
@@ -42,8 +42,10 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert st == 1
     st = lib.dspark_commit_kv(None, None, None, None, None, None, None, None, None, 1, 1, 1, 1, 0, None)
     assert st == 1
-    st = lib.dspark_rope_table(None, None, None, 1, 1, None, None)
-    assert st == 1
+    assert lib.dspark_rope_table(None, 8, None, None, 1, 1, None, None) == 1
+    fake = ctypes.c_void_p(256)
+    assert lib.dspark_rope_table(fake, 0, fake, fake, 1, 1, fake, None) == 1          # empty cache
+    assert lib.dspark_rope_table(ctypes.c_void_p(264), 8, fake, fake, 1, 1, fake, None) == 1   # unaligned cache
     size = ctypes.c_size_t(0)
     assert lib.dspark_attention_workspace_size(0, None) == 1
     # training layout, acceptance and Markov entries refuse before touching the device
@@ -227,3 +229,23 @@ def test_packed_layout_mirror_matches_reference_fixture(pkg, golden):
                                    ([1], [1], [1, 1], [0, 2]), ([], [], [], [])]:
         with pytest.raises(ValueError):
             pkg.PackedLayout.from_metadata(*(torch.tensor(x, dtype=torch.long) for x in [qreq, qpos, kreq, kpos]))
+
+
+def test_gather_kv_packs_the_layout_rows(pkg, golden):
+    """``gather_kv`` returns, request after request, the cache rows the layout names as
+    [sum K, Hkv, D] (checked element-wise against the cache), and refuses mismatched pairs."""
+    g = golden('layout1')
+    L = lambda x: torch.tensor(x.tolist(), dtype=torch.long)  # noqa: E731
+    lay = pkg.PackedLayout.from_metadata(L(g['qr']), L(g['qp']), L(g['kr']), L(g['kp']))
+    n = lay.physical_key_tokens
+    key = torch.randn((1, 8, n, 128))
+    value = torch.randn((1, 8, n, 128))
+    k, v = lay.gather_kv(key, value)
+    assert k.shape == v.shape == (lay.gathered_key_tokens, 8, 128) and k.is_contiguous()
+    for packed_row, cache_row in enumerate(g['gather'].tolist()):
+        assert torch.equal(k[packed_row], key[0, :, cache_row])
+        assert torch.equal(v[packed_row], value[0, :, cache_row])
+    for bad_k, bad_v in ((key[:, :, :-1], value[:, :, :-1]), (key, value.double()), (key[0], value[0]),
+                         (key, value[:, :4])):
+        with pytest.raises(ValueError):
+            lay.gather_kv(bad_k, bad_v)

@@ -140,9 +140,9 @@ def test_destination_outside_pool_is_skipped_and_flagged(pkg):
     before_k, before_v = pools(pd)
     rows = pd.pool_k[0].shape[0]
     context = torch.randn((4, 256), device=dev()).to(torch.bfloat16)
-    kv_w, kn_w, inv_freq = pd._append_operands()
+    kv_w, kn_w, rope = pd._append_operands()
     meta = torch.tensor([0, 4, rows - 2, 0, 4], dtype=torch.int32, device=dev())   # rows - 2 + j: j >= 2 outside
-    pkg.kernels.draft_append(context, kv_w, kn_w, inv_freq, meta, 1, pd.pool_k, pd.pool_v,
+    pkg.kernels.draft_append(context, kv_w, kn_w, rope, meta, 1, pd.pool_k, pd.pool_v,
                              pd.trash_row, 1e-6)
     assert pkg.read_device_status(clear=True) & pkg._lib.DEVICE_BAD_ARGUMENT
     for new, old in zip(pd.pool_k + pd.pool_v, before_k + before_v):

@@ -1,10 +1,11 @@
 """GPU parity of the verify layer (QK-norm + RoPE + KV append + attention) and commit/rollback,
 through both the fused kernel and the prep-kernel path.
 
-Checked against the oracle: ``qk_norm_rope_bf16`` for the appended K (bf16, at
-most one bf16 ulp from transformers' float32 transcendental rounding), the
-two-source bottom-right attention for the output, and ``OracleKVStore.commit``
-for the resident state after commit (bit-exact: commit is a byte copy).
+Checked against the oracle: ``qk_norm_rope_bf16`` for the appended K (bit-exact:
+the oracle equals transformers' CPU evaluation bit for bit, and the kernels use its
+summation order and its cos/sin), the two-source bottom-right attention for the
+output, and ``OracleKVStore.commit`` for the resident state after commit
+(bit-exact: commit is a byte copy).
 """
 import numpy as np
 import pytest
@@ -23,14 +24,6 @@ def bits_to_dev(bits):
 
 def dev_to_bits(t):
     return t.contiguous().view(torch.int16).cpu().numpy().astype(np.uint16)
-
-
-def ulp_close(a_bits, b_bits, max_ulps=1):
-    a = a_bits.astype(np.int32)
-    b = b_bits.astype(np.int32)
-    # same-sign bf16 patterns are monotone in magnitude; allow +-1 step (and +-0)
-    same = (a == b) | (np.abs(a - b) <= max_ulps) | ((a & 0x7FFF) == 0) & ((b & 0x7FFF) == 0)
-    return same
 
 
 def make_store(pkg, layers, caps, max_q, g):
@@ -79,8 +72,7 @@ def test_fused_verify_commit_rollback(pkg, weights, path):
         sk = dev_to_bits(store.scratch_keys[layer * store.max_query_tokens:][:nq])
         sv = dev_to_bits(store.scratch_values[layer * store.max_query_tokens:][:nq])
         assert np.array_equal(sv, vr)
-        assert ulp_close(sk, k_o).all()
-        assert np.mean(sk == k_o) > 0.995
+        assert np.array_equal(sk, k_o)          # the reference's CPU k_norm + RoPE, bit for bit
         staged_k.append(sk)
         staged_v.append(sv)
         # attention over resident prefix + own new rows
