@@ -60,6 +60,12 @@ int dspark_attention_workspace_size(int device, size_t* bytes);
  * clears it when `clear` is non-zero. */
 int dspark_read_device_status(unsigned int* status, int clear);
 
+/* Enqueues on `stream` a copy of the current device's status word into `dst`
+ * (pinned host or device memory), without synchronising: a decode loop that runs
+ * ahead of the host reads it with the round's results. No reference counterpart
+ * (the reference's kernels raise on the host instead). */
+int dspark_copy_device_status(unsigned int* dst, cudaStream_t stream);
+
 /*
  * Non-causal packed varlen attention: every query row of request i sees all
  * keys rows [cu_k[i], cu_k[i+1]).
@@ -235,7 +241,8 @@ int dspark_rms_norm(const void* x, long long ld_x, const void* weight, float eps
  * Residual add + Qwen3RMSNorm in one launch (bf16): sum_out = bf16(x + delta),
  * torch's bf16 add of a decoder layer's residual and sublayer output, and out =
  * dspark_rms_norm(sum_out). Same rules as dspark_rms_norm for every pointer and
- * stride; x and delta must not overlap out or sum_out.
+ * stride; x and delta must not overlap out or sum_out, nor out sum_out: such a call
+ * (an in-place residual update, say) is refused with DSPARK_ERR_INVALID_ARGUMENT.
  */
 int dspark_add_rms_norm(const void* x, long long ld_x, const void* delta, long long ld_d, const void* weight,
                         float eps, int rows, int hidden, void* out, long long ld_out, void* sum_out,
@@ -291,8 +298,20 @@ int dspark_silu_mul(const void* gate_up, long long ld, int rows, int inter, void
  * [num_requests]): the projection weight streams on across steps and the CTAs
  * meet at a bounded grid barrier between steps. If the cooperative launch is
  * refused (not every CTA could be resident), it launches the steps one by one.
+ * A call whose barrier wait gives up (DSPARK_DEVICE_WAIT_TIMEOUT in the device
+ * status) returns unusable tokens but leaves the scratch zero again: its last CTA
+ * to finish resets it, so the next call on the stream is correct.
  */
 size_t dspark_markov_scratch_bytes(void);
+
+/*
+ * Sets the time limit (nanoseconds of the GPU's global timer, on the current
+ * device) of the grid barrier in dspark_markov_block; the default is two
+ * seconds, like every other bounded wait of the library. A diagnostic for
+ * failure handling: a test lowers it to make the barrier give up, checks the
+ * status word and the next call, and puts it back. No reference counterpart.
+ */
+int dspark_set_grid_barrier_timeout(unsigned long long ns);
 int dspark_markov_step(const void* proj_weight, const void* emb_table, int vocab, int rank, const void* base,
                        long long base_stride_r, int k, const long long* prev, long long prev_stride,
                        const void* hidden, int hidden_dim, const void* conf_w, float conf_b, long long* tokens,

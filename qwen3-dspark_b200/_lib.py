@@ -24,6 +24,7 @@ SIGNATURES = {
     'dspark_status_string': (ctypes.c_char_p, [_i]),
     'dspark_attention_workspace_size': (_i, [_i, ctypes.POINTER(_sz)]),
     'dspark_read_device_status': (_i, [ctypes.POINTER(ctypes.c_uint), _i]),
+    'dspark_copy_device_status': (_i, [_vp, _vp]),
     'dspark_draft_attn': (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
     'dspark_varlen_attn': (_i, [_vp, _vp, _vp, _vp, _vp, _i, _i, _ll, _i, _i, _f, _i, _vp, _vp, _sz, _vp]),
     'dspark_segment_attn': (_i, [_vp, _vp, _vp, _ll, _vp, _vp, _ll, _vp, _vp, _vp, _vp, _vp, _i, _i, _i, _i, _i,
@@ -37,6 +38,7 @@ SIGNATURES = {
     'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
     'dspark_row_argmax': (_i, [_vp, _ll, _i, _i, _i, _vp, _vp]),
     'dspark_markov_scratch_bytes': (_sz, []),
+    'dspark_set_grid_barrier_timeout': (_i, [ctypes.c_ulonglong]),
     'dspark_markov_step': (_i, [_vp, _vp, _i, _i, _vp, _ll, _i, _vp, _ll, _vp, _i, _vp, _f, _vp, _vp, _ll, _i,
                                 _vp, _vp]),
     'dspark_markov_block': (_i, [_vp, _vp, _i, _i, _vp, _i, _vp, _vp, _i, _vp, _f, _vp, _vp, _i, _vp, _vp]),
@@ -95,6 +97,20 @@ def read_device_status(clear=True):
     v = ctypes.c_uint(0)
     check(load_library().dspark_read_device_status(ctypes.byref(v), int(clear)), 'dspark_read_device_status')
     return v.value
+
+
+STATUS_NAMES = {DEVICE_WAIT_TIMEOUT: 'a bounded wait ran out', DEVICE_BAD_SCHEDULE: 'tile schedules disagreed',
+                DEVICE_BAD_ARGUMENT: 'a kernel refused an out-of-range index'}
+
+
+def describe_status(status):
+    return ', '.join(name for bit, name in STATUS_NAMES.items() if status & bit) or 'unknown bits'
+
+
+def set_grid_barrier_timeout(ns=2_000_000_000):
+    """Time limit of the Markov block kernel's grid barrier on the current device
+    (nanoseconds; default two seconds). For failure-handling tests."""
+    check(load_library().dspark_set_grid_barrier_timeout(int(ns)), 'dspark_set_grid_barrier_timeout')
 
 
 _workspaces = {}

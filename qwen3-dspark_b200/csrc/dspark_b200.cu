@@ -12,6 +12,7 @@
 #include <mutex>
 #include <numeric>
 #include <queue>
+#include <utility>
 #include <vector>
 
 #include "accept.cuh"
@@ -332,6 +333,14 @@ int dspark_read_device_status(unsigned int* status, int clear) {
   return DSPARK_OK;
 }
 
+int dspark_copy_device_status(unsigned int* dst, cudaStream_t stream) {
+  if (dst == nullptr) return DSPARK_ERR_INVALID_ARGUMENT;
+  void* src = nullptr;
+  if (cudaGetSymbolAddress(&src, g_device_status) != cudaSuccess || src == nullptr) return DSPARK_ERR_CUDA;
+  return cudaMemcpyAsync(dst, src, sizeof(unsigned int), cudaMemcpyDefault, stream) == cudaSuccess ? DSPARK_OK
+                                                                                                  : DSPARK_ERR_CUDA;
+}
+
 int dspark_draft_attn(const void* q, const void* k, const void* v, const int32_t* cu_q, const int32_t* cu_k,
                       int num_requests, int total_q, long long key_rows, int max_q, int max_k, float scale,
                       int dtype, void* out, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
@@ -556,6 +565,18 @@ int dspark_add_rms_norm(const void* x, long long ld_x, const void* delta, long l
   if (!x || !delta || !weight || !out || !sum_out || !aligned(x, 16) || !aligned(delta, 16) ||
       !aligned(weight, 16) || !aligned(out, 16) || !aligned(sum_out, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
+  // the second pass re-reads x and delta after the first pass's stores: an output that
+  // shares bytes with an input (an in-place residual update) would change it mid-row
+  auto span = [&](const void* p, long long ld) {
+    const uintptr_t a = reinterpret_cast<uintptr_t>(p);
+    return std::make_pair(a, a + static_cast<uintptr_t>(((rows - 1) * ld + hidden) * 2));
+  };
+  auto overlap = [](std::pair<uintptr_t, uintptr_t> u, std::pair<uintptr_t, uintptr_t> v) {
+    return u.first < v.second && v.first < u.second;
+  };
+  const auto sx = span(x, ld_x), sd = span(delta, ld_d), so = span(out, ld_out), ss = span(sum_out, ld_sum);
+  if (overlap(sx, so) || overlap(sx, ss) || overlap(sd, so) || overlap(sd, ss) || overlap(so, ss))
+    return DSPARK_ERR_INVALID_ARGUMENT;
   const float inv_hidden = 1.0f / static_cast<float>(hidden);
   rms_norm_kernel<true><<<(rows + kNormRowsPerCta - 1) / kNormRowsPerCta, kNormThreads, 0, stream>>>(
       static_cast<const __nv_bfloat16*>(x), ld_x, static_cast<const __nv_bfloat16*>(delta), ld_d,
@@ -613,6 +634,10 @@ int dspark_greedy_accept(const int32_t* pred, const long long* tokens, const int
 
 size_t dspark_markov_scratch_bytes(void) { return markov::kScratchBytes; }
 
+int dspark_set_grid_barrier_timeout(unsigned long long ns) {
+  return cudaMemcpyToSymbol(g_grid_barrier_limit_ns, &ns, sizeof(ns)) == cudaSuccess ? DSPARK_OK : DSPARK_ERR_CUDA;
+}
+
 namespace {
 
 // Shared argument checks and parameter block of the Markov entries.
@@ -652,6 +677,8 @@ int markov_setup(const void* proj_weight, const void* emb_table, int vocab, int 
   p.best = static_cast<unsigned long long*>(scratch);
   p.arrivals = reinterpret_cast<unsigned int*>(static_cast<uint8_t*>(scratch) + 3 * markov::kRows * 8);
   p.generation = p.arrivals + 1;
+  p.exits = p.arrivals + 2;
+  p.failed = p.arrivals + 3;
   p.num_requests = num_requests;
   p.dup = num_requests <= 64;
   p.vocab = vocab;

@@ -78,9 +78,10 @@ constexpr uint32_t kSmemBytes = 1024 + kSmemLast + 4;
 // rows, bf16 pairs: column j of lane m = elements 2j, 2j+1 of row m).
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemA = 256;
-// Scratch (zero between calls): three best buffers of kRows packed maxima, the
-// CTA arrival counter, the grid-barrier generation (the only word that is not
-// returned to zero: it only ever advances).
+// Scratch (zero between calls): three best buffers of kRows packed maxima, then four
+// 32-bit words: the CTA arrival counter, the grid-barrier generation (the only word
+// that is not returned to zero: it only ever advances), the CTA exit counter and the
+// failed flag of the block kernel (a CTA gave up; the last CTA out resets the scratch).
 constexpr size_t kScratchBytes = 3 * kRows * sizeof(unsigned long long) + 16;
 
 struct Params {
@@ -102,6 +103,8 @@ struct Params {
   unsigned long long* best;         // 3 x [kRows] packed maxima (zero between calls)
   unsigned int* arrivals;           // CTA arrival counter (zero between calls)
   unsigned int* generation;         // grid-barrier generation
+  unsigned int* exits;              // CTAs that left the block kernel (zero between calls)
+  unsigned int* failed;             // a CTA of the block kernel gave up (zero between calls)
   int num_requests;                 // R <= 128
   int dup;                          // R <= 64: request r also in row r + 64 (column halves split)
   int vocab;                        // V, multiple of 8
@@ -327,9 +330,13 @@ __device__ __forceinline__ void grid_barrier(const Params& p, volatile int* abor
     atomicAdd(p.generation, 1u);
     return;
   }
+  // A lowered limit (a failure-handling test) is checked on every poll, so that a wait
+  // shorter than 64 polls gives up too; the default one every 64 polls.
+  const unsigned long long limit = g_grid_barrier_limit_ns;
+  const uint32_t every = limit < kWaitLimitNs ? 0u : 63u;
   const unsigned long long t0 = globaltimer();
   for (uint32_t it = 1; *gen == g; ++it) {
-    if ((it & 63u) == 0 && globaltimer() - t0 > kWaitLimitNs) {
+    if ((it & every) == 0 && globaltimer() - t0 >= limit) {
       atomicOr(&g_device_status, kStatusWaitTimeout);
       *abort_flag = 1;
       return;
@@ -494,6 +501,28 @@ __device__ __forceinline__ void markov_body(const CUtensorMap* wmap, const Param
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    // Calls on a stream share the scratch. A call in which some CTA gave up leaves it
+    // dirty: an arrival count short of the grid (the CTAs that aborted skip the later
+    // barriers) and maxima published after CTA 0 cleared their buffer. Every CTA
+    // counts itself out once all its roles are done; the last one out, when any CTA
+    // failed, returns the maxima and the arrival counter to zero for the next call.
+    volatile int* last = reinterpret_cast<volatile int*>(smem + kSmemLast);
+    if (threadIdx.x == 0) {
+      if (*abort_flag) atomicOr(p.failed, 1u);
+      __threadfence();
+      int verdict = 0;
+      if (atomicAdd(p.exits, 1u) == gridDim.x - 1) {
+        __threadfence();
+        verdict = atomicExch(p.failed, 0u) != 0u ? 2 : 1;
+        atomicExch(p.exits, 0u);
+      }
+      *last = verdict;
+    }
+    __syncthreads();
+    if (*last == 2) {
+      for (int i = threadIdx.x; i < 3 * kRows; i += blockDim.x) atomicExch(p.best + i, 0ull);
+      if (threadIdx.x == 0) atomicExch(p.arrivals, 0u);
+    }
   }
   if (warp == 4) tmem_dealloc(tmem, kTmemCols);
 }

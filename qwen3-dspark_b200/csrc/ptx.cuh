@@ -21,6 +21,12 @@ __device__ unsigned int g_device_status;
 // last microseconds; reaching the limit means a schedule bug, never a slow GPU.
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
+// Time limit of the grid barrier between block positions of the cooperative Markov
+// kernel. The host may lower it (dspark_set_grid_barrier_timeout) so that a test can
+// make that barrier give up on purpose and check the recovery; every other wait,
+// including the waits that drain copies and MMAs after an abort, keeps kWaitLimitNs.
+__device__ unsigned long long g_grid_barrier_limit_ns = kWaitLimitNs;
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

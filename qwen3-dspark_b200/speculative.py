@@ -14,6 +14,8 @@ from dataclasses import dataclass
 
 import torch
 
+from . import _lib
+
 
 @dataclass(frozen=True)
 class QueryBucket:
@@ -38,6 +40,20 @@ def accept_greedy(proposals, predictions, eos_ids=()):
     if eos is not None:
         committed = committed[:eos + 1]
     return accepted, committed
+
+
+def _round_status(target=None, verified=None, where='decode round'):
+    """Read and clear the library's device status word once per round, where the round's
+    results are already synchronised. The kernels report a wait that ran out or an index
+    they refused there instead of faulting, so a non-zero word means this round's logits or
+    tokens may be partly written: the verify transaction is aborted (no KV is committed,
+    the draft pool is untouched until the commit) and the loop raises."""
+    status = _lib.read_device_status(clear=True)
+    if status:
+        if verified is not None:
+            target.abort(verified)
+        raise RuntimeError(f'device status {status:#x} after the {where} ({_lib.describe_status(status)}); '
+                           'nothing of the round was kept')
 
 
 def _pinned(values, dtype, device):
@@ -88,6 +104,7 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
     features = target.prefill(prompts)
     last = target.predict(features, last_only=True)
     output = {r: [int(last[r].argmax(-1).item())] for r in prompts}
+    _round_status(where='prefill')
     draft.append_committed({r: features.context_for(r) for r in prompts})
     active = [r for r in prompts if output[r][-1] not in eos_ids and max_new_tokens > 1]
     rounds = []
@@ -121,6 +138,7 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
             for i, (r, v) in enumerate(logits.items()):
                 accepted, committed = accept_greedy(host_ids[i][1:], v[0].argmax(-1).tolist(), eos_ids)
                 decided[r] = (accepted, committed[:max_new_tokens - len(output[r])])
+        _round_status(target, verified)
         commit, stats = {}, {}
         for r in active:
             accepted, committed = decided[r]
@@ -176,6 +194,7 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
     law = float64_law(torch.cat([last[r].reshape(1, -1) for r in requests]), temperature)
     first = sample_rows(law, first_u).tolist()
     output = {r: [first[i]] for i, r in enumerate(requests)}
+    _round_status(where='prefill')
     draft.append_committed({r: features.context_for(r) for r in prompts})
     active = [r for r in requests if output[r][-1] not in eos_ids and max_new_tokens > 1]
     size = draft.draft.spec.block_size
@@ -207,6 +226,12 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
             eos_ids)
         res = result.cpu().tolist()
         em = emitted.cpu().tolist()
+        try:
+            _round_status(target, verified)
+        except RuntimeError:
+            for r in active:
+                generators[r].set_state(states[r])
+            raise
         bad = [(r, res[i][6]) for i, r in enumerate(active) if res[i][6]]
         if bad:
             # nothing of this round is kept: the caches roll back and the generators
@@ -251,7 +276,6 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
     needs a bf16 draft whose Markov head runs on the fused kernel. Returns
     ({request: tokens}, rounds)."""
     from .kernels import greedy_accept
-    from . import _lib
     if type(max_new_tokens) is not int or max_new_tokens < 0:
         raise ValueError('max_new_tokens must be a nonnegative integer')
     if not draft._graph_ready():
@@ -267,6 +291,7 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
     last = target.predict(features, last_only=True)
     requests = list(prompts)
     output = {r: [int(last[r].argmax(-1).item())] for r in requests}
+    _round_status(where='prefill')
     draft.append_committed({r: features.context_for(r) for r in requests})
     if max_new_tokens == 1 or all(output[r][-1] in eos_ids for r in requests):
         return output, []
@@ -315,6 +340,9 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
     lib = _lib.load_library()
     stream = torch.cuda.current_stream(dev)
     res_host = [torch.empty(2 * R + R * width, dtype=torch.long).pin_memory() for _ in range(2)]
+    # the device status word after each round, copied with the round's results (a
+    # synchronous read would wait for the round enqueued behind it)
+    status_host = torch.zeros(2, dtype=torch.int32).pin_memory()
     events = [torch.cuda.Event() for _ in range(2)]
 
     def launch_round(k):
@@ -347,6 +375,8 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
         budget.copy_(torch.where(hit, torch.zeros_like(budget), budget - n_commit))
         buf = res_host[k & 1]
         buf.copy_(torch.cat((accepted.long(), n_commit.long(), emitted)), non_blocking=True)
+        _lib.check(lib.dspark_copy_device_status(status_host[k & 1:].data_ptr(), stream.cuda_stream),
+                   'dspark_copy_device_status')
         events[k & 1].record(stream)
 
     rounds = []
@@ -357,6 +387,15 @@ def speculative_greedy_pipelined(target, draft, prompts, max_new_tokens, eos_ids
         if not all(done.values()):
             launch_round(k + 1)                        # enqueued before round k is read
         events[k & 1].synchronize()
+        status = int(status_host[k & 1])
+        if status:
+            # this round (and the one enqueued behind it) already committed on the
+            # device, so nothing can be rolled back: the store refuses further use
+            torch.cuda.synchronize(dev)
+            _lib.read_device_status(clear=True)
+            store.failed = True
+            raise RuntimeError(f'device status {status:#x} in a pipelined decode round '
+                               f'({_lib.describe_status(status)}); the KV store is invalidated')
         host = res_host[k & 1].tolist()
         stats = {}
         for i, r in enumerate(requests):

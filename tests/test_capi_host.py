@@ -67,6 +67,13 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     assert lib.dspark_add_rms_norm(fake16, 1024, fake16, 1020, fake16, 1e-6, 4, 1024, fake16, 1024, fake16, 1024,
                                    None) == 1                                                  # short stride
     assert lib.dspark_add_rms_norm(None, 1024, None, 1024, None, 1e-6, 0, 1024, None, 1024, None, 1024, None) == 0
+    # outputs that share bytes with an input, or with each other, are refused: the second
+    # pass re-reads x and delta after the stores (4 rows x 1024 bf16 = 8 KiB spans)
+    x, d, o, s = (ctypes.c_void_p(a) for a in (0x100000, 0x200000, 0x300000, 0x400000))
+    for args in ((x, d, o, x), (x, d, d, s), (x, d, o, ctypes.c_void_p(0x100000 + 6 * 1024)),
+                 (x, d, ctypes.c_void_p(0x200000 + 2048 * 3), s), (x, d, o, ctypes.c_void_p(0x300000 + 2048))):
+        xa, da, oa, sa = args
+        assert lib.dspark_add_rms_norm(xa, 1024, da, 1024, fake16, 1e-6, 4, 1024, oa, 1024, sa, 1024, None) == 1
     # draft q/k norm + RoPE: strides shorter than the heads, unaligned pointers, null pointers
     f = ctypes.c_void_p(256)
     assert lib.dspark_qk_norm_rope(f, 2000, f, 1024, f, f, 1e-6, 1e-6, f, f, 128, 4, 16, 8, f, f, None) == 1
@@ -249,3 +256,25 @@ def test_gather_kv_packs_the_layout_rows(pkg, golden):
                          (key, value[:, :4])):
         with pytest.raises(ValueError):
             lay.gather_kv(bad_k, bad_v)
+
+
+def test_noalloc_entry_size_and_refusals(pkg):
+    """The allocation-free verify entry: its static scratch is the workspace of 148 CTAs
+    (two fp32 partial slots of 8 heads x 16 rows x 128 d plus their (m, l) pairs, eight
+    48-byte merge records and a tile range per CTA), and bad arguments are refused before
+    any device work."""
+    lib = pkg.load_library()
+    lib.dspark_varlen_attn_noalloc_scratch_bytes.restype = ctypes.c_size_t
+    per_cta = 2 * (8 * 16 * 128 + 8 * 16 * 2) * 4 + 8 * 48 + 2 * 8
+    assert lib.dspark_varlen_attn_noalloc_scratch_bytes() == 148 * per_cta
+    fn = lib.dspark_varlen_attn_noalloc
+    vp = ctypes.c_void_p
+    fn.restype = ctypes.c_int
+    fn.argtypes = [vp, vp, vp, vp, vp, ctypes.c_int, ctypes.c_int, ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
+                   ctypes.c_float, vp, vp]
+    f = vp(256)
+    good = [f, f, f, f, f, 1, 7, 64, 7, 64, 128 ** -0.5, f, None]
+    for i, bad in ((1, None), (2, None), (4, None), (7, 0), (5, 0), (6, 0), (10, 0.0), (0, vp(258))):
+        args = list(good)
+        args[i] = bad
+        assert fn(*args) == 1, (i, bad)

@@ -195,3 +195,32 @@ def test_markov_block_sizes_equal_step_launches(pkg, block):
         key = (dev().index, torch.cuda.current_stream().cuda_stream)
         assert int(kern._markov_scratch[key][:3 * 128 * 8 + 4].count_nonzero()) == 0
     status_clean(pkg)
+
+
+def test_grid_barrier_timeout_is_reported_and_the_next_call_is_correct(pkg):
+    """Failure handling of the block kernel's grid barrier, made on purpose without a GPU
+    fault: with the barrier's limit lowered to zero, CTAs that wait for the others give up
+    at the first barrier, raise their abort flags and leave after draining their copies
+    and MMAs (those waits keep the two-second limit). The call returns, the status word
+    reports DSPARK_DEVICE_WAIT_TIMEOUT, and the next call on the same stream, with the
+    limit restored, gives exactly the tokens and confidences of a clean call: the last CTA
+    out of the failed call returned the shared scratch to zero."""
+    r, vocab, rank, hdim, block = 64, 32768, 256, 1024, 7
+    w, e, cw, hidden, base, anchors, cb = make(77, r, vocab, rank, hdim, block)
+    pkg.read_device_status(clear=True)
+    clean, clean_conf = pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+    torch.cuda.synchronize()
+    assert pkg.read_device_status(clear=True) == 0
+    try:
+        pkg._lib.set_grid_barrier_timeout(0)
+        pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+        torch.cuda.synchronize()
+    finally:
+        pkg._lib.set_grid_barrier_timeout()
+    assert pkg.read_device_status(clear=True) & pkg._lib.DEVICE_WAIT_TIMEOUT
+    for _ in range(2):
+        again, conf = pkg.markov_greedy(w, e, cw, cb, hidden, base, anchors, block)
+        torch.cuda.synchronize()
+        assert torch.equal(again, clean)
+        assert torch.equal(conf, clean_conf)
+    status_clean(pkg)
