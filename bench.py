@@ -8,7 +8,8 @@ One step = one speculative round's attention on one GPU:
     bottom-right attention (B200PersistentTargetKV.verify_layer), then one commit of
     the accepted prefixes (accept ~ U{0..6} + anchor) and rollback of the rest.
 Metric: query-token-layers per second = (64*7*5 + 128*7*28) / step time, summed
-over ranks (weak scaling: every rank runs its own full batch, seed s*1000 + rank).
+over ranks (weak scaling: every rank runs its own full batch: the same context lengths,
+K/V values seeded by rank).
 
     python bench.py [--gpus N --steps K --warmup W] [--impl reference]
                     [--case round|draft|verify] [--layers L]

@@ -6,16 +6,19 @@ to the allocator that owns the GPU, or a server whose KV-cache pool already hold
 nearly all HBM. Its scratch is a static device array inside the library that
 keeps the previous call's contents, so the test makes two calls in a row on
 different inputs and compares each, through the C ABI, with dspark_varlen_attn
-(caller-provided workspace) on the same inputs.
+(caller-provided workspace) on the same inputs: on a 148-SM B200 both launch the same
+kernel on the same grid, so the outputs must be identical bit for bit; each output
+also meets the bf16 gate against the oracle's bottom-right attention. The documented
+scratch size and the argument refusals are checked without a GPU in test_capi_host.py.
 """
 import ctypes
 
-import numpy as np
 import pytest
 import torch
 
 import inputs as I
-from gpu_util import ATOL, RTOL, dev, status_clean, to_dev
+from gpu_util import assert_bf16_close, dev, status_clean, to_dev
+from oracle import bottom_right_varlen
 
 pytestmark = pytest.mark.gpu
 
@@ -51,8 +54,8 @@ def test_noalloc_matches_workspace_entry_on_two_calls(pkg):
                     I.SCALE, out.data_ptr(), torch.cuda.current_stream().cuda_stream)
         assert status == 0, lib.dspark_status_string(status)
         torch.cuda.synchronize()
-        a = out.float().cpu().numpy()
-        e = expected.float().cpu().numpy()
-        assert np.isfinite(a).all()
-        np.testing.assert_allclose(a, e, atol=ATOL, rtol=RTOL)
+        if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+            assert torch.equal(out.view(torch.int16), expected.view(torch.int16))
+        assert_bf16_close(out, bottom_right_varlen(q, k, v, qlens, klens, I.SCALE))
+        assert_bf16_close(expected, bottom_right_varlen(q, k, v, qlens, klens, I.SCALE))
     status_clean(pkg)
