@@ -150,6 +150,81 @@ class ClockSampler:
                     reasons=sorted(reasons), samples=len(sm))
 
 
+# --------------------------------------------------------------------------- config 2 inputs
+def build_draft_06b(pkg, device):
+    """Random-init DSparkDraft at the Qwen3-0.6B draft geometry (hidden 1024, FFN 3072,
+    16/8 heads, 5 layers fed by 5 target layers, theta 1e6, block 7), bf16, seeded; its
+    q/k and context norm weights are N(1, 0.1) so that they are not the identity. A
+    7-layer target with a 1024-token vocabulary supplies the shared embedding (config 2
+    needs no vocabulary)."""
+    import torch
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    torch.manual_seed(1)
+    cfg = Qwen3Config(vocab_size=1024, hidden_size=1024, intermediate_size=3072, num_hidden_layers=7,
+                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
+                      rms_norm_eps=1e-6, tie_word_embeddings=True,
+                      rope_parameters={'rope_type': 'default', 'rope_theta': 1e6})
+    with torch.device(device), torch.no_grad():
+        target = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
+        spec = pkg.DraftSpec(layer_ids=(0, 1, 2, 3, 4), num_layers=5, block_size=BLOCK, markov_rank=64,
+                             mask_token_id=1000)
+        draft = pkg.DSparkDraftModel(target, spec).to(torch.bfloat16).eval()
+        for layer in draft.layers:
+            for w in (layer.attention.k_norm.weight, layer.attention.q_norm.weight):
+                w.copy_(1 + 0.1 * torch.randn_like(w))
+        draft.context_norm.weight.copy_(1 + 0.1 * torch.randn_like(draft.context_norm.weight))
+    return draft
+
+
+def draft_cfg2_inputs(pkg, device, rank=0, layers=DRAFT['layers']):
+    """Config 2's draft-layer inputs as its statement builds them: context K/V from the
+    draft's own projection chain on N(0,1) target features [sum(c), 5 x 1024] (fc
+    5x1024->1024, context RMSNorm, per-layer k_proj / k_norm / RoPE and v_proj: the fused
+    append into the paged pool, packed_draft.py:129-168), block rows from the q/k/v
+    projections of N(0,1) block states at positions c..c+6 (model.py:41-45). Returns the
+    draft, its pool, the features and block states, and per layer the packed
+    ``[sum(c + 7), 8, 128]`` K/V (each request's context rows, then its block rows), the
+    ``[64 * 7, 16, 128]`` queries and the layout. Features are seeded 1 + 1000 * rank."""
+    import torch
+    ctx = contexts(DRAFT)
+    R = DRAFT['requests']
+    draft = build_draft_06b(pkg, device)
+    pd = pkg.B200PackedDraft(draft, max_requests=R, context_capacity=max(ctx), slot_capacities=ctx)
+    names = [f'd{i}' for i in range(R)]
+    for r in names:
+        pd.add_request(r)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(1 + 1000 * rank)
+    bf = torch.bfloat16
+    feats = torch.randn((1, sum(ctx), 5 * 1024), generator=gen, device=device, dtype=bf)
+    chunks, o = {}, 0
+    for r, c in zip(names, ctx):
+        chunks[r] = feats[:, o:o + c]
+        o += c
+    with torch.no_grad():
+        pd.append_committed(chunks)
+    block_states = torch.randn((1, R * BLOCK, 1024), generator=gen, device=device, dtype=bf)
+    bpos = torch.cat([torch.arange(c, c + BLOCK, device=device) for c in ctx])
+    # row index of every packed key into cat(pool rows, block rows)
+    pool_rows = pd.pool_k[0].shape[0]
+    index = []
+    for i, (r, c) in enumerate(zip(names, ctx)):
+        r0 = pd.slot_rows[pd._slots[r]]
+        index += list(range(r0, r0 + c)) + list(range(pool_rows + i * BLOCK, pool_rows + (i + 1) * BLOCK))
+    index = torch.tensor(index, dtype=torch.long, device=device)
+    qs, ks, vs = [], [], []
+    with torch.no_grad():
+        cos, sin = draft.rotary(block_states, bpos[None])
+        for li, layer in enumerate(draft.layers[:layers]):
+            q, bk, bv = pd._project(layer.attention, block_states, cos, sin)
+            qs.append(q.contiguous())
+            ks.append(torch.cat((pd.pool_k[li], bk)).index_select(0, index))
+            vs.append(torch.cat((pd.pool_v[li], bv)).index_select(0, index))
+    layout = pkg.PackedLayout.from_lengths([BLOCK] * R, [c + BLOCK for c in ctx], device)
+    return dict(draft=draft, pool=pd, names=names, contexts=ctx, features=feats, block_states=block_states,
+                q=qs, k=ks, v=vs, layout=layout)
+
+
 # --------------------------------------------------------------------------- workload
 class Workload:
     """Device-resident synthetic inputs of one rank (inputs larger than L2: ~62 GB of KV)."""
@@ -166,16 +241,19 @@ class Workload:
         def randn(*shape):
             return torch.randn(*shape, device=device, dtype=bf, generator=gen)
 
-        # draft: packed [sum(c+7), 8, 128] K/V per layer (context cache rows + block rows)
+        # draft: packed [sum(c+7), 8, 128] K/V per layer (context cache rows + block rows),
+        # projected by the draft's own chain as config 2 states
         self.draft_ctx = contexts(DRAFT)
         self.draft_qlens = [BLOCK] * DRAFT['requests']
         self.draft_klens = [c + BLOCK for c in self.draft_ctx]
-        self.draft_layout = pkg.PackedLayout.from_lengths(self.draft_qlens, self.draft_klens, device)
-        nk = sum(self.draft_klens)
-        nq = sum(self.draft_qlens)
-        self.draft_k = [randn(nk, HKV, D) for _ in range(draft_layers)]
-        self.draft_v = [randn(nk, HKV, D) for _ in range(draft_layers)]
-        self.draft_q = [randn(nq, HQ, D) for _ in range(draft_layers)]
+        if draft_layers:
+            d2 = draft_cfg2_inputs(pkg, device, rank, draft_layers)
+            self.draft_layout = d2['layout']
+            self.draft_q, self.draft_k, self.draft_v = d2['q'], d2['k'], d2['v']
+            del d2
+        else:
+            self.draft_layout = pkg.PackedLayout.from_lengths(self.draft_qlens, self.draft_klens, device)
+            self.draft_q, self.draft_k, self.draft_v = [], [], []
         self.draft_kernel = pkg.B200DraftKernel(device)
         # verify: ragged persistent store, capacity = context + growth of every step
         self.verify_ctx = contexts(VERIFY)
@@ -296,6 +374,34 @@ class Workload:
         read = torch.cuda.Event()
         read.record(io['d2h'])
         cur.wait_event(read)
+
+    def step_copies(self, host):
+        """The host copies of ``step_e2e`` alone: the same bytes on the same two copy
+        streams, no kernels. Timed with every rank copying at once, its time beside
+        ``step_e2e``'s shows whether the host copy path bounds the end-to-end step."""
+        import torch
+        cur = torch.cuda.current_stream(self.device)
+        io = self._io
+        begin = torch.cuda.Event()
+        begin.record(cur)
+        for st in (io['h2d'], io['d2h']):
+            st.wait_event(begin)
+        with torch.cuda.stream(io['h2d']):
+            for layer in range(self.draft_layers):
+                io['slots']['draft'][layer % 2]['inp'][0].copy_(host['dq'][layer], non_blocking=True)
+            for layer in range(self.verify_layers):
+                srcs = (host['vq'][layer], host['vk'][layer], host['vv'][layer])
+                for dst, src in zip(io['slots']['verify'][layer % 2]['inp'], srcs):
+                    dst.copy_(src, non_blocking=True)
+        with torch.cuda.stream(io['d2h']):
+            for layer in range(self.draft_layers):
+                host['do'][layer].copy_(self.draft_q[layer], non_blocking=True)
+            for layer in range(self.verify_layers):
+                host['vo'][layer].copy_(self.vq[layer], non_blocking=True)
+        for st in (io['h2d'], io['d2h']):
+            done = torch.cuda.Event()
+            done.record(st)
+            cur.wait_event(done)
 
     @staticmethod
     def _event(events):
@@ -810,16 +916,26 @@ def round5_leg(pkg, device, rank, warmup):
         ps = prompts(f'w{w}_')
         pkg.speculative_greedy(target, pdraft, ps, 4)
         release(ps)
+    def device_timer():
+        """(start, stop): CUDA events on the current stream; stop() synchronises and returns s."""
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(device)
+        e0.record()
+
+        def stop():
+            e1.record()
+            torch.cuda.synchronize(device)
+            return e0.elapsed_time(e1) / 1e3
+        return stop
+
     def timed_loop(tag, graph):
         ps = prompts(tag)
-        torch.cuda.synchronize(device)
-        t0 = time.perf_counter()
+        stop = device_timer()
         if graph == 'pipelined':
             out, rounds = pkg.speculative_greedy_pipelined(target, pdraft, ps, ROUND5['new_tokens'])
         else:
             out, rounds = pkg.speculative_greedy(target, pdraft, ps, ROUND5['new_tokens'], graph=graph)
-        torch.cuda.synchronize(device)
-        dt = time.perf_counter() - t0
+        dt = stop()
         release(ps)
         return out, rounds, dt
 
@@ -835,12 +951,10 @@ def round5_leg(pkg, device, rank, warmup):
     for r in ps:
         target.add_request(r)
         pdraft.add_request(r)
-    torch.cuda.synchronize(device)
-    t1 = time.perf_counter()
+    stop = device_timer()
     feats = target.prefill(ps)
     pdraft.append_committed({r: feats.context_for(r) for r in ps})
-    torch.cuda.synchronize(device)
-    prefill_s = time.perf_counter() - t1
+    prefill_s = stop()
     release(ps)
     generated = sum(len(v) for v in out.values())
     accepted = [s['accepted'] for rd in rounds for s in rd.values()]
@@ -862,38 +976,101 @@ def round5_leg(pkg, device, rank, warmup):
 
 
 # --------------------------------------------------------------------------- CPU legs
-def cpu_sample(seconds=12.0, rank=0):
-    """Oracle port (numpy, all host threads) on a bounded sample of the same workload:
-    per repetition 8 draft requests (1 layer) + 8 verify requests (1 layer, QK-norm/RoPE +
-    bottom-right attention), until ``seconds`` of wall time. Returns query-tok/s."""
-    import numpy as np
-    from oracle import bottom_right_varlen, noncausal_varlen, qk_norm_rope_bf16
-    import inputs as I
-    g = I.rng(99)
-    dctx = contexts(DRAFT)[:8]
-    vctx = contexts(VERIFY)[:8]
-    dq = g.standard_normal((8 * BLOCK, HQ, D), dtype=np.float32)
-    dk = g.standard_normal((sum(dctx) + 8 * BLOCK, HKV, D), dtype=np.float32)
-    dv = g.standard_normal(dk.shape, dtype=np.float32)
-    vq = g.standard_normal((8 * VERIFY['q'], HQ, D), dtype=np.float32)
-    vk = g.standard_normal((sum(vctx) + 8 * VERIFY['q'], HKV, D), dtype=np.float32)
-    vv = g.standard_normal(vk.shape, dtype=np.float32)
-    from oracle import f32_to_bf16_bits
-    qb = f32_to_bf16_bits(vq)
-    kb = f32_to_bf16_bits(vk[:8 * VERIFY['q']])
-    ones = f32_to_bf16_bits(np.ones(D, np.float32))
-    pos = np.concatenate([np.arange(c, c + VERIFY['q']) for c in vctx])
-    reps, units, t0 = 0, 0, time.perf_counter()
+CPU_SAMPLE = dict(draft_requests=8, verify_requests=4)
+
+
+def quantile_requests(ctx, n):
+    """Indices of n requests at the (2i+1)/(2n) quantiles of the sorted context draw, so a
+    small sample spans the whole distribution (shortest to longest)."""
+    order = sorted(range(len(ctx)), key=ctx.__getitem__)
+    return [order[(2 * i + 1) * len(ctx) // (2 * n)] for i in range(n)]
+
+
+def set_host_threads():
+    """Every host thread this process may use, set explicitly: torchrun exports
+    OMP_NUM_THREADS=1, which an environment default would not override. Returns the
+    thread count torch reports in effect."""
+    import torch
+    n = host_threads()
+    os.environ['OMP_NUM_THREADS'] = str(n)
+    os.environ['MKL_NUM_THREADS'] = str(n)
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
+class CPURound:
+    """The reference's CPU round on a bounded sample of the bench's own workload: the
+    torch operations of its draft and verify attention paths (``oracle/torch_cpu.py``,
+    pinned to fixtures made by the reference's functions), float32 as the reference's
+    CPU store defaults to, on all host threads.
+
+    One sample step = one whole round for a subset of the requests: the draft attention
+    of 8 config-2 requests for each of the 5 draft layers, then ``begin`` for 4 config-3
+    requests, the 28 verify layers (q/k RMSNorm + RoPE, stage, gather, SDPA) and the
+    commit of accept ~ U{0..6} + anchor. The requests sit at evenly spaced quantiles of
+    their config's context draw, so the sample's mean context matches the full batch's."""
+
+    def __init__(self, steps_total, seed=99):
+        import torch
+        from oracle.torch_cpu import VerifyRoundCPU
+        from oracle.rope_norm import inv_freq
+        import numpy as np
+        self.threads = set_host_threads()
+        gen = torch.Generator().manual_seed(seed)
+        dall, vall = contexts(DRAFT), contexts(VERIFY)
+        self.dctx = [dall[i] for i in quantile_requests(dall, CPU_SAMPLE['draft_requests'])]
+        self.vctx = [vall[i] for i in quantile_requests(vall, CPU_SAMPLE['verify_requests'])]
+        nd, nv, Q = len(self.dctx), len(self.vctx), VERIFY['q']
+        self.dklens = [c + BLOCK for c in self.dctx]
+        f32 = torch.float32
+        self.dq = [torch.randn((nd * BLOCK, HQ, D), generator=gen) for _ in range(DRAFT['layers'])]
+        self.dk = [torch.randn((sum(self.dklens), HKV, D), generator=gen) for _ in range(DRAFT['layers'])]
+        self.dv = [torch.randn((sum(self.dklens), HKV, D), generator=gen) for _ in range(DRAFT['layers'])]
+        growth = Q * (steps_total + 2)
+        self.store = VerifyRoundCPU(VERIFY['layers'], self.vctx, nv * Q, HKV, D,
+                                    slot_capacities=[c + growth for c in self.vctx], dtype=f32, generator=gen)
+        self.vq = [torch.randn((nv * Q, HQ, D), generator=gen) for _ in range(VERIFY['layers'])]
+        self.vk = [torch.randn((nv * Q, HKV, D), generator=gen) for _ in range(VERIFY['layers'])]
+        self.vv = [torch.randn((nv * Q, HKV, D), generator=gen) for _ in range(VERIFY['layers'])]
+        self.ones = torch.ones(D, dtype=f32)
+        self.freqs = torch.from_numpy(inv_freq(1e6, D))
+        self.accept = np.random.Generator(np.random.PCG64(seed))
+        self.units = nd * BLOCK * DRAFT['layers'] + nv * Q * VERIFY['layers']
+        self.fraction = self.units / query_units()
+
+    def step(self):
+        from oracle.torch_cpu import noncausal_varlen_sdpa
+        for layer in range(DRAFT['layers']):
+            noncausal_varlen_sdpa(self.dq[layer], self.dk[layer], self.dv[layer], [BLOCK] * len(self.dctx),
+                                  self.dklens, D ** -0.5)
+        store, Q = self.store, VERIFY['q']
+        ws = store.begin([Q] * len(self.vctx))
+        for layer in range(VERIFY['layers']):
+            store.layer(ws, layer, self.vq[layer], self.vk[layer], self.vv[layer], self.ones, self.ones, self.freqs,
+                        1e-6, D ** -0.5)
+        store.commit(ws, [int(a) + 1 for a in self.accept.integers(0, Q, len(self.vctx))])
+
+    def describe(self):
+        return (f'torch CPU float32 restatement of the reference round (oracle/torch_cpu.py): per step one whole '
+                f'round for {len(self.dctx)} cfg2 draft requests x{DRAFT["layers"]} layers (contexts '
+                f'{self.dctx}) and {len(self.vctx)} cfg3 verify requests x{VERIFY["layers"]} layers with begin, '
+                f'q/k norm + RoPE, stage, gather, SDPA and commit (contexts {self.vctx}); '
+                f'{self.units} of the full step\'s {query_units()} query units ({self.fraction:.4f})')
+
+
+def cpu_sample(seconds=12.0):
+    """The GPU arm's ``cpu_baseline`` leg: CPURound steps after one warm-up step until
+    ``seconds`` of host time. Returns (query-tok/s, steps, seconds, CPURound)."""
+    rnd = CPURound(steps_total=64)
+    rnd.step()
+    steps, t0 = 0, time.perf_counter()
     while True:
-        noncausal_varlen(dq, dk, dv, [BLOCK] * 8, [c + BLOCK for c in dctx], D ** -0.5, np.float32)
-        qk_norm_rope_bf16(qb, kb, ones, ones, pos, 1e6, 1e-6)
-        bottom_right_varlen(vq, vk, vv, [VERIFY['q']] * 8, [c + VERIFY['q'] for c in vctx], D ** -0.5, np.float32)
-        reps += 1
-        units += 8 * BLOCK + 8 * VERIFY['q']
+        rnd.step()
+        steps += 1
         el = time.perf_counter() - t0
-        if el >= seconds:
+        if el >= seconds or steps >= 60:
             break
-    return units / el, reps, el
+    return rnd.units * steps / el, steps, el, rnd
 
 
 def host_threads():
@@ -904,38 +1081,41 @@ def host_threads():
 
 
 def run_reference(args):
+    """``--impl reference``: the reference's CPU round (CPURound) timed on the host
+    threads, rank 0 only; other ranks exit without work. Each step is one measured
+    sample step; ``ms_per_step`` is that measured time, not an extrapolation."""
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    import numpy as np  # noqa: F401
-    cores = host_threads()
-    os.environ.setdefault('OMP_NUM_THREADS', str(cores))
-    vals = []
+    rnd = CPURound(steps_total=args.warmup + args.steps)
     for _ in range(args.warmup):
-        cpu_sample(seconds=1.0)
-    t_all = 0.0
+        rnd.step()
+    times = []
     for _ in range(args.steps):
-        v, reps, el = cpu_sample(seconds=max(2.0, 20.0 / max(args.steps, 1)))
-        vals.append(v)
-        t_all += el
-    value = statistics.median(vals)
-    units = query_units()
+        t0 = time.perf_counter()
+        rnd.step()
+        times.append(time.perf_counter() - t0)
+    total = sum(times)
+    value = rnd.units * args.steps / total
+    ms = total / args.steps * 1e3
     print(json.dumps(dict(
         impl='reference', metric=METRIC, value=value, unit='query-tok/s', n_gpus=args.gpus, steps=args.steps,
-        warmup=args.warmup, ms_per_step=units / value * 1e3, higher_is_better=True, scaling='weak',
-        vs_baseline=None, dtype='f32', data='synthetic',
-        config=dict(workload='cfg2 draft x5 layers + cfg3 verify x28 layers (CPU oracle port, bounded sample)',
-                    parallelism='host threads'),
-        cpu_baseline=dict(value=value, unit='query-tok/s', cores=cores, kind='port',
-                          sample='per step: 8 cfg2 draft requests x1 layer + 8 cfg3 verify requests x1 layer '
-                                 '(QK-norm/RoPE + bottom-right attention), numpy float32, repeated ~%.0f s'
-                                 % (t_all / max(args.steps, 1))),
+        warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='f32',
+        data='synthetic (seeded N(0,1); config 2 and 3 context draws)',
+        config=dict(workload='cfg2 draft x5 layers + cfg3 verify x28 layers (+ begin/commit): the reference CPU '
+                             'round on a quantile sample of the requests',
+                    parallelism=f'{rnd.threads} host threads, rank 0 only'),
+        sample=dict(query_units_per_step=rnd.units, full_step_query_units=query_units(), fraction=rnd.fraction,
+                    measured_ms_per_sample_step=ms, draft_contexts=rnd.dctx, verify_contexts=rnd.vctx),
+        cpu_baseline=dict(value=value, unit='query-tok/s', cores=rnd.threads, kind='port', sample=rnd.describe()),
         e2e=dict(value=value, unit='query-tok/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
 
 # --------------------------------------------------------------------------- ranks
 def gather_stats(stats, world):
-    """All ranks' stats rows [elapsed_ms, e2e_ms, device_status, launches] -> [world, 4] on the host.
+    """All ranks' stats rows [elapsed_ms, e2e_ms, device_status, launches, ...] -> [world, n]
+    on the host (the main leg adds algorithmic bytes per step, copy-only ms and the
+    verify context tokens as columns 4-6).
 
     The only collective of the benchmark: one all_gather after timing (NCCL on GPUs)."""
     import torch
@@ -970,15 +1150,39 @@ def run_b200(args):
     pkg = importlib.import_module('qwen3-dspark_b200')
     pkg.read_device_status(clear=True)
     if args.case == 'round5':
+        import torch
         res = round5_leg(pkg, device, rank, args.warmup)
         status = pkg.read_device_status(clear=True)
+        # whole job: every rank's tokens over the slowest rank's device time, per loop kind
+        row = torch.tensor([res['generated_tokens'], res['generated_tokens'] - ROUND5['requests'], res['total_s'],
+                            res['graph_total_s'], res['pipelined_total_s'], res['prefill_s'], float(status),
+                            res['rounds']], dtype=torch.float64, device=device)
+        table = gather_stats(row, world)
         if rank == 0:
-            print(json.dumps(_finite(dict(metric='config-5 greedy speculative decode tokens/s per GPU',
-                                          value=max(res['decode_tok_per_s'], res['graph_decode_tok_per_s'],
-                                                    res['pipelined_decode_tok_per_s']), unit='tok/s', n_gpus=world, steps=1,
-                                          warmup=args.warmup, ms_per_step=res['total_s'] * 1e3 / max(res['rounds'], 1),
-                                          higher_is_better=True, dtype='bf16', data='synthetic (random weights)',
-                                          round5=res, device_status=status))), flush=True)
+            gen_all, dec_all = float(table[:, 0].sum()), float(table[:, 1].sum())
+            pre = float(table[:, 5].max())
+            job = {}
+            for name, col in (('eager', 2), ('graph', 3), ('pipelined', 4)):
+                t_max = float(table[:, col].max())
+                job[name] = dict(total_s=t_max, total_tok_per_s=gen_all / t_max,
+                                 decode_tok_per_s=dec_all / max(t_max - pre, 1e-9))
+            best = max(job.values(), key=lambda j: j['total_tok_per_s'])
+            st = 0
+            for x in table[:, 6].tolist():
+                st |= int(x)
+            print(json.dumps(_finite(dict(
+                metric='config-5 greedy speculative decode: generated tokens/s (whole job)',
+                value=best['total_tok_per_s'], unit='tok/s', n_gpus=world, steps=1, warmup=args.warmup,
+                ms_per_step=best['total_s'] * 1e3 / max(res['rounds'], 1), higher_is_better=True, scaling='weak',
+                dtype='bf16', data='synthetic (random weights, uniform-random prompt ids)',
+                config=dict(workload=f'config 5: {ROUND5["requests"]} requests per GPU x {world} GPUs, prompts '
+                                     f'{ROUND5["prompts"]} cycling, {ROUND5["new_tokens"]} new tokens each',
+                            requests_total=ROUND5['requests'] * world, parallelism=f'dp{world}'),
+                job=job, tok_per_s_per_gpu=best['total_tok_per_s'] / world,
+                per_rank=dict(total_s=table[:, 2].tolist(), graph_total_s=table[:, 3].tolist(),
+                              pipelined_total_s=table[:, 4].tolist(), prefill_s=table[:, 5].tolist(),
+                              rounds=table[:, 7].tolist()),
+                round5_rank0=res, device_status=st))), flush=True)
         if world > 1:
             dist.barrier()
             dist.destroy_process_group()
@@ -1105,6 +1309,17 @@ def run_b200(args):
     e_end.record()
     barrier()
     e2e_ms = e_start.elapsed_time(e_end)
+    # ---- the same host copies without kernels, every rank at once (the e2e limiter) ----
+    for _ in range(2):
+        wl.step_copies(host)
+    barrier()
+    c_start, c_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    c_start.record()
+    for _ in range(args.steps):
+        wl.step_copies(host)
+    c_end.record()
+    barrier()
+    copy_ms = c_start.elapsed_time(c_end)
     # config 4 (training layout): its own roofline, reported beside the headline step
     train = train_layout_leg(pkg, device, rank, args.warmup) if args.case == 'round' else None
     status = pkg.read_device_status(clear=True)
@@ -1115,7 +1330,10 @@ def run_b200(args):
         per[kind].append(e0.elapsed_time(e1))
         if kind == 'verify':
             vbytes.append(wl.verify_layer_bytes(ctx))
-    stats = torch.tensor([elapsed_ms, e2e_ms, float(status), float(launches)], dtype=torch.float64, device=device)
+    alg_bytes_step = (wl.draft_layer_bytes() * dl + sum(vbytes) / args.steps) if dl or vl else 0.0
+    h2d_b, d2h_b = wl.host_bytes(host)
+    stats = torch.tensor([elapsed_ms, e2e_ms, float(status), float(launches), alg_bytes_step, copy_ms,
+                          float(sum(wl.verify_ctx))], dtype=torch.float64, device=device)
     allstats = gather_stats(stats, world)
     if rank == 0:
         agg = aggregate_stats(allstats)
@@ -1130,11 +1348,18 @@ def run_b200(args):
         d_ms = statistics.mean(per['draft']) if per['draft'] else float('nan')
         d_achieved = wl.draft_layer_bytes() / (d_ms / 1e3) / 1e9
         h2d, d2h = wl.host_bytes(host)
-        cpu_v, reps, el = (float('nan'), 0, 0.0) if args.no_cpu_baseline else cpu_sample(seconds=12.0)
+        if args.no_cpu_baseline or world > 1:
+            cpu_base = dict(value=None, unit='query-tok/s', cores=None, kind='port',
+                            sample='not run: the CPU leg runs on rank 0 at N=1 only' if world > 1 else 'skipped')
+        else:
+            cpu_v, reps, el, rnd = cpu_sample(seconds=12.0)
+            cpu_base = dict(value=cpu_v, unit='query-tok/s', cores=rnd.threads, kind='port',
+                            sample=f'{reps} measured steps in {el:.1f} s; ' + rnd.describe())
         line = dict(
             metric=METRIC, value=value, unit='query-tok/s', n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=max_ms / args.steps, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',
-            data='synthetic (seeded N(0,1) q/k/v and KV cache; shapes of BASELINE configs 2 and 3)',
+            data='synthetic: config-2 K/V projected by a random-init 0.6B draft from N(0,1) features; '
+                 'config-3 seeded N(0,1) q/k/v and KV cache',
             config=dict(workload=f'cfg2 draft x{dl} layers + cfg3 verify x{vl} layers (+ commit/rollback) per step',
                         draft_requests=DRAFT['requests'], draft_ctx='U[128,4096] seed 1', verify_requests=VERIFY['requests'],
                         verify_ctx='U[256,8192] seed 2', verify_q=VERIFY['q'], heads='16/8', head_dim=D,
@@ -1148,13 +1373,20 @@ def run_b200(args):
             draft_roofline=dict(kernel='draft layer: non-causal attention + split merge', achieved=d_achieved,
                                 frac=d_achieved / hbm, alg_bytes_per_launch=wl.draft_layer_bytes(), avg_launch_ms=d_ms,
                                 traffic=captured_traffic('draft_layer_cfg2')),
-            cpu_baseline=dict(value=cpu_v, unit='query-tok/s', cores=host_threads(), kind='port',
-                              sample=f'{reps} reps of 8 cfg2 draft + 8 cfg3 verify requests x1 layer, numpy float32, '
-                                     f'{el:.1f} s'),
+            cpu_baseline=cpu_base,
             e2e=dict(value=e2e_value, unit='query-tok/s', h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
                      path='B200DraftKernel / B200PersistentTargetKV.verify_layer with pinned host q/k/v in, '
                           'attention outputs out; copies on two copy streams overlapping the kernels'),
-            gpu_launches=agg['launches'], clocks=clocks.summary(), device_status=agg['status'])
+            gpu_launches=agg['launches'], clocks=clocks.summary(), device_status=agg['status'],
+            per_rank=dict(ms_per_step=[x / args.steps for x in allstats[:, 0].tolist()],
+                          e2e_ms_per_step=[x / args.steps for x in allstats[:, 1].tolist()],
+                          copy_only_ms_per_step=[x / args.steps for x in allstats[:, 5].tolist()],
+                          alg_gb_per_step=[x / 1e9 for x in allstats[:, 4].tolist()],
+                          device_gbs=[b / (ms / args.steps) / 1e6 for b, ms in
+                                      zip(allstats[:, 4].tolist(), allstats[:, 0].tolist())],
+                          host_copy_gbs=[(h2d_b + d2h_b) / (ms / args.steps) / 1e6
+                                         for ms in allstats[:, 5].tolist()],
+                          verify_context_tokens=[int(x) for x in allstats[:, 6].tolist()]))
         if train is not None:
             line['train_layout'] = train
         print(json.dumps(_finite(line)), flush=True)

@@ -143,73 +143,33 @@ def test_config3_verify_layer_and_commit_full_shape(pkg, weights, path):
     status_clean(pkg)
 
 
-def build_draft_06b(pkg):
-    """Random-init DSparkDraft at the Qwen3-0.6B draft geometry (hidden 1024, FFN 3072,
-    16/8 heads, 5 layers fed by 5 target layers, theta 1e6), bf16, seeded. A 7-layer
-    target with a small vocabulary supplies the shared embedding (config 2 needs none)."""
-    from transformers import Qwen3Config, Qwen3ForCausalLM
-    torch.manual_seed(1)
-    cfg = Qwen3Config(vocab_size=1024, hidden_size=1024, intermediate_size=3072, num_hidden_layers=7,
-                      num_attention_heads=16, num_key_value_heads=8, head_dim=128, max_position_embeddings=40960,
-                      rms_norm_eps=EPS, tie_word_embeddings=True,
-                      rope_parameters={'rope_type': 'default', 'rope_theta': THETA})
-    with torch.device(dev()), torch.no_grad():
-        target = Qwen3ForCausalLM(cfg).to(torch.bfloat16).eval()
-        spec = pkg.DraftSpec(layer_ids=(0, 1, 2, 3, 4), num_layers=5, block_size=7, markov_rank=64,
-                             mask_token_id=1000)
-        draft = pkg.DSparkDraftModel(target, spec).to(torch.bfloat16).eval()
-        for layer in draft.layers:      # non-trivial norm weights
-            for w in (layer.attention.k_norm.weight, layer.attention.q_norm.weight):
-                w.copy_(1 + 0.1 * torch.randn_like(w))
-        draft.context_norm.weight.copy_(1 + 0.1 * torch.randn_like(draft.context_norm.weight))
-    return draft
-
-
 def test_config2_draft_layers_full_shape(pkg):
+    """The bench's own config-2 inputs (``bench.draft_cfg2_inputs``, rank 0) through
+    ``B200DraftKernel`` for every draft layer, against the oracle."""
     R, B = bench.DRAFT['requests'], bench.BLOCK
-    ctx = bench.contexts(bench.DRAFT)
+    d2 = bench.draft_cfg2_inputs(pkg, dev())
+    ctx = d2['contexts']
     assert (R, B, len(ctx)) == (64, 7, 64) and min(ctx) >= 128 and max(ctx) <= 4096
-    draft = build_draft_06b(pkg)
-    pd = pkg.B200PackedDraft(draft, max_requests=R, context_capacity=max(ctx), slot_capacities=ctx)
+    pd, draft, names = d2['pool'], d2['draft'], d2['names']
     assert pd._fused_append_ready()
-    names = [f'd{i}' for i in range(R)]
-    for r in names:
-        pd.add_request(r)
-    gen = torch.Generator(device=dev())
-    gen.manual_seed(1)
-    bf = torch.bfloat16
-    feats = torch.randn((1, sum(ctx), 5 * 1024), generator=gen, device=dev(), dtype=bf)
-    chunks, o = {}, 0
-    for r, c in zip(names, ctx):
-        chunks[r] = feats[:, o:o + c]
-        o += c
-    pd.append_committed(chunks)
     torch.cuda.synchronize()
     status_clean(pkg)
-    # the block rows: q/k/v of N(0,1) block states at positions c..c+6, per draft layer
-    block_states = torch.randn((1, R * B, 1024), generator=gen, device=dev(), dtype=bf)
-    bpos = torch.cat([torch.arange(c, c + B, device=dev()) for c in ctx])
     kernel = pkg.B200DraftKernel(dev())
     qlens, klens = [B] * R, [c + B for c in ctx]
-    layout = pkg.PackedLayout.from_lengths(qlens, klens, dev())
-    with torch.no_grad():
-        cos, sin = draft.rotary(block_states, bpos[None])
-    for li, layer in enumerate(draft.layers):
-        att = layer.attention
-        with torch.no_grad():
-            q, bk, bv = pd._project(att, block_states, cos, sin)
-        ks, vs = [], []
-        for r, c, i in zip(names, ctx, range(R)):
-            r0 = pd.slot_rows[pd._slots[r]]
-            ks += [pd.pool_k[li][r0:r0 + c], bk[i * B:(i + 1) * B]]
-            vs += [pd.pool_v[li][r0:r0 + c], bv[i * B:(i + 1) * B]]
-        k, v = torch.cat(ks).contiguous(), torch.cat(vs).contiguous()
-        q = q.contiguous()
-        out = kernel(q, k, v, layout, scale=I.SCALE)
+    for li in range(len(draft.layers)):
+        q, k, v = d2['q'][li], d2['k'][li], d2['v'][li]
+        out = kernel(q, k, v, d2['layout'], scale=I.SCALE)
         torch.cuda.synchronize()
         ref = noncausal_varlen(bf16_bits_to_f32(bits(q)), bf16_bits_to_f32(bits(k)), bf16_bits_to_f32(bits(v)),
                                qlens, klens, I.SCALE)
         assert_bf16_close(out, ref)
+        # the packed keys are each request's pool rows followed by its block rows
+        o = 0
+        for r, c in zip(names[:4], ctx[:4]):
+            r0 = pd.slot_rows[pd._slots[r]]
+            assert torch.equal(k[o:o + c].view(torch.int16), pd.pool_k[li][r0:r0 + c].view(torch.int16))
+            o += c + B
+    feats = d2['features']
     status_clean(pkg)
     # pool K/V of a seeded sample of context rows against the oracle's projection chain:
     # context = bf16(context_norm(bf16(fc(features)))) is the library's input, then per layer
