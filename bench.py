@@ -876,14 +876,15 @@ def stochastic_leg(pkg, device, warmup, iters=10, r=128, n=6, vocab=151936, temp
 ROUND5 = dict(requests=32, prompts=(64, 256, 2048), new_tokens=128, seed=5)
 
 
-def round5_leg(pkg, device, rank, warmup):
+def round5_leg(pkg, device, rank, warmup, pipelined_only=False):
     """Config 5: a full greedy speculative round loop on a Qwen3-0.6B-shaped target (28
     layers, hidden 1024, FFN 3072, vocab 151936, tied embeddings) and the 5-layer DSpark
     draft of the 0.6B config (layers 1/7/14/21/26, block 7, markov_rank 256), random
     weights (seeded), bf16, 32 requests with prompts cycling 64/256/2048 tokens, 128 new
     tokens each. Everything the round needs runs on this library: fused verify layers,
     commit/rollback, draft attention over the paged pool, the fused Markov proposal and
-    on-device acceptance; the GEMMs are the library GEMMs of torch."""
+    on-device acceptance; the GEMMs are the library GEMMs of torch. ``pipelined_only``
+    warms and times only the pipelined loop (the default bench line's config-5 leg)."""
     import numpy as np
     import torch
     from transformers import Qwen3Config, Qwen3ForCausalLM
@@ -912,10 +913,12 @@ def round5_leg(pkg, device, rank, warmup):
             target.remove_request(r)
             pdraft.remove_request(r)
 
-    for w in range(max(1, warmup // 3)):                  # warm-up: library handles, allocator
-        ps = prompts(f'w{w}_')
-        pkg.speculative_greedy(target, pdraft, ps, 4)
-        release(ps)
+    if not pipelined_only:
+        for w in range(max(1, warmup // 3)):              # warm-up: library handles, allocator
+            ps = prompts(f'w{w}_')
+            pkg.speculative_greedy(target, pdraft, ps, 4)
+            release(ps)
+
     def device_timer():
         """(start, stop): CUDA events on the current stream; stop() synchronises and returns s."""
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -939,6 +942,16 @@ def round5_leg(pkg, device, rank, warmup):
         release(ps)
         return out, rounds, dt
 
+    if pipelined_only:
+        pkg.speculative_greedy_pipelined(target, pdraft, prompts('pw'), 4)   # capture and warm the loop
+        release([f'pw{i}' for i in range(len(lens))])
+        out_p, rounds_p, total_p = timed_loop('q', 'pipelined')
+        generated = sum(len(v) for v in out_p.values())
+        return dict(workload=f'Qwen3-0.6B-shaped target + 5-layer DSpark draft (random weights, bf16), '
+                             f'{ROUND5["requests"]} requests, prompts {ROUND5["prompts"]} cycling, '
+                             f'{ROUND5["new_tokens"]} new tokens each, speculative_greedy_pipelined',
+                    generated_tokens=generated, rounds=len(rounds_p), total_s=total_p,
+                    total_tok_per_s=generated / total_p)
     out, rounds, total_s = timed_loop('m', False)
     pkg.speculative_greedy(target, pdraft, prompts('gw'), 4, graph=True)   # capture + warm the replayed path
     release([f'gw{i}' for i in range(len(lens))])
@@ -1115,7 +1128,7 @@ def run_reference(args):
 def gather_stats(stats, world):
     """All ranks' stats rows [elapsed_ms, e2e_ms, device_status, launches, ...] -> [world, n]
     on the host (the main leg adds algorithmic bytes per step, copy-only ms and the
-    verify context tokens as columns 4-6).
+    verify context tokens as columns 4-6, config 5 tokens and seconds as 7-8).
 
     The only collective of the benchmark: one all_gather after timing (NCCL on GPUs)."""
     import torch
@@ -1322,6 +1335,8 @@ def run_b200(args):
     copy_ms = c_start.elapsed_time(c_end)
     # config 4 (training layout): its own roofline, reported beside the headline step
     train = train_layout_leg(pkg, device, rank, args.warmup) if args.case == 'round' else None
+    # config 5 at its stated shape: 32 requests per GPU through the pipelined greedy loop
+    r5 = round5_leg(pkg, device, rank, args.warmup, pipelined_only=True) if args.case == 'round' else None
     status = pkg.read_device_status(clear=True)
     # per-layer event durations inside the timed region
     per = {'draft': [], 'verify': []}
@@ -1333,7 +1348,8 @@ def run_b200(args):
     alg_bytes_step = (wl.draft_layer_bytes() * dl + sum(vbytes) / args.steps) if dl or vl else 0.0
     h2d_b, d2h_b = wl.host_bytes(host)
     stats = torch.tensor([elapsed_ms, e2e_ms, float(status), float(launches), alg_bytes_step, copy_ms,
-                          float(sum(wl.verify_ctx))], dtype=torch.float64, device=device)
+                          float(sum(wl.verify_ctx)), float(r5['generated_tokens'] if r5 else 0),
+                          float(r5['total_s'] if r5 else 0)], dtype=torch.float64, device=device)
     allstats = gather_stats(stats, world)
     if rank == 0:
         agg = aggregate_stats(allstats)
@@ -1389,6 +1405,11 @@ def run_b200(args):
                           verify_context_tokens=[int(x) for x in allstats[:, 6].tolist()]))
         if train is not None:
             line['train_layout'] = train
+        if r5 is not None:
+            gen_all, t_max = float(allstats[:, 7].sum()), float(allstats[:, 8].max())
+            line['round5'] = dict(workload=r5['workload'] + f' per GPU x {world} GPUs',
+                                  generated_tok_per_s=gen_all / t_max, tok_per_s_per_gpu=gen_all / t_max / world,
+                                  total_s=t_max, rounds=r5['rounds'], timing='CUDA events, slowest rank')
         print(json.dumps(_finite(line)), flush=True)
     if world > 1:
         dist.barrier()
