@@ -1071,6 +1071,33 @@ class CPURound:
                 f'{self.units} of the full step\'s {query_units()} query units ({self.fraction:.4f})')
 
 
+def cpu_train_layout(seconds=3.0, threads=None):
+    """Config 4 on the host as the reference's training forward runs it (oracle/torch_cpu.py:
+    `block_mask` + dense-mask SDPA per sequence, float32), the whole workload per call:
+    8 sequences x 2048 context, 32 sorted anchors each, block 7. Returns (query-tok/s, calls,
+    seconds)."""
+    import numpy as np
+    import torch
+    from oracle.torch_cpu import training_layout_sdpa
+    if threads is None:
+        set_host_threads()
+    g = np.random.Generator(np.random.PCG64(TRAIN['seed'] * 1000))
+    S, C, N = TRAIN['seqs'], TRAIN['ctx'], TRAIN['anchors']
+    anchors = [sorted(g.choice(C - 1, N, replace=False).tolist()) for _ in range(S)]
+    gen = torch.Generator().manual_seed(TRAIN['seed'])
+    nq, nk = S * N * BLOCK, S * (C + N * BLOCK)
+    q, k, v = (torch.randn((n, h, D), generator=gen) for n, h in ((nq, HQ), (nk, HKV), (nk, HKV)))
+    training_layout_sdpa(q, k, v, [C] * S, anchors, BLOCK)
+    calls, t0 = 0, time.perf_counter()
+    while True:
+        training_layout_sdpa(q, k, v, [C] * S, anchors, BLOCK)
+        calls += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return nq * calls / el, calls, el
+
+
 def cpu_sample(seconds=12.0):
     """The GPU arm's ``cpu_baseline`` leg: CPURound steps after one warm-up step until
     ``seconds`` of host time. Returns (query-tok/s, steps, seconds, CPURound)."""
@@ -1121,6 +1148,9 @@ def run_reference(args):
         sample=dict(query_units_per_step=rnd.units, full_step_query_units=query_units(), fraction=rnd.fraction,
                     measured_ms_per_sample_step=ms, draft_contexts=rnd.dctx, verify_contexts=rnd.vctx),
         cpu_baseline=dict(value=value, unit='query-tok/s', cores=rnd.threads, kind='port', sample=rnd.describe()),
+        train_layout_cpu=dict(zip(('query_tok_per_s', 'calls', 'seconds'), cpu_train_layout(threads=rnd.threads)),
+                              workload='config 4, whole workload per call: block_mask + dense SDPA per sequence, '
+                                       'float32'),
         e2e=dict(value=value, unit='query-tok/s', h2d_bytes_per_step=0, d2h_bytes_per_step=0))), flush=True)
 
 
@@ -1371,6 +1401,11 @@ def run_b200(args):
             cpu_v, reps, el, rnd = cpu_sample(seconds=12.0)
             cpu_base = dict(value=cpu_v, unit='query-tok/s', cores=rnd.threads, kind='port',
                             sample=f'{reps} measured steps in {el:.1f} s; ' + rnd.describe())
+            if train is not None:
+                tv, tc, te = cpu_train_layout(threads=rnd.threads)
+                train['cpu_query_tok_per_s'] = tv
+                train['cpu_sample'] = (f'{tc} calls of the whole config-4 workload in {te:.1f} s on {rnd.threads} '
+                                       'threads: block_mask + dense SDPA per sequence, float32')
         line = dict(
             metric=METRIC, value=value, unit='query-tok/s', n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=max_ms / args.steps, higher_is_better=True, scaling='weak', vs_baseline=None, dtype='bf16',

@@ -20,7 +20,9 @@ order so that its time is the reference's time on the same host threads:
   per request with the bottom-right boolean mask);
 * per round: ``begin`` (persistent_target_kv.py:369-415: host index lists for the
   bucket, uploaded with ``torch.tensor``) and ``commit`` (463-491: per-request copies of
-  the accepted scratch prefix into every layer's resident rows).
+  the accepted scratch prefix into every layer's resident rows);
+* the training layout (config 4): ``block_mask`` and the dense-mask SDPA of
+  ``DraftAttention.forward`` per sequence (dspark_qwen/model.py:12-19,47-61).
 
 The one departure is storage: the reference's resident cache is one dense
 ``[layers, slots, context_capacity, heads, dim]`` tensor; this store gives each slot
@@ -85,6 +87,37 @@ def apply_rope(x, cos, sin):
     half = x.shape[-1] // 2
     rotated = torch.cat((-x[..., half:], x[..., :half]), dim=-1)
     return x * cos[:, None] + rotated * sin[:, None]
+
+
+def block_mask(anchors, block_size, context_length):
+    """model.py:12-19: context j < anchor of the query's block; the own block is
+    bidirectional; [1, 1, n * bs, ctx + n * bs] booleans."""
+    n = anchors.numel()
+    q_block = torch.arange(n * block_size) // block_size
+    ctx = torch.arange(context_length)
+    visible_context = ctx[None, :] < anchors[q_block, None]
+    visible_block = q_block[:, None] == q_block[None, :]
+    return torch.cat((visible_context, visible_block), dim=-1)[None, None]
+
+
+def training_layout_sdpa(query, key, value, context_lengths, anchors, block_size):
+    """The training layout's attention as `DraftAttention.forward` runs it per sequence
+    (model.py:47-61): K/V repeated per GQA group, one dense `block_mask` SDPA with the
+    default 1/sqrt(d) scale; sequences packed back to back never see each other."""
+    rows, qo, ko = [], 0, 0
+    for ctx, anc in zip(context_lengths, anchors):
+        nq = len(anc) * block_size
+        nk = ctx + nq
+        mask = block_mask(torch.as_tensor(anc, dtype=torch.long), block_size, ctx)
+        groups = query.shape[1] // key.shape[1]
+        q = query[qo:qo + nq].transpose(0, 1)[None]
+        k = key[ko:ko + nk].transpose(0, 1)[None].repeat_interleave(groups, dim=1)
+        v = value[ko:ko + nk].transpose(0, 1)[None].repeat_interleave(groups, dim=1)
+        out = F.scaled_dot_product_attention(q, k, v, attn_mask=mask, dropout_p=0.0, is_causal=False)
+        rows.append(out[0].transpose(0, 1))
+        qo += nq
+        ko += nk
+    return torch.cat(rows)
 
 
 class VerifyRoundCPU:

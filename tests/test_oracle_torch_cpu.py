@@ -4,8 +4,8 @@ import numpy as np
 import torch
 
 import inputs as I
-from oracle.torch_cpu import (VerifyRoundCPU, apply_rope, noncausal_varlen_sdpa, persistent_sdpa, qwen3_rms_norm,
-                              rotary_cos_sin)
+from oracle.torch_cpu import (VerifyRoundCPU, apply_rope, block_mask, noncausal_varlen_sdpa, persistent_sdpa,
+                              qwen3_rms_norm, rotary_cos_sin, training_layout_sdpa)
 
 
 def t(x):
@@ -112,3 +112,20 @@ def test_verify_layer_matches_the_numpy_oracle():
     for i, c in enumerate(ctx):
         np.testing.assert_array_equal(keys[o:o + c], store.keys[0, store.offsets[i]:store.offsets[i] + c].numpy())
         o += c + 7
+
+
+def test_training_layout_equals_reference_fixtures(golden):
+    """block_mask's truth table and the packed training-layout attention, both made by the
+    reference's own functions."""
+    m = block_mask(torch.tensor([2, 4]), 3, 7)[0, 0].numpy()
+    np.testing.assert_array_equal(m, golden('block_mask_truth')['mask'])
+    g = I.rng(3)
+    ctxs = [c for c, _ in I.TRAIN_SEQS]
+    anchors = [a for _, a in I.TRAIN_SEQS]
+    nq = sum(len(a) * I.BLOCK for a in anchors)
+    nk = sum(c + len(a) * I.BLOCK for c, a in I.TRAIN_SEQS)
+    q = I.normal(g, (nq, I.HQ, I.D), True)
+    k = I.normal(g, (nk, I.HKV, I.D), True)
+    v = I.normal(g, (nk, I.HKV, I.D), True)
+    out = training_layout_sdpa(t(q), t(k), t(v), ctxs, anchors, I.BLOCK).numpy()
+    np.testing.assert_allclose(out, golden('train_layout')['output'], atol=1e-6, rtol=1e-6)
