@@ -710,6 +710,70 @@ def markov_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, hdim
                 peak_source=kind)
 
 
+def propose_leg(pkg, device, warmup, iters=10, r=64, vocab=151936, rank=256, temperature=0.8):
+    """Stochastic Markov proposal of one draft block (config 2's 64 requests, Qwen3 vocab,
+    markov_rank 256, block 7, T = 0.8): per position the embedding gather and projection
+    GEMM (torch), then one ``stochastic_propose`` launch (x = base + proj, the float64 law
+    written out, the CDF draw) vs the reference's formula in torch on the same inputs
+    (``float64_law`` + ``sample_rows``, DSparkDraft._sample_stochastic batched). Bytes
+    per block: 7 x (projection weight + per request two bf16 rows read and a float64
+    law row written)."""
+    import torch
+    gen = torch.Generator(device=device)
+    gen.manual_seed(13)
+    bf = torch.bfloat16
+    proj = torch.nn.Linear(rank, vocab, bias=False, device=device, dtype=bf)
+    proj.weight.data.copy_(torch.randn(vocab, rank, device=device, dtype=bf, generator=gen) * 0.05)
+    emb = torch.nn.Embedding(vocab, rank, device=device, dtype=bf)
+    emb.weight.data.copy_(torch.randn(vocab, rank, device=device, dtype=bf, generator=gen) * 0.5)
+    base = torch.randn(r, BLOCK, vocab, device=device, dtype=bf, generator=gen) * 2
+    anchors = torch.randint(0, vocab, (r,), device=device, generator=gen)
+    u = torch.rand(r, BLOCK, device=device, dtype=torch.float64, generator=gen)
+    laws = torch.empty(r, BLOCK, vocab, device=device, dtype=torch.float64)
+    idx = torch.arange(r, device=device, dtype=torch.int32)
+
+    def fused():
+        prev = anchors
+        for k in range(BLOCK):
+            pj = proj(emb(prev)).contiguous()
+            prev, _ = pkg.stochastic_propose(base[:, k], idx, pj, temperature, u[:, k].contiguous(), laws[:, k])
+        return prev
+
+    def torch_formula():
+        prev = anchors
+        for k in range(BLOCK):
+            law = pkg.float64_law(base[:, k] + proj(emb(prev)), temperature)
+            prev = pkg.sample_rows(law, u[:, k])
+            laws[:, k].copy_(law)
+        return prev
+
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed(fn):
+        for _ in range(warmup):
+            fn()
+        pairs = []
+        for _ in range(iters):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            pairs.append((a, b))
+        torch.cuda.synchronize(device)
+        return statistics.median(a.elapsed_time(b) for a, b in pairs)
+
+    assert torch.equal(fused(), torch_formula())          # same final tokens on these inputs
+    ms, torch_ms = timed(fused), timed(torch_formula)
+    nbytes = BLOCK * (vocab * rank * 2 + r * vocab * (2 + 2 + 8))
+    hbm, kind = peaks()
+    return dict(workload=f'{r} requests x block {BLOCK}, vocab {vocab}, markov_rank {rank}, T {temperature}, '
+                         'float64 laws written out',
+                ms_per_block=ms, torch_formula_ms_per_block=torch_ms, speedup=torch_ms / ms, alg_bytes=nbytes,
+                achieved_gbs=nbytes / (ms / 1e3) / 1e9, frac=nbytes / (ms / 1e3) / 1e9 / hbm, peak_gbs=hbm,
+                peak_source=kind)
+
+
 def append_leg(pkg, device, warmup, iters=10):
     """Draft-context append at the 0.6B draft geometry (hidden 1024, five draft layers,
     five captured target layers of features; random weights, bf16): every layer's
@@ -1270,6 +1334,19 @@ def run_b200(args):
             dist.barrier()
             dist.destroy_process_group()
         return
+    if args.case == 'propose':
+        res = propose_leg(pkg, device, args.warmup, iters=args.steps)
+        status = pkg.read_device_status(clear=True)
+        if rank == 0:
+            print(json.dumps(_finite(dict(metric='stochastic Markov proposal per draft block',
+                                          value=res['ms_per_block'], unit='ms', n_gpus=world, steps=args.steps,
+                                          warmup=args.warmup, ms_per_step=res['ms_per_block'],
+                                          higher_is_better=False, dtype='f64', data='synthetic', propose=res,
+                                          device_status=status))), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.case == 'accept':
         res = accept_leg(pkg, device, args.warmup, iters=args.steps)
         status = pkg.read_device_status(clear=True)
@@ -1457,7 +1534,7 @@ def main():
     ap.add_argument('--steps', type=int, default=30)
     ap.add_argument('--warmup', type=int, default=5)
     ap.add_argument('--impl', default='b200', choices=['b200', 'reference'])
-    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'append', 'round5', 'graph5', 'stochastic'])
+    ap.add_argument('--case', default='round', choices=['round', 'draft', 'verify', 'train', 'graph', 'accept', 'markov', 'propose', 'append', 'round5', 'graph5', 'stochastic'])
     ap.add_argument('--layers', type=int, default=None, help='cap the layer count of each selected path')
     ap.add_argument('--no-cpu-baseline', action='store_true', help='skip the timed CPU oracle leg')
     args = ap.parse_args()

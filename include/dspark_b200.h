@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define DSPARK_ABI_VERSION 17
+#define DSPARK_ABI_VERSION 18
 
 #define DSPARK_OK 0
 #define DSPARK_ERR_INVALID_ARGUMENT 1
@@ -369,6 +369,28 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
  * logits (the table first), two for f32.
  */
 size_t dspark_stochastic_scratch_bytes(int rows);
+
+/*
+ * Stochastic draft proposal of one Markov position for `rows` requests
+ * (DSparkDraft._sample_stochastic, dspark_qwen/model.py:193-208, batched over
+ * requests as packed_sampling.py:73-94 does; bf16 logits). Launch row r reads
+ * request row i = row_index[r] (row_index NULL: i = r): its LM-head row at
+ * base + i * ld_base and its Markov projection row at proj + r * ld_proj (bf16
+ * elements); x = bf16(base + proj) as torch adds them. It writes the float64 law
+ * q = softmax(x / T) normalised once more (logits_to_probabilities,
+ * tensor_sampling.py:38-51) to law + i * ld_law, draws one token with uniforms[r]
+ * by the strict CDF rule, the last positive index past the end
+ * (sample_categorical, tensor_sampling.py:77-84), into tokens[r], and sets
+ * status[r] to 0, or 1 when x / T is not finite. Scratch of
+ * dspark_propose_scratch_bytes() bytes (the x / T table of the 65536 bf16 bit
+ * patterns, rebuilt per call), 16-byte aligned; law 8-byte aligned. rows == 0
+ * launches nothing. Device memory.
+ */
+size_t dspark_propose_scratch_bytes(void);
+int dspark_stochastic_propose(const void* base, long long ld_base, const int32_t* row_index, const void* proj,
+                              long long ld_proj, int vocab, double temperature, const double* uniforms, int rows,
+                              double* law, long long ld_law, long long* tokens, int32_t* status, void* scratch,
+                              size_t scratch_bytes, cudaStream_t stream);
 int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vocab, double temperature,
                              int target_rows, const double* q, int draft_rows, const long long* tokens,
                              const int32_t* cu_n, int num_requests, const double* uniforms, int u_stride,

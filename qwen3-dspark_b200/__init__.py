@@ -16,7 +16,7 @@ from . import _lib
 from .build import LIB_PATH, build
 from .kernels import (add_rms_norm, BACKEND, CAPACITY_BACKEND, DRAFT_BACKEND, SCALE, TRAIN_BACKEND, B200CapacityKernel,
                       B200DraftKernel, B200TrainingLayoutKernel, B200VarlenKernel, draft_append, float64_law, greedy_accept, markov_greedy, qk_norm_rope, rms_norm, silu_mul,
-                      sample_rows, stochastic_accept,
+                      sample_rows, stochastic_accept, stochastic_propose,
                       runtime_identity, segment_attention)
 from .kv_store import B200PersistentTargetKV, Slot, Transaction, rope_inv_freq
 from .layout import PackedLayout, PersistentAttentionLayout, TrainingLayout
@@ -44,5 +44,5 @@ __all__ = ['add_rms_norm', 'BACKEND', 'CAPACITY_BACKEND', 'DRAFT_BACKEND', 'SCAL
            'B200DraftKernel', 'B200TrainingLayoutKernel', 'B200VarlenKernel', 'B200PersistentTargetKV', 'LIB_PATH',
            'PackedLayout', 'PersistentAttentionLayout', 'TrainingLayout', 'Slot', 'Transaction', 'B200PackedDraft',
            'DSparkDraftModel', 'DraftSpec', 'B200Qwen3Target', 'speculative_greedy', 'speculative_greedy_pipelined', 'speculative_sample', 'accept_greedy', 'build',
-           'draft_append', 'float64_law', 'greedy_accept', 'markov_greedy', 'qk_norm_rope', 'rms_norm', 'silu_mul', 'sample_rows', 'stochastic_accept', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
+           'draft_append', 'float64_law', 'greedy_accept', 'markov_greedy', 'qk_norm_rope', 'rms_norm', 'silu_mul', 'sample_rows', 'stochastic_accept', 'stochastic_propose', 'launch_count', 'load_library', 'read_device_status', 'rope_inv_freq', 'runtime_identity',
            'segment_attention']

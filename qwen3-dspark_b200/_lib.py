@@ -38,6 +38,9 @@ SIGNATURES = {
     'dspark_train_plan': (_i, [_i, _vp, _vp, _vp, _i, _i, _vp, _ll, ctypes.POINTER(_ll)]),
     'dspark_row_argmax': (_i, [_vp, _ll, _i, _i, _i, _vp, _vp]),
     'dspark_markov_scratch_bytes': (_sz, []),
+    'dspark_propose_scratch_bytes': (_sz, []),
+    'dspark_stochastic_propose': (_i, [_vp, _ll, _vp, _vp, _ll, _i, ctypes.c_double, _vp, _i, _vp, _ll, _vp, _vp,
+                                       _vp, _sz, _vp]),
     'dspark_set_grid_barrier_timeout': (_i, [ctypes.c_ulonglong]),
     'dspark_markov_step': (_i, [_vp, _vp, _i, _i, _vp, _ll, _i, _vp, _ll, _vp, _i, _vp, _f, _vp, _vp, _ll, _i,
                                 _vp, _vp]),
@@ -73,7 +76,7 @@ def load_library(path=LIB_PATH):
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.dspark_abi_version() != 17:
+        if lib.dspark_abi_version() != 18:
             raise RuntimeError('dspark B200 library ABI version mismatch')
         _lib = lib
         return lib

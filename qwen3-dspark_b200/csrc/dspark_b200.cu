@@ -865,6 +865,41 @@ int dspark_stochastic_accept(const void* logits, long long ld, int dtype, int vo
   return launch_status();
 }
 
+size_t dspark_propose_scratch_bytes(void) { return sampling::kScaledTableSize * sizeof(double); }
+
+int dspark_stochastic_propose(const void* base, long long ld_base, const int32_t* row_index, const void* proj,
+                              long long ld_proj, int vocab, double temperature, const double* uniforms, int rows,
+                              double* law, long long ld_law, long long* tokens, int32_t* status, void* scratch,
+                              size_t scratch_bytes, cudaStream_t stream) {
+  if (rows < 0 || vocab < 1 || ld_base < vocab || ld_proj < vocab || ld_law < vocab || !(temperature > 0.0) ||
+      !std::isfinite(temperature))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  if (rows == 0) return DSPARK_OK;
+  if (!base || !proj || !uniforms || !law || !tokens || !status || !scratch ||
+      scratch_bytes < dspark_propose_scratch_bytes() || !aligned(scratch, 16) || !aligned(law, 8))
+    return DSPARK_ERR_INVALID_ARGUMENT;
+  double* table = static_cast<double*>(scratch);
+  sampling::scaled_table_kernel<<<sampling::kScaledTableSize / 256, 256, 0, stream>>>(table, temperature);
+  int st = launch_status();
+  if (st != DSPARK_OK) return st;
+  sampling::ProposeParams p{};
+  p.base = static_cast<const unsigned short*>(base);
+  p.ld_base = ld_base;
+  p.row_index = row_index;
+  p.proj = static_cast<const unsigned short*>(proj);
+  p.ld_proj = ld_proj;
+  p.vocab = vocab;
+  p.scaled = table;
+  p.uniforms = uniforms;
+  p.law = law;
+  p.ld_law = ld_law;
+  p.tokens = tokens;
+  p.status = status;
+  p.rows = rows;
+  sampling::propose_law_kernel<<<rows, sampling::kThreads, 0, stream>>>(p);
+  return launch_status();
+}
+
 int dspark_train_plan(int num_seqs, const int32_t* ctx_len, const int32_t* num_blocks, const int32_t* anchors,
                       int block_size, int grid_limit, int32_t* plan, long long plan_capacity, long long* plan_words) {
   using namespace train;

@@ -378,5 +378,174 @@ __global__ void __launch_bounds__(kThreads) stochastic_accept_kernel(const Param
   }
 }
 
+// ---------------------------------------------------------------------------
+// Draft proposal of one Markov position (DSparkDraft._sample_stochastic,
+// dspark_qwen/model.py:193-208): per request the bf16 logits x = base + proj (the
+// LM-head row of the position plus the Markov projection of the previous token's
+// embedding, rounded to bf16 as torch adds them), the float64 law
+// q = softmax(x / T) normalised once more (logits_to_probabilities,
+// tensor_sampling.py:38-51) written out for the later acceptance test, and one
+// token drawn by the strict CDF rule with the last positive index past the end
+// (sample_categorical, tensor_sampling.py:77-84). One CTA per request row, each
+// thread owning one contiguous chunk of the row: the max of x / T, the sum of
+// exp(x / T - max) (the exponentials stored in the law row), the sum of the
+// normalised weights, then the law itself with each chunk's sum; the chunk
+// holding the crossing of u scans its values in order.
+struct ProposeParams {
+  const unsigned short* base;   // bf16 rows: request r's at base + row_index[r] * ld_base
+  long long ld_base;
+  const int* row_index;         // [rows]: the request row each launch row reads and writes
+  const unsigned short* proj;   // bf16 [rows, ld_proj]: Markov projection of launch row r
+  long long ld_proj;
+  int vocab;
+  const double* scaled;         // x / T for the 65536 bf16 bit patterns
+  const double* uniforms;       // [rows]
+  double* law;                  // request r's law at law + row_index[r] * ld_law
+  long long ld_law;
+  long long* tokens;            // [rows]
+  int* status;                  // [rows]: kOk or kBadLogits (non-finite x / T)
+  int rows;
+};
+
+// bf16 bits of x = bf16(float(a) + float(b)), the rounding of torch's bf16 add.
+__device__ __forceinline__ unsigned short add_bf16_bits(unsigned short a, unsigned short b) {
+  const float f = __bfloat162float(__ushort_as_bfloat16(a)) + __bfloat162float(__ushort_as_bfloat16(b));
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+__global__ void __launch_bounds__(kThreads) propose_law_kernel(const ProposeParams p) {
+  __shared__ double dscr[kThreads / 32];
+  __shared__ int iscr[kThreads / 32];
+  __shared__ double chunk_sum[kThreads];
+  const int r = blockIdx.x;
+  if (r >= p.rows) return;
+  const long long row = p.row_index ? p.row_index[r] : r;
+  const unsigned short* br = p.base + row * p.ld_base;
+  const unsigned short* pr = p.proj + static_cast<long long>(r) * p.ld_proj;
+  double* law = p.law + row * p.ld_law;
+  // Every pass walks the row coalesced, 8 consecutive elements per thread per step
+  // (one 16-byte load of each bf16 row, their 8 table reads in flight together); the
+  // exponentials are formed again in each pass rather than stored and re-read.
+  const bool vec = ((reinterpret_cast<uintptr_t>(br) | reinterpret_cast<uintptr_t>(pr)) & 15) == 0;
+  auto scaled8 = [&](int i0, double (&x)[8]) {      // x / T of elements i0 .. i0 + 7 (0 past the row)
+    if (vec && i0 + 8 <= p.vocab) {
+      const uint4 ra = __ldg(reinterpret_cast<const uint4*>(br + i0));
+      const uint4 rb = __ldg(reinterpret_cast<const uint4*>(pr + i0));
+      const unsigned short* ha = reinterpret_cast<const unsigned short*>(&ra);
+      const unsigned short* hb = reinterpret_cast<const unsigned short*>(&rb);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __ldg(p.scaled + add_bf16_bits(ha[e], hb[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = i0 + e < p.vocab ? p.scaled[add_bf16_bits(br[i0 + e], pr[i0 + e])] : 0.0;
+    }
+  };
+  constexpr int kTile = kThreads * 8;
+  int bad = 0;
+  double m = -INFINITY;
+  for (int i0 = threadIdx.x * 8; i0 < p.vocab; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) {
+        if (!isfinite(x[e])) bad = 1;
+        m = x[e] > m ? x[e] : m;
+      }
+  }
+  bad = block_reduce(bad, iscr, OrOp());
+  m = block_reduce(m, dscr, MaxOp());
+  double sum = 0.0;
+  for (int i0 = threadIdx.x * 8; i0 < p.vocab; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) sum += exp(x[e] - m);
+  }
+  sum = block_reduce(sum, dscr, SumOp());
+  double sum2 = 0.0;
+  for (int i0 = threadIdx.x * 8; i0 < p.vocab; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) sum2 += exp(x[e] - m) / sum;
+  }
+  sum2 = block_reduce(sum2, dscr, SumOp());
+  // The law, tile by tile in index order: each thread's 8 values, a block-wide scan
+  // of their sums (thread order = index order inside a tile) and the CDF carried
+  // across tiles; the first element whose CDF exceeds u is the draw.
+  const double u = p.uniforms[r];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool law16 = (reinterpret_cast<uintptr_t>(law) & 15) == 0;   // 16-byte stores only when aligned
+  double carry = 0.0;
+  int found = p.vocab, last_pos = -1;
+  for (int t0 = 0; t0 < p.vocab; t0 += kTile) {
+    const int i0 = t0 + threadIdx.x * 8;
+    double v[8], seg = 0.0;
+    if (i0 < p.vocab) {
+      double x[8];
+      scaled8(i0, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] = i0 + e < p.vocab ? exp(x[e] - m) / sum / sum2 : 0.0;
+        seg += v[e];
+        if (v[e] > 0.0) last_pos = i0 + e;
+      }
+      if (law16 && i0 + 8 <= p.vocab) {
+#pragma unroll
+        for (int e = 0; e < 8; e += 2) *reinterpret_cast<double2*>(law + i0 + e) = make_double2(v[e], v[e + 1]);
+      } else {
+        for (int e = 0; i0 + e < p.vocab; ++e) law[i0 + e] = v[e];
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.0;
+    }
+    // inclusive scan of seg over the CTA's threads
+    double incl = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) chunk_sum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      double w = lane < kThreads / 32 ? chunk_sum[lane] : 0.0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      chunk_sum[32 + lane] = w;                       // inclusive warp prefixes
+    }
+    __syncthreads();
+    const double excl = (warp > 0 ? chunk_sum[32 + warp - 1] : 0.0) + incl - seg;
+    double cdf = carry + excl;
+    if (found == p.vocab && cdf + seg > u - 1e-12) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        cdf += v[e];
+        if (cdf > u && i0 + e < p.vocab) {
+          found = i0 + e;
+          break;
+        }
+      }
+    }
+    carry += chunk_sum[32 + kThreads / 32 - 1];
+    __syncthreads();                                  // chunk_sum is rewritten by the next tile
+  }
+  found = block_reduce(found, iscr, MinIntOp());
+  last_pos = block_reduce(last_pos, iscr, MaxIntOp());
+  if (threadIdx.x == 0) {
+    // a row without positive mass (non-finite logits) gets token 0 and a bad status,
+    // so that no out-of-range index reaches the next position's embedding gather
+    p.tokens[r] = found < p.vocab ? found : (last_pos >= 0 ? last_pos : 0);
+    p.status[r] = bad || last_pos < 0 ? kBadLogits : kOk;
+  }
+}
+
 }  // namespace sampling
 }  // namespace dspark

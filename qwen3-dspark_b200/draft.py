@@ -26,7 +26,7 @@ from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
 
 from .kernels import (HEAD_DIM, HKV, HQ, add_rms_norm, draft_append, rope_cache, float64_law, markov_greedy, merged_mlp_ready, qk_norm_rope,
-                      rms_norm, sample_rows, segment_attention, silu_mul)
+                      rms_norm, sample_rows, segment_attention, silu_mul, stochastic_propose)
 from .kv_store import _upload
 
 
@@ -546,9 +546,11 @@ class B200PackedDraft:
         backbone + LM head for all requests, then per position k < limits[r] the float64
         law q = softmax((base_k + markov_projection(emb(prev))) / T) (normalised twice)
         and a token drawn by the strict CDF rule with ``uniforms[i, k]`` (request i of
-        ``anchors``' order). Returns ({request: tokens [n] long}, {request: laws [n, V]
-        float64}) on the device; the raw confidence logits are not part of acceptance
-        and are not computed."""
+        ``anchors``' order). A bf16 draft runs each position's law and draw as one
+        ``stochastic_propose`` launch writing into one float64 [R, block, V] buffer;
+        other dtypes take the torch formula. Returns ({request: tokens [n] long},
+        {request: laws [n, V] float64}) on the device; the raw confidence logits are not
+        part of acceptance and are not computed. A non-finite logit raises."""
         d = self.draft
         requests = tuple(anchors)
         n = [int(limits[r]) for r in requests]
@@ -560,9 +562,38 @@ class B200PackedDraft:
         hidden = feats.hidden.reshape(r, size, -1)
         base = d.lm_head(hidden.to(d.lm_head.weight.dtype))
         prev = torch.cat([anchors[q].view(1) for q in requests])
+        steps = max(n) if n else 0
+        vocab = base.shape[-1]
+        fused = base.dtype == torch.bfloat16 and d.markov_projection.weight.dtype == torch.bfloat16
+        if fused:
+            laws_buf = torch.empty((r, size, vocab), dtype=torch.float64, device=self.device)
+            uniforms = uniforms.to(torch.float64)
+            toks = torch.empty((r, size), dtype=torch.long, device=self.device)
+            rows_all = [[i for i in range(r) if k < n[i]] for k in range(steps)]
+            # one upload of every position's active rows
+            flat = [i for rows in rows_all for i in rows]
+            idx_all = _upload(flat, self.device) if flat else None
+            off = 0
+            bad = []
+            for k in range(steps):
+                m = len(rows_all[k])
+                idx32 = idx_all[off:off + m]
+                idx = idx32.long()
+                off += m
+                emb = d.markov_embedding(prev[idx])
+                proj = d.markov_projection(emb).contiguous()
+                tok, status = stochastic_propose(base[:, k], idx32, proj, temperature,
+                                                 uniforms[idx, k].contiguous(), laws_buf[:, k])
+                prev = prev.index_copy(0, idx, tok)
+                toks[idx, k] = tok
+                bad.append(status)
+            if bad and bool(torch.cat(bad).any()):
+                raise ValueError('Non-finite draft logits in a stochastic proposal')
+            return ({q: toks[i, :n[i]] for i, q in enumerate(requests)},
+                    {q: laws_buf[i, :n[i]] for i, q in enumerate(requests)})
         tokens = [[] for _ in requests]
         laws = [[] for _ in requests]
-        for k in range(max(n) if n else 0):
+        for k in range(steps):
             rows = [i for i in range(r) if k < n[i]]
             idx = torch.tensor(rows, dtype=torch.long, device=self.device)
             emb = d.markov_embedding(prev[idx])

@@ -580,6 +580,42 @@ def stochastic_accept(target_logits, tokens, draft_probs, cu_proposals, temperat
     return emitted, result
 
 
+def stochastic_propose(base, row_index, proj, temperature, uniforms, law):
+    """One Markov position of the stochastic draft proposal for several requests on the
+    GPU (DSparkDraft._sample_stochastic, dspark_qwen/model.py:193-208): launch row r
+    takes request row i = ``row_index[r]`` of ``base`` (bf16 [R, V] LM-head rows of the
+    position, rows may be strided), adds ``proj[r]`` (bf16 [n, V] Markov projection) as
+    torch adds bf16, writes the float64 law softmax(x / T) normalised once more into
+    ``law[i]`` (float64 [R, V], rows may be strided) and draws a token with
+    ``uniforms[r]`` by the strict CDF rule. Returns (tokens [n] int64, status [n] int32:
+    0, or 1 for non-finite logits)."""
+    device = base.device
+    n = proj.shape[0]
+    if (base.ndim != 2 or base.dtype != torch.bfloat16 or base.stride(1) != 1 or proj.ndim != 2
+            or proj.dtype != torch.bfloat16 or proj.stride(1) != 1 or proj.shape[1] != base.shape[1]
+            or law.ndim != 2 or law.dtype != torch.float64 or law.stride(1) != 1 or law.shape != base.shape
+            or row_index.dtype != torch.int32 or row_index.shape != (n,) or not row_index.is_contiguous()
+            or uniforms.dtype != torch.float64 or uniforms.shape != (n,) or not uniforms.is_contiguous()
+            or any(t.device != device for t in (row_index, proj, uniforms, law)) or not base.is_cuda):
+        raise ValueError('stochastic_propose: bf16 [R, V] base rows, int32 [n] row indices, bf16 [n, V] '
+                         'projections, float64 [n] uniforms and a float64 [R, V] law on one CUDA device required')
+    temperature = float(temperature)
+    if not math.isfinite(temperature) or temperature <= 0:
+        raise ValueError('temperature must be finite and strictly positive')
+    tokens = torch.empty(n, dtype=torch.long, device=device)
+    status = torch.empty(n, dtype=torch.int32, device=device)
+    if n == 0:
+        return tokens, status
+    lib = _lib.load_library()
+    nbytes = int(lib.dspark_propose_scratch_bytes())
+    scratch = torch.empty(nbytes, dtype=torch.uint8, device=device)
+    _lib.check(lib.dspark_stochastic_propose(
+        base.data_ptr(), base.stride(0), row_index.data_ptr(), proj.data_ptr(), proj.stride(0), base.shape[1],
+        temperature, uniforms.data_ptr(), n, law.data_ptr(), law.stride(0), tokens.data_ptr(), status.data_ptr(),
+        scratch.data_ptr(), nbytes, _stream(device)), 'dspark_stochastic_propose')
+    return tokens, status
+
+
 def float64_law(logits, temperature):
     """The reference's sampling law of logits rows (tensor_sampling.py:38-51): float64
     softmax of logits / T, normalised once more. Torch ops on the logits' device."""

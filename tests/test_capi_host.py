@@ -31,7 +31,7 @@ def test_library_exports_every_declared_symbol(pkg):
     assert len(names) >= 10
     for name in names:
         assert hasattr(raw, name), name
-    assert lib.dspark_abi_version() == 17
+    assert lib.dspark_abi_version() == 18
     assert lib.dspark_status_string(1) == b'invalid argument'
     assert pkg.launch_count() >= 0
 
