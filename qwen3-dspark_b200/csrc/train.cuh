@@ -261,6 +261,25 @@ __device__ __forceinline__ bool wait_or_abort(uint32_t bar, uint32_t parity, vol
   }
 }
 
+// Maximum of 64 values as a tree of three-input maxima (depth 4 instead of a
+// 64-long dependent chain).
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+__device__ __forceinline__ float max64(const float (&s)[64]) {
+  float a[22], b[8];
+#pragma unroll
+  for (int j = 0; j < 21; ++j) a[j] = max3f(s[3 * j], s[3 * j + 1], s[3 * j + 2]);
+  a[21] = s[63];
+#pragma unroll
+  for (int j = 0; j < 7; ++j) b[j] = max3f(a[3 * j], a[3 * j + 1], a[3 * j + 2]);
+  b[7] = a[21];
+  return max3f(max3f(b[0], b[1], b[2]), max3f(b[3], b[4], b[5]), fmaxf(b[6], b[7]));
+}
+
 // ---------------------------------------------------------------- item
 struct Item {
   int q_row0, nq, head, k_base, ctx_keys, blk_key0, phase, nblocks, bs;
@@ -468,20 +487,18 @@ __device__ __forceinline__ void softmax_role(const int* items, int first, int la
         hi = min(lo + x.bs, kKeyBlock);
       }
       if (!row_ok) hi = lo;
-      lo -= half * 64;                             // into this half's key index
-      hi -= half * 64;
-      float mb = -INFINITY;
-      if (lo <= 0 && hi >= 64) {
+      lo = max(lo - half * 64, 0);                 // into this half's key index
+      hi = min(hi - half * 64, 64);
+      // Rows of a warp mostly share their visibility; a warp whose rows all see
+      // the whole half skips the select. Otherwise the visible keys [lo, hi)
+      // are a bit mask and every value is selected against its bit.
+      if (!__all_sync(0xffffffffu, lo == 0 && hi == 64)) {
+        const uint64_t bits = hi > lo ? ((hi >= 64 ? ~0ull : (1ull << hi) - 1) & ~((1ull << lo) - 1)) : 0ull;
+        const uint32_t b0 = static_cast<uint32_t>(bits), b1 = static_cast<uint32_t>(bits >> 32);
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mb = fmaxf(mb, s[i]);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const bool vis = i >= lo && i < hi;
-          s[i] = vis ? s[i] : -INFINITY;
-          mb = fmaxf(mb, s[i]);
-        }
+        for (int i = 0; i < 64; ++i) s[i] = (((i < 32 ? b0 : b1) >> (i & 31)) & 1u) ? s[i] : -INFINITY;
       }
+      float mb = max64(s);
       float mo;
       if (!(ok = exchange(kTmemX + (xcount & 1) * 2, mb, mo))) break;
       mb = fmaxf(mb, mo);
