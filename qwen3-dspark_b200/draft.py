@@ -21,6 +21,8 @@ state dict loads unchanged; ``embedding`` and ``lm_head`` are the target's.
 """
 from dataclasses import dataclass, field
 
+import math
+
 import torch
 from torch import nn
 from transformers.models.qwen3.modeling_qwen3 import Qwen3MLP, Qwen3RMSNorm, Qwen3RotaryEmbedding
@@ -449,6 +451,44 @@ class B200PackedDraft:
         """Backbone + LM head + greedy Markov loop over fixed-address inputs (bf16 drafts
         whose Markov head runs on the fused kernel)."""
         d, size = self.draft, self.draft.spec.block_size
+        hidden, base = self._backbone_body(anchor_buf, pos_buf, meta, r)
+        return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),
+                             self._confidence_bias(), hidden, base, anchor_buf, size)
+
+    def _stochastic_positions(self, base, prev, uniforms, temperature, steps):
+        """Positions 0..steps-1 of the stochastic proposal for all r requests (bf16
+        drafts): per position the embedding of the previous token, the Markov
+        projection and one ``stochastic_propose`` launch writing the float64 law and
+        drawing the token. Every position runs over all rows, whatever their limits, so
+        the eager and the captured proposal compute the same things; the caller keeps
+        each request's first limits[i] positions. Returns tokens [r, size] int64, laws
+        [r, size, V] float64 and status [r, size] int32 (positions past ``steps`` are
+        not written)."""
+        d = self.draft
+        r, size, vocab = base.shape
+        laws = torch.empty((r, size, vocab), dtype=torch.float64, device=self.device)
+        toks = torch.zeros((r, size), dtype=torch.long, device=self.device)
+        status = torch.zeros((r, size), dtype=torch.int32, device=self.device)
+        rows = torch.arange(r, dtype=torch.int32, device=self.device)
+        for k in range(steps):
+            proj = d.markov_projection(d.markov_embedding(prev)).contiguous()
+            tok, st = stochastic_propose(base[:, k], rows, proj, temperature, uniforms[:, k].contiguous(), laws[:, k])
+            toks[:, k] = tok
+            status[:, k] = st
+            prev = tok
+        return toks, laws, status
+
+    def _propose_stochastic_body(self, anchor_buf, pos_buf, meta, r, u_buf, temperature):
+        """Backbone + LM head + every block position's law and draw over fixed-address
+        inputs (the captured stochastic proposal)."""
+        size = self.draft.spec.block_size
+        hidden, base = self._backbone_body(anchor_buf, pos_buf, meta, r)
+        return self._stochastic_positions(base.view(r, size, -1), anchor_buf, u_buf, temperature, size)
+
+    def _backbone_body(self, anchor_buf, pos_buf, meta, r):
+        """Backbone + final norm + LM head over fixed-address inputs: (hidden [r * block,
+        H], base logits [r * block, V])."""
+        d, size = self.draft, self.draft.spec.block_size
         cu_q, a_start, a_len, b_len = meta[:r + 1], meta[r + 1:2 * r + 1], meta[2 * r + 1:3 * r + 1], meta[3 * r + 1:]
         b_start = cu_q[:r]
         block = torch.full((r, size), d.spec.mask_token_id, dtype=torch.long, device=self.device)
@@ -471,9 +511,7 @@ class B200PackedDraft:
             pending = self._mlp(layer.mlp, x)
         hidden = (self._norm(d.norm, z) if pending is None
                   else self._add_norm(d.norm, z, pending)[1])[0].contiguous()
-        base = d.lm_head(hidden).contiguous()
-        return markov_greedy(d.markov_projection.weight, d.markov_embedding.weight, d.confidence.weight.reshape(-1),
-                             self._confidence_bias(), hidden, base, anchor_buf, size)
+        return hidden, d.lm_head(hidden).contiguous()
 
     def _graph_ready(self):
         d = self.draft
@@ -508,15 +546,9 @@ class B200PackedDraft:
         graphs[r] = dict(graph=graph, anchors=anchor_buf, pos=pos_buf, meta=meta, tokens=toks, conf=conf)
         return graph
 
-    @torch.no_grad()
-    def propose_greedy_graph(self, anchors, on_device=False):
-        """``propose_greedy`` through the program captured for ``len(anchors)`` requests.
-        ``on_device`` returns the program's output buffers (tokens [R, block] int64,
-        confidences [R, block] float32, valid until the next replay) without a host
-        read."""
-        ex = self.__dict__.get('_graphs', {}).get(len(anchors))
-        if ex is None:
-            raise ValueError('Capture the request count first')
+    def _fill_propose(self, ex, anchors):
+        """Writes a round's anchors, block positions and attention metadata into a
+        captured proposal's fixed buffers."""
         size = self.draft.spec.block_size
         requests = tuple(anchors)
         positions = []
@@ -533,11 +565,87 @@ class B200PackedDraft:
         ex['meta'].copy_(torch.tensor(host, dtype=torch.int32).pin_memory(), non_blocking=True)
         ex['pos'].copy_(torch.tensor(positions, dtype=torch.long).pin_memory(), non_blocking=True)
         ex['anchors'].copy_(torch.cat([anchors[q].view(1) for q in requests]))
+        return requests
+
+    @torch.no_grad()
+    def propose_greedy_graph(self, anchors, on_device=False):
+        """``propose_greedy`` through the program captured for ``len(anchors)`` requests.
+        ``on_device`` returns the program's output buffers (tokens [R, block] int64,
+        confidences [R, block] float32, valid until the next replay) without a host
+        read."""
+        ex = self.__dict__.get('_graphs', {}).get(len(anchors))
+        if ex is None:
+            raise ValueError('Capture the request count first')
+        requests = self._fill_propose(ex, anchors)
         ex['graph'].replay()
         if on_device:
             return ex['tokens'], ex['conf']
         toks, confs = ex['tokens'].tolist(), ex['conf'].tolist()
         return {q: (toks[i], confs[i]) for i, q in enumerate(requests)}
+
+    @torch.no_grad()
+    def capture_propose_stochastic(self, num_requests, temperature):
+        """Capture the stochastic proposal (``propose_stochastic``) of ``num_requests``
+        requests at ``temperature`` into a CUDA graph (bf16 drafts with the fused Markov
+        head): anchors, block positions, attention metadata and the round's proposal
+        uniforms live in fixed buffers that ``propose_stochastic_graph`` fills; every
+        block position runs for every request and each request keeps its first
+        limits[i] positions, as the eager proposal does."""
+        if not self._graph_ready():
+            raise ValueError('Graph proposal needs a bf16 draft whose Markov head runs on the fused kernel')
+        temperature = float(temperature)
+        if not math.isfinite(temperature) or temperature <= 0:
+            raise ValueError('temperature must be finite and strictly positive')
+        graphs = self.__dict__.setdefault('_sgraphs', {})
+        key = (num_requests, temperature)
+        if key in graphs:
+            raise ValueError('Request count and temperature already captured')
+        r, size = num_requests, self.draft.spec.block_size
+        anchor_buf = torch.zeros(r, dtype=torch.long, device=self.device)
+        pos_buf = torch.arange(r * size, dtype=torch.long, device=self.device) % size
+        meta = torch.tensor([size * i for i in range(r + 1)] + [self.slot_rows[0]] * r + [0] * r + [size] * r,
+                            dtype=torch.int32, device=self.device)
+        u_buf = torch.zeros((r, size), dtype=torch.float64, device=self.device)
+        side = torch.cuda.Stream(self.device)
+        side.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(side):                       # warm-up: handles, allocator, workspace
+            self._propose_stochastic_body(anchor_buf, pos_buf, meta, r, u_buf, temperature)
+        torch.cuda.current_stream(self.device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=side):
+            toks, laws, status = self._propose_stochastic_body(anchor_buf, pos_buf, meta, r, u_buf, temperature)
+        graphs[key] = dict(graph=graph, anchors=anchor_buf, pos=pos_buf, meta=meta, u=u_buf, tokens=toks, laws=laws,
+                           status=status)
+        return graph
+
+    @torch.no_grad()
+    def propose_stochastic_graph(self, anchors, limits, uniforms, temperature):
+        """``propose_stochastic`` through the program captured for ``len(anchors)``
+        requests and ``temperature``: the same ({request: tokens [n] long}, {request:
+        laws [n, V] float64}), as views of the program's buffers (valid until its next
+        replay). A non-finite logit raises."""
+        ex = self.__dict__.get('_sgraphs', {}).get((len(anchors), float(temperature)))
+        if ex is None:
+            raise ValueError('Capture the request count and temperature first')
+        size = self.draft.spec.block_size
+        requests = tuple(anchors)
+        n = [int(limits[q]) for q in requests]
+        if any(not 0 <= x <= size for x in n) or uniforms.shape != (len(requests), size):
+            raise ValueError('limits in [0, block_size] and [R, block_size] uniforms required')
+        self._fill_propose(ex, anchors)
+        ex['u'].copy_(uniforms)
+        ex['graph'].replay()
+        return self._stochastic_result(requests, n, ex['tokens'], ex['laws'], ex['status'])
+
+    def _stochastic_result(self, requests, n, toks, laws, status):
+        """Per request its first n[i] proposed tokens and laws; a non-finite logit at one
+        of those positions raises."""
+        size = toks.shape[1]
+        keep = torch.arange(size, device=self.device)[None, :] < _upload(n, self.device)[:, None]
+        if bool(((status != 0) & keep).any()):
+            raise ValueError('Non-finite draft logits in a stochastic proposal')
+        return ({q: toks[i, :n[i]] for i, q in enumerate(requests)},
+                {q: laws[i, :n[i]] for i, q in enumerate(requests)})
 
     @torch.no_grad()
     def propose_stochastic(self, anchors, limits, uniforms, temperature):
@@ -566,31 +674,9 @@ class B200PackedDraft:
         vocab = base.shape[-1]
         fused = base.dtype == torch.bfloat16 and d.markov_projection.weight.dtype == torch.bfloat16
         if fused:
-            laws_buf = torch.empty((r, size, vocab), dtype=torch.float64, device=self.device)
-            uniforms = uniforms.to(torch.float64)
-            toks = torch.empty((r, size), dtype=torch.long, device=self.device)
-            rows_all = [[i for i in range(r) if k < n[i]] for k in range(steps)]
-            # one upload of every position's active rows
-            flat = [i for rows in rows_all for i in rows]
-            idx_all = _upload(flat, self.device) if flat else None
-            off = 0
-            bad = []
-            for k in range(steps):
-                m = len(rows_all[k])
-                idx32 = idx_all[off:off + m]
-                idx = idx32.long()
-                off += m
-                emb = d.markov_embedding(prev[idx])
-                proj = d.markov_projection(emb).contiguous()
-                tok, status = stochastic_propose(base[:, k], idx32, proj, temperature,
-                                                 uniforms[idx, k].contiguous(), laws_buf[:, k])
-                prev = prev.index_copy(0, idx, tok)
-                toks[idx, k] = tok
-                bad.append(status)
-            if bad and bool(torch.cat(bad).any()):
-                raise ValueError('Non-finite draft logits in a stochastic proposal')
-            return ({q: toks[i, :n[i]] for i, q in enumerate(requests)},
-                    {q: laws_buf[i, :n[i]] for i, q in enumerate(requests)})
+            toks, laws_buf, status = self._stochastic_positions(base, prev, uniforms.to(torch.float64), temperature,
+                                                                steps)
+            return self._stochastic_result(requests, n, toks, laws_buf, status)
         tokens = [[] for _ in requests]
         laws = [[] for _ in requests]
         for k in range(steps):

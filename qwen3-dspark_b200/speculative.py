@@ -160,7 +160,8 @@ def speculative_greedy(target, draft, prompts, max_new_tokens, eos_ids=(), devic
 
 
 @torch.no_grad()
-def speculative_sample(target, draft, prompts, max_new_tokens, generators, temperature=1.0, eos_ids=()):
+def speculative_sample(target, draft, prompts, max_new_tokens, generators, temperature=1.0, eos_ids=(),
+                       graph=False):
     """Batched stochastic speculative decoding; per request the rule of
     ``cached_speculative_sample`` (dspark_qwen/cached_sampling.py:80-175) under the
     reference's float64 law. ``generators``: {request: CPU torch.Generator}. Each
@@ -169,7 +170,11 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
     after each round the generator is left exactly where the reference's would be,
     so a request's tokens equal the reference's single-request run with the same
     seed. Acceptance runs on the GPU (``stochastic_accept``); the host reads back one
-    small result per round. Returns ({request: tokens}, rounds)."""
+    small result per round. ``graph`` replays the target's verify forward from a CUDA
+    graph per set of chunk lengths and, for bf16 drafts with the fused Markov head, the
+    stochastic proposal from a graph per (request count, temperature) and the draft
+    append of whole chunks from a graph per shape; the tokens are those of the eager
+    loop. Returns ({request: tokens}, rounds)."""
     from .kernels import STOCHASTIC_STATUS, float64_law, sample_rows, stochastic_accept
     import math
     if type(max_new_tokens) is not int or max_new_tokens < 0:
@@ -212,9 +217,21 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
         u_prop = u_prop.pin_memory().to(dev, non_blocking=True)
         u_acc = u_acc.pin_memory().to(dev, non_blocking=True)
         anchors = {r: torch.tensor([[output[r][-1]]], dtype=torch.long, device=dev) for r in active}
-        tokens, laws = draft.propose_stochastic(anchors, n, u_prop, temperature)
+        use_graph = graph and getattr(draft, '_graph_ready', lambda: False)()
+        if use_graph:
+            if (len(active), temperature) not in draft.__dict__.get('_sgraphs', {}):
+                draft.capture_propose_stochastic(len(active), temperature)
+            tokens, laws = draft.propose_stochastic_graph(anchors, n, u_prop, temperature)
+        else:
+            tokens, laws = draft.propose_stochastic(anchors, n, u_prop, temperature)
         chunks = {r: torch.cat((anchors[r][0], tokens[r]))[None] for r in active}
-        verified = target.verify(chunks)
+        if graph:
+            bucket = QueryBucket(tuple(n[r] + 1 for r in active))
+            if bucket not in target._graphs:
+                target.capture(bucket)
+            verified = target.verify_graph(chunks, bucket)
+        else:
+            verified = target.verify(chunks)
         logits = target.model.get_output_embeddings()(verified.last)[0]
         cu = [0]
         for r in active:
@@ -252,7 +269,14 @@ def speculative_sample(target, draft, prompts, max_new_tokens, generators, tempe
                             extra_token_kind={0: None, 1: 'residual', 2: 'bonus'}[extra],
                             stop_reason=('round_complete', 'eos', 'budget')[reason])
         target.commit(verified, commit)
-        draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
+        width = size + 1
+        if use_graph and hasattr(draft, 'capture_append') and all(n[r] + 1 == width for r in active):
+            # whole verified chunks through the captured fixed-shape append
+            if (len(active), width) not in draft.__dict__.get('_append_graphs', {}):
+                draft.capture_append(len(active), width)
+            draft.append_verified_graph(verified.context, tuple(active), [commit[r] for r in active])
+        else:
+            draft.append_committed({r: verified.context_for(r)[:, :commit[r]] for r in active if commit[r]})
         rounds.append(stats)
         active = [r for r in active if len(output[r]) < max_new_tokens and stats[r]['stop_reason'] != 'eos']
     return output, rounds

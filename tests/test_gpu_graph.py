@@ -153,3 +153,37 @@ def test_speculative_loop_with_graph_replay_gives_the_same_tokens(pkg):
         target.close()
     assert outs[0] == outs[1] == outs[2]
     status_clean(pkg)
+
+
+def test_stochastic_loop_with_graph_replay_gives_the_same_tokens(pkg):
+    """speculative_sample(graph=True) (stochastic proposal, target verify and draft
+    append replayed from CUDA graphs) emits the tokens, round statistics and generator
+    states of the eager loop on the same bf16 model, prompts and seeds; requests whose
+    budgets end mid-block exercise proposals with limits below the block size."""
+    model = tiny_bf16_model()
+    spec = pkg.DraftSpec(**dict(I.TINY_DRAFT, markov_rank=64))
+    results = []
+    for graph in (False, True):
+        draft = pkg.DSparkDraftModel(model, spec).eval()
+        dshapes = {k: tuple(v.shape) for k, v in draft.state_dict().items()
+                   if not k.startswith(('embedding.', 'lm_head.'))}
+        draft.load_state_dict({k: torch.from_numpy(v) for k, v in I.deterministic_state(dshapes, 2).items()},
+                              strict=False)
+        draft = draft.to(dev(), torch.bfloat16)
+        target = pkg.B200Qwen3Target(model, spec.layer_ids, slots=4, context_capacity=400, max_query_tokens=700)
+        pdraft = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=400)
+        prompts = {f'r{i}': torch.from_numpy(ids)[None].to(dev()) for i, ids in enumerate(I.greedy_prompts()[3:6])}
+        gens = {}
+        for i, r in enumerate(prompts):
+            gens[r] = torch.Generator()
+            gens[r].manual_seed(1000 + i)
+        out, rounds = pkg.speculative_sample(target, pdraft, prompts, 23, gens, temperature=0.9, eos_ids=(7,),
+                                             graph=graph)
+        results.append((out, rounds, {r: g.get_state() for r, g in gens.items()}))
+        if graph:
+            assert pdraft.__dict__.get('_sgraphs'), 'the proposal ran from a captured graph'
+        target.close()
+    (o0, r0, g0), (o1, r1, g1) = results
+    assert o0 == o1 and r0 == r1
+    assert all(torch.equal(g0[r], g1[r]) for r in g0)
+    status_clean(pkg)
