@@ -23,15 +23,20 @@
 // (a row no request owns): a fixed-shape append of whole verified chunks then
 // writes only the committed rows, with no host-side slicing.
 //
-// Roles (320 threads, persistent CTAs over (row tile, head tile) pairs):
+// Roles (320 threads, persistent CTAs over (row tile, head tile) pairs; a head
+// tile is kHeads consecutive heads of one layer's K or V, N = 128 kHeads):
 //   warps 0-7  epilogue: warp w reads TMEM lanes 32(w%4).. (tile rows) and writes
-//              half w/4 of the head: d in [32h, 32h+32) and the rotate partners
+//              half w/4 of each head: d in [32h, 32h+32) and the rotate partners
 //              d + 64, so each RoPE pair is thread-local; for k_norm's sum of
 //              squares it also reads the row's other 64 values (TMEM reads are
 //              cheap, and the two warps never wait on each other);
-//   warp 8     TMEM owner and MMA issuer (one thread), two 128-column
-//              accumulators so one tile's epilogue overlaps the next one's MMAs;
-//   warp 9     TMA producer: context and weight 64-wide K chunks, six stages.
+//   warp 8     TMEM owner and MMA issuer (one thread), two accumulators of
+//              128 kHeads columns so one tile's epilogue overlaps the next one's
+//              MMAs;
+//   warp 9     TMA producer: context and weight 64-wide K chunks (six stages
+//              with one head per tile, four with two).
+// Two heads per tile (large appends: prefill) halve the context bytes streamed
+// from L2 per MMA flop; one head per tile keeps small appends spread over the SMs.
 #pragma once
 #include "train.cuh"
 #include "verify.cuh"
@@ -54,18 +59,28 @@ constexpr int kEpilogueWarps = 8;
 constexpr int kMmaWarp = kEpilogueWarps, kTmaWarp = kEpilogueWarps + 1;
 constexpr int kThreads = (kEpilogueWarps + 2) * 32;
 constexpr int kTileRows = 128;        // context rows per tile (MMA M)
-constexpr int kHeadCols = 128;        // one head (MMA N)
-constexpr int kStages = 6;
+constexpr int kHeadCols = 128;        // one head
 constexpr int kMaxLayers = 8;
-constexpr uint32_t kStageBytes = 32768;            // context chunk 16 KB + weight chunk 16 KB
-constexpr uint32_t kSmemBar = kStages * kStageBytes;
-enum Barrier { kBarFull0 = 0, kBarEmpty0 = kStages, kBarDFull0 = 2 * kStages, kBarDFull1, kBarDFree0, kBarDFree1,
-               kBarDrain, kNumBarriers };
-constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
-constexpr uint32_t kSmemAbort = kSmemSlot + 4;
-constexpr uint32_t kSmemNormW = kSmemAbort + 12;                    // float [kMaxLayers][128]
-constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
-constexpr uint32_t kTmemCols = 256;
+
+// Layout of the kernel with kHeads heads per tile (MMA N = 128 kHeads).
+template <int kHeads>
+struct Cfg {
+  static constexpr int kStages = kHeads == 1 ? 6 : 4;
+  static constexpr uint32_t kStageBytes = 16384 * (1 + kHeads);   // context chunk + weight chunk
+  static constexpr uint32_t kSmemBar = kStages * kStageBytes;
+  enum Barrier { kBarFull0 = 0, kBarEmpty0 = kStages, kBarDFull0 = 2 * kStages, kBarDFull1, kBarDFree0, kBarDFree1,
+                 kBarDrain, kNumBarriers };
+  static constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
+  static constexpr uint32_t kSmemAbort = kSmemSlot + 4;
+  static constexpr uint32_t kSmemNormW = kSmemAbort + 12;                 // float [kMaxLayers][128]
+  static constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
+  static constexpr uint32_t kAccCols = kHeadCols * kHeads;
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;
+  // fp32 D, bf16 A and B, both K-major, M = 128, N = 128 kHeads
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((kAccCols >> 3) << 17) | ((128u >> 4) << 24);
+};
+static_assert(Cfg<1>::kSmemBytes <= 232448 && Cfg<2>::kSmemBytes <= 232448, "dynamic shared memory above 227 KB");
+static_assert(Cfg<1>::kIdesc == instr_desc(0), "one-head tiles use the plain M128 N128 descriptor");
 
 struct Params {
   const __nv_bfloat16* k_norm_w;      // [layers, 128] k_norm.weight of each layer
@@ -81,7 +96,7 @@ struct Params {
   int num_requests;
   int rows;                           // input rows
   int k_chunks;                       // hidden / 64
-  int head_tiles;                     // layers * 16
+  int head_tiles;                     // layers * 16 / kHeads
   int row_tiles;
   int layers;
   float eps;
@@ -97,9 +112,18 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* x) 
                       pack_bf16x2(x[8 * q + 4], x[8 * q + 5]), pack_bf16x2(x[8 * q + 6], x[8 * q + 7]));
 }
 
+template <int kHeads>
 __global__ void __launch_bounds__(kThreads, 1)
     draft_append_kernel(const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap wmap,
                         Params p) {
+  using C = Cfg<kHeads>;
+  constexpr int kStages = C::kStages;
+  constexpr uint32_t kStageBytes = C::kStageBytes, kSmemBar = C::kSmemBar, kSmemSlot = C::kSmemSlot;
+  constexpr uint32_t kSmemAbort = C::kSmemAbort, kSmemNormW = C::kSmemNormW, kTmemCols = C::kTmemCols;
+  constexpr uint32_t kAccCols = C::kAccCols;
+  constexpr int kBarFull0 = C::kBarFull0, kBarEmpty0 = C::kBarEmpty0, kBarDFull0 = C::kBarDFull0;
+  constexpr int kBarDFree0 = C::kBarDFree0, kBarDFree1 = C::kBarDFree1, kBarDrain = C::kBarDrain;
+  constexpr int kNumBarriers = C::kNumBarriers;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const uint32_t sbase = smem_u32(smem);
@@ -141,8 +165,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < n_mine; ++t) {
       const int b = t & 1;
       const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
-      const int rt = tile / p.head_tiles, ht = tile - rt * p.head_tiles;
-      const int layer = ht >> 4, is_v = (ht >> 3) & 1, head = ht & 7;
+      const int rt = tile / p.head_tiles, ht = (tile - rt * p.head_tiles) * kHeads;   // first head tile
+      const int layer = ht >> 4, is_v = (ht >> 3) & 1, head0 = ht & 7;
       if (rt != cur_rt) {                       // destination row of this thread's input row
         cur_rt = rt;
         g = rt * kTileRows + m;
@@ -158,6 +182,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       // this row's cos/sin for d in [32 half, 32 half + 32), fetched before the wait
+      // (the same for every head of the tile)
       uint4 cs4[8];
       if (!is_v) {
         const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64 +
@@ -168,7 +193,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-      const uint32_t acc = tmem + lane_addr + b * kHeadCols;
+#pragma unroll 1
+      for (int hh = 0; hh < kHeads; ++hh) {
+      const int head = head0 + hh;
+      const uint32_t acc = tmem + lane_addr + b * kAccCols + hh * kHeadCols;
       __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) + (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) +
                            head * kHeadDim;
       if (is_v) {
@@ -220,13 +248,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           store_row32(out + 64 + half * 32, hi);
         }
       }
+      }
       tc_fence_before();
       mbar_arrive(bar(kBarDFree0 + b));
     }
     if (!ok) *abort_flag = 1;
   } else if (warp == kMmaWarp) {
     if (lane == 0) {
-      constexpr uint32_t kIdesc = instr_desc(0);
+      constexpr uint32_t kIdesc = C::kIdesc;
       bool ok = true;
       int st = 0;
       uint32_t ph = 0;
@@ -240,7 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t a = sbase + st * kStageBytes, w = a + 16384;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            umma_bf16(tmem + b * kHeadCols, smem_desc(a + kk * 32, 16, 1024), smem_desc(w + kk * 32, 16, 1024),
+            umma_bf16(tmem + b * kAccCols, smem_desc(a + kk * 32, 16, 1024), smem_desc(w + kk * 32, 16, 1024),
                       kIdesc, (c | kk) != 0);
           umma_commit(bar(kBarEmpty0 + st));
           if (++st == kStages) {
@@ -271,7 +300,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(kBarFull0 + st), kStageBytes);
           const uint32_t dst = sbase + st * kStageBytes;
           tma_load_2d(dst, &cmap, c * 64, rt * kTileRows, bar(kBarFull0 + st));
-          tma_load_2d(dst + 16384, &wmap, c * 64, ht * kHeadCols, bar(kBarFull0 + st));
+#pragma unroll
+          for (int hh = 0; hh < kHeads; ++hh)           // the heads' weight rows, one after the other
+            tma_load_2d(dst + 16384 * (1 + hh), &wmap, c * 64, (ht * kHeads + hh) * kHeadCols, bar(kBarFull0 + st));
           ++armed[st];
           if (++st == kStages) {
             st = 0;

@@ -85,8 +85,10 @@ int device_info(int dev, DeviceInfo* out) {
                              static_cast<int>(markov::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(markov::markov_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(markov::kSmemBytes)) != cudaSuccess ||
-        cudaFuncSetAttribute(append::draft_append_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(append::kSmemBytes)) != cudaSuccess)
+        cudaFuncSetAttribute(append::draft_append_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(append::Cfg<1>::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(append::draft_append_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(append::Cfg<2>::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
@@ -795,14 +797,21 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
   p.num_requests = num_requests;
   p.rows = rows;
   p.k_chunks = hidden / 64;
-  p.head_tiles = num_layers * 16;
   p.layers = num_layers;
   p.row_tiles = (rows + append::kTileRows - 1) / append::kTileRows;
   p.eps = eps;
+  // Two heads per tile once those tiles alone fill every SM (prefill-sized appends):
+  // each context chunk then feeds twice the MMA work. Smaller appends keep one head
+  // per tile, so their few row tiles still spread over the SMs.
+  const bool pair = static_cast<long long>(p.row_tiles) * num_layers * 8 >= dev.sms;
+  p.head_tiles = num_layers * (pair ? 8 : 16);
   const long long tiles = static_cast<long long>(p.row_tiles) * p.head_tiles;
   if (tiles >= (1ll << 31)) return DSPARK_ERR_UNSUPPORTED;
   const int grid = tiles < dev.sms ? static_cast<int>(tiles) : dev.sms;
-  append::draft_append_kernel<<<grid, append::kThreads, append::kSmemBytes, stream>>>(cm, wm, p);
+  if (pair)
+    append::draft_append_kernel<2><<<grid, append::kThreads, append::Cfg<2>::kSmemBytes, stream>>>(cm, wm, p);
+  else
+    append::draft_append_kernel<1><<<grid, append::kThreads, append::Cfg<1>::kSmemBytes, stream>>>(cm, wm, p);
   return launch_status();
 }
 
