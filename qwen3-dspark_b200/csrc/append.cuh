@@ -38,6 +38,7 @@
 // Two heads per tile (large appends: prefill) halve the context bytes streamed
 // from L2 per MMA flop; one head per tile keeps small appends spread over the SMs.
 #pragma once
+#include "pair.cuh"
 #include "train.cuh"
 #include "verify.cuh"
 
@@ -110,6 +111,64 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* x) 
   for (int q = 0; q < 4; ++q)
     d[q] = make_uint4(pack_bf16x2(x[8 * q], x[8 * q + 1]), pack_bf16x2(x[8 * q + 2], x[8 * q + 3]),
                       pack_bf16x2(x[8 * q + 4], x[8 * q + 5]), pack_bf16x2(x[8 * q + 6], x[8 * q + 7]));
+}
+
+// The epilogue of one head of a tile for this thread's row (TMEM lane) and column
+// half: V stored as projected (bf16); K rounded to bf16, k_norm'ed (sum of squares
+// over the row's 128 values, two of them read from the other half) and rotated
+// with the row's cos/sin, each step rounded as the reference's bf16 ops round.
+// dest < 0: nothing is written (a padding row, or a rejected destination).
+__device__ __forceinline__ void write_head(const Params& p, uint32_t acc, __nv_bfloat16* out, bool is_v,
+                                           const float* norm_w, int half, const uint4 (&cs4)[8], long long dest) {
+  if (is_v) {
+#pragma unroll 1
+    for (int c = 0; c < 2; ++c) {
+      float d[32];
+      tmem_ld32(acc + half * 64 + c * 32, d);
+      if (dest >= 0) store_row32(out + half * 64 + c * 32, d);
+    }
+  } else {
+    // k_proj output (bf16) of d in [32 half, +32) and of the partners d + 64;
+    // the row's other 64 values (the other warp's) are read too, for the sum
+    float lo[32], hi[32];
+    float ss = 0.f;
+    {
+      float o1[32], o2[32];
+      tmem_ld32(acc + (half ^ 1) * 32, o1);
+      tmem_ld32(acc + 64 + (half ^ 1) * 32, o2);
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float x1 = bf16r(o1[e]), x2 = bf16r(o2[e]);
+        ss = fmaf(x1, x1, ss);
+        ss = fmaf(x2, x2, ss);
+      }
+    }
+    tmem_ld32(acc + half * 32, lo);
+    tmem_ld32(acc + 64 + half * 32, hi);
+#pragma unroll
+    for (int e = 0; e < 32; ++e) {
+      lo[e] = bf16r(lo[e]);
+      hi[e] = bf16r(hi[e]);
+      ss = fmaf(lo[e], lo[e], ss);
+      ss = fmaf(hi[e], hi[e], ss);
+    }
+    const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
+    const float* w = norm_w + half * 32;
+    if (dest >= 0) {
+#pragma unroll
+      for (int e = 0; e < 32; ++e) {
+        const float a = bf16r(w[e] * bf16r(lo[e] * rs));
+        const float bb = bf16r(w[e + 64] * bf16r(hi[e] * rs));
+        const uint32_t cw = e % 4 == 0 ? cs4[e / 4].x : e % 4 == 1 ? cs4[e / 4].y : e % 4 == 2 ? cs4[e / 4].z
+                                                                                               : cs4[e / 4].w;
+        const float2 r = unpack_bf16x2(cw);   // .x cos, .y sin
+        lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
+        hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
+      }
+      store_row32(out + half * 32, lo);
+      store_row32(out + 64 + half * 32, hi);
+    }
+  }
 }
 
 template <int kHeads>
@@ -199,55 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = tmem + lane_addr + b * kAccCols + hh * kHeadCols;
       __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) + (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) +
                            head * kHeadDim;
-      if (is_v) {
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          float d[32];
-          tmem_ld32(acc + half * 64 + c * 32, d);
-          if (dest >= 0) store_row32(out + half * 64 + c * 32, d);
-        }
-      } else {
-        // k_proj output (bf16) of d in [32 half, +32) and of the partners d + 64;
-        // the row's other 64 values (the other warp's) are read too, for the sum
-        float lo[32], hi[32];
-        float ss = 0.f;
-        {
-          float o1[32], o2[32];
-          tmem_ld32(acc + (half ^ 1) * 32, o1);
-          tmem_ld32(acc + 64 + (half ^ 1) * 32, o2);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float x1 = bf16r(o1[e]), x2 = bf16r(o2[e]);
-            ss = fmaf(x1, x1, ss);
-            ss = fmaf(x2, x2, ss);
-          }
-        }
-        tmem_ld32(acc + half * 32, lo);
-        tmem_ld32(acc + 64 + half * 32, hi);
-#pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          lo[e] = bf16r(lo[e]);
-          hi[e] = bf16r(hi[e]);
-          ss = fmaf(lo[e], lo[e], ss);
-          ss = fmaf(hi[e], hi[e], ss);
-        }
-        const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
-        const float* w = norm_w + layer * kHeadDim + half * 32;
-        if (dest >= 0) {
-#pragma unroll
-          for (int e = 0; e < 32; ++e) {
-            const float a = bf16r(w[e] * bf16r(lo[e] * rs));
-            const float bb = bf16r(w[e + 64] * bf16r(hi[e] * rs));
-            const uint32_t cw = e % 4 == 0 ? cs4[e / 4].x : e % 4 == 1 ? cs4[e / 4].y : e % 4 == 2 ? cs4[e / 4].z
-                                                                                                   : cs4[e / 4].w;
-            const float2 r = unpack_bf16x2(cw);   // .x cos, .y sin
-            lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
-            hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
-          }
-          store_row32(out + half * 32, lo);
-          store_row32(out + 64 + half * 32, hi);
-        }
-      }
+      write_head(p, acc, out, is_v, norm_w + layer * kHeadDim, half, cs4, dest);
       }
       tc_fence_before();
       mbar_arrive(bar(kBarDFree0 + b));
@@ -322,6 +333,213 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   if (warp == kMmaWarp) tmem_dealloc(tmem, kTmemCols);
+}
+
+// ---------------------------------------------------------------------------
+// 2-SM version for large appends: a cluster of two CTAs computes one tile of
+// 256 context rows x 2 heads with tcgen05.mma.cta_group::2 (M = 256, N = 256):
+// each CTA loads its own 128 context rows (the A operand) and ONE head's weight
+// chunk (its half of B, rank r: head 2 ht + r), so every 16 KB of context and
+// 16 KB of weights a CTA streams from L2 feeds 4.2 MFLOP, twice the single-CTA
+// one-head tile. Each CTA's TMEM holds its 128 rows x both heads; its epilogue
+// writes them as the single-CTA kernel does. Rank 0 issues the MMAs; rank 1's
+// copies are relayed to rank 0 by one thread of rank 1 (a bounded wait for each
+// stage, then a remote arrival); MMA completion reaches both CTAs through
+// multicast commits; the epilogue warps of both CTAs release an accumulator on
+// rank 0's barrier. Every wait is bounded and both CTAs meet at a cluster
+// barrier before TMEM is released.
+// ---------------------------------------------------------------------------
+struct PairCfg {
+  static constexpr int kStages = 6;
+  static constexpr uint32_t kStageBytes = 32768;    // own 128-row context chunk + own head's weight chunk
+  static constexpr uint32_t kSmemBar = kStages * kStageBytes;
+  enum Barrier { kBarFull0 = 0, kBarPeer0 = kStages, kBarEmpty0 = 2 * kStages, kBarDFull0 = 3 * kStages, kBarDFull1,
+                 kBarDFree0, kBarDFree1, kBarDrain, kNumBarriers };
+  static constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
+  static constexpr uint32_t kSmemAbort = kSmemSlot + 4;
+  static constexpr uint32_t kSmemNormW = kSmemAbort + 12;                 // float [kMaxLayers][128]
+  static constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
+  static constexpr uint32_t kAccCols = 2 * kHeadCols;
+  static constexpr uint32_t kTmemCols = 2 * kAccCols;
+  // fp32 D, bf16 A and B, both K-major, M = 256 (the pair), N = 256
+  static constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((256u >> 3) << 17) | ((256u >> 4) << 24);
+};
+static_assert(PairCfg::kSmemBytes <= 232448, "dynamic shared memory above 227 KB");
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    draft_append_pair_kernel(const __grid_constant__ CUtensorMap cmap, const __grid_constant__ CUtensorMap wmap,
+                             Params p) {
+  using C = PairCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bars = sbase + C::kSmemBar;
+  auto bar = [&](int i) { return bars + 8u * i; };
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kSmemAbort);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = pair::cluster_rank();
+  const int pair_id = static_cast<int>(pair::cluster_index()), n_pairs = static_cast<int>(gridDim.x) / 2;
+
+  float* norm_w = reinterpret_cast<float*>(smem + C::kSmemNormW);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < C::kNumBarriers; ++i)
+      mbar_init(bar(i), (i == C::kBarDFree0 || i == C::kBarDFree1) ? 2u * kEpilogueWarps : 1u);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < p.layers * 128; i += kThreads) norm_w[i] = __bfloat162float(p.k_norm_w[i]);
+  if (warp == kTmaWarp && lane == 0) {
+    prefetch_tmap(&cmap);
+    prefetch_tmap(&wmap);
+  }
+  if (warp == kMmaWarp) pair::tmem_alloc_pair(sbase + C::kSmemSlot, C::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  pair::cluster_sync();                 // both CTAs' barriers initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem + C::kSmemSlot);
+  // tiles: (256-row pair tile rt, head pair ht); p.row_tiles / p.head_tiles count them
+  const int tiles = p.row_tiles * p.head_tiles;
+  const int n_mine = tiles > pair_id ? (tiles - 1 - pair_id) / n_pairs + 1 : 0;
+
+  if (warp < kEpilogueWarps) {
+    const int quarter = warp & 3, half = warp >> 2;
+    const int m = quarter * 32 + lane;                  // tile row of this thread in this CTA
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    bool ok = true;
+    int cur_rt = -1;
+    long long dest = -1;
+    int g = 0;
+    for (int t = 0; t < n_mine; ++t) {
+      const int b = t & 1;
+      const int tile = pair_id + t * n_pairs;
+      const int rt = tile / p.head_tiles, ht = (tile - rt * p.head_tiles) * 2;   // first head tile
+      const int layer = ht >> 4, is_v = (ht >> 3) & 1, head0 = ht & 7;
+      if (rt != cur_rt) {                       // destination row of this thread's input row
+        cur_rt = rt;
+        g = rt * 2 * kTileRows + static_cast<int>(rank) * kTileRows + m;
+        dest = -1;
+        if (g < p.rows) {
+          const int i = min(find_request(p.cu_rows, p.num_requests + 1, g), p.num_requests - 1);
+          const int j = g - p.cu_rows[i];
+          dest = j < p.count[i] ? static_cast<long long>(p.slot_row[i]) + p.ctx_len[i] + j : p.trash_row;
+          if (dest < 0 || dest >= p.pool_rows) {
+            atomicOr(&g_device_status, kStatusBadArgument);
+            dest = -1;
+          }
+        }
+      }
+      uint4 cs4[8];
+      if (!is_v) {
+        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64 +
+                                                         half * 32);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) cs4[q] = __ldg(cs + q);
+      }
+      ok = pair::pair_wait(bar(C::kBarDFull0 + b), (t >> 1) & 1, abort_flag);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      tc_fence_after();
+#pragma unroll 1
+      for (int hh = 0; hh < 2; ++hh) {
+        const uint32_t acc = tmem + lane_addr + b * C::kAccCols + hh * kHeadCols;
+        __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) +
+                             (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) + (head0 + hh) * kHeadDim;
+        write_head(p, acc, out, is_v, norm_w + layer * kHeadDim, half, cs4, dest);
+      }
+      // one arrival per warp on rank 0's barrier once the warp's TMEM reads are done
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) pair::arrive_rank0(bar(C::kBarDFree0 + b));
+    }
+    if (!ok) *abort_flag = 1;
+  } else if (warp == kMmaWarp) {
+    if (lane == 0 && rank == 0) {
+      bool ok = true;
+      int st = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < n_mine && ok; ++t) {
+        const int b = t & 1;
+        if (!(ok = pair::pair_wait(bar(C::kBarDFree0 + b), ((t >> 1) & 1) ^ 1, abort_flag))) break;
+        tc_fence_after();
+        for (int c = 0; c < p.k_chunks; ++c) {
+          if (!(ok = pair::pair_wait(bar(C::kBarFull0 + st), ph, abort_flag))) break;
+          if (!(ok = pair::pair_wait(bar(C::kBarPeer0 + st), ph, abort_flag))) break;
+          tc_fence_after();
+          const uint32_t a = sbase + st * C::kStageBytes, w = a + 16384;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            pair::umma_pair_ss(tmem + b * C::kAccCols, smem_desc(a + kk * 32, 16, 1024),
+                               smem_desc(w + kk * 32, 16, 1024), C::kIdesc, (c | kk) != 0);
+          pair::umma_commit_pair(bar(C::kBarEmpty0 + st));
+          if (++st == C::kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        pair::umma_commit_pair(bar(C::kBarDFull0 + b));
+      }
+      if (!ok) *abort_flag = 1;
+      pair::umma_commit_pair_local(bar(C::kBarDrain));
+      volatile int never = 0;
+      wait_or_abort(bar(C::kBarDrain), 0, &never);
+    } else if (lane == 0) {
+      // rank 1: relay each landed stage to rank 0's MMA thread
+      bool ok = true;
+      int st = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < n_mine && ok; ++t)
+        for (int c = 0; c < p.k_chunks; ++c) {
+          if (!(ok = pair::relay_wait(bar(C::kBarFull0 + st), ph, abort_flag))) break;
+          pair::arrive_rank0(bar(C::kBarPeer0 + st));
+          if (++st == C::kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+      if (!ok) *abort_flag = 1;
+    }
+    __syncwarp();
+  } else {
+    if (lane == 0) {
+      int issued = 0;
+      bool ok = true;
+      int st = 0;
+      uint32_t ph = 0;
+      for (int t = 0; t < n_mine && ok; ++t) {
+        const int tile = pair_id + t * n_pairs;
+        const int rt = tile / p.head_tiles, ht = tile - rt * p.head_tiles;
+        for (int c = 0; c < p.k_chunks; ++c) {
+          if (!(ok = pair::pair_wait(bar(C::kBarEmpty0 + st), ph ^ 1, abort_flag))) break;
+          mbar_arrive_expect_tx(bar(C::kBarFull0 + st), C::kStageBytes);
+          const uint32_t dst = sbase + st * C::kStageBytes;
+          tma_load_2d(dst, &cmap, c * 64, (rt * 2 + static_cast<int>(rank)) * kTileRows, bar(C::kBarFull0 + st));
+          tma_load_2d(dst + 16384, &wmap, c * 64, (ht * 2 + static_cast<int>(rank)) * kHeadCols,
+                      bar(C::kBarFull0 + st));
+          ++issued;
+          if (++st == C::kStages) {
+            st = 0;
+            ph ^= 1;
+          }
+        }
+      }
+      if (!ok) *abort_flag = 1;
+      // Wait until the MMAs have released every stage (or, after an abort, until the
+      // copies in flight have landed), so no commit or copy outlives this CTA.
+      volatile int never = 0;
+#pragma unroll 1
+      for (int s2 = 0; s2 < C::kStages; ++s2) {
+        const int armed = issued > s2 ? (issued - 1 - s2) / C::kStages + 1 : 0;
+        if (armed && !pair::pair_wait(bar(C::kBarEmpty0 + s2), (armed - 1) & 1, ok ? &never : abort_flag))
+          wait_or_abort(bar(C::kBarFull0 + s2), (armed - 1) & 1, &never);
+      }
+    }
+    __syncwarp();
+  }
+  tc_fence_before();
+  pair::cluster_sync();
+  tc_fence_after();
+  if (warp == kMmaWarp) pair::tmem_dealloc_pair(tmem, C::kTmemCols);
 }
 
 }  // namespace append

@@ -34,6 +34,7 @@ constexpr int kMaxDevices = 64;
 struct DeviceInfo {
   bool ready = false;
   int sms = 0;
+  int append_pairs = 0;   // CTA pairs of the 2-SM append kernel resident at once (0: not used)
   int max_smem_optin = 0;
   int cc_major = 0, cc_minor = 0;
 };
@@ -88,8 +89,24 @@ int device_info(int dev, DeviceInfo* out) {
         cudaFuncSetAttribute(append::draft_append_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(append::Cfg<1>::kSmemBytes)) != cudaSuccess ||
         cudaFuncSetAttribute(append::draft_append_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(append::Cfg<2>::kSmemBytes)) != cudaSuccess)
+                             static_cast<int>(append::Cfg<2>::kSmemBytes)) != cudaSuccess ||
+        cudaFuncSetAttribute(append::draft_append_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(append::PairCfg::kSmemBytes)) != cudaSuccess)
       return DSPARK_ERR_CUDA;
+    {
+      // CTA pairs of the 2-SM append the GPU holds at once (a pair needs two SMs of
+      // one GPC); a refused query leaves the single-CTA kernels in use.
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(static_cast<unsigned>(d.sms & ~1));
+      cfg.blockDim = dim3(append::kThreads);
+      cfg.dynamicSmemBytes = append::PairCfg::kSmemBytes;
+      int clusters = 0;
+      if (cudaOccupancyMaxActiveClusters(&clusters, append::draft_append_pair_kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = 0;
+      }
+      d.append_pairs = clusters < d.sms / 2 ? clusters : d.sms / 2;
+    }
     if (!g_encode) {
       cudaDriverEntryPointQueryResult q;
       void* fn = nullptr;
@@ -803,6 +820,16 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
   // Two heads per tile once those tiles alone fill every SM (prefill-sized appends):
   // each context chunk then feeds twice the MMA work. Smaller appends keep one head
   // per tile, so their few row tiles still spread over the SMs.
+  // Largest appends: 2-SM tiles of 256 rows x 2 heads, once they give every CTA pair
+  // at least two tiles.
+  const long long pair_tiles = static_cast<long long>((p.row_tiles + 1) / 2) * num_layers * 8;
+  if (dev.append_pairs > 0 && pair_tiles >= 2ll * dev.append_pairs && pair_tiles < (1ll << 31)) {
+    p.row_tiles = (p.row_tiles + 1) / 2;
+    p.head_tiles = num_layers * 8;
+    const int grid = 2 * dev.append_pairs;
+    append::draft_append_pair_kernel<<<grid, append::kThreads, append::PairCfg::kSmemBytes, stream>>>(cm, wm, p);
+    return launch_status();
+  }
   const bool pair = static_cast<long long>(p.row_tiles) * num_layers * 8 >= dev.sms;
   p.head_tiles = num_layers * (pair ? 8 : 16);
   const long long tiles = static_cast<long long>(p.row_tiles) * p.head_tiles;

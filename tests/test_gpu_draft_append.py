@@ -46,15 +46,21 @@ def features(g, n, hidden):
                                                                                                 torch.bfloat16)
 
 
-@pytest.mark.parametrize('hidden,layers', [(1024, 5), (256, 2)])
-def test_fused_append_matches_torch_formula(pkg, hidden, layers):
+# (1024, 5) with the 1131-row first append runs the 2-SM kernel (tiles of 256 rows x 2
+# heads over CTA pairs; the last pair tile's second CTA reads past the input rows), the
+# others the single-CTA kernels with one or two heads per tile.
+@pytest.mark.parametrize('hidden,layers,lens,capacity', [
+    (1024, 5, [(1, 37), (300, 5), (129, 128), (2, 0)], 700),
+    (256, 2, [(1, 37), (300, 5), (129, 128), (2, 0)], 700),
+    (1024, 5, [(700, 37), (300, 5), (129, 128), (2, 0)], 1000),
+])
+def test_fused_append_matches_torch_formula(pkg, hidden, layers, lens, capacity):
     draft = build_draft(pkg, hidden, layers)
-    fused = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=700)
-    plain = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=700)
+    fused = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=capacity)
+    plain = pkg.B200PackedDraft(draft, max_requests=4, context_capacity=capacity)
     assert fused._fused_append_ready()
     plain._fused_append_ready = lambda: False
     g = np.random.Generator(np.random.PCG64(5))
-    lens = [(1, 37), (300, 5), (129, 128), (2, 0)]
     for i in range(4):
         for pd in (fused, plain):
             pd.add_request(f'r{i}')
