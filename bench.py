@@ -106,37 +106,65 @@ def query_units(draft_layers=DRAFT['layers'], verify_layers=VERIFY['layers']):
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
+    """nvidia-smi clock samples (every 50 ms) of the GPU this rank drives, kept when they
+    fall inside the `with` block. nvidia-smi takes longer to start than a short timed
+    region lasts, so entering waits (up to 10 s) for its first sample, and leaving waits
+    (up to 1 s) for the first sample after the block, which is kept as well: a region
+    shorter than the sampling period still gets the sample taken at its end."""
     FIELDS = ('index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,'
               'clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,'
               'clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap')
 
     def __init__(self, gpu):
-        self.gpu, self.proc = gpu, None
+        self.gpu, self.proc, self.samples, self.lines = gpu, None, [], []
+        self.t0 = self.t1 = None
+
+    def _read(self):
+        for ln in self.proc.stdout:
+            if ln.strip():
+                self.samples.append((time.monotonic(), ln))
+
+    def _wait_for_sample(self, after, limit):
+        deadline = time.monotonic() + limit
+        while time.monotonic() < deadline:
+            if any(t > after for t, _ in list(self.samples)):
+                return
+            time.sleep(0.01)
 
     def __enter__(self):
+        import threading
         try:
             self.proc = subprocess.Popen(['nvidia-smi', '-i', str(self.gpu), f'--query-gpu={self.FIELDS}',
                                           '--format=csv,noheader,nounits', '-lms', '50'],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
+        if self.proc is not None:
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            self._wait_for_sample(0.0, 10.0)
+        self.t0 = time.monotonic()
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except Exception:
-                self.proc.kill()
-                out = ''
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        self.t1 = time.monotonic()
+        if self.proc is None:
+            return
+        self._wait_for_sample(self.t1, 1.0)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.reader.join(timeout=5)
+        inside = [ln for t, ln in self.samples if self.t0 <= t <= self.t1]
+        after = [ln for t, ln in self.samples if t > self.t1][:1]
+        self.lines = inside + after
 
     def summary(self):
         sm, mx, reasons = [], 0.0, set()
         names = ('hw_slowdown', 'hw_thermal_slowdown', 'sw_thermal_slowdown', 'sw_power_cap')
-        for ln in getattr(self, 'lines', []):
+        for ln in self.lines:
             f = [x.strip() for x in ln.split(',')]
             try:
                 sm.append(float(f[1]))
