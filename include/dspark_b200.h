@@ -335,8 +335,10 @@ int dspark_markov_block(const void* proj_weight, const void* emb_table, int voca
  * with fixed shapes and only the committed rows become visible). pool_k / pool_v:
  * host arrays of num_layers (<= 8) device pointers, each [pool_rows, 8, 128];
  * destination rows outside [0, pool_rows) are skipped and flagged in the device
- * status. Arithmetic follows the reference's bf16 ops (projection output, RMSNorm,
- * weight product, each RoPE product and the sum rounded to bf16).
+ * status. context, kv_weight, k_norm_weight, rope_table and every pool pointer
+ * 16-byte aligned (DSPARK_ERR_INVALID_ARGUMENT otherwise). Arithmetic follows the
+ * reference's bf16 ops (projection output, RMSNorm, weight product, each RoPE
+ * product and the sum rounded to bf16).
  * Replaces PackedDraft.append_committed's per-layer project_kv and cache
  * concatenation (dspark_qwen/packed_draft.py:146-158; model.py:41-45).
  */

@@ -118,8 +118,20 @@ __device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* x) 
 // over the row's 128 values, two of them read from the other half) and rotated
 // with the row's cos/sin, each step rounded as the reference's bf16 ops round.
 // dest < 0: nothing is written (a padding row, or a rejected destination).
+// k_norm weights of one layer, as floats staged in shared memory or as the bf16
+// parameter read from global memory (same values: bf16 -> float is exact).
+struct SmemNormW {
+  const float* w;
+  __device__ __forceinline__ float operator()(int i) const { return w[i]; }
+};
+struct GlobalNormW {
+  const __nv_bfloat16* w;
+  __device__ __forceinline__ float operator()(int i) const { return __bfloat162float(__ldg(w + i)); }
+};
+
+template <typename NormW>
 __device__ __forceinline__ void write_head(const Params& p, uint32_t acc, __nv_bfloat16* out, bool is_v,
-                                           const float* norm_w, int half, const uint4 (&cs4)[8], long long dest) {
+                                           NormW norm_w, int half, const uint4 (&cs4)[8], long long dest) {
   if (is_v) {
 #pragma unroll 1
     for (int c = 0; c < 2; ++c) {
@@ -153,12 +165,11 @@ __device__ __forceinline__ void write_head(const Params& p, uint32_t acc, __nv_b
       ss = fmaf(hi[e], hi[e], ss);
     }
     const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
-    const float* w = norm_w + half * 32;
     if (dest >= 0) {
 #pragma unroll
       for (int e = 0; e < 32; ++e) {
-        const float a = bf16r(w[e] * bf16r(lo[e] * rs));
-        const float bb = bf16r(w[e + 64] * bf16r(hi[e] * rs));
+        const float a = bf16r(norm_w(half * 32 + e) * bf16r(lo[e] * rs));
+        const float bb = bf16r(norm_w(half * 32 + e + 64) * bf16r(hi[e] * rs));
         const uint32_t cw = e % 4 == 0 ? cs4[e / 4].x : e % 4 == 1 ? cs4[e / 4].y : e % 4 == 2 ? cs4[e / 4].z
                                                                                                : cs4[e / 4].w;
         const float2 r = unpack_bf16x2(cw);   // .x cos, .y sin
@@ -168,6 +179,124 @@ __device__ __forceinline__ void write_head(const Params& p, uint32_t acc, __nv_b
       store_row32(out + half * 32, lo);
       store_row32(out + 64 + half * 32, hi);
     }
+  }
+}
+
+// 32 columns of this warp's TMEM lanes into registers, without waiting for them.
+__device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr)
+               : "memory");
+}
+
+// Waits for this thread's TMEM loads. The registers of each load pass through a
+// statement ordered after the wait, so that no use of them is scheduled earlier.
+__device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_ld_landed(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+               : "memory");
+}
+
+// bf16 pair helpers: value 2j in the low half, 2j + 1 in the high half.
+__device__ __forceinline__ float bf_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+// round-to-nearest-even bf16 products of two bf16 pairs (the exact product of two
+// bf16 values fits a float, so this equals the float product rounded to bf16)
+__device__ __forceinline__ uint32_t mul_bf16x2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t perm(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+
+// The epilogue of one head of a tile for this thread's row (TMEM lane), all 128
+// columns: four TMEM loads and one wait. V stored as projected (bf16); K rounded to
+// bf16, k_norm'ed (sum of squares of the row's 128 bf16 values in four partial
+// sums) and rotated with the row's cos/sin, each step rounded as the reference's
+// bf16 ops round: x * rsqrt in float then bf16, the weight and cos/sin products
+// bf16 x bf16 (one rounding), the rotation's sums in float then bf16.
+// w2: the layer's k_norm weight as bf16 pairs; cs: the row's 64 cos|sin words.
+// dest < 0: nothing is written (a padding row, or a rejected destination).
+__device__ __forceinline__ void drain_row(const Params& p, uint32_t acc, __nv_bfloat16* out, bool is_v,
+                                          const uint32_t* w2, const uint4* cs, long long dest) {
+  uint32_t r0[32], r1[32], r2[32], r3[32];
+  if (!is_v) {  // the row's 256 bytes of cos|sin into L1 while TMEM is read
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(cs));
+    asm volatile("prefetch.global.L1 [%0];" ::"l"(cs + 8));
+  }
+  tmem_ld32_async(acc, r0);
+  tmem_ld32_async(acc + 32, r1);
+  tmem_ld32_async(acc + 64, r2);
+  tmem_ld32_async(acc + 96, r3);
+  tmem_ld_wait();
+  tmem_ld_landed(r0);
+  tmem_ld_landed(r1);
+  tmem_ld_landed(r2);
+  tmem_ld_landed(r3);
+  uint32_t pk[64];                             // bf16 pairs (x[2i], x[2i + 1])
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    pk[i] = pack_bf16x2(__uint_as_float(r0[2 * i]), __uint_as_float(r0[2 * i + 1]));
+    pk[16 + i] = pack_bf16x2(__uint_as_float(r1[2 * i]), __uint_as_float(r1[2 * i + 1]));
+    pk[32 + i] = pack_bf16x2(__uint_as_float(r2[2 * i]), __uint_as_float(r2[2 * i + 1]));
+    pk[48 + i] = pack_bf16x2(__uint_as_float(r3[2 * i]), __uint_as_float(r3[2 * i + 1]));
+  }
+  if (!is_v) {
+    float s[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      const float lo = bf_lo(pk[i]), hi = bf_hi(pk[i]);
+      s[i & 3] = fmaf(lo, lo, s[i & 3]);
+      s[i & 3] = fmaf(hi, hi, s[i & 3]);
+    }
+    const float rs = 1.f / sqrtf(((s[0] + s[1]) + (s[2] + s[3])) / 128.f + p.eps);
+    // pairs (2j, 2j + 1) rotate with (2j + 64, 2j + 65); two halves of 16 pairs, each
+    // with its own cos|sin words and weights (the pointers pass through an empty
+    // statement so that the second half's loads are not hoisted over the first half)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint4* csh = cs + 8 * h;                 // words of columns [32 h, 32 h + 32)
+      const uint32_t* wh = w2 + 16 * h;              // weight pairs 16 h.. and 32 + 16 h..
+      asm volatile("" : "+l"(csh), "+l"(wh));
+      uint4 c[8], wa[4], wb[4];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) c[q] = __ldg(csh + q);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        wa[q] = __ldg(reinterpret_cast<const uint4*>(wh) + q);
+        wb[q] = __ldg(reinterpret_cast<const uint4*>(wh + 32) + q);
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; ++jj) {
+        const int j = 16 * h + jj;
+        const uint32_t xa = pk[j], xb = pk[32 + j];
+        const uint32_t ya = pack_bf16x2(bf_lo(xa) * rs, bf_hi(xa) * rs);
+        const uint32_t yb = pack_bf16x2(bf_lo(xb) * rs, bf_hi(xb) * rs);
+        const uint4 ua = wa[jj / 4], ub = wb[jj / 4];
+        const uint32_t wpa = (jj & 3) == 0 ? ua.x : (jj & 3) == 1 ? ua.y : (jj & 3) == 2 ? ua.z : ua.w;
+        const uint32_t wpb = (jj & 3) == 0 ? ub.x : (jj & 3) == 1 ? ub.y : (jj & 3) == 2 ? ub.z : ub.w;
+        const uint32_t a2 = mul_bf16x2(wpa, ya), b2 = mul_bf16x2(wpb, yb);
+        const uint4 cq = c[jj / 2];
+        const uint32_t w0 = (jj & 1) ? cq.z : cq.x, w1 = (jj & 1) ? cq.w : cq.y;   // columns 2j, 2j + 1
+        const uint32_t cos2 = perm(w0, w1, 0x5410u), sin2 = perm(w0, w1, 0x7632u);
+        const uint32_t ac = mul_bf16x2(a2, cos2), bs = mul_bf16x2(b2, sin2);
+        const uint32_t bc = mul_bf16x2(b2, cos2), as = mul_bf16x2(a2, sin2);
+        pk[j] = pack_bf16x2(bf_lo(ac) - bf_lo(bs), bf_hi(ac) - bf_hi(bs));
+        pk[32 + j] = pack_bf16x2(bf_lo(bc) + bf_lo(as), bf_hi(bc) + bf_hi(as));
+      }
+    }
+  }
+  if (dest >= 0) {
+    uint4* d = reinterpret_cast<uint4*>(out);
+#pragma unroll
+    for (int q = 0; q < 16; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
   }
 }
 
@@ -258,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t acc = tmem + lane_addr + b * kAccCols + hh * kHeadCols;
       __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) + (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) +
                            head * kHeadDim;
-      write_head(p, acc, out, is_v, norm_w + layer * kHeadDim, half, cs4, dest);
+      write_head(p, acc, out, is_v, SmemNormW{norm_w + layer * kHeadDim}, half, cs4, dest);
       }
       tc_fence_before();
       mbar_arrive(bar(kBarDFree0 + b));
@@ -342,23 +471,22 @@ __global__ void __launch_bounds__(kThreads, 1)
 // chunk (its half of B, rank r: head 2 ht + r), so every 16 KB of context and
 // 16 KB of weights a CTA streams from L2 feeds 4.2 MFLOP, twice the single-CTA
 // one-head tile. Each CTA's TMEM holds its 128 rows x both heads; its epilogue
-// writes them as the single-CTA kernel does. Rank 0 issues the MMAs; rank 1's
-// copies are relayed to rank 0 by one thread of rank 1 (a bounded wait for each
-// stage, then a remote arrival); MMA completion reaches both CTAs through
-// multicast commits; the epilogue warps of both CTAs release an accumulator on
-// rank 0's barrier. Every wait is bounded and both CTAs meet at a cluster
-// barrier before TMEM is released.
+// writes them. Rank 0 issues the MMAs; both CTAs' copies of a stage count their
+// bytes on rank 0's full barrier (`.cta_group::2` loads, no multicast); MMA
+// completion reaches both CTAs through multicast commits; the epilogue warps of
+// both CTAs release an accumulator on rank 0's barrier. Every wait is bounded
+// and both CTAs meet at a cluster barrier before TMEM is released.
 // ---------------------------------------------------------------------------
 struct PairCfg {
-  static constexpr int kStages = 6;
+  static constexpr int kStages = 7;
   static constexpr uint32_t kStageBytes = 32768;    // own 128-row context chunk + own head's weight chunk
   static constexpr uint32_t kSmemBar = kStages * kStageBytes;
-  enum Barrier { kBarFull0 = 0, kBarPeer0 = kStages, kBarEmpty0 = 2 * kStages, kBarDFull0 = 3 * kStages, kBarDFull1,
+  enum Barrier { kBarFull0 = 0, kBarEmpty0 = kStages, kBarDFull0 = 2 * kStages, kBarDFull1,
                  kBarDFree0, kBarDFree1, kBarDrain, kNumBarriers };
   static constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
   static constexpr uint32_t kSmemAbort = kSmemSlot + 4;
-  static constexpr uint32_t kSmemNormW = kSmemAbort + 12;                 // float [kMaxLayers][128]
-  static constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
+  // (the k_norm weights are read from global memory: seven stages leave no room)
+  static constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 16;
   static constexpr uint32_t kAccCols = 2 * kHeadCols;
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   // fp32 D, bf16 A and B, both K-major, M = 256 (the pair), N = 256
@@ -380,14 +508,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const uint32_t rank = pair::cluster_rank();
   const int pair_id = static_cast<int>(pair::cluster_index()), n_pairs = static_cast<int>(gridDim.x) / 2;
 
-  float* norm_w = reinterpret_cast<float*>(smem + C::kSmemNormW);
   if (threadIdx.x == 0) {
     for (int i = 0; i < C::kNumBarriers; ++i)
       mbar_init(bar(i), (i == C::kBarDFree0 || i == C::kBarDFree1) ? 2u * kEpilogueWarps : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < p.layers * 128; i += kThreads) norm_w[i] = __bfloat162float(p.k_norm_w[i]);
   if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&cmap);
     prefetch_tmap(&wmap);
@@ -429,22 +555,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           }
         }
       }
-      uint4 cs4[8];
-      if (!is_v) {
-        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64 +
-                                                         half * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) cs4[q] = __ldg(cs + q);
-      }
       ok = pair::pair_wait(bar(C::kBarDFull0 + b), (t >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int hh = 0; hh < 2; ++hh) {
-        const uint32_t acc = tmem + lane_addr + b * C::kAccCols + hh * kHeadCols;
+      {  // warp half h drains head 2 ht + h of the tile, whole rows
+        const uint32_t acc = tmem + lane_addr + b * C::kAccCols + half * kHeadCols;
         __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) +
-                             (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) + (head0 + hh) * kHeadDim;
-        write_head(p, acc, out, is_v, norm_w + layer * kHeadDim, half, cs4, dest);
+                             (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) + (head0 + half) * kHeadDim;
+        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64);
+        drain_row(p, acc, out, is_v, reinterpret_cast<const uint32_t*>(p.k_norm_w + layer * kHeadDim), cs, dest);
       }
       // one arrival per warp on rank 0's barrier once the warp's TMEM reads are done
       tc_fence_before();
@@ -463,7 +582,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         tc_fence_after();
         for (int c = 0; c < p.k_chunks; ++c) {
           if (!(ok = pair::pair_wait(bar(C::kBarFull0 + st), ph, abort_flag))) break;
-          if (!(ok = pair::pair_wait(bar(C::kBarPeer0 + st), ph, abort_flag))) break;
           tc_fence_after();
           const uint32_t a = sbase + st * C::kStageBytes, w = a + 16384;
 #pragma unroll
@@ -483,21 +601,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       pair::umma_commit_pair_local(bar(C::kBarDrain));
       volatile int never = 0;
       wait_or_abort(bar(C::kBarDrain), 0, &never);
-    } else if (lane == 0) {
-      // rank 1: relay each landed stage to rank 0's MMA thread
-      bool ok = true;
-      int st = 0;
-      uint32_t ph = 0;
-      for (int t = 0; t < n_mine && ok; ++t)
-        for (int c = 0; c < p.k_chunks; ++c) {
-          if (!(ok = pair::relay_wait(bar(C::kBarFull0 + st), ph, abort_flag))) break;
-          pair::arrive_rank0(bar(C::kBarPeer0 + st));
-          if (++st == C::kStages) {
-            st = 0;
-            ph ^= 1;
-          }
-        }
-      if (!ok) *abort_flag = 1;
     }
     __syncwarp();
   } else {
@@ -511,11 +614,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         const int rt = tile / p.head_tiles, ht = tile - rt * p.head_tiles;
         for (int c = 0; c < p.k_chunks; ++c) {
           if (!(ok = pair::pair_wait(bar(C::kBarEmpty0 + st), ph ^ 1, abort_flag))) break;
-          mbar_arrive_expect_tx(bar(C::kBarFull0 + st), C::kStageBytes);
-          const uint32_t dst = sbase + st * C::kStageBytes;
-          tma_load_2d(dst, &cmap, c * 64, (rt * 2 + static_cast<int>(rank)) * kTileRows, bar(C::kBarFull0 + st));
-          tma_load_2d(dst + 16384, &wmap, c * 64, (ht * 2 + static_cast<int>(rank)) * kHeadCols,
-                      bar(C::kBarFull0 + st));
+          if (rank == 0) mbar_arrive_expect_tx(bar(C::kBarFull0 + st), 2 * C::kStageBytes);
+          const uint32_t dst = sbase + st * C::kStageBytes, full = pair::cluster_addr(bar(C::kBarFull0 + st), 0);
+          pair::tma_load_2d_pair(dst, &cmap, c * 64, (rt * 2 + static_cast<int>(rank)) * kTileRows, full);
+          pair::tma_load_2d_pair(dst + 16384, &wmap, c * 64, (ht * 2 + static_cast<int>(rank)) * kHeadCols, full);
           ++issued;
           if (++st == C::kStages) {
             st = 0;
@@ -530,8 +632,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int s2 = 0; s2 < C::kStages; ++s2) {
         const int armed = issued > s2 ? (issued - 1 - s2) / C::kStages + 1 : 0;
-        if (armed && !pair::pair_wait(bar(C::kBarEmpty0 + s2), (armed - 1) & 1, ok ? &never : abort_flag))
-          wait_or_abort(bar(C::kBarFull0 + s2), (armed - 1) & 1, &never);
+        if (armed && !pair::pair_wait(bar(C::kBarEmpty0 + s2), (armed - 1) & 1, ok ? &never : abort_flag)) {
+          if (rank == 0) {
+            wait_or_abort(bar(C::kBarFull0 + s2), (armed - 1) & 1, &never);
+          } else {
+            // rank 1's copies count on rank 0's barrier: after an abort it cannot see
+            // them land, so it waits 1 ms (copies land in microseconds), once
+            const uint64_t t0 = globaltimer();
+            while (globaltimer() - t0 < 1000000ull) __nanosleep(1000);
+            break;
+          }
+        }
       }
     }
     __syncwarp();

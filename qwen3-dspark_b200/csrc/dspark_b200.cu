@@ -777,7 +777,7 @@ int dspark_draft_append(const void* context, int rows, int hidden, const void* k
       !pool_k || !pool_v || rows < 1 || hidden < 64 || hidden % 64 != 0 || num_layers < 1 ||
       num_layers > append::kMaxLayers || num_requests < 1 || !(eps > 0.f) || pool_rows < 1 ||
       pool_rows >= (1ll << 40) || trash_row < 0 || trash_row >= pool_rows || !aligned(context, 16) ||
-      !aligned(kv_weight, 16) || !aligned(rope_table, 16))
+      !aligned(kv_weight, 16) || !aligned(k_norm_weight, 16) || !aligned(rope_table, 16))
     return DSPARK_ERR_INVALID_ARGUMENT;
   for (int l = 0; l < num_layers; ++l)
     if (!pool_k[l] || !pool_v[l] || !aligned(pool_k[l], 16) || !aligned(pool_v[l], 16))

@@ -4,7 +4,7 @@
 // of two CTAs; rank 0 issues every MMA, whose A rows and accumulator rows are each
 // CTA's own 128 rows and whose B operand is split by N between the two CTAs'
 // shared memory at the same address. No copy here multicasts: each CTA loads its
-// own half with ordinary TMA copies.
+// own half with its own TMA copies, whose bytes may count on rank 0's barrier.
 #pragma once
 #include "train.cuh"
 
@@ -55,37 +55,21 @@ __device__ __forceinline__ void arrive_rank0(uint32_t local) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr(local, 0)) : "memory");
 }
 
+// A 2-D TMA load into this CTA's shared memory whose bytes are counted on an
+// mbarrier of either CTA of the pair (cluster address; `.cta_group::2`, no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, int c0, int c1,
+                                                 uint32_t cluster_bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(c0), "r"(c1), "r"(cluster_bar)
+      : "memory");
+}
+
 // The pair kernel's bounded wait (default .acquire.cta semantics, as for a
 // barrier that only this CTA arrives on).
 __device__ __forceinline__ bool pair_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   return wait_or_abort(bar, parity, abort_flag);
-}
-
-// Bounded wait that sleeps between polls, for threads whose waits are long and
-// not latency-critical (rank 1's relays), so that they leave the issue slots of
-// their SM sub-partition to the warps sharing it.
-__device__ __forceinline__ bool relay_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
-  const unsigned long long t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
-    if (ok) return true;
-    __nanosleep(64);
-    if ((it & 15u) == 15u) {
-      if (*abort_flag) return false;
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        atomicOr(&g_device_status, kStatusWaitTimeout);
-        *abort_flag = 1;
-        return false;
-      }
-    }
-  }
 }
 
 // TMEM of both CTAs at the same columns: one warp of each CTA (the same warp).

@@ -119,6 +119,9 @@ def test_null_arguments_are_refused_before_any_device_work(pkg):
     nul = (ctypes.c_void_p * 1)(None)
     assert lib.dspark_draft_append(fake, 8, 1024, fake, 1, fake, fake, 1e-6, fake, fake, fake, fake, 1, nul, ptrs,
                                    16, 15, None) == 1
+    # the k_norm weights are read as 16-byte vectors
+    assert lib.dspark_draft_append(fake, 8, 1024, fake, 1, ctypes.c_void_p(264), fake, 1e-6, fake, fake, fake, fake, 1, ptrs,
+                                   ptrs, 16, 15, None) == 1
 
 
 def _fixture(pkg):
