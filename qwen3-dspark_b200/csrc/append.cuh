@@ -25,11 +25,12 @@
 //
 // Roles (320 threads, persistent CTAs over (row tile, head tile) pairs; a head
 // tile is kHeads consecutive heads of one layer's K or V, N = 128 kHeads):
-//   warps 0-7  epilogue: warp w reads TMEM lanes 32(w%4).. (tile rows) and writes
-//              half w/4 of each head: d in [32h, 32h+32) and the rotate partners
-//              d + 64, so each RoPE pair is thread-local; for k_norm's sum of
-//              squares it also reads the row's other 64 values (TMEM reads are
-//              cheap, and the two warps never wait on each other);
+//   warps 0-7  epilogue: warp w reads TMEM lanes 32(w%4).. (tile rows); a thread
+//              drains one head of its row, all 128 columns, with four TMEM loads
+//              and one wait (each wait costs about a microsecond while the tensor
+//              pipe is busy), so k_norm's sum and each RoPE pair are thread-local.
+//              With two heads per tile warp half w/4 takes head w/4 of every tile;
+//              with one, the tiles of accumulator w/4 (every other tile);
 //   warp 8     TMEM owner and MMA issuer (one thread), two accumulators of
 //              128 kHeads columns so one tile's epilogue overlaps the next one's
 //              MMAs;
@@ -37,6 +38,7 @@
 //              with one head per tile, four with two).
 // Two heads per tile (large appends: prefill) halve the context bytes streamed
 // from L2 per MMA flop; one head per tile keeps small appends spread over the SMs.
+// The largest appends run the 2-SM version below (tiles of 256 rows x 2 heads).
 #pragma once
 #include "pair.cuh"
 #include "train.cuh"
@@ -51,7 +53,6 @@ using train::tc_fence_after;
 using train::tc_fence_before;
 using train::tmem_alloc;
 using train::tmem_dealloc;
-using train::tmem_ld32;
 using train::umma_bf16;
 using train::umma_commit;
 using train::wait_or_abort;
@@ -73,8 +74,7 @@ struct Cfg {
                  kBarDrain, kNumBarriers };
   static constexpr uint32_t kSmemSlot = kSmemBar + kNumBarriers * 8;
   static constexpr uint32_t kSmemAbort = kSmemSlot + 4;
-  static constexpr uint32_t kSmemNormW = kSmemAbort + 12;                 // float [kMaxLayers][128]
-  static constexpr uint32_t kSmemBytes = 1024 + kSmemNormW + kMaxLayers * 128 * 4;
+  static constexpr uint32_t kSmemBytes = 1024 + kSmemAbort + 16;
   static constexpr uint32_t kAccCols = kHeadCols * kHeads;
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   // fp32 D, bf16 A and B, both K-major, M = 128, N = 128 kHeads
@@ -103,91 +103,18 @@ struct Params {
   float eps;
 };
 
-__device__ __forceinline__ float bf16r(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
-
-__device__ __forceinline__ void store_row32(__nv_bfloat16* dst, const float* x) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
-#pragma unroll
-  for (int q = 0; q < 4; ++q)
-    d[q] = make_uint4(pack_bf16x2(x[8 * q], x[8 * q + 1]), pack_bf16x2(x[8 * q + 2], x[8 * q + 3]),
-                      pack_bf16x2(x[8 * q + 4], x[8 * q + 5]), pack_bf16x2(x[8 * q + 6], x[8 * q + 7]));
-}
-
-// The epilogue of one head of a tile for this thread's row (TMEM lane) and column
-// half: V stored as projected (bf16); K rounded to bf16, k_norm'ed (sum of squares
-// over the row's 128 values, two of them read from the other half) and rotated
-// with the row's cos/sin, each step rounded as the reference's bf16 ops round.
-// dest < 0: nothing is written (a padding row, or a rejected destination).
-// k_norm weights of one layer, as floats staged in shared memory or as the bf16
-// parameter read from global memory (same values: bf16 -> float is exact).
-struct SmemNormW {
-  const float* w;
-  __device__ __forceinline__ float operator()(int i) const { return w[i]; }
-};
-struct GlobalNormW {
-  const __nv_bfloat16* w;
-  __device__ __forceinline__ float operator()(int i) const { return __bfloat162float(__ldg(w + i)); }
-};
-
-template <typename NormW>
-__device__ __forceinline__ void write_head(const Params& p, uint32_t acc, __nv_bfloat16* out, bool is_v,
-                                           NormW norm_w, int half, const uint4 (&cs4)[8], long long dest) {
-  if (is_v) {
-#pragma unroll 1
-    for (int c = 0; c < 2; ++c) {
-      float d[32];
-      tmem_ld32(acc + half * 64 + c * 32, d);
-      if (dest >= 0) store_row32(out + half * 64 + c * 32, d);
-    }
-  } else {
-    // k_proj output (bf16) of d in [32 half, +32) and of the partners d + 64;
-    // the row's other 64 values (the other warp's) are read too, for the sum
-    float lo[32], hi[32];
-    float ss = 0.f;
-    {
-      float o1[32], o2[32];
-      tmem_ld32(acc + (half ^ 1) * 32, o1);
-      tmem_ld32(acc + 64 + (half ^ 1) * 32, o2);
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float x1 = bf16r(o1[e]), x2 = bf16r(o2[e]);
-        ss = fmaf(x1, x1, ss);
-        ss = fmaf(x2, x2, ss);
-      }
-    }
-    tmem_ld32(acc + half * 32, lo);
-    tmem_ld32(acc + 64 + half * 32, hi);
-#pragma unroll
-    for (int e = 0; e < 32; ++e) {
-      lo[e] = bf16r(lo[e]);
-      hi[e] = bf16r(hi[e]);
-      ss = fmaf(lo[e], lo[e], ss);
-      ss = fmaf(hi[e], hi[e], ss);
-    }
-    const float rs = 1.f / sqrtf(ss / 128.f + p.eps);
-    if (dest >= 0) {
-#pragma unroll
-      for (int e = 0; e < 32; ++e) {
-        const float a = bf16r(norm_w(half * 32 + e) * bf16r(lo[e] * rs));
-        const float bb = bf16r(norm_w(half * 32 + e + 64) * bf16r(hi[e] * rs));
-        const uint32_t cw = e % 4 == 0 ? cs4[e / 4].x : e % 4 == 1 ? cs4[e / 4].y : e % 4 == 2 ? cs4[e / 4].z
-                                                                                               : cs4[e / 4].w;
-        const float2 r = unpack_bf16x2(cw);   // .x cos, .y sin
-        lo[e] = bf16r(bf16r(a * r.x) + bf16r(-bb * r.y));
-        hi[e] = bf16r(bf16r(bb * r.x) + bf16r(a * r.y));
-      }
-      store_row32(out + half * 32, lo);
-      store_row32(out + 64 + half * 32, hi);
-    }
-  }
-}
-
 // 32 columns of this warp's TMEM lanes into registers, without waiting for them.
 __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32]) {
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-               : "r"(taddr)
-               : "memory");
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      :
+        "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
 }
 
 // Waits for this thread's TMEM loads. The registers of each load pass through a
@@ -195,7 +122,12 @@ __device__ __forceinline__ void tmem_ld32_async(uint32_t taddr, uint32_t (&r)[32
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_ld_landed(uint32_t (&r)[32]) {
   asm volatile(""
-               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
+               :
+                 "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                 "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]),
+                 "+r"(r[15]), "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]),
+                 "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]),
+                 "+r"(r[29]), "+r"(r[30]), "+r"(r[31])
                :
                : "memory");
 }
@@ -307,7 +239,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = Cfg<kHeads>;
   constexpr int kStages = C::kStages;
   constexpr uint32_t kStageBytes = C::kStageBytes, kSmemBar = C::kSmemBar, kSmemSlot = C::kSmemSlot;
-  constexpr uint32_t kSmemAbort = C::kSmemAbort, kSmemNormW = C::kSmemNormW, kTmemCols = C::kTmemCols;
+  constexpr uint32_t kSmemAbort = C::kSmemAbort, kTmemCols = C::kTmemCols;
   constexpr uint32_t kAccCols = C::kAccCols;
   constexpr int kBarFull0 = C::kBarFull0, kBarEmpty0 = C::kBarEmpty0, kBarDFull0 = C::kBarDFull0;
   constexpr int kBarDFree0 = C::kBarDFree0, kBarDFree1 = C::kBarDFree1, kBarDrain = C::kBarDrain;
@@ -320,15 +252,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kSmemAbort);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  constexpr uint32_t kEpiThreads = kEpilogueWarps * 32;
-  float* norm_w = reinterpret_cast<float*>(smem + kSmemNormW);
+  // threads that release an accumulator: all epilogue threads with two heads per
+  // tile (warp half h drains head h), half of them with one (warp half h drains
+  // the tiles of accumulator h)
+  constexpr uint32_t kFreeThreads = kEpilogueWarps * 32 / (kHeads == 1 ? 2 : 1);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kNumBarriers; ++i)
-      mbar_init(bar(i), (i == kBarDFree0 || i == kBarDFree1) ? kEpiThreads : 1u);
+      mbar_init(bar(i), (i == kBarDFree0 || i == kBarDFree1) ? kFreeThreads : 1u);
     *abort_flag = 0;
     fence_barrier_init();
   }
-  for (int i = threadIdx.x; i < p.layers * 128; i += kThreads) norm_w[i] = __bfloat162float(p.k_norm_w[i]);
   if (warp == kTmaWarp && lane == 0) {
     prefetch_tmap(&cmap);
     prefetch_tmap(&wmap);
@@ -350,7 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int cur_rt = -1;
     long long dest = -1;
     int g = 0;
-    for (int t = 0; t < n_mine; ++t) {
+    for (int t = kHeads == 1 ? half : 0; t < n_mine; t += kHeads == 1 ? 2 : 1) {
       const int b = t & 1;
       const int tile = static_cast<int>(blockIdx.x) + t * static_cast<int>(gridDim.x);
       const int rt = tile / p.head_tiles, ht = (tile - rt * p.head_tiles) * kHeads;   // first head tile
@@ -369,25 +302,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      // this row's cos/sin for d in [32 half, 32 half + 32), fetched before the wait
-      // (the same for every head of the tile)
-      uint4 cs4[8];
-      if (!is_v) {
-        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64 +
-                                                         half * 32);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) cs4[q] = __ldg(cs + q);
-      }
       ok = wait_or_abort(bar(kBarDFull0 + b), (t >> 1) & 1, abort_flag);
       if (!__all_sync(0xffffffffu, ok)) break;
       tc_fence_after();
-#pragma unroll 1
-      for (int hh = 0; hh < kHeads; ++hh) {
-      const int head = head0 + hh;
-      const uint32_t acc = tmem + lane_addr + b * kAccCols + hh * kHeadCols;
-      __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) + (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) +
-                           head * kHeadDim;
-      write_head(p, acc, out, is_v, SmemNormW{norm_w + layer * kHeadDim}, half, cs4, dest);
+      {
+        const int hh = kHeads == 1 ? 0 : half;
+        const uint32_t acc = tmem + lane_addr + b * kAccCols + hh * kHeadCols;
+        __nv_bfloat16* out = (is_v ? p.pool_v[layer] : p.pool_k[layer]) +
+                             (dest < 0 ? 0 : dest) * (kKVHeads * kHeadDim) + (head0 + hh) * kHeadDim;
+        const uint4* cs = reinterpret_cast<const uint4*>(p.rope + static_cast<size_t>(g < p.rows ? g : 0) * 64);
+        drain_row(p, acc, out, is_v, reinterpret_cast<const uint32_t*>(p.k_norm_w + layer * kHeadDim), cs, dest);
       }
       tc_fence_before();
       mbar_arrive(bar(kBarDFree0 + b));
