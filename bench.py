@@ -657,6 +657,8 @@ def accept_leg(pkg, device, warmup, iters=20, vocab=151936):
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
     for _ in range(warmup):
         pkg.greedy_accept(logits, tokens, cu, eos, budget)
+    torch.cuda.synchronize(device)
+    torch.cuda._sleep(4_000_000)            # every launch below is enqueued before it runs: device time only
     pairs = []
     for _ in range(iters):
         flush.zero_()                       # L2 written over: no logits carried over from the last round
