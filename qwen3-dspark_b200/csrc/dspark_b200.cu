@@ -932,7 +932,16 @@ int dspark_stochastic_propose(const void* base, long long ld_base, const int32_t
   p.tokens = tokens;
   p.status = status;
   p.rows = rows;
-  sampling::propose_law_kernel<<<rows, sampling::kThreads, 0, stream>>>(p);
+  // Two CTAs per row (a cluster) when twice the rows still fit the SMs at once and
+  // each half of the row fits the per-CTA tile totals; one CTA per row otherwise.
+  DeviceInfo dev;
+  st = current_device_info(&dev);
+  if (st != DSPARK_OK) return st;
+  const long long tiles = (static_cast<long long>(vocab) + sampling::kThreads * 8 - 1) / (sampling::kThreads * 8);
+  if (2ll * rows <= dev.sms && (tiles + 1) / 2 <= sampling::kPairMaxTiles)
+    sampling::propose_law_pair_kernel<<<2 * rows, sampling::kThreads, 0, stream>>>(p);
+  else
+    sampling::propose_law_kernel<<<rows, sampling::kThreads, 0, stream>>>(p);
   return launch_status();
 }
 

@@ -17,6 +17,7 @@
 // in the reference's draw order; a residual or bonus sample is a CTA-wide pass
 // (mass, then a chunked CDF scan). All arithmetic is float64.
 #pragma once
+#include "pair.cuh"
 #include "ptx.cuh"
 
 namespace dspark {
@@ -545,6 +546,221 @@ __global__ void __launch_bounds__(kThreads) propose_law_kernel(const ProposePara
     p.tokens[r] = found < p.vocab ? found : (last_pos >= 0 ? last_pos : 0);
     p.status[r] = bad || last_pos < 0 ? kBadLogits : kOk;
   }
+}
+
+
+// The same proposal with each request row split between a cluster of two CTAs, so
+// that a launch of few rows (64 requests) fills twice the SMs. Rank 0 takes the
+// row's first ceil(tiles / 2) tiles of kThreads * 8 values, rank 1 the rest; after
+// each pass the two partial results (max and bad flag, sum, sum of normalised
+// weights) cross through shared memory and both CTAs combine them in rank order,
+// so both hold the same statistics. The law pass records each tile's total; rank 1
+// starts its CDF from rank 0's total, which is the running CDF the one-CTA kernel
+// carries at that tile, and each CTA scans again only the tile holding the crossing
+// of u (values formed as in the law pass, the same scan), so the draw follows the
+// same CDF association as the one-CTA kernel.
+constexpr int kPairMaxTiles = 64;     // tiles per CTA (vocabularies up to 128 tiles)
+
+__device__ __forceinline__ double ld_cluster_f64(const double* local, uint32_t rank) {
+  double v;
+  asm volatile("ld.shared::cluster.f64 %0, [%1];" : "=d"(v) : "r"(pair::cluster_addr(smem_u32(local), rank))
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ int ld_cluster_s32(const int* local, uint32_t rank) {
+  int v;
+  asm volatile("ld.shared::cluster.s32 %0, [%1];" : "=r"(v) : "r"(pair::cluster_addr(smem_u32(local), rank))
+               : "memory");
+  return v;
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads) propose_law_pair_kernel(const ProposeParams p) {
+  __shared__ double dscr[kThreads / 32];
+  __shared__ int iscr[kThreads / 32];
+  __shared__ double chunk_sum[kThreads];
+  __shared__ double tile_total[kPairMaxTiles];
+  __shared__ double xd[4];    // crossing the cluster: max, sum, sum of normalised weights, CDF total
+  __shared__ int xi[3];       // crossing the cluster: bad flag, last positive index, draw
+  const uint32_t rank = pair::cluster_rank();
+  const int r = static_cast<int>(blockIdx.x >> 1);   // the grid is exactly two CTAs per row
+  const long long row = p.row_index ? p.row_index[r] : r;
+  const unsigned short* br = p.base + row * p.ld_base;
+  const unsigned short* pr = p.proj + static_cast<long long>(r) * p.ld_proj;
+  double* law = p.law + row * p.ld_law;
+  constexpr int kTile = kThreads * 8;
+  const int ntiles = (p.vocab + kTile - 1) / kTile;
+  const int split = min(p.vocab, ((ntiles + 1) / 2) * kTile);
+  const int lo = rank == 0 ? 0 : split, hi = rank == 0 ? split : p.vocab;
+  const bool vec = ((reinterpret_cast<uintptr_t>(br) | reinterpret_cast<uintptr_t>(pr)) & 15) == 0;
+  auto scaled8 = [&](int i0, double (&x)[8]) {      // x / T of elements i0 .. i0 + 7 (0 past the row)
+    if (vec && i0 + 8 <= p.vocab) {
+      const uint4 ra = __ldg(reinterpret_cast<const uint4*>(br + i0));
+      const uint4 rb = __ldg(reinterpret_cast<const uint4*>(pr + i0));
+      const unsigned short* ha = reinterpret_cast<const unsigned short*>(&ra);
+      const unsigned short* hb = reinterpret_cast<const unsigned short*>(&rb);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = __ldg(p.scaled + add_bf16_bits(ha[e], hb[e]));
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) x[e] = i0 + e < p.vocab ? p.scaled[add_bf16_bits(br[i0 + e], pr[i0 + e])] : 0.0;
+    }
+  };
+  // pass 1: max of x / T and non-finite values
+  int bad = 0;
+  double m = -INFINITY;
+  for (int i0 = lo + threadIdx.x * 8; i0 < hi; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) {
+        if (!isfinite(x[e])) bad = 1;
+        m = x[e] > m ? x[e] : m;
+      }
+  }
+  bad = block_reduce(bad, iscr, OrOp());
+  m = block_reduce(m, dscr, MaxOp());
+  if (threadIdx.x == 0) {
+    xd[0] = m;
+    xi[0] = bad;
+  }
+  pair::cluster_sync();
+  m = MaxOp()(ld_cluster_f64(&xd[0], 0), ld_cluster_f64(&xd[0], 1));
+  bad = ld_cluster_s32(&xi[0], 0) | ld_cluster_s32(&xi[0], 1);
+  // pass 2: sum of exp(x / T - max)
+  double sum = 0.0;
+  for (int i0 = lo + threadIdx.x * 8; i0 < hi; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) sum += exp(x[e] - m);
+  }
+  sum = block_reduce(sum, dscr, SumOp());
+  if (threadIdx.x == 0) xd[1] = sum;
+  pair::cluster_sync();
+  sum = ld_cluster_f64(&xd[1], 0) + ld_cluster_f64(&xd[1], 1);
+  // pass 3: sum of the normalised weights
+  double sum2 = 0.0;
+  for (int i0 = lo + threadIdx.x * 8; i0 < hi; i0 += kTile) {
+    double x[8];
+    scaled8(i0, x);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (i0 + e < p.vocab) sum2 += exp(x[e] - m) / sum;
+  }
+  sum2 = block_reduce(sum2, dscr, SumOp());
+  if (threadIdx.x == 0) xd[2] = sum2;
+  pair::cluster_sync();
+  sum2 = ld_cluster_f64(&xd[2], 0) + ld_cluster_f64(&xd[2], 1);
+  // One tile's values (written to the law when `store`), this thread's 8-value sum and
+  // the CTA-wide exclusive prefix of those sums; returns the tile's total.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const bool law16 = (reinterpret_cast<uintptr_t>(law) & 15) == 0;
+  int last_pos = -1;
+  auto tile = [&](int t0, bool store, double (&v)[8], double& seg, double& excl) {
+    const int i0 = t0 + threadIdx.x * 8;
+    seg = 0.0;
+    if (i0 < hi) {
+      double x[8];
+      scaled8(i0, x);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        v[e] = i0 + e < p.vocab ? exp(x[e] - m) / sum / sum2 : 0.0;
+        seg += v[e];
+        if (v[e] > 0.0) last_pos = i0 + e;
+      }
+      if (store) {
+        if (law16 && i0 + 8 <= p.vocab) {
+#pragma unroll
+          for (int e = 0; e < 8; e += 2) *reinterpret_cast<double2*>(law + i0 + e) = make_double2(v[e], v[e + 1]);
+        } else {
+          for (int e = 0; i0 + e < p.vocab; ++e) law[i0 + e] = v[e];
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[e] = 0.0;
+    }
+    double incl = seg;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const double n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) chunk_sum[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      double w = lane < kThreads / 32 ? chunk_sum[lane] : 0.0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const double n = __shfl_up_sync(0xffffffffu, w, o);
+        if (lane >= o) w += n;
+      }
+      chunk_sum[32 + lane] = w;                       // inclusive warp prefixes
+    }
+    __syncthreads();
+    excl = (warp > 0 ? chunk_sum[32 + warp - 1] : 0.0) + incl - seg;
+    const double total = chunk_sum[32 + kThreads / 32 - 1];
+    __syncthreads();                                  // chunk_sum is rewritten by the next tile
+    return total;
+  };
+  // pass 4: the law of this CTA's tiles, each tile's total recorded
+  int my_tiles = 0;
+  double carry = 0.0;
+  for (int t0 = lo; t0 < hi; t0 += kTile, ++my_tiles) {
+    double v[8], seg, excl;
+    const double total = tile(t0, true, v, seg, excl);
+    if (threadIdx.x == 0) tile_total[my_tiles] = total;
+    carry += total;
+  }
+  last_pos = block_reduce(last_pos, iscr, MaxIntOp());
+  if (threadIdx.x == 0) {
+    xd[3] = carry;
+    xi[1] = last_pos;
+  }
+  pair::cluster_sync();
+  // (kept apart from last_pos, which the rescans below update per thread)
+  const int last_all = max(ld_cluster_s32(&xi[1], 0), ld_cluster_s32(&xi[1], 1));
+  // the draw: the first element whose CDF exceeds u, searched in the tiles whose
+  // running total can reach it (the CDF of rank 1 starts at rank 0's total)
+  const double u = p.uniforms[r];
+  int found = p.vocab;
+  carry = rank == 0 ? 0.0 : ld_cluster_f64(&xd[3], 0);
+  for (int k = 0; k < my_tiles; ++k) {
+    if (carry + tile_total[k] > u - 1e-12) {
+      double v[8], seg, excl;
+      tile(lo + k * kTile, false, v, seg, excl);
+      const int i0 = lo + k * kTile + threadIdx.x * 8;
+      int f = p.vocab;
+      double cdf = carry + excl;
+      if (cdf + seg > u - 1e-12) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          cdf += v[e];
+          if (cdf > u && i0 + e < p.vocab) {
+            f = i0 + e;
+            break;
+          }
+        }
+      }
+      f = block_reduce(f, iscr, MinIntOp());
+      if (f < p.vocab) {
+        found = f;
+        break;
+      }
+    }
+    carry += tile_total[k];
+  }
+  if (threadIdx.x == 0) xi[2] = found;
+  pair::cluster_sync();
+  if (rank == 0 && threadIdx.x == 0) {
+    found = min(ld_cluster_s32(&xi[2], 0), ld_cluster_s32(&xi[2], 1));
+    p.tokens[r] = found < p.vocab ? found : (last_all >= 0 ? last_all : 0);
+    p.status[r] = bad || last_all < 0 ? kBadLogits : kOk;
+  }
+  pair::cluster_sync();                               // rank 1's shared memory is read until here
 }
 
 }  // namespace sampling

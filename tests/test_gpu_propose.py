@@ -19,11 +19,13 @@ def torch_formula(pkg, base, proj, temperature, uniforms):
     return pkg.sample_rows(law, uniforms), law
 
 
-@pytest.mark.parametrize('vocab,temperature', [(151936, 0.8), (151936, 1.3), (1000, 1.0), (997, 0.6)])
-def test_law_and_token_equal_the_torch_formula(pkg, vocab, temperature):
+# 24 rows run two CTAs per row (a cluster; with vocab 1000 / 997 the second CTA's half
+# is empty), 100 rows one CTA per row (twice the rows would not fit the SMs at once).
+@pytest.mark.parametrize('vocab,temperature,n', [(151936, 0.8, 24), (151936, 1.3, 24), (1000, 1.0, 24),
+                                                 (997, 0.6, 24), (151936, 0.8, 100)])
+def test_law_and_token_equal_the_torch_formula(pkg, vocab, temperature, n):
     g = torch.Generator(device=dev())
-    g.manual_seed(vocab + int(temperature * 10))
-    n = 24
+    g.manual_seed(vocab + int(temperature * 10) + n)
     # strided base / law rows (every other row of a larger buffer), row indices reversed
     base_buf = (torch.randn((2 * n, vocab), generator=g, device=dev()) * 3).to(torch.bfloat16)
     base = base_buf[::2]
